@@ -1,0 +1,365 @@
+"""Verify-step benchmark (driver contract: one JSON line from rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                    [--workload accept]
+
+Default workload: BASELINE config 2, the acceptance microbench (B=64 sequences,
+k=8 draft tokens, V=32000, fp32 logits, T=0.8, target ~ N(0,2^2), draft =
+target + N(0,0.5^2)).  A step is one fused acceptance launch over one batch:
+vocabulary softmax statistics for the 9 target and 8 draft rows of every
+sequence, accept/reject, and the residual / bonus draw.  Inputs are resident in
+HBM; two input sets (2 x 139 MB > 126 MB L2) alternate so no step reads a
+cache warmed by the previous one.
+
+value  = accepted tokens/s over all ranks = sum_b (accepted_len_b + 1) per
+         step / device time (CUDA events, max over ranks);
+e2e    = the same metric through the host-buffer C ABI call velo_cuda_accept
+         (pinned host inputs copied in, results copied back, every step);
+roofline: algorithmic bytes (every logit read once) / kernel time vs the
+         measured HBM copy bandwidth;
+cpu_baseline: the CPU port of the same step (oracle/) on this host's cores.
+
+Multi-GPU: one process per GPU (torchrun), each rank runs its own batch (data
+parallel over sequences, no collective on the data path): "scaling": "weak".
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "velo-core_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+import numpy as np  # noqa: E402
+
+BASELINE_METRIC = "accepted tokens/sec & µs per verify step (device-timed) at 1/2/4/8 B200"
+HBM_FALLBACK_GBS = 6650.0
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+def load_traffic(name):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu
+    summary (profiles/<name>.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", name + ".json")) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while running."""
+
+    def __init__(self, device_index, period=0.02):
+        self.samples = []
+        self.period = period
+        self.idx = device_index
+        self._stop = threading.Event()
+        self._t = None
+        self.max_mhz = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+            return self
+        self._sample()
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def _sample(self):
+        nv = self._nv
+        try:
+            mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+            reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            self.samples.append((mhz, reasons))
+        except Exception:
+            pass
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def __exit__(self, *a):
+        if self._nv is None:
+            return
+        self._stop.set()
+        if self._t:
+            self._t.join()
+        self._sample()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        nv = self._nv
+        names = {
+            "gpu_idle": getattr(nv, "nvmlClocksEventReasonGpuIdle", 0x1),
+            "sw_power_cap": getattr(nv, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_slowdown": getattr(nv, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "sw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "hw_thermal_slowdown": getattr(nv, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "hw_power_brake_slowdown": getattr(nv, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+        seen = set()
+        for _, r in self.samples:
+            for n, bit in names.items():
+                if r & bit and n != "gpu_idle":
+                    seen.add(n)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(seen),
+                "samples": len(self.samples)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def accepted_tokens(acc):
+    return int(np.sum(acc.astype(np.int64) + 1))
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args):
+    """CPU implementation of the same step (the oracle port of the reference's
+    CPU path + the acceptance spec) on this host's cores."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import vo
+    import synthetic
+    threads = os.cpu_count() or 1
+    B, k, V, T = 64, 8, 32000, 0.8
+    tgt, drf, tok, u = synthetic.acceptance_inputs(B, k, V, T)
+    # size each step so the whole run stays within ~2 minutes
+    t0 = time.perf_counter()
+    vo.accept(tgt[:8], drf[:8], tok[:8], u[:8], T, n_threads=threads)
+    per_seq = (time.perf_counter() - t0) / 8
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    bs = int(max(1, min(B, budget / max(per_seq, 1e-9))))
+    toks, secs = 0, 0.0
+    for s in range(args.warmup + args.steps):
+        lo = (s * bs) % B
+        idx = np.arange(lo, lo + bs) % B
+        t0 = time.perf_counter()
+        acc, _ = vo.accept(tgt[idx], drf[idx], tok[idx], u[idx], T, n_threads=threads)
+        dt = time.perf_counter() - t0
+        if s >= args.warmup:
+            toks += accepted_tokens(acc)
+            secs += dt
+    value = toks / secs
+    line = {
+        "impl": "reference", "metric": BASELINE_METRIC, "value": value,
+        "unit": "accepted tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * secs / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Philox, BASELINE config 2 distributions)",
+        "config": {"workload": "acceptance microbench (BASELINE config 2)", "B": B, "k": k,
+                   "V": V, "temperature": T, "parallelism": "replicas"},
+        "cpu_baseline": {"value": value, "unit": "accepted tokens/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"{bs} of {B} sequences per step (k=8, V=32000), "
+                                   f"{threads} threads over sequences"},
+        "e2e": {"value": value, "unit": "accepted tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- CUDA arm
+def run_cuda(args):
+    import torch
+    import torch.distributed as dist
+    import synthetic
+    import velo_cuda
+
+    ws, rank, local = dist_env()
+    if args.gpus != ws and ws > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {ws}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    B, k, V, T = 64, 8, 32000, 0.8
+    n_sets = 2
+    sets = []
+    for sidx in range(n_sets):
+        tgt, drf, tok, u = synthetic.acceptance_inputs(B, k, V, T, seed=rank * 16 + sidx)
+        sets.append(tuple(torch.from_numpy(a).to(dev) for a in
+                          (tgt, drf, tok.view(np.int32), u)))
+    acc = torch.empty(B, dtype=torch.int32, device=dev)
+    bonus = torch.empty(B, dtype=torch.int32, device=dev)
+    ctx = velo_cuda.Context(device=local)
+    stream = torch.cuda.current_stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+
+    def step(i):
+        t, d, tk, uu = sets[i % n_sets]
+        ctx.accept_device(t, d, tk, uu, T, acc, bonus)
+
+    # accepted tokens per step of each input set (deterministic)
+    tok_per_set = []
+    for sidx in range(n_sets):
+        step(sidx)
+        torch.cuda.synchronize()
+        tok_per_set.append(accepted_tokens(acc.cpu().numpy()))
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps):
+            step(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    toks = sum(tok_per_set[i % n_sets] for i in range(args.steps))
+    if ws > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        tt = torch.tensor([toks], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+        toks = float(tt.item())
+    ms_per_step = ms / args.steps
+    value = toks / (ms / 1e3)
+
+    # ---- e2e through the host-buffer C ABI (pinned host memory) ----------
+    host = []
+    for sidx in range(n_sets):
+        hs = []
+        for a in sets[sidx]:
+            h = torch.empty(a.shape, dtype=a.dtype, pin_memory=True)
+            h.copy_(a)
+            hs.append(h.numpy())
+        host.append(hs)
+    ctx.set_stream(None)
+    e2e_steps = max(3, min(args.steps, 50))
+    for i in range(2):
+        t, d, tk, uu = host[i % n_sets]
+        ctx.accept(t, d, tk.view(np.uint32), uu, T)
+    if ws > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    e2e_toks = 0
+    for i in range(e2e_steps):
+        t, d, tk, uu = host[i % n_sets]
+        a, _ = ctx.accept(t, d, tk.view(np.uint32), uu, T)
+        e2e_toks += accepted_tokens(a)
+    e2e_s = time.perf_counter() - t0
+    if ws > 1:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+        tt = torch.tensor([e2e_toks], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+        e2e_toks = float(tt.item())
+    h2d = sum(x.nbytes for x in host[0])
+    d2h = 2 * B * 4
+
+    line = None
+    if rank == 0:
+        peak, peak_kind = load_peaks()
+        alg_bytes = B * V * 4 * ((k + 1) + k)  # every logit read once
+        achieved = alg_bytes / (ms_per_step * 1e-3) / 1e9
+        clocks = clk.summary()
+        line = {
+            "metric": BASELINE_METRIC, "value": value, "unit": "accepted tokens/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "us_per_step": ms_per_step * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Philox, BASELINE config 2 distributions)",
+            "config": {"workload": "acceptance microbench (BASELINE config 2)", "B": B, "k": k,
+                       "V": V, "temperature": T,
+                       "l2": "2 alternating input sets of 139 MB (> 126 MB L2)",
+                       "parallelism": f"replicas x{ws} (sequences sharded, no collective)"},
+            "accepted_per_step": toks / args.steps / ws,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": load_traffic("accept_c2"),
+                         "algorithmic_bytes": alg_bytes, "kernel": "accept_kernel<false>"},
+            "clocks": clocks,
+            "e2e": {"value": e2e_toks / e2e_s, "unit": "accepted tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "ms_per_step": 1e3 * e2e_s / e2e_steps},
+            "gpu_launches": args.steps,
+        }
+    ctx.close()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_baseline():
+    """The CPU port (oracle) on this host, full C2 batch repeated ~10 s."""
+    import vo
+    import synthetic
+    threads = os.cpu_count() or 1
+    B, k, V, T = 64, 8, 32000, 0.8
+    tgt, drf, tok, u = synthetic.acceptance_inputs(B, k, V, T)
+    toks, secs, reps = 0, 0.0, 0
+    while secs < 10.0 or reps < 1:
+        t0 = time.perf_counter()
+        acc, _ = vo.accept(tgt, drf, tok, u, T, n_threads=threads)
+        secs += time.perf_counter() - t0
+        toks += accepted_tokens(acc)
+        reps += 1
+    return {"value": toks / secs, "unit": "accepted tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} full steps of config 2 (64 sequences, k=8, V=32000), "
+                      f"{threads} threads over sequences, {secs:.1f} s"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
+    ap.add_argument("--workload", default="accept", choices=["accept"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_cuda(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

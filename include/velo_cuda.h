@@ -1,0 +1,138 @@
+/*
+ * velo_cuda.h -- C ABI of the B200 (sm_100a) speculative-decoding verify step.
+ *
+ * This is the drop-in boundary a velo-core backend binds with `extern "C"`
+ * (see INTEGRATION.md for the Rust side).  Plain pointers and sizes only; no
+ * CUDA or torch types appear in any signature.  Device pointers are passed as
+ * `void*` / typed pointers to device memory and are documented as such.
+ *
+ * Conventions (mirroring the reference):
+ *   - Every entry returns velo_status (int32): 0 = OK.  Codes mirror
+ *     SpeculativeError (src/speculative.rs:294-305) and PageManagerError
+ *     (src/paged_attention.rs:72-79).  velo_cuda_last_error() returns the
+ *     message of the last failure on the calling thread.
+ *   - Host arrays are caller-owned and only read (inputs) or written
+ *     (outputs) during the call.  Output arrays are caller-allocated.
+ *   - A context owns one CUDA stream and its device buffers.  Contexts are not
+ *     thread-safe (the reference backends take `&mut self`).
+ */
+#ifndef VELO_CUDA_H
+#define VELO_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VELO_CUDA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define VELO_API __attribute__((visibility("default")))
+#else
+#define VELO_API
+#endif
+
+typedef enum velo_status {
+    VELO_OK = 0,
+    VELO_ERR_INVALID_ARGUMENT = 1,     /* SpeculativeError::Model("...") for bad input */
+    VELO_ERR_EMPTY_DRAFT_WINDOW = 2,   /* SpeculativeError::EmptyDraftWindow */
+    VELO_ERR_DRAFT_TOO_MANY = 3,       /* SpeculativeError::DraftReturnedTooMany */
+    VELO_ERR_TARGET_WRONG_LENGTH = 4,  /* SpeculativeError::TargetReturnedWrongLength */
+    VELO_ERR_OUT_OF_PAGES = 5,         /* PageManagerError::OutOfPages */
+    VELO_ERR_UNKNOWN_HANDLE = 6,       /* PageManagerError::UnknownHandle */
+    VELO_ERR_INVALID_BLOCK_SIZE = 7,   /* PageManagerError::InvalidBlockSize */
+    VELO_ERR_CUDA = 8,                 /* a CUDA runtime call failed */
+    VELO_ERR_NO_DEVICE = 9,            /* no usable sm_100 device */
+    VELO_ERR_TIMEOUT = 10,             /* velo_cuda_sync deadline passed */
+    VELO_ERR_OUT_OF_MEMORY = 11,
+    VELO_ERR_NCCL = 12,
+    VELO_ERR_DEVICE_FLAG = 13          /* a kernel reported a bad input on device */
+} velo_status;
+
+typedef struct velo_cuda_ctx velo_cuda_ctx;
+
+/* Mirrors MemoryRuntimeConfig (src/runtime.rs:46-61) / EngineConfig
+ * (src/engine.rs:60-67) / MetalBackendConfig (src/metal/config.rs:7-22) for
+ * what the verify step needs.  Zero fields take the defaults in brackets. */
+typedef struct velo_cuda_config {
+    uint32_t struct_size;  /* sizeof(velo_cuda_config) */
+    uint32_t page_size;    /* tokens per KV page [16] (PagedAttentionConfig::block_size) */
+    uint32_t kv_dtype;     /* velo_kv_dtype [VELO_KV_F16] */
+    uint32_t max_slots;    /* page-table rows [1] */
+    uint32_t total_pages;  /* pages in the pool [0: no KV pool] */
+    uint32_t max_pages_per_slot; /* page-table width [total_pages] */
+} velo_cuda_config;
+
+typedef enum velo_kv_dtype { VELO_KV_F16 = 0, VELO_KV_INT8 = 1 } velo_kv_dtype;
+
+/* ---- lifecycle ---------------------------------------------------------- */
+
+/* Create a context on `device` (CUDA ordinal).  tp_rank / tp_size give the
+ * tensor-parallel position (1 GPU: 0 / 1); nccl_unique_id (128 bytes) is
+ * required when tp_size > 1 and ignored otherwise.
+ * Replaces constructing MetalMemoryRuntime + MetalBackend
+ * (src/metal/runtime.rs, src/metal/backend.rs:115-286). */
+VELO_API int32_t velo_cuda_create(const velo_cuda_config *cfg, int32_t device, int32_t tp_rank,
+                         int32_t tp_size, const void *nccl_unique_id,
+                         velo_cuda_ctx **out);
+VELO_API void velo_cuda_destroy(velo_cuda_ctx *ctx);
+
+/* Message of the last failure on the calling thread ("" if none). */
+VELO_API const char *velo_cuda_last_error(void);
+VELO_API int32_t velo_cuda_abi_version(void);
+
+/* Use `stream` (a cudaStream_t, may be NULL for the context's own stream) for
+ * all following asynchronous work of this context. */
+VELO_API int32_t velo_cuda_set_stream(velo_cuda_ctx *ctx, void *stream);
+
+/* Wait for the context's stream, giving up after timeout_ns (<0: forever).
+ * Returns VELO_ERR_TIMEOUT instead of hanging; also reports a device-side
+ * input flag raised by an earlier kernel (VELO_ERR_DEVICE_FLAG). */
+VELO_API int32_t velo_cuda_sync(velo_cuda_ctx *ctx, int64_t timeout_ns);
+
+/* ---- acceptance --------------------------------------------------------- */
+
+/* Fused vocabulary-wide softmax + acceptance for linear drafts.
+ *
+ * Replaces the host loop GreedyTargetModel::verify_batch + GreedySampler
+ * (src/backend.rs:337-369, src/sampling.rs:39-58) followed by the prefix rule
+ * of SpeculativeSession::draft / commit (src/speculative.rs:441-467, 473-519).
+ *
+ *   target_logits [B][k+1][V] f32: row i is the target's distribution after
+ *                 draft position i-1 (row 0 after the last committed token).
+ *   draft_logits  [B][k][V]   f32: row i is the distribution draft token i was
+ *                 drawn from (unused, may be NULL, when temperature == 0).
+ *   draft_tokens  [B][k]  u32, each < V.
+ *   uniforms      [B][k+1] f32 in [0,1): u[b][i] for the accept test of
+ *                 position i, u[b][k] for the residual / bonus draw.
+ *   temperature   0 => greedy (accept while token == argmax, last maximal
+ *                 index wins as GreedySampler), > 0 => rejection sampling:
+ *                 accept x_i iff u_i * q(x_i) <= p(x_i); at the first
+ *                 rejection draw from norm(max(0, p - q)); if all k are
+ *                 accepted draw the bonus from p of row k.
+ *   accepted_len  [B] i32 out: accepted draft tokens (0..k).
+ *   bonus_token   [B] u32 out: the token emitted after the accepted prefix.
+ *
+ * Host-buffer form: copies inputs to the device, runs, copies outputs back and
+ * waits.  Pinned host memory gives the fastest copies. */
+VELO_API int32_t velo_cuda_accept(velo_cuda_ctx *ctx, const float *target_logits,
+                         const float *draft_logits, const uint32_t *draft_tokens,
+                         const float *uniforms, int32_t B, int32_t k, int32_t V,
+                         float temperature, int32_t *accepted_len,
+                         uint32_t *bonus_token);
+
+/* Device-buffer form of velo_cuda_accept: every pointer is device memory;
+ * asynchronous on the context stream.  Intermediate statistics live in a
+ * workspace the context allocates and keeps. */
+VELO_API int32_t velo_cuda_accept_device(velo_cuda_ctx *ctx, const float *target_logits,
+                                const float *draft_logits, const uint32_t *draft_tokens,
+                                const float *uniforms, int32_t B, int32_t k, int32_t V,
+                                float temperature, int32_t *accepted_len,
+                                uint32_t *bonus_token);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VELO_CUDA_H */

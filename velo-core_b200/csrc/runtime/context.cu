@@ -1,0 +1,274 @@
+// context.cu -- lifecycle, errors, workspace and the acceptance entry points
+// of the C ABI (include/velo_cuda.h).
+#include "runtime/context.h"
+
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <thread>
+
+#include "kernels/accept.h"
+
+namespace velo {
+
+static thread_local std::string g_last_error;
+
+void set_last_error(const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+}
+
+void clear_last_error() { g_last_error.clear(); }
+
+int32_t fail(int32_t st, const char* fmt, ...) {
+    char buf[1024];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return st;
+}
+
+int32_t DeviceBuffer::ensure(size_t need, cudaStream_t stream, bool zero_new) {
+    if (need <= bytes) return VELO_OK;
+    size_t want = need + need / 4;  // headroom so small growth does not thrash
+    if (ptr) {
+        VELO_CUDA_TRY(cudaStreamSynchronize(stream));
+        VELO_CUDA_TRY(cudaFree(ptr));
+        ptr = nullptr;
+        bytes = 0;
+    }
+    VELO_CUDA_TRY(cudaMalloc(&ptr, want));
+    if (zero_new) VELO_CUDA_TRY(cudaMemsetAsync(ptr, 0, want, stream));
+    bytes = want;
+    return VELO_OK;
+}
+
+void DeviceBuffer::release() {
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+}
+
+}  // namespace velo
+
+using velo::fail;
+
+extern "C" {
+
+int32_t velo_cuda_abi_version(void) { return VELO_CUDA_ABI_VERSION; }
+
+const char* velo_cuda_last_error(void) { return velo::g_last_error.c_str(); }
+
+int32_t velo_cuda_create(const velo_cuda_config* cfg, int32_t device, int32_t tp_rank,
+                         int32_t tp_size, const void* nccl_unique_id, velo_cuda_ctx** out) {
+    velo::clear_last_error();
+    if (!out) return fail(VELO_ERR_INVALID_ARGUMENT, "velo_cuda_create: out is NULL");
+    *out = nullptr;
+    if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "tp_rank %d / tp_size %d invalid", tp_rank, tp_size);
+    if (tp_size > 1 && !nccl_unique_id)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "tp_size > 1 needs an NCCL unique id");
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return fail(VELO_ERR_NO_DEVICE, "no CUDA device available");
+    }
+    if (device < 0 || device >= n)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "device %d out of range (%d devices)", device, n);
+    cudaDeviceProp prop;
+    VELO_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(VELO_ERR_NO_DEVICE, "device %d is sm_%d%d; this build is sm_100a only", device,
+                    prop.major, prop.minor);
+    velo_cuda_ctx* c = new (std::nothrow) velo_cuda_ctx();
+    if (!c) return fail(VELO_ERR_OUT_OF_MEMORY, "host allocation failed");
+    c->device = device;
+    c->tp_rank = tp_rank;
+    c->tp_size = tp_size;
+    c->sm_count = prop.multiProcessorCount;
+    if (cfg) {
+        if (cfg->struct_size != 0 && cfg->struct_size != sizeof(velo_cuda_config)) {
+            delete c;
+            return fail(VELO_ERR_INVALID_ARGUMENT, "velo_cuda_config.struct_size %u != %zu",
+                        cfg->struct_size, sizeof(velo_cuda_config));
+        }
+        c->cfg = *cfg;
+    }
+    c->cfg.struct_size = sizeof(velo_cuda_config);
+    if (c->cfg.page_size == 0) c->cfg.page_size = 16;
+    if (c->cfg.max_slots == 0) c->cfg.max_slots = 1;
+    if (c->cfg.max_pages_per_slot == 0) c->cfg.max_pages_per_slot = c->cfg.total_pages;
+    if (c->cfg.kv_dtype > VELO_KV_INT8) {
+        const unsigned kd = c->cfg.kv_dtype;
+        delete c;
+        return fail(VELO_ERR_INVALID_ARGUMENT, "kv_dtype %u unknown", kd);
+    }
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&c->err_flag, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemsetAsync(c->err_flag, 0, sizeof(int), c->own_stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->own_stream);
+    if (e != cudaSuccess) {
+        int32_t st = fail(VELO_ERR_CUDA, "context setup failed: %s", cudaGetErrorString(e));
+        velo_cuda_destroy(c);
+        return st;
+    }
+    c->stream = c->own_stream;
+    *out = c;
+    return VELO_OK;
+}
+
+void velo_cuda_destroy(velo_cuda_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->own_stream) cudaStreamSynchronize(c->own_stream);
+    if (c->stream && c->stream != c->own_stream) cudaStreamSynchronize(c->stream);
+    c->workspace.release();
+    c->counters.release();
+    c->io.release();
+    if (c->err_flag) cudaFree(c->err_flag);
+    if (c->own_stream) cudaStreamDestroy(c->own_stream);
+    delete c;
+}
+
+int32_t velo_cuda_set_stream(velo_cuda_ctx* c, void* stream) {
+    if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    c->stream = stream ? (cudaStream_t)stream : c->own_stream;
+    return VELO_OK;
+}
+
+int32_t velo_cuda_sync(velo_cuda_ctx* c, int64_t timeout_ns) {
+    if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    cudaSetDevice(c->device);
+    const auto start = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t e = cudaStreamQuery(c->stream);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady)
+            return fail(VELO_ERR_CUDA, "stream error: %s", cudaGetErrorString(e));
+        if (timeout_ns >= 0) {
+            auto el = std::chrono::duration_cast<std::chrono::nanoseconds>(
+                          std::chrono::steady_clock::now() - start).count();
+            if (el > timeout_ns)
+                return fail(VELO_ERR_TIMEOUT, "velo_cuda_sync: work still running after %lld ns",
+                            (long long)timeout_ns);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    int flag = 0;
+    VELO_CUDA_TRY(cudaMemcpy(&flag, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
+    if (flag) {
+        VELO_CUDA_TRY(cudaMemset(c->err_flag, 0, sizeof(int)));
+        return fail(VELO_ERR_DEVICE_FLAG, "a kernel flagged invalid input (code %d)", flag);
+    }
+    return VELO_OK;
+}
+
+// ---------------------------------------------------------------- acceptance
+
+static int32_t check_accept_args(int32_t B, int32_t k, int32_t V, float temperature,
+                                 const void* tgt, const void* drf, const void* tok,
+                                 const void* u, const void* acc, const void* bonus) {
+    if (B < 0) return fail(VELO_ERR_INVALID_ARGUMENT, "B = %d < 0", B);
+    if (k < 0 || k > velo::kAcceptMaxK)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "k = %d outside [0, %d]", k, velo::kAcceptMaxK);
+    if (V < 1 || V > velo::kAcceptMaxV)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "V = %d outside [1, %d]", V, velo::kAcceptMaxV);
+    if (!(temperature >= 0.0f) || std::isinf(temperature))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "temperature must be finite and >= 0");
+    if (B == 0) return VELO_OK;
+    if (!tgt || !acc || !bonus || (k > 0 && !tok))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "NULL target_logits / draft_tokens / outputs");
+    if (temperature > 0.0f && ((k > 0 && !drf) || !u))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "sampling needs draft_logits and uniforms");
+    return VELO_OK;
+}
+
+static int32_t run_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
+                          const uint32_t* tok, const float* u, int32_t B, int32_t k, int32_t V,
+                          float temperature, int32_t* acc, uint32_t* bonus) {
+    const bool greedy = temperature == 0.0f;
+    const size_t ws = velo::accept_workspace_bytes(B, k, V, greedy);
+    int32_t st = c->workspace.ensure(ws, c->stream);
+    if (st) return st;
+    st = c->counters.ensure((size_t)B * sizeof(unsigned), c->stream, /*zero_new=*/true);
+    if (st) return st;
+    velo::AcceptParams p{};
+    p.tgt = tgt;
+    p.drf = drf;
+    p.tok = tok;
+    p.u = u;
+    p.acc_len = acc;
+    p.bonus = bonus;
+    p.part = (float2*)c->workspace.ptr;
+    p.counters = (unsigned*)c->counters.ptr;
+    p.err_flag = c->err_flag;
+    p.B = B;
+    p.k = k;
+    p.V = V;
+    p.inv_t = greedy ? 0.0f : 1.0f / temperature;
+    p.vec4 = (V % 4 == 0) && ((uintptr_t)tgt % 16 == 0) && (greedy || k == 0 || (uintptr_t)drf % 16 == 0);
+    VELO_CUDA_TRY(velo::launch_accept(p, greedy, c->stream));
+    return VELO_OK;
+}
+
+int32_t velo_cuda_accept_device(velo_cuda_ctx* c, const float* tgt, const float* drf,
+                                const uint32_t* tok, const float* u, int32_t B, int32_t k,
+                                int32_t V, float temperature, int32_t* acc, uint32_t* bonus) {
+    velo::clear_last_error();
+    if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    int32_t st = check_accept_args(B, k, V, temperature, tgt, drf, tok, u, acc, bonus);
+    if (st || B == 0) return st;
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    return run_accept(c, tgt, drf, tok, u, B, k, V, temperature, acc, bonus);
+}
+
+int32_t velo_cuda_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
+                         const uint32_t* tok, const float* u, int32_t B, int32_t k, int32_t V,
+                         float temperature, int32_t* acc, uint32_t* bonus) {
+    velo::clear_last_error();
+    if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    int32_t st = check_accept_args(B, k, V, temperature, tgt, drf, tok, u, acc, bonus);
+    if (st || B == 0) return st;
+    for (size_t i = 0; i < (size_t)B * k; ++i)
+        if (tok[i] >= (uint32_t)V)
+            return fail(VELO_ERR_INVALID_ARGUMENT, "draft token %u at %zu is >= V = %d", tok[i], i, V);
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    const bool greedy = temperature == 0.0f;
+    const size_t n_t = (size_t)B * (k + 1) * V * sizeof(float);
+    const size_t n_d = greedy ? 0 : (size_t)B * k * V * sizeof(float);
+    const size_t n_tok = (size_t)B * k * sizeof(uint32_t);
+    const size_t n_u = greedy ? 0 : (size_t)B * (k + 1) * sizeof(float);
+    auto up16 = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t off_d = up16(n_t), off_tok = off_d + up16(n_d), off_u = off_tok + up16(n_tok);
+    const size_t off_acc = off_u + up16(n_u), off_bonus = off_acc + up16((size_t)B * 4);
+    const size_t total = off_bonus + up16((size_t)B * 4);
+    st = c->io.ensure(total, c->stream);
+    if (st) return st;
+    char* base = (char*)c->io.ptr;
+    float* d_t = (float*)base;
+    float* d_d = greedy ? nullptr : (float*)(base + off_d);
+    uint32_t* d_tok = (uint32_t*)(base + off_tok);
+    float* d_u = greedy ? nullptr : (float*)(base + off_u);
+    int32_t* d_acc = (int32_t*)(base + off_acc);
+    uint32_t* d_bonus = (uint32_t*)(base + off_bonus);
+    VELO_CUDA_TRY(cudaMemcpyAsync(d_t, tgt, n_t, cudaMemcpyHostToDevice, c->stream));
+    if (n_d) VELO_CUDA_TRY(cudaMemcpyAsync(d_d, drf, n_d, cudaMemcpyHostToDevice, c->stream));
+    if (n_tok) VELO_CUDA_TRY(cudaMemcpyAsync(d_tok, tok, n_tok, cudaMemcpyHostToDevice, c->stream));
+    if (n_u) VELO_CUDA_TRY(cudaMemcpyAsync(d_u, u, n_u, cudaMemcpyHostToDevice, c->stream));
+    st = run_accept(c, d_t, d_d, d_tok, d_u, B, k, V, temperature, d_acc, d_bonus);
+    if (st) return st;
+    VELO_CUDA_TRY(cudaMemcpyAsync(acc, d_acc, (size_t)B * 4, cudaMemcpyDeviceToHost, c->stream));
+    VELO_CUDA_TRY(cudaMemcpyAsync(bonus, d_bonus, (size_t)B * 4, cudaMemcpyDeviceToHost, c->stream));
+    return velo_cuda_sync(c, -1);
+}
+
+}  // extern "C"

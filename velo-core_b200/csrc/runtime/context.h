@@ -1,0 +1,54 @@
+// context.h -- internal definition of velo_cuda_ctx and runtime helpers.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+#include <string>
+
+#include "velo_cuda.h"
+
+namespace velo {
+
+// Thread-local last-error message (velo_cuda_last_error).
+void set_last_error(const char* fmt, ...);
+void clear_last_error();
+
+// Records a message and returns `st`.
+int32_t fail(int32_t st, const char* fmt, ...);
+
+// CUDA error -> VELO_ERR_CUDA with the call site.
+#define VELO_CUDA_TRY(expr)                                                              \
+    do {                                                                                 \
+        cudaError_t _e = (expr);                                                         \
+        if (_e != cudaSuccess)                                                           \
+            return ::velo::fail(_e == cudaErrorMemoryAllocation ? VELO_ERR_OUT_OF_MEMORY \
+                                                                : VELO_ERR_CUDA,         \
+                                "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e),  \
+                                __FILE__, __LINE__);                                     \
+    } while (0)
+
+// A device buffer that only grows.  Growing waits for `stream` first.
+struct DeviceBuffer {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    int32_t ensure(size_t need, cudaStream_t stream, bool zero_new = false);
+    void release();
+};
+
+}  // namespace velo
+
+struct velo_cuda_ctx {
+    int device = 0;
+    int tp_rank = 0, tp_size = 1;
+    velo_cuda_config cfg{};
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    int sm_count = 0;
+
+    velo::DeviceBuffer workspace;  // per-launch scratch (tile statistics, partials)
+    velo::DeviceBuffer counters;   // completion tickets, zero between launches
+    velo::DeviceBuffer io;         // device copies for the host-buffer entries
+    int* err_flag = nullptr;       // device-side input flag
+};

@@ -1,0 +1,170 @@
+"""Python view of the velo_cuda C ABI (include/velo_cuda.h), through ctypes.
+
+This is the host-side harness the tests and bench.py use; it calls the same
+extern "C" entry points a Rust backend binds.  There is
+no fallback: if libvelo_cuda.so is missing, importing fails loudly.
+
+Errors mirror the reference: every non-zero status raises VeloError whose
+`status` is the velo_status code (SpeculativeError / PageManagerError
+analogues) and whose message is velo_cuda_last_error().
+"""
+import ctypes
+import os
+import re
+
+import numpy as np
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libvelo_cuda.so")
+HEADER = os.path.join(os.path.dirname(_PKG), "include", "velo_cuda.h")
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_EMPTY_DRAFT_WINDOW = 2
+ERR_DRAFT_TOO_MANY = 3
+ERR_TARGET_WRONG_LENGTH = 4
+ERR_OUT_OF_PAGES = 5
+ERR_UNKNOWN_HANDLE = 6
+ERR_INVALID_BLOCK_SIZE = 7
+ERR_CUDA = 8
+ERR_NO_DEVICE = 9
+ERR_TIMEOUT = 10
+ERR_OUT_OF_MEMORY = 11
+ERR_NCCL = 12
+ERR_DEVICE_FLAG = 13
+
+KV_F16, KV_INT8 = 0, 1
+
+_P = ctypes.c_void_p
+_I32 = ctypes.c_int32
+_lib = None
+
+
+class VeloError(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"velo_cuda status {status}: {message}")
+        self.status = status
+        self.message = message
+
+
+class Config(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("page_size", ctypes.c_uint32),
+                ("kv_dtype", ctypes.c_uint32), ("max_slots", ctypes.c_uint32),
+                ("total_pages", ctypes.c_uint32), ("max_pages_per_slot", ctypes.c_uint32)]
+
+
+_SIGS = {
+    "velo_cuda_abi_version": (_I32, []),
+    "velo_cuda_last_error": (ctypes.c_char_p, []),
+    "velo_cuda_create": (_I32, [_P, _I32, _I32, _I32, _P, ctypes.POINTER(_P)]),
+    "velo_cuda_destroy": (None, [_P]),
+    "velo_cuda_set_stream": (_I32, [_P, _P]),
+    "velo_cuda_sync": (_I32, [_P, ctypes.c_int64]),
+    "velo_cuda_accept": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float, _P, _P]),
+    "velo_cuda_accept_device": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float,
+                                       _P, _P]),
+}
+
+
+def lib():
+    """Load libvelo_cuda.so (built in-tree by velo-core_b200/build.py)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is not built; run __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+def header_functions():
+    """Names of the functions include/velo_cuda.h declares."""
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(velo_cuda_\w+)\s*\(", src)))
+
+
+def last_error():
+    return lib().velo_cuda_last_error().decode()
+
+
+def check(status):
+    if status != OK:
+        raise VeloError(status, last_error())
+    return status
+
+
+def _ptr(a):
+    """Host numpy array or device torch tensor -> void*."""
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data_as(_P)
+    return ctypes.c_void_p(a.data_ptr())  # torch tensor
+
+
+class Context:
+    """One velo_cuda_ctx: a device, a stream and the device buffers."""
+
+    def __init__(self, device=0, page_size=16, kv_dtype=KV_F16, max_slots=1, total_pages=0,
+                 max_pages_per_slot=0, tp_rank=0, tp_size=1, nccl_id=None):
+        cfg = Config(ctypes.sizeof(Config), page_size, kv_dtype, max_slots, total_pages,
+                     max_pages_per_slot)
+        h = _P()
+        nid = None if nccl_id is None else ctypes.c_char_p(bytes(nccl_id))
+        check(lib().velo_cuda_create(ctypes.byref(cfg), device, tp_rank, tp_size, nid,
+                                     ctypes.byref(h)))
+        self._h = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().velo_cuda_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    @property
+    def handle(self):
+        return self._h
+
+    def set_stream(self, stream_ptr):
+        check(lib().velo_cuda_set_stream(self._h, _P(stream_ptr) if stream_ptr else None))
+
+    def sync(self, timeout_ns=-1):
+        check(lib().velo_cuda_sync(self._h, timeout_ns))
+
+    # ------------------------------------------------------------ acceptance
+    def accept(self, target_logits, draft_logits, draft_tokens, uniforms, temperature):
+        """Host-buffer acceptance.  Returns (accepted_len[B] i32, bonus[B] u32)."""
+        t = np.ascontiguousarray(target_logits, np.float32)
+        B, k1, V = t.shape
+        k = k1 - 1
+        d = None if draft_logits is None else np.ascontiguousarray(draft_logits, np.float32)
+        tok = np.ascontiguousarray(draft_tokens, np.uint32).reshape(B, k)
+        u = None if uniforms is None else np.ascontiguousarray(uniforms, np.float32)
+        acc = np.zeros(B, np.int32)
+        bonus = np.zeros(B, np.uint32)
+        check(lib().velo_cuda_accept(self._h, _ptr(t), _ptr(d), _ptr(tok), _ptr(u), B, k, V,
+                                     float(temperature), _ptr(acc), _ptr(bonus)))
+        return acc, bonus
+
+    def accept_device(self, target_logits, draft_logits, draft_tokens, uniforms, temperature,
+                      accepted_len, bonus_token):
+        """Device-buffer acceptance on torch CUDA tensors (asynchronous)."""
+        B, k1, V = target_logits.shape
+        check(lib().velo_cuda_accept_device(
+            self._h, _ptr(target_logits), _ptr(draft_logits), _ptr(draft_tokens),
+            _ptr(uniforms), B, k1 - 1, V, float(temperature), _ptr(accepted_len),
+            _ptr(bonus_token)))
