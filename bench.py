@@ -214,7 +214,10 @@ def run_cuda(args):
     acc = torch.empty(B, dtype=torch.int32, device=dev)
     bonus = torch.empty(B, dtype=torch.int32, device=dev)
     ctx = velo_cuda.Context(device=local)
-    stream = torch.cuda.current_stream(dev)
+    # a real (non-default) stream shared by torch and the context, so the
+    # CUDA events below bracket exactly the launches of the timed steps
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
 
     def step(i):
@@ -308,12 +311,12 @@ def run_cuda(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind,
                          "traffic": load_traffic("accept_c2"),
-                         "algorithmic_bytes": alg_bytes, "kernel": "accept_kernel<false>"},
+                         "algorithmic_bytes": alg_bytes, "kernel": "accept_stream_kernel<false> + accept_finish_kernel<false>"},
             "clocks": clocks,
             "e2e": {"value": e2e_toks / e2e_s, "unit": "accepted tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "ms_per_step": 1e3 * e2e_s / e2e_steps},
-            "gpu_launches": args.steps,
+            "gpu_launches": 2 * args.steps,  # stream + finish kernels per step
         }
     ctx.close()
     if ws > 1:

@@ -514,10 +514,12 @@ size_t vo_find_best_path(const int32_t *parents, const uint32_t *tokens,
  * Horner form, scaled by 2^k built from the exponent bits.  Constants:
  *   LN2_HI = 45426/65536 = 0.693145751953125 (15 significant bits, so k*LN2_HI
  *            is exact for |k| < 512), LN2_LO = ln2 - LN2_HI rounded to float,
- *   ROUND  = 1.5*2^23: adding it rounds y*log2(e) to an integer k held in the
- *            low mantissa bits.
- * The input is clamped to [-87, 88] so 2^k stays a normal float (NaN maps to
- * -87).  Max relative error vs e^y is below 3e-7 (tests check it). */
+ *   ROUND  = 1.5*2^23: fma(y, log2e, ROUND) rounds y*log2(e) to an integer k
+ *            held in the low mantissa bits; (bits(t) << 23) + bits(1.0f) is
+ *            then the bit pattern of 2^k.
+ * The input is clamped below at -87 so 2^k stays a normal float (NaN maps to
+ * -87); the domain is y <= 88 (every use has y <= 0 up to one rounding).
+ * Max relative error vs e^y is below 3e-7 (tests check it). */
 #define SPEC_LOG2E 1.44269504088896341f
 #define SPEC_LN2_HI 0.693145751953125f
 #define SPEC_LN2_LO 1.42860682030941723e-6f
@@ -527,20 +529,18 @@ static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
 
 float vo_spec_exp(float y) {
-    y = fminf(fmaxf(y, -87.0f), 88.0f);
+    y = fmaxf(y, -87.0f);
     float t = fmaf(y, SPEC_LOG2E, SPEC_ROUND);
-    float kf = t - SPEC_ROUND;
-    int32_t k = (int32_t)(f2u(t) - f2u(SPEC_ROUND));
-    float r = fmaf(-kf, SPEC_LN2_HI, y);
-    r = fmaf(-kf, SPEC_LN2_LO, r);
-    float p = 1.38888888888888889e-3f;       /* 1/720 */
-    p = fmaf(p, r, 8.33333333333333333e-3f); /* 1/120 */
-    p = fmaf(p, r, 4.16666666666666667e-2f); /* 1/24  */
-    p = fmaf(p, r, 1.66666666666666667e-1f); /* 1/6   */
+    float kf = t + (-SPEC_ROUND);
+    float r = fmaf(kf, -SPEC_LN2_HI, y);
+    r = fmaf(kf, -SPEC_LN2_LO, r);
+    float p = fmaf(1.38888888888888889e-3f, r, 8.33333333333333333e-3f); /* 1/720, 1/120 */
+    p = fmaf(p, r, 4.16666666666666667e-2f); /* 1/24 */
+    p = fmaf(p, r, 1.66666666666666667e-1f); /* 1/6  */
     p = fmaf(p, r, 0.5f);
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
-    return p * u2f((uint32_t)(k + 127) << 23);
+    return p * u2f((f2u(t) << 23) + 0x3F800000u);
 }
 
 /* Vocabulary enumeration of the spec: tiles of 1024 elements; in tile t,

@@ -272,7 +272,7 @@ def accept(tgt, drf, tok, u, temperature, n_threads=0):
     k = k1 - 1
     drf = None if drf is None else c_arr(drf, np.float32)
     tok = c_arr(tok, np.uint32).reshape(B, k)
-    u = c_arr(u, np.float32).reshape(B, k + 1)
+    u = np.zeros((B, k + 1), np.float32) if u is None else c_arr(u, np.float32).reshape(B, k + 1)
     acc = np.zeros(B, np.int32)
     bonus = np.zeros(B, np.uint32)
     rc = lib().vo_accept(ptr(tgt), ptr(drf), ptr(tok), ptr(u), B, k, V, temperature,

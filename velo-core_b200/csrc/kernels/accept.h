@@ -1,4 +1,4 @@
-// accept.h -- launch interface of the fused acceptance kernel (accept.cu).
+// accept.h -- launch interface of the fused acceptance kernels (accept.cu).
 #pragma once
 #include <cuda_runtime.h>
 #include <cstddef>
@@ -8,7 +8,7 @@ namespace velo {
 
 constexpr int kAcceptMaxK = 64;                     // draft positions per sequence
 constexpr int kAcceptMaxRows = 2 * kAcceptMaxK + 1; // target k+1 rows + draft k rows
-constexpr int kAcceptMaxTiles = 256;                // vocabulary <= 256 * 1024
+constexpr int kAcceptMaxTiles = 128;                // vocabulary <= 128 * 1024
 constexpr int kAcceptMaxV = kAcceptMaxTiles * 1024;
 
 struct AcceptParams {
@@ -18,19 +18,30 @@ struct AcceptParams {
     const float* u;         // [B][k+1]
     int32_t* acc_len;       // [B]
     uint32_t* bonus;        // [B]
-    float2* part;           // workspace: [B][nrows][ntiles] tile statistics
-    unsigned* counters;     // [B] completion tickets, zero between launches
+    // workspace (per launch; contents need no initialisation)
+    float2* part;           // [B][nrows][ntiles] tile statistics
+    float* tokval;          // [B][nrows] logit of row i at its draft token (rows != k)
+    float* lane_w;          // [B][ntiles][32] draw lane weights
+    float* tile_w;          // [B][ntiles] draw tile weights
+    // per-sequence ticket of the finish CTAs; zeroed at allocation, reset by
+    // the CTA that takes the last ticket, so it is zero between launches
+    unsigned* done;         // [B]
     int* err_flag;          // device flag: bad draft token seen
     int B, k, V;
     float inv_t;
     bool vec4;              // rows are 16-byte aligned (V % 4 == 0, aligned bases)
+    int grid;               // stream CTAs (0: 4 per SM)
     // filled by launch_accept
-    int ntiles, nrows, ctas_per_seq;
+    int ntiles, nrows;
 };
 
-// Bytes of the tile-statistics workspace for one launch.
+// Bytes of the per-launch workspace.
 size_t accept_workspace_bytes(int B, int k, int V, bool greedy);
+// Bytes of the ticket block (must be zero before the first launch).
+size_t accept_counter_bytes(int B);
+// Carve `ws` (workspace) and `cnt` (tickets) into the params' pointers.
+void accept_bind_buffers(AcceptParams& p, void* ws, void* cnt, bool greedy);
 
-cudaError_t launch_accept(const AcceptParams& p, bool greedy, cudaStream_t stream);
+cudaError_t launch_accept(const AcceptParams& p, bool greedy, int sm_count, cudaStream_t stream);
 
 }  // namespace velo

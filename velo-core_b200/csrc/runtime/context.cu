@@ -196,10 +196,10 @@ static int32_t run_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
                           const uint32_t* tok, const float* u, int32_t B, int32_t k, int32_t V,
                           float temperature, int32_t* acc, uint32_t* bonus) {
     const bool greedy = temperature == 0.0f;
-    const size_t ws = velo::accept_workspace_bytes(B, k, V, greedy);
-    int32_t st = c->workspace.ensure(ws, c->stream);
+    int32_t st = c->workspace.ensure(velo::accept_workspace_bytes(B, k, V, greedy), c->stream);
     if (st) return st;
-    st = c->counters.ensure((size_t)B * sizeof(unsigned), c->stream, /*zero_new=*/true);
+    // ticket block: zeroed when (re)allocated, then kept at zero by the kernel
+    st = c->counters.ensure(velo::accept_counter_bytes(B), c->stream, /*zero_new=*/true);
     if (st) return st;
     velo::AcceptParams p{};
     p.tgt = tgt;
@@ -208,15 +208,14 @@ static int32_t run_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
     p.u = u;
     p.acc_len = acc;
     p.bonus = bonus;
-    p.part = (float2*)c->workspace.ptr;
-    p.counters = (unsigned*)c->counters.ptr;
     p.err_flag = c->err_flag;
     p.B = B;
     p.k = k;
     p.V = V;
     p.inv_t = greedy ? 0.0f : 1.0f / temperature;
     p.vec4 = (V % 4 == 0) && ((uintptr_t)tgt % 16 == 0) && (greedy || k == 0 || (uintptr_t)drf % 16 == 0);
-    VELO_CUDA_TRY(velo::launch_accept(p, greedy, c->stream));
+    velo::accept_bind_buffers(p, c->workspace.ptr, c->counters.ptr, greedy);
+    VELO_CUDA_TRY(velo::launch_accept(p, greedy, c->sm_count, c->stream));
     return VELO_OK;
 }
 
