@@ -132,6 +132,26 @@ VELO_API int32_t velo_cuda_accept_device(velo_cuda_ctx *ctx, const float *target
                                 float temperature, int32_t *accepted_len,
                                 uint32_t *bonus_token);
 
+/* Allocation-free form of velo_cuda_accept_device, for callers that must not
+ * allocate device memory on this path (an engine that owns all of HBM through
+ * its own pools, or a latency-critical loop where cudaMalloc would
+ * synchronise).  No counterpart in the reference: velo-core has no device-side
+ * acceptance.  Needs no context: runs on the calling thread's current device
+ * and on `stream` (a cudaStream_t; NULL = default stream), asynchronously.
+ * Inputs and outputs are caller-provided device buffers; intermediate
+ * statistics live in a fixed 4 MiB block of device memory inside the library
+ * (one per GPU, held until process exit), so it allocates nothing.  Sizes
+ * whose statistics exceed that block (roughly B*(2k+1)*ceil(V/1024) > 250k)
+ * are rejected with VELO_ERR_INVALID_ARGUMENT.  The first call on each device
+ * looks up the block's address; make it before any stream capture.  All calls
+ * on a device share the block: calls that overlap on the GPU race and must be
+ * serialised by the caller. */
+VELO_API int32_t velo_cuda_accept_static(const float *target_logits, const float *draft_logits,
+                                         const uint32_t *draft_tokens, const float *uniforms,
+                                         int32_t B, int32_t k, int32_t V, float temperature,
+                                         int32_t *accepted_len, uint32_t *bonus_token,
+                                         void *stream);
+
 #ifdef __cplusplus
 }
 #endif

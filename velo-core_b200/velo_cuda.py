@@ -63,6 +63,8 @@ _SIGS = {
     "velo_cuda_accept": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float, _P, _P]),
     "velo_cuda_accept_device": (_I32, [_P, _P, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float,
                                        _P, _P]),
+    "velo_cuda_accept_static": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float, _P, _P,
+                                       _P]),
 }
 
 
@@ -168,3 +170,14 @@ class Context:
             self._h, _ptr(target_logits), _ptr(draft_logits), _ptr(draft_tokens),
             _ptr(uniforms), B, k1 - 1, V, float(temperature), _ptr(accepted_len),
             _ptr(bonus_token)))
+
+
+def accept_static(target_logits, draft_logits, draft_tokens, uniforms, temperature,
+                  accepted_len, bonus_token, stream_ptr=None):
+    """velo_cuda_accept_static on torch CUDA tensors: no context and no device
+    allocation; asynchronous on `stream_ptr` (None: the default stream)."""
+    B, k1, V = target_logits.shape
+    check(lib().velo_cuda_accept_static(
+        _ptr(target_logits), _ptr(draft_logits), _ptr(draft_tokens), _ptr(uniforms), B, k1 - 1,
+        V, float(temperature), _ptr(accepted_len), _ptr(bonus_token),
+        _P(stream_ptr) if stream_ptr else None))
