@@ -152,6 +152,40 @@ VELO_API int32_t velo_cuda_accept_static(const float *target_logits, const float
                                          int32_t *accepted_len, uint32_t *bonus_token,
                                          void *stream);
 
+/* ---- q4_0 linear layers ------------------------------------------------- */
+
+/* Epilogues of velo_cuda_gemm_q4_0 (y has row stride ldy elements). */
+typedef enum velo_gemm_epilogue {
+    VELO_EPI_STORE_F32 = 0, /* y[m][n] = acc                       f32 */
+    VELO_EPI_STORE_F16 = 1, /* y[m][n] = acc                       f16 */
+    VELO_EPI_ADD_F32 = 2,   /* y[m][n] += acc (residual stream)    f32 */
+    VELO_EPI_SWIGLU = 3     /* y[m][j] = silu(gate_j) * up_j        f16, j < N/2 */
+} velo_gemm_epilogue;
+
+/* Device bytes of a repacked q4_0 weight with N rows of K elements (0 if
+ * K is not a positive multiple of 32). */
+VELO_API size_t velo_cuda_q4_0_repacked_bytes(int32_t N, int32_t K);
+
+/* Repack q4_0 rows as velo-core stores them ([N][K/32] blocks of 18 bytes:
+ * fp16 scale d, then 16 bytes whose byte i holds element 2i (low nibble) and
+ * 2i+1 (high nibble), value d * (q - 8); src/quant.rs:50-64) into the tiled
+ * layout the tensor-core GEMM streams.  src / src_b / dst are device memory.
+ * With src_b != NULL the weight is a SwiGLU pair: src holds the N/2 gate rows
+ * (ffn w1) and src_b the N/2 up rows (ffn w3), for VELO_EPI_SWIGLU.
+ * Asynchronous on the context stream.  Replaces the per-row dequant_row of
+ * matvec_quant (src/llama_cpu.rs:75-90), done once at load instead. */
+VELO_API int32_t velo_cuda_q4_0_repack(velo_cuda_ctx *ctx, const void *src, const void *src_b,
+                                       int32_t N, int32_t K, void *dst);
+
+/* Y = X * W^T on the tensor cores: X f16 [M][K] (device, 16-byte aligned,
+ * row stride K), W a repacked q4_0 weight of N rows, fp32 accumulation, then
+ * the epilogue `mode` (velo_gemm_epilogue).  Asynchronous on the context
+ * stream.  Replaces matvec_quant (src/llama_cpu.rs:75-90) for all M rows of a
+ * verify step at once. */
+VELO_API int32_t velo_cuda_gemm_q4_0(velo_cuda_ctx *ctx, const void *w_repacked, const void *x,
+                                     int32_t M, int32_t N, int32_t K, void *y, int32_t ldy,
+                                     int32_t mode);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,62 @@
+// q4gemm.h -- q4_0 weight repack and the tcgen05 dequant-fused GEMM (q4gemm.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace velo {
+
+// Repacked q4_0 weight: tiles of kQ4TileN weight rows x kQ4TileK elements,
+// ordered [n_tile][k_tile], each kQ4TileBytes contiguous bytes:
+//   [0, 4096)     block 0 (k 0..31 of the tile) of rows 0..255, 16 B per row
+//   [4096, 8192)  block 1 (k 32..63), 16 B per row
+//   [8192, 9216)  fp16 scales [row][2] (block 0, block 1)
+// Inside a row's 16 bytes, 32-bit word g carries elements 8g..8g+7 of the
+// block as nibbles e0 e2 | e4 e6 | e1 e3 | e5 e7 (byte 0 .. byte 3, low nibble
+// first), so that two masks and a shift yield f16 pairs in element order.
+// Rows past N and blocks past K hold weight 0 (nibble 8, scale 0).
+constexpr int kQ4TileN = 256;
+constexpr int kQ4TileK = 64;
+constexpr int kQ4TileBytes = 9216;
+
+inline int q4_n_tiles(int N) { return (N + kQ4TileN - 1) / kQ4TileN; }
+inline int q4_k_tiles(int K) { return (K + kQ4TileK - 1) / kQ4TileK; }
+inline size_t q4_repacked_bytes(int N, int K) {
+    return (size_t)q4_n_tiles(N) * q4_k_tiles(K) * kQ4TileBytes;
+}
+
+// Repacks GGUF/velo-core q4_0 rows ([rows][K/32] blocks of 18 B: fp16 d then
+// 16 bytes, element 2i = low nibble of byte i, 2i+1 = high nibble;
+// src/quant.rs:50-64).  pair == false: src_a is [N][K], out row r = src_a row r.
+// pair == true (SwiGLU gate/up): src_a, src_b are [N/2][K] each; in out tile t
+// rows 0..127 are src_a rows 128t.. and rows 128..255 are src_b rows 128t..
+cudaError_t launch_q4_repack(const uint8_t* src_a, const uint8_t* src_b, bool pair, int N, int K,
+                             uint8_t* dst, cudaStream_t stream);
+
+enum Q4Epilogue : int {
+    kEpiStoreF32 = 0,  // y[m][n] = acc                       (f32)
+    kEpiStoreF16 = 1,  // y[m][n] = f16(acc)                  (f16)
+    kEpiAddF32 = 2,    // y[m][n] += acc                      (f32, residual stream)
+    kEpiSwiGLU = 3,    // y[m][j] = f16(silu(gate) * up)      (f16, pair-repacked weight)
+};
+
+struct Q4GemmArgs {
+    const uint8_t* w;  // repacked weight
+    int N, K, M;       // weight rows (pair: 2 x F), reduction length, activation rows
+    void* y;           // output, row stride ldy elements
+    int ldy;
+    int mode;          // Q4Epilogue
+    int* err;          // device error word (a barrier wait gave up)
+};
+
+// X: f16 [M][K] row-major device buffer (K % 8 == 0, 16-byte aligned base).
+cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, cudaStream_t stream);
+
+// Builds the 2-D TMA descriptor of an f16 [rows][cols] row-major matrix with a
+// box of 64 x box_rows elements and 128-byte swizzle.
+cudaError_t make_tmap_f16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                             uint64_t row_stride_bytes, uint32_t box_rows);
+
+}  // namespace velo

@@ -65,7 +65,12 @@ _SIGS = {
                                        _P, _P]),
     "velo_cuda_accept_static": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float, _P, _P,
                                        _P]),
+    "velo_cuda_q4_0_repacked_bytes": (ctypes.c_size_t, [_I32, _I32]),
+    "velo_cuda_q4_0_repack": (_I32, [_P, _P, _P, _I32, _I32, _P]),
+    "velo_cuda_gemm_q4_0": (_I32, [_P, _P, _P, _I32, _I32, _I32, _P, _I32, _I32]),
 }
+
+EPI_STORE_F32, EPI_STORE_F16, EPI_ADD_F32, EPI_SWIGLU = 0, 1, 2, 3
 
 
 def lib():
@@ -170,6 +175,20 @@ class Context:
             self._h, _ptr(target_logits), _ptr(draft_logits), _ptr(draft_tokens),
             _ptr(uniforms), B, k1 - 1, V, float(temperature), _ptr(accepted_len),
             _ptr(bonus_token)))
+
+    # ------------------------------------------------------------ q4_0 GEMM
+    def q4_0_repack(self, src, N, K, out, src_b=None):
+        """Repack q4_0 rows (device uint8 [N][K/32*18], or two halves for a
+        SwiGLU pair) into `out` (device, q4_0_repacked_bytes(N, K) bytes)."""
+        check(lib().velo_cuda_q4_0_repack(self._h, _ptr(src), _ptr(src_b), N, K, _ptr(out)))
+
+    def gemm_q4_0(self, w, x, M, N, K, y, ldy, mode):
+        """y (+)= x[M][K] (f16) * W^T on the tensor cores; asynchronous."""
+        check(lib().velo_cuda_gemm_q4_0(self._h, _ptr(w), _ptr(x), M, N, K, _ptr(y), ldy, mode))
+
+
+def q4_0_repacked_bytes(N, K):
+    return int(lib().velo_cuda_q4_0_repacked_bytes(N, K))
 
 
 def accept_static(target_logits, draft_logits, draft_tokens, uniforms, temperature,
