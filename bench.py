@@ -329,6 +329,77 @@ def run_cuda(args):
     return 0
 
 
+# ---------------------------------------------------------------- q4_0 GEMM workload
+Q4_SHAPES_C3 = [  # (name, N, K, mode) of one Llama-2-7B layer + LM head at M = 32 x 16 nodes
+    ("wqkv", 3 * 4096, 4096, 1), ("wo", 4096, 4096, 2), ("w1w3", 2 * 11008, 4096, 3),
+    ("w2", 4096, 11008, 2), ("output", 32000, 4096, 0)]
+
+
+def run_q4gemm(args):
+    """tcgen05 q4_0 GEMMs at BASELINE config 3 shapes (M = 512 verify rows).
+    Weights of `layers` distinct layers (> L2 in total) are cycled so no launch
+    finds its weight tile in L2."""
+    import torch
+    import synthetic
+    import velo_cuda
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    M, layers = 512, 8
+    ctx = velo_cuda.Context(device=0)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    x = torch.from_numpy(synthetic.rng(0, 20).normal(0, 1, (M, 11008)).astype(np.float16)).to(dev)
+    res = []
+    for name, N, K, mode in Q4_SHAPES_C3:
+        ws = []
+        for l in range(layers if name != "output" else 2):
+            raw = torch.randint(0, 256, (N, K // 32, 18), dtype=torch.uint8, device=dev)
+            raw[:, :, 1] &= 0x3B  # keep the f16 scales finite and modest
+            w = torch.empty(velo_cuda.q4_0_repacked_bytes(N, K), dtype=torch.uint8, device=dev)
+            if mode == 3:
+                ctx.q4_0_repack(raw[: N // 2], N, K, w, src_b=raw[N // 2:])
+            else:
+                ctx.q4_0_repack(raw, N, K, w)
+            ws.append(w)
+        ncol = N // 2 if mode == 3 else N
+        y = torch.zeros((M, ncol), dtype=torch.float16 if mode in (1, 3) else torch.float32,
+                        device=dev)
+        xk = x[:, :K].contiguous()
+        for i in range(max(3, args.warmup)):
+            ctx.gemm_q4_0(ws[i % len(ws)], xk, M, N, K, y, ncol, mode)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            ctx.gemm_q4_0(ws[i % len(ws)], xk, M, N, K, y, ncol, mode)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ctx.sync()
+        us = e0.elapsed_time(e1) * 1e3 / args.steps
+        flops = 2.0 * M * N * K
+        res.append({"gemm": name, "M": M, "N": N, "K": K, "us": us,
+                    "tflops": flops / us / 1e6})
+        del ws
+        torch.cuda.empty_cache()
+    peak = 1665.7
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        pass
+    tot_us = sum(r["us"] for r in res[:-1])
+    tot_fl = sum(2.0 * r["M"] * r["N"] * r["K"] for r in res[:-1])
+    line = {"workload": "q4_0 tcgen05 GEMM at BASELINE config 3 shapes (M=512)",
+            "per_gemm": res, "layer_us": tot_us, "layer_tflops": tot_fl / tot_us / 1e6,
+            "roofline": {"bound": "tensor", "achieved": tot_fl / tot_us / 1e6, "peak": peak,
+                         "unit": "TFLOP/s", "frac": tot_fl / tot_us / 1e6 / peak,
+                         "peak_kind": "measured bf16 burst (f16 operands here)"}}
+    ctx.close()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def cpu_baseline():
     """The CPU port (oracle) on this host, full C2 batch repeated ~10 s."""
     import vo
@@ -354,13 +425,15 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    ap.add_argument("--workload", default="accept", choices=["accept"])
+    ap.add_argument("--workload", default="accept", choices=["accept", "q4gemm"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "q4gemm":
+        return run_q4gemm(args)
     return run_cuda(args)
 
 

@@ -24,6 +24,7 @@ def test_f16_operand_model():
 
 
 def test_repacked_bytes():
+    # tiles of 256 rows x 64 elements, 36 bytes per row and tile (32 nibble + 4 scale)
     assert velo_cuda.q4_0_repacked_bytes(4096, 4096) == 16 * 64 * 9216
     assert velo_cuda.q4_0_repacked_bytes(300, 96) == 2 * 2 * 9216
     assert velo_cuda.q4_0_repacked_bytes(10, 33) == 0

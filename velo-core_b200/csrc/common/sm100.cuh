@@ -46,14 +46,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+// One potentially blocking test: the thread may be suspended until the phase
+// completes or about `hint_ns` pass, whichever is first.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity,
+                                              uint32_t hint_ns = 20000) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
         : "memory");
     return ok != 0;
 }
@@ -68,7 +71,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(b, parity)) return true;
-        if ((i & 255u) == 0) {
+        if ((i & 15u) == 0) {
             if (*abort) return false;
             if (global_ns() - t0 > kWaitLimitNs) {
                 atomicCAS(err, 0, code);

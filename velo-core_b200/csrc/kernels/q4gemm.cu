@@ -5,14 +5,20 @@
 // step, where all drafted tokens of all sequences form the M side of one GEMM:
 //   Y[m][n] = sum_k X[m][k] * W[n][k],   W = q4_0 dequantised (d * (q - 8)).
 //
-// One CTA computes a 128 (activation rows) x 256 (weight rows) tile with the
-// accumulator in tensor memory:
-//   warp 0      TMA producer: X tile (64 k, 128-byte swizzle) + the raw q4_0
-//               tile (one 9216-byte bulk copy) per k step into a 3-stage ring
-//   warp 1      one thread issues tcgen05.mma (M=128, N=256, K=16) x 4 per stage
-//   warp 2      allocates / frees 256 TMEM columns
-//   warps 4-11  dequantise their weight row of each stage into the swizzled
-//               f16 operand tile, then run the fused epilogue out of TMEM
+// A persistent CTA per SM walks 128 (activation rows) x 256 (weight rows)
+// output tiles with a double-buffered accumulator in tensor memory (all 512
+// columns), so the epilogue of one tile overlaps the main loop of the next.
+// The 256-row weight side halves the activation bytes per MMA compared with
+// 128-row tiles: the main loop is bound by L2 -> SM latency x bytes in flight,
+// not by the tensor pipe, at 128.
+//   warp 0      TMA producer of the X tile (64 k, 128-byte swizzle) per k step
+//   warp 3      bulk-copy producer of the raw q4_0 tile (9216 B) per k step
+//   warp 1      one thread issues tcgen05.mma (M=128, N=256, K=16) x 4 per step
+//   warp 2      allocates / frees 512 TMEM columns
+//   warps 4-11  dequantise their weight row of each k step into a 3-slot ring
+//               of swizzled f16 operand tiles
+//   warps 12-15 epilogue out of TMEM (tcgen05.ld), fused store / residual
+//               add / SwiGLU
 // Dequantisation: the nibble order chosen at repack time turns a 32-bit word
 // into f16 pairs with one LOP3 each (0x6400 | q = 1024 + q), an exact subtract
 // (or exact FMA for the high nibbles) gives q - 8, and one HMUL2 by the block
@@ -30,18 +36,33 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = kQ4TileN, BK = kQ4TileK, STAGES = 3;
+constexpr int BM = 128, BK = kQ4TileK;
 constexpr int X_BYTES = BM * BK * 2;      // 16 KiB
-constexpr int W_BYTES = BN * BK * 2;      // 32 KiB
-constexpr int RAW_BYTES = kQ4TileBytes;   // 9 KiB
-constexpr int kThreads = 384;
-constexpr int kDequantThreads = 256;      // warps 4..11, one weight row each
-constexpr int kTmemCols = 256;
-constexpr size_t kSmemBytes = (size_t)STAGES * (X_BYTES + W_BYTES + RAW_BYTES) + 1024 + 256;
+constexpr int kEpilogueThreads = 128;     // last four warps, one accumulator lane each
+
+// Per-width configuration: BN weight rows per CTA tile (one or two repacked
+// 128-row tiles per k step).
+template <int BN>
+struct Cfg {
+    static constexpr int SUB = BN / kQ4TileN;               // repacked tiles per step
+    static constexpr int XSTAGES = BN == 256 ? 5 : 7;       // activation tile ring (TMA)
+    static constexpr int RSTAGES = BN == 256 ? 4 : 8;       // raw q4_0 ring (bulk copy)
+    static constexpr int WSTAGES = BN == 256 ? 3 : 4;       // dequantised f16 weight ring
+    static constexpr int W_BYTES = BN * BK * 2;             // 32 / 16 KiB
+    static constexpr int RAW_BYTES = SUB * kQ4TileBytes;    // 9 / 4.5 KiB
+    static constexpr int kDequantThreads = BN;              // warps 4.. : one weight row each
+    static constexpr int kThreads = 128 + BN + kEpilogueThreads;
+    static constexpr int kEpiWarp0 = (128 + BN) / 32;
+    static constexpr int kTmemCols = 2 * BN;                // double-buffered accumulator
+    static constexpr size_t kSmemBytes = (size_t)XSTAGES * X_BYTES +
+                                         (size_t)RSTAGES * RAW_BYTES +
+                                         (size_t)WSTAGES * W_BYTES + 1024 + 512;
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
 
 // error codes written to Q4GemmArgs::err when a wait gives up
 constexpr int kErrWaitEmpty = 0x4101, kErrWaitReady = 0x4102, kErrWaitFull = 0x4103,
-              kErrWaitAccum = 0x4104;
+              kErrWaitAccum = 0x4104, kErrWaitAccEmpty = 0x4105, kErrWaitWEmpty = 0x4106;
 
 // ---------------------------------------------------------------- repack
 __global__ void q4_repack_kernel(const uint8_t* __restrict__ a, const uint8_t* __restrict__ b,
@@ -85,8 +106,9 @@ __global__ void q4_repack_kernel(const uint8_t* __restrict__ a, const uint8_t* _
     }
     const int k_tiles = (kblocks + 1) / 2;
     uint8_t* tile = dst + ((size_t)t * k_tiles + kb / 2) * kQ4TileBytes;
-    *reinterpret_cast<uint4*>(tile + (kb & 1) * 4096 + l * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-    *reinterpret_cast<uint16_t*>(tile + 8192 + l * 4 + (kb & 1) * 2) = d;
+    *reinterpret_cast<uint4*>(tile + (kb & 1) * kQ4Block1Off + l * 16) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint16_t*>(tile + kQ4ScaleOff + l * 4 + (kb & 1) * 2) = d;
 }
 
 // ---------------------------------------------------------------- dequant
@@ -170,33 +192,64 @@ __device__ __forceinline__ void store_row32(const Q4GemmArgs& a, int m, int n, c
 }
 
 // ---------------------------------------------------------------- GEMM
-__global__ void __launch_bounds__(kThreads, 1)
+// Persistent: CTA c takes output tiles c, c + grid, ... (activation-row tile
+// fastest, so the CTAs sharing a weight tile run together and read it from
+// HBM once).  The k-step counter g runs on across tiles, so every ring keeps
+// its phase from one tile to the next.  Three rings, each released as early
+// as its consumer allows:
+//   X   (XSTAGES x 16 KiB)  TMA -> MMA; freed by the MMA commit
+//   raw (RSTAGES x 9 KiB)   bulk copy -> dequant; freed once dequantised
+//   W   (WSTAGES x 32 KiB)  dequant -> MMA; freed by the MMA commit
+// Each CTA walks the k steps of a tile starting at its own offset kt0: all
+// CTAs read the same few activation tiles otherwise, and those L2 lines turn
+// into a hot spot that stretches the TMA latency to ~2 us.
+template <int BN>
+__global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     q4_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
+    using C = Cfg<BN>;
+    constexpr int XSTAGES = C::XSTAGES, RSTAGES = C::RSTAGES, WSTAGES = C::WSTAGES;
+    constexpr int W_BYTES = C::W_BYTES, RAW_BYTES = C::RAW_BYTES;
+    constexpr int kDequantThreads = C::kDequantThreads, kTmemCols = C::kTmemCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* sx = base;
-    uint8_t* sw = sx + STAGES * X_BYTES;
-    uint8_t* sr = sw + STAGES * W_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sr + STAGES * RAW_BYTES);
-    uint64_t* full = bars;
-    uint64_t* wready = bars + STAGES;
-    uint64_t* empty = bars + 2 * STAGES;
-    uint64_t* accum = bars + 3 * STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 1);
+    uint8_t* sx = base;                              // 1024-aligned tiles
+    uint8_t* sw = sx + XSTAGES * X_BYTES;            // 1024-aligned tiles
+    uint8_t* sr = sw + WSTAGES * W_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sr + RSTAGES * RAW_BYTES);
+    uint64_t* xfull = bars;                          // X tile landed (tx bytes)
+    uint64_t* xempty = xfull + XSTAGES;              // MMAs reading it done
+    uint64_t* rfull = xempty + XSTAGES;              // raw q4_0 tile landed (tx bytes)
+    uint64_t* rempty = rfull + RSTAGES;              // dequant group read it
+    uint64_t* wfull = rempty + RSTAGES;              // f16 weight tile written
+    uint64_t* wempty = wfull + WSTAGES;              // MMAs reading it done
+    uint64_t* afull = wempty + WSTAGES;              // accumulator b complete
+    uint64_t* aempty = afull + 2;                    // accumulator b drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * BM;
-    const int nt = blockIdx.y;
     const int KT = (a.K + BK - 1) / BK;
+    const int MT = (a.M + BM - 1) / BM;
+    const int n_tiles = MT * (q4_n_tiles(a.N) / C::SUB);
+    const int kt0 = (int)((blockIdx.x * 5u) % (unsigned)KT);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&wready[s], kDequantThreads);
-            mbar_init(&empty[s], 1);
+        for (int s = 0; s < XSTAGES; ++s) {
+            mbar_init(&xfull[s], 1);
+            mbar_init(&xempty[s], 1);
         }
-        mbar_init(accum, 1);
+        for (int s = 0; s < RSTAGES; ++s) {
+            mbar_init(&rfull[s], 1);
+            mbar_init(&rempty[s], kDequantThreads);
+        }
+        for (int s = 0; s < WSTAGES; ++s) {
+            mbar_init(&wfull[s], kDequantThreads);
+            mbar_init(&wempty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&afull[b], 1);
+            mbar_init(&aempty[b], kEpilogueThreads);
+        }
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -211,79 +264,123 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
+        // X producer
         if (lane == 0) {
-            const uint8_t* wt = a.w + (size_t)nt * KT * RAW_BYTES;
-            for (int kt = 0; kt < KT; ++kt) {
-                const int s = kt % STAGES;
-                const uint32_t ph = (kt / STAGES) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, a.err, kErrWaitEmpty, abort_flag)) break;
-                mbar_arrive_expect_tx(&full[s], X_BYTES + RAW_BYTES);
-                tma_load_2d(sx + s * X_BYTES, &tmx, &full[s], kt * BK, m0);
-                bulk_load(sr + s * RAW_BYTES, wt + (size_t)kt * RAW_BYTES, RAW_BYTES, &full[s]);
+            uint32_t g = 0;
+            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+                const int mt = tile % MT;
+                for (int kt = 0; kt < KT; ++kt, ++g) {
+                    const int s = g % XSTAGES;
+                    if (!mbar_wait(&xempty[s], ((g / XSTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag))
+                        goto done;
+                    const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
+                    mbar_arrive_expect_tx(&xfull[s], X_BYTES);
+                    tma_load_2d(sx + s * X_BYTES, &tmx, &xfull[s], kk * BK, mt * BM);
+                }
+            }
+        }
+    } else if (warp == 3) {
+        // raw q4_0 producer
+        if (lane == 0) {
+            uint32_t g = 0;
+            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+                const int nt = tile / MT;
+                const uint8_t* wt = a.w + (size_t)nt * C::SUB * KT * kQ4TileBytes;
+                for (int kt = 0; kt < KT; ++kt, ++g) {
+                    const int s = g % RSTAGES;
+                    if (!mbar_wait(&rempty[s], ((g / RSTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag))
+                        goto done;
+                    const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
+                    mbar_arrive_expect_tx(&rfull[s], RAW_BYTES);
+#pragma unroll
+                    for (int sub = 0; sub < C::SUB; ++sub)
+                        bulk_load(sr + s * RAW_BYTES + sub * kQ4TileBytes,
+                                  wt + ((size_t)sub * KT + kk) * kQ4TileBytes, kQ4TileBytes, &rfull[s]);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             const uint32_t idesc = idesc_f16_f32(BM, BN);
-            bool ok = true;
-            for (int kt = 0; kt < KT; ++kt) {
-                const int s = kt % STAGES;
-                const uint32_t ph = (kt / STAGES) & 1;
-                if (!mbar_wait(&wready[s], ph, a.err, kErrWaitReady, abort_flag)) {
-                    ok = false;
-                    break;
-                }
+            uint32_t g = 0, it = 0;
+            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+                const int b = it & 1;
+                const uint32_t aph = (it >> 1) & 1;
+                if (!mbar_wait(&aempty[b], aph ^ 1, a.err, kErrWaitAccEmpty, abort_flag)) goto done;
                 tc_fence_after();
-                const uint64_t ad = desc_kmajor_sw128(smem_u32(sx + s * X_BYTES));
-                const uint64_t bd = desc_kmajor_sw128(smem_u32(sw + s * W_BYTES));
+                const uint32_t d = tmem + b * BN;
+                for (int kt = 0; kt < KT; ++kt, ++g) {
+                    const int s = g % XSTAGES, ws = g % WSTAGES;
+                    if (!mbar_wait(&xfull[s], (g / XSTAGES) & 1, a.err, kErrWaitFull, abort_flag) ||
+                        !mbar_wait(&wfull[ws], (g / WSTAGES) & 1, a.err, kErrWaitReady, abort_flag))
+                        goto done;
+                    tc_fence_after();
+                    const uint64_t ad = desc_kmajor_sw128(smem_u32(sx + s * X_BYTES));
+                    const uint64_t bd = desc_kmajor_sw128(smem_u32(sw + ws * W_BYTES));
 #pragma unroll
-                for (int k = 0; k < BK / 16; ++k)
-                    mma_f16_ss(tmem, ad + 2 * k, bd + 2 * k, idesc, (kt | k) != 0);
-                mma_commit(&empty[s]);
+                    for (int k = 0; k < BK / 16; ++k)
+                        mma_f16_ss(d, ad + 2 * k, bd + 2 * k, idesc, (kt | k) != 0);
+                    mma_commit(&xempty[s]);
+                    mma_commit(&wempty[ws]);
+                }
+                mma_commit(&afull[b]);
             }
-            if (ok) mma_commit(accum);
         }
-    } else if (warp >= 4) {
-        const int i = threadIdx.x - 128;  // weight row within the tile
-        uint8_t* wrow_base = sw + (i >> 3) * 1024 + (i & 7) * 128;
+    } else if (warp >= 4 && warp < C::kEpiWarp0) {
+        // dequantisation: thread i owns weight row i of every tile
+        const int i = threadIdx.x - 128;
+        const int rsub = (i / kQ4TileN) * kQ4TileBytes + (i % kQ4TileN) * 16;  // raw offset
+        const int rsc = (i / kQ4TileN) * kQ4TileBytes + kQ4ScaleOff + (i % kQ4TileN) * 4;
         const int sx7 = i & 7;
-        bool ok = true;
-        for (int kt = 0; kt < KT; ++kt) {
-            const int s = kt % STAGES;
-            const uint32_t ph = (kt / STAGES) & 1;
-            if (!mbar_wait(&full[s], ph, a.err, kErrWaitFull, abort_flag)) {
-                ok = false;
-                break;
+        uint8_t* wrow_base = sw + (i >> 3) * 1024 + (i & 7) * 128;
+        uint32_t g = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % RSTAGES, ws = g % WSTAGES;
+                if (!mbar_wait(&rfull[s], (g / RSTAGES) & 1, a.err, kErrWaitFull, abort_flag)) goto done;
+                const uint8_t* raw = sr + s * RAW_BYTES;
+                const uint4 c0 = *reinterpret_cast<const uint4*>(raw + rsub);
+                const uint4 c1 = *reinterpret_cast<const uint4*>(raw + rsub + kQ4Block1Off);
+                const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + rsc);
+                if (!mbar_wait(&wempty[ws], ((g / WSTAGES) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag))
+                    goto done;
+                const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc & 0xFFFF)));
+                const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc >> 16)));
+                uint8_t* wrow = wrow_base + ws * W_BYTES;
+                const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
+                const uint32_t w1[4] = {c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<uint4*>(wrow + ((q ^ sx7) << 4)) = dequant8(w0[q], d0);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<uint4*>(wrow + (((4 + q) ^ sx7) << 4)) = dequant8(w1[q], d1);
+                // the raw slot is released only now: the shared loads above have
+                // returned (their values were consumed), so the next bulk copy into
+                // it (async proxy) cannot overtake them
+                mbar_arrive(&rempty[s]);
+                fence_async_smem();
+                mbar_arrive(&wfull[ws]);
             }
-            const uint8_t* raw = sr + s * RAW_BYTES;
-            const uint4 c0 = *reinterpret_cast<const uint4*>(raw + i * 16);
-            const uint4 c1 = *reinterpret_cast<const uint4*>(raw + 4096 + i * 16);
-            const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + 8192 + i * 4);
-            const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc & 0xFFFF)));
-            const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc >> 16)));
-            uint8_t* wrow = wrow_base + s * W_BYTES;
-            const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
-            const uint32_t w1[4] = {c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-            for (int g = 0; g < 4; ++g)
-                *reinterpret_cast<uint4*>(wrow + ((g ^ sx7) << 4)) = dequant8(w0[g], d0);
-#pragma unroll
-            for (int g = 0; g < 4; ++g)
-                *reinterpret_cast<uint4*>(wrow + (((4 + g) ^ sx7) << 4)) = dequant8(w1[g], d1);
-            fence_async_smem();
-            mbar_arrive(&wready[s]);
         }
-        if (ok) ok = mbar_wait(accum, 0, a.err, kErrWaitAccum, abort_flag);
-        __syncwarp();
-        if (__all_sync(0xffffffffu, ok)) {
+    } else if (warp >= C::kEpiWarp0) {
+        // epilogue: the last four warps; warp with (warp % 4) == q drains TMEM
+        // lanes 32q .. 32q + 31
+        const int q = warp & 3;
+        uint32_t it = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+            const int mt = tile % MT, nt = tile / MT;
+            const int b = it & 1;
+            const bool ok = mbar_wait(&afull[b], (it >> 1) & 1, a.err, kErrWaitAccum, abort_flag);
+            __syncwarp();
+            if (!__all_sync(0xffffffffu, ok)) goto done;
             tc_fence_after();
-            const int q = warp & 3, h = (warp - 4) >> 2;
-            const int m = m0 + q * 32 + lane;
-            const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+            const int m = mt * BM + q * 32 + lane;
+            const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + b * BN;
             if (a.mode != kEpiSwiGLU) {
 #pragma unroll 1
-                for (int j = 0; j < 4; ++j) {
-                    const int col = h * 128 + j * 32;
+                for (int j = 0; j < BN / 32; ++j) {
+                    const int col = j * 32;
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(trow + col, r);
                     tmem_ld_wait();
@@ -291,22 +388,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (m < a.M && n < a.N) store_row32(a, m, n, r);
                 }
             } else {
+                // each repacked 128-row tile holds 64 gate rows then 64 up rows
                 const int F = a.N / 2;
 #pragma unroll 1
-                for (int j = 0; j < 2; ++j) {
-                    const int col = h * 64 + j * 32;
-                    uint32_t g[32], u[32];
-                    tmem_ld_32x32b_x32(trow + col, g);
-                    tmem_ld_32x32b_x32(trow + BN / 2 + col, u);
+                for (int j = 0; j < BN / 64; ++j) {
+                    const int col = (j >> 1) * kQ4TileN + (j & 1) * 32;
+                    uint32_t gt[32], up[32];
+                    tmem_ld_32x32b_x32(trow + col, gt);
+                    tmem_ld_32x32b_x32(trow + col + kQ4TileN / 2, up);
                     tmem_ld_wait();
-                    const int n = nt * (BN / 2) + col;
+                    const int n = nt * (BN / 2) + j * 32;
                     if (m < a.M && n < F) {
                         __half* y = static_cast<__half*>(a.y) + (size_t)m * a.ldy + n;
 #pragma unroll
                         for (int e = 0; e < 32; e += 2) {
                             if (n + e >= F) break;
-                            const float v0 = silu(__uint_as_float(g[e])) * __uint_as_float(u[e]);
-                            const float v1 = silu(__uint_as_float(g[e + 1])) * __uint_as_float(u[e + 1]);
+                            const float v0 = silu(__uint_as_float(gt[e])) * __uint_as_float(up[e]);
+                            const float v1 = silu(__uint_as_float(gt[e + 1])) * __uint_as_float(up[e + 1]);
                             if (n + e + 1 < F && ((a.ldy | n) & 1) == 0 && ((uintptr_t)a.y & 3) == 0) {
                                 *reinterpret_cast<__half2*>(y + e) = __floats2half2_rn(v0, v1);
                             } else {
@@ -317,8 +415,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
+            tc_fence_before();
+            mbar_arrive(&aempty[b]);
         }
     }
+done:
     tc_fence_before();
     __syncthreads();
     if (warp == 2) {
@@ -375,20 +476,34 @@ cudaError_t launch_q4_repack(const uint8_t* src_a, const uint8_t* src_b, bool pa
     return cudaGetLastError();
 }
 
-cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, cudaStream_t stream) {
+template <int BN>
+cudaError_t launch_width(const Q4GemmArgs& a, const CUtensorMap& map, int tiles, int sm_count,
+                         cudaStream_t stream) {
+    using C = Cfg<BN>;
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(q4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)kSmemBytes);
+        attr_err = cudaFuncSetAttribute(q4_gemm_kernel<BN>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)C::kSmemBytes);
     });
     if (attr_err != cudaSuccess) return attr_err;
+    const int grid = tiles < sm_count ? tiles : sm_count;
+    q4_gemm_kernel<BN><<<grid, C::kThreads, C::kSmemBytes, stream>>>(map, a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
+                           cudaStream_t stream) {
     CUtensorMap map;
     cudaError_t e = make_tmap_f16_2d(&map, x, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.K * 2, BM);
     if (e != cudaSuccess) return e;
-    dim3 grid((a.M + BM - 1) / BM, q4_n_tiles(a.N));
-    q4_gemm_kernel<<<grid, kThreads, kSmemBytes, stream>>>(map, a);
-    return cudaGetLastError();
+    // 256-row tiles halve the activation traffic per MMA; 128-row tiles when
+    // 256-row ones would leave SMs idle.
+    const int mt = (a.M + BM - 1) / BM;
+    const int t256 = mt * (q4_n_tiles(a.N) / 2);
+    if (t256 >= sm_count) return launch_width<256>(a, map, t256, sm_count, stream);
+    return launch_width<128>(a, map, mt * q4_n_tiles(a.N), sm_count, stream);
 }
 
 }  // namespace velo

@@ -10,19 +10,22 @@ namespace velo {
 
 // Repacked q4_0 weight: tiles of kQ4TileN weight rows x kQ4TileK elements,
 // ordered [n_tile][k_tile], each kQ4TileBytes contiguous bytes:
-//   [0, 4096)     block 0 (k 0..31 of the tile) of rows 0..255, 16 B per row
-//   [4096, 8192)  block 1 (k 32..63), 16 B per row
-//   [8192, 9216)  fp16 scales [row][2] (block 0, block 1)
+//   [0, 2048)     block 0 (k 0..31 of the tile) of rows 0..127, 16 B per row
+//   [2048, 4096)  block 1 (k 32..63), 16 B per row
+//   [4096, 4608)  fp16 scales [row][2] (block 0, block 1)
 // Inside a row's 16 bytes, 32-bit word g carries elements 8g..8g+7 of the
 // block as nibbles e0 e2 | e4 e6 | e1 e3 | e5 e7 (byte 0 .. byte 3, low nibble
 // first), so that two masks and a shift yield f16 pairs in element order.
-// Rows past N and blocks past K hold weight 0 (nibble 8, scale 0).
-constexpr int kQ4TileN = 256;
+// Rows past N and blocks past K hold weight 0 (nibble 8, scale 0); the row
+// count is padded to a multiple of 256 so a GEMM may take tiles in pairs.
+constexpr int kQ4TileN = 128;
 constexpr int kQ4TileK = 64;
-constexpr int kQ4TileBytes = 9216;
+constexpr int kQ4TileBytes = kQ4TileN * 36;             // 4608
+constexpr int kQ4ScaleOff = kQ4TileN * 32;              // 4096
+constexpr int kQ4Block1Off = kQ4TileN * 16;             // 2048
 
-inline int q4_n_tiles(int N) { return (N + kQ4TileN - 1) / kQ4TileN; }
-inline int q4_k_tiles(int K) { return (K + kQ4TileK - 1) / kQ4TileK; }
+__host__ __device__ inline int q4_n_tiles(int N) { return 2 * ((N + 255) / 256); }
+__host__ __device__ inline int q4_k_tiles(int K) { return (K + kQ4TileK - 1) / kQ4TileK; }
 inline size_t q4_repacked_bytes(int N, int K) {
     return (size_t)q4_n_tiles(N) * q4_k_tiles(K) * kQ4TileBytes;
 }
@@ -31,7 +34,7 @@ inline size_t q4_repacked_bytes(int N, int K) {
 // 16 bytes, element 2i = low nibble of byte i, 2i+1 = high nibble;
 // src/quant.rs:50-64).  pair == false: src_a is [N][K], out row r = src_a row r.
 // pair == true (SwiGLU gate/up): src_a, src_b are [N/2][K] each; in out tile t
-// rows 0..127 are src_a rows 128t.. and rows 128..255 are src_b rows 128t..
+// rows 0..63 are src_a rows 64t.. and rows 64..127 are src_b rows 64t..
 cudaError_t launch_q4_repack(const uint8_t* src_a, const uint8_t* src_b, bool pair, int N, int K,
                              uint8_t* dst, cudaStream_t stream);
 
@@ -52,7 +55,9 @@ struct Q4GemmArgs {
 };
 
 // X: f16 [M][K] row-major device buffer (K % 8 == 0, 16-byte aligned base).
-cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, cudaStream_t stream);
+// Persistent launch: min(output tiles, sm_count) CTAs.
+cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
+                           cudaStream_t stream);
 
 // Builds the 2-D TMA descriptor of an f16 [rows][cols] row-major matrix with a
 // box of 64 x box_rows elements and 128-byte swizzle.

@@ -53,7 +53,7 @@ int32_t velo_cuda_gemm_q4_0(velo_cuda_ctx* c, const void* w, const void* x, int3
     a.ldy = ldy;
     a.mode = mode;
     a.err = c->err_flag;
-    VELO_CUDA_TRY(velo::launch_q4_gemm(a, static_cast<const __half*>(x), c->stream));
+    VELO_CUDA_TRY(velo::launch_q4_gemm(a, static_cast<const __half*>(x), c->sm_count, c->stream));
     return VELO_OK;
 }
 
