@@ -186,6 +186,38 @@ VELO_API int32_t velo_cuda_gemm_q4_0(velo_cuda_ctx *ctx, const void *w_repacked,
                                      int32_t M, int32_t N, int32_t K, void *y, int32_t ldy,
                                      int32_t mode);
 
+/* ---- tree-masked paged attention ---------------------------------------- */
+
+/* Attention of every draft-tree node over the sequence's cached KV pages and
+ * its own root->node path, on the tensor cores.  All pointers are device
+ * memory; asynchronous on the context stream.
+ *   q         [B][n_nodes][n_head][head_dim] f16 (RoPE applied)
+ *   k_pool, v_pool  [pool_pages][n_kv][16][head_dim], f16 (kv_dtype
+ *             VELO_KV_F16) or int8 (VELO_KV_INT8, value = q * scale)
+ *   k_scale, v_scale  [pool_pages][n_kv][16] f16 per-token-per-head scales
+ *             (INT8 only, else NULL)
+ *   page_table [B][max_pages] u32 page ids; ctx_len [B] cached tokens
+ *   node_k, node_v  [B][n_nodes][n_kv][head_dim] f16: K/V of the tree nodes
+ *   parents   [B][n_nodes] i32, -1 for the root, parents[n] < n
+ *   out       [B][n_nodes][n_head][head_dim], f32 (out_dtype 0) or f16 (1)
+ * Node n attends to cached tokens [0, ctx_len) and to the nodes on its
+ * root->n path (itself included); scale 1/sqrt(head_dim); GQA head
+ * h -> h / (n_head / n_kv).  head_dim must be 128, n_nodes <= 64.  Pools
+ * must hold finite values in every slot a page table names (zero-initialise
+ * them), since masked keys still pass through the tensor cores with weight 0.
+ * Replaces paged_attention_tree / paged_attention_flash_int8
+ * (src/kernels.metal:512-599, 672-732) driven by LlamaMetalModel::forward_tree
+ * (src/metal/model.rs:574-731). */
+VELO_API int32_t velo_cuda_tree_attention(velo_cuda_ctx *ctx, const void *q, const void *k_pool,
+                                          const void *v_pool, const void *k_scale,
+                                          const void *v_scale, int32_t pool_pages,
+                                          const uint32_t *page_table, int32_t max_pages,
+                                          const int32_t *ctx_len, const void *node_k,
+                                          const void *node_v, const int32_t *parents, int32_t B,
+                                          int32_t n_nodes, int32_t n_head, int32_t n_kv,
+                                          int32_t head_dim, int32_t kv_dtype, void *out,
+                                          int32_t out_dtype);
+
 #ifdef __cplusplus
 }
 #endif

@@ -28,3 +28,13 @@ def test_repacked_bytes():
     assert velo_cuda.q4_0_repacked_bytes(4096, 4096) == 16 * 64 * 9216
     assert velo_cuda.q4_0_repacked_bytes(300, 96) == 2 * 2 * 9216
     assert velo_cuda.q4_0_repacked_bytes(10, 33) == 0
+
+
+def test_kv_int8_quantiser_matches_oracle():
+    x = synthetic.rng(0, 31).normal(0, 1, (40, 128)).astype(np.float32)
+    x[3] = 0.0
+    q, s = synthetic.quantize_kv_int8(x)
+    for r in range(x.shape[0]):
+        rq, rs = vo.quantize_kv_int8(x[r])
+        assert np.array_equal(q[r], rq)
+        assert s[r].view(np.uint16) == rs

@@ -149,13 +149,29 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor of tcgen05.mma kind::f16: f16 x f16 -> f32, both
-// operands K-major, shape M x N.
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
-    return (1u << 4)                      // D format f32
-           | (0u << 7) | (0u << 10)       // A, B format f16
-           | ((uint32_t)(N >> 3) << 17)   // N / 8
-           | ((uint32_t)(M >> 4) << 24);  // M / 16
+// UMMA shared-memory descriptor of an MN-major operand in the 128-byte
+// swizzle layout: each 128-byte row holds 64 consecutive M/N elements of one
+// K index, 8 K rows form a 1024-byte atom (SBO apart), and the next 64 M/N
+// elements start `mn_stride` bytes further (LBO).  Advancing K by 16 adds
+// 2048 B to the start.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t mn_stride) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((mn_stride >> 4) & 0x3FFFu) << 16;  // leading byte offset: next 64 M/N
+    d |= (uint64_t)(1024u >> 4) << 32;                   // stride byte offset: next 8 K rows
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+// Instruction descriptor of tcgen05.mma kind::f16: f16 x f16 -> f32, shape
+// M x N; A K-major, B K-major (b_mn_major = false) or MN-major (true).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major = false) {
+    return (1u << 4)                          // D format f32
+           | (0u << 7) | (0u << 10)           // A, B format f16
+           | ((b_mn_major ? 1u : 0u) << 16)   // B major-ness
+           | ((uint32_t)(N >> 3) << 17)       // N / 8
+           | ((uint32_t)(M >> 4) << 24);      // M / 16
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
@@ -195,6 +211,30 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 }
 __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Store 32 consecutive 32-bit columns of lane (base lane + t) from thread t.
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 }  // namespace velo::sm100

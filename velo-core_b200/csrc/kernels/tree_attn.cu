@@ -1,0 +1,495 @@
+// tree_attn.cu -- tree-masked paged attention for the verify step on the
+// sm_100a tensor cores.
+//
+// Semantics follow the reference's tree attention (src/kernels.metal:512-599
+// paged_attention_tree, :672-732 the INT8 flash variant): every query row of
+// tree node n attends to the sequence's cached tokens [0, ctx_len) through
+// its 16-token page table, and to the tree nodes on its own root -> n path;
+// scores are q.k / sqrt(head_dim), softmax over that key set, output the
+// probability-weighted V.  INT8 pages carry one fp16 scale per token and
+// head (value = q * scale).  GQA: query head hq reads KV head hq / (Hq/Hkv).
+//
+// One CTA = one (sequence, KV head, 128 query rows) item.  Query rows are the
+// (node, group head) pairs of the KV head, node-major.  Keys stream in tiles
+// of 64 (4 pages), the tree nodes form a final tile with an ancestor mask.
+//   warp 0     producer: TMA (f16 pools, 128-byte swizzle straight into the
+//              operand tiles) or bulk copies of the raw int8 pages + scales
+//   warp 1     one thread issues S = Q K^T (M=128, N=64) into a double-
+//              buffered TMEM tile and O += P V (M=128, N=128, V MN-major)
+//   warp 2     TMEM allocation (S0, S1: 64 columns each; O: 128 columns)
+//   warps 4-7  softmax, thread = query row: S from TMEM, exp2 on the SFU,
+//              P (f16) to shared memory for the PV MMA; O rescaled in TMEM
+//              only when the running max grows by more than 2^8
+//   warps 8-11 int8 -> f16 conversion of K/V tiles into the swizzled operand
+//              layout, and the tree tile (node K/V) for both pool types
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+#include "common/sm100.cuh"
+#include "kernels/q4gemm.h"  // make_tmap_f16_2d
+#include "kernels/tree_attn.h"
+
+namespace velo {
+namespace {
+
+using namespace sm100;
+
+constexpr int D = kAttnHeadDim;        // 128
+constexpr int TK = 64;                 // keys per tile
+constexpr int BMQ = 128;               // query rows per CTA
+constexpr int kThreads = 384;
+constexpr int Q_BYTES = BMQ * D * 2;           // 32 KiB (two 64-wide halves)
+constexpr int KV_HALF = TK * 64 * 2;           // 8 KiB: 64 keys x 64 dims
+constexpr int KV_STAGE = 4 * KV_HALF;          // K halves + V halves: 32 KiB
+constexpr int P_BYTES = BMQ * TK * 2;          // 16 KiB
+constexpr int RAW_KV = TK * D;                 // int8 tile of K (or V): 8 KiB
+constexpr int RAW_STAGE = 2 * RAW_KV + 2 * TK * 2;  // K, V, K scales, V scales
+constexpr float kRescaleLog2 = 8.0f;           // lazy O rescale threshold
+
+constexpr int kErrPage = 0x5101, kErrWait = 0x5102;
+
+template <bool INT8>
+struct AttnCfg {
+    static constexpr int KS = INT8 ? 3 : 4;    // f16 operand ring
+    static constexpr int RS = INT8 ? 3 : 0;    // raw int8 ring
+    static constexpr size_t kSmem = (size_t)Q_BYTES + (size_t)KS * KV_STAGE + 2 * P_BYTES +
+                                    (size_t)RS * RAW_STAGE + (size_t)KS * 2 * TK * 4 + 1024 + 512;
+    static_assert(kSmem <= 227 * 1024, "shared memory budget");
+};
+
+// swizzled byte offset of 16-byte chunk c of row r in a 128-byte-row tile
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+__global__ void tree_ancestors_kernel(const int32_t* __restrict__ parents, int B, int N,
+                                      uint64_t* __restrict__ anc, int* err) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * N) return;
+    const int b = i / N, n = i % N;
+    uint64_t m = 0;
+    int c = n;
+    for (int step = 0; step <= N && c >= 0; ++step) {
+        m |= 1ull << c;
+        const int p = parents[b * N + c];
+        if (p >= c || p < -1) {  // parents must precede their children
+            atomicCAS(err, 0, kErrPage + 16);
+            break;
+        }
+        c = p;
+    }
+    anc[i] = m;
+}
+
+template <bool INT8>
+__global__ void __launch_bounds__(kThreads, 1)
+    tree_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                     const TreeAttnArgs a) {
+    using C = AttnCfg<INT8>;
+    constexpr int KS = C::KS, RS = C::RS;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sq = base;                                // Q: 2 halves x 16 KiB
+    uint8_t* skv = sq + Q_BYTES;                       // KS x (K0 K1 V0 V1) 8 KiB each
+    uint8_t* sp = skv + KS * KV_STAGE;                 // P: 2 x 16 KiB
+    uint8_t* sraw = sp + 2 * P_BYTES;                  // RS x raw int8 stage
+    float* sscale = reinterpret_cast<float*>(sraw + RS * RAW_STAGE);  // KS x (ks[64], vs[64])
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sscale + KS * 2 * TK);
+    uint64_t* kv_full = bars;
+    uint64_t* kv_empty = kv_full + KS;
+    uint64_t* raw_full = kv_empty + KS;                // RS entries (int8)
+    uint64_t* raw_empty = raw_full + (RS ? RS : 1);
+    uint64_t* s_full = raw_empty + (RS ? RS : 1);      // 2
+    uint64_t* s_free = s_full + 2;                     // 2
+    uint64_t* p_full = s_free + 2;                     // 2
+    uint64_t* pv_done = p_full + 2;                    // 1: phase j <-> PV_j done
+    uint64_t* o_full = pv_done + 1;                    // 1: the last PV done
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = a.Hq / a.Hkv;
+    const int rows_total = a.N * G;
+    const int MT = (rows_total + BMQ - 1) / BMQ;
+    const int mt = blockIdx.x % MT;
+    const int h = (blockIdx.x / MT) % a.Hkv;
+    const int b = blockIdx.x / (MT * a.Hkv);
+    const int L = a.ctx_len[b] > 0 ? a.ctx_len[b] : 0;
+    const int T_pre = (L + TK - 1) / TK;
+    const int T = T_pre + 1;  // + the tree tile
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < KS; ++s) {
+            mbar_init(&kv_full[s], INT8 ? 128 : 1 + 128);
+            mbar_init(&kv_empty[s], 1);
+        }
+        for (int s = 0; s < RS; ++s) {
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], 128);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], 128);
+            mbar_init(&p_full[i], 128);
+        }
+        mbar_init(pv_done, 1);
+        mbar_init(o_full, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, 256);
+        tmem_relinquish();
+    }
+    // Q tile (all threads): row r = node-major (node, group head), 16 chunks
+    for (int idx = threadIdx.x; idx < BMQ * 16; idx += kThreads) {
+        const int r = idx >> 4, c = idx & 15;
+        const int row = mt * BMQ + r;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (row < rows_total) {
+            const int node = row / G, g = row % G;
+            const __half* src = a.q + (((size_t)b * a.N + node) * a.Hq + h * G + g) * D + c * 8;
+            v = *reinterpret_cast<const uint4*>(src);
+        }
+        *reinterpret_cast<uint4*>(sq + (c >> 3) * (Q_BYTES / 2) + sw128(r, c & 7)) = v;
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem_o = tmem + 128;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            const uint32_t* pt = a.page_table + (size_t)b * a.max_pages;
+            for (int j = 0; j < T; ++j) {
+                if constexpr (!INT8) {
+                    const int s = j % KS;
+                    if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag))
+                        goto done;
+                    if (j == T_pre) {  // tree tile: filled by the converter warps
+                        mbar_arrive(&kv_full[s]);
+                        continue;
+                    }
+                    mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
+                    uint8_t* st = skv + s * KV_STAGE;
+                    for (int i = 0; i < TK / kKvPage; ++i) {
+                        const int pi = j * (TK / kKvPage) + i;
+                        uint32_t pg = pi < a.max_pages ? pt[pi] : 0u;
+                        if (pg >= (uint32_t)a.pool_pages) {
+                            atomicCAS(a.err, 0, kErrPage);
+                            pg = 0;
+                        }
+                        const int row = (int)((pg * a.Hkv + h) * kKvPage);
+                        for (int dh = 0; dh < 2; ++dh) {
+                            tma_load_2d(st + dh * KV_HALF + i * 2048, &tmk, &kv_full[s], dh * 64, row);
+                            tma_load_2d(st + 2 * KV_HALF + dh * KV_HALF + i * 2048, &tmv, &kv_full[s],
+                                        dh * 64, row);
+                        }
+                    }
+                } else {
+                    if (j == T_pre) continue;  // tree tile: converters only
+                    const int r = j % RS;
+                    if (!mbar_wait(&raw_empty[r], ((j / RS) & 1) ^ 1, a.err, kErrWait, abort_flag))
+                        goto done;
+                    mbar_arrive_expect_tx(&raw_full[r], RAW_STAGE);
+                    uint8_t* st = sraw + r * RAW_STAGE;
+                    for (int i = 0; i < TK / kKvPage; ++i) {
+                        const int pi = j * (TK / kKvPage) + i;
+                        uint32_t pg = pi < a.max_pages ? pt[pi] : 0u;
+                        if (pg >= (uint32_t)a.pool_pages) {
+                            atomicCAS(a.err, 0, kErrPage);
+                            pg = 0;
+                        }
+                        const size_t blk = (size_t)pg * a.Hkv + h;  // (page, head) block
+                        bulk_load(st + i * 2048, static_cast<const int8_t*>(a.k_pool) + blk * 2048, 2048,
+                                  &raw_full[r]);
+                        bulk_load(st + RAW_KV + i * 2048, static_cast<const int8_t*>(a.v_pool) + blk * 2048,
+                                  2048, &raw_full[r]);
+                        bulk_load(st + 2 * RAW_KV + i * 32, a.k_scale + blk * kKvPage, 32, &raw_full[r]);
+                        bulk_load(st + 2 * RAW_KV + TK * 2 + i * 32, a.v_scale + blk * kKvPage, 32,
+                                  &raw_full[r]);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issue
+        if (lane == 0) {
+            const uint32_t id_s = idesc_f16_f32(BMQ, TK);
+            const uint32_t id_pv = idesc_f16_f32(BMQ, D, /*b_mn_major=*/true);
+            const uint32_t q_addr = smem_u32(sq);
+            for (int j = 0; j <= T; ++j) {
+                if (j < T) {
+                    const int s = j % KS, sb = j & 1;
+                    if (!mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag) ||
+                        !mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, a.err, kErrWait, abort_flag))
+                        goto done;
+                    tc_fence_after();
+                    const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
+#pragma unroll
+                    for (int k = 0; k < D / 16; ++k) {
+                        const uint64_t ad = desc_kmajor_sw128(q_addr + (k >> 2) * (Q_BYTES / 2)) + (k & 3) * 2;
+                        const uint64_t bd = desc_kmajor_sw128(k_addr + (k >> 2) * KV_HALF) + (k & 3) * 2;
+                        mma_f16_ss(tmem + sb * TK, ad, bd, id_s, k > 0);
+                    }
+                    mma_commit(&s_full[sb]);
+                }
+                if (j >= 1) {
+                    const int jj = j - 1, pb = jj & 1, sv = jj % KS;
+                    if (!mbar_wait(&p_full[pb], (jj >> 1) & 1, a.err, kErrWait, abort_flag)) goto done;
+                    tc_fence_after();
+                    const uint32_t p_addr = smem_u32(sp + pb * P_BYTES);
+                    const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
+#pragma unroll
+                    for (int kk = 0; kk < TK / 16; ++kk) {
+                        const uint64_t ad = desc_kmajor_sw128(p_addr) + kk * 2;
+                        const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
+                        mma_f16_ss(tmem_o, ad, bd, id_pv, (jj | kk) != 0);
+                    }
+                    mma_commit(&kv_empty[sv]);
+                    mma_commit(pv_done);
+                    if (jj == T - 1) mma_commit(o_full);
+                }
+            }
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------------------ softmax
+        const int r = threadIdx.x - 128;           // TMEM lane = query row
+        const int row = mt * BMQ + r;
+        const bool row_ok = row < rows_total;
+        const int node = row_ok ? row / G : 0;
+        const uint64_t anc = row_ok ? a.anc[(size_t)b * a.N + node] : 0ull;
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        float m = -INFINITY, l = 0.0f;
+        for (int j = 0; j < T; ++j) {
+            const int sb = j & 1, s = j % KS;
+            const bool got = mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag);
+            if (!__all_sync(0xffffffffu, got)) goto done;
+            tc_fence_after();
+            uint32_t sr[64];
+            tmem_ld_32x32b_x32(tmem + lane_base + sb * TK, *reinterpret_cast<uint32_t(*)[32]>(sr));
+            tmem_ld_32x32b_x32(tmem + lane_base + sb * TK + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(&s_free[sb]);
+            const bool tree = j == T_pre;
+            const float* ks = sscale + s * 2 * TK;
+            if constexpr (INT8) {
+                // scales of this stage were written by the converter warps
+                const bool ok = mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+            }
+            // scaled scores (log2 domain) overwrite the raw ones in place
+            float* x = reinterpret_cast<float*>(sr);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int t = 0; t < 64; ++t) {
+                const bool ok = tree ? ((anc >> t) & 1ull) != 0 : (j * TK + t < L);
+                float v = x[t] * a.scale_log2;
+                if constexpr (INT8) v *= ks[t];
+                v = ok ? v : -INFINITY;
+                x[t] = v;
+                mx = fmaxf(mx, v);
+            }
+            // lazy rescale, decided per warp so the TMEM accesses stay convergent:
+            // a row whose max grew by more than 2^8 (or its first valid key)
+            // moves the whole warp to the new maxima
+            if (__any_sync(0xffffffffu, mx > m + kRescaleLog2)) {
+                const float m_new = fmaxf(m, mx);
+                const float f = m == -INFINITY ? 0.0f : ex2_approx(m - m_new);
+                l *= f;
+                if (j > 0) {
+                    // O holds PV_0..PV_{j-1}; wait for PV_{j-1}.  Its phase is the
+                    // only one in doubt: S_j was issued after PV_{j-2} (so phase
+                    // j-2 is complete) and PV_j needs this tile's P (so phase j
+                    // is not), hence a parity wait is exact here.
+                    const bool ok = mbar_wait(pv_done, (j - 1) & 1, a.err, kErrWait, abort_flag);
+                    if (!__all_sync(0xffffffffu, ok)) goto done;
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c = 0; c < D / 32; ++c) {
+                        uint32_t o[32];
+                        tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+                        tmem_st_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                    }
+                    tmem_st_wait();
+                }
+                m = m_new;
+            }
+            // P (times the V scale for int8 pages) -> f16, row r of the P tile
+            uint8_t* prow = sp + sb * P_BYTES;
+            const float* vs = ks + TK;
+            float lsum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int t = c * 8 + 2 * e;
+                    float p0 = x[t] == -INFINITY ? 0.0f : ex2_approx(x[t] - m);
+                    float p1 = x[t + 1] == -INFINITY ? 0.0f : ex2_approx(x[t + 1] - m);
+                    lsum += p0 + p1;
+                    if constexpr (INT8) {
+                        p0 *= vs[t];
+                        p1 *= vs[t + 1];
+                    }
+                    __half2 hp = __floats2half2_rn(p0, p1);
+                    w[e] = *reinterpret_cast<uint32_t*>(&hp);
+                }
+                *reinterpret_cast<uint4*>(prow + sw128(r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            l += lsum;
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(&p_full[sb]);
+        }
+        // epilogue: O / l after the last PV
+        {
+            const bool ok = mbar_wait(o_full, 0, a.err, kErrWait, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) goto done;
+        }
+        tc_fence_after();
+        {
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const int g = row_ok ? row % G : 0;
+            const size_t obase = (((size_t)b * a.N + node) * a.Hq + h * G + g) * D;
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t o[32];
+                tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                tmem_ld_wait();
+                if (!row_ok) continue;
+                if (a.out_f16) {
+                    __half* dst = static_cast<__half*>(a.out) + obase + c * 32;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            __half2 hv = __floats2half2_rn(__uint_as_float(o[q * 8 + 2 * e]) * inv,
+                                                           __uint_as_float(o[q * 8 + 2 * e + 1]) * inv);
+                            w[e] = *reinterpret_cast<uint32_t*>(&hv);
+                        }
+                        reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                } else {
+                    float* dst = static_cast<float*>(a.out) + obase + c * 32;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        reinterpret_cast<float4*>(dst)[q] =
+                            make_float4(__uint_as_float(o[4 * q]) * inv, __uint_as_float(o[4 * q + 1]) * inv,
+                                        __uint_as_float(o[4 * q + 2]) * inv, __uint_as_float(o[4 * q + 3]) * inv);
+                }
+            }
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------------------ converters
+        const int t = threadIdx.x - 256;  // 0..127
+        const int kr = t >> 1, hh = t & 1;  // key row, 64-dim half
+        for (int j = 0; j < T; ++j) {
+            const int s = j % KS;
+            if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag)) goto done;
+            uint8_t* st = skv + s * KV_STAGE;
+            float* ssc = sscale + s * 2 * TK;
+            if (j == T_pre) {
+                // tree tile: node K/V rows (f16), zero past the last node
+                const bool ok = kr < a.N;
+                const size_t src = (((size_t)b * a.N + (ok ? kr : 0)) * a.Hkv + h) * D + hh * 64;
+#pragma unroll
+                for (int kvs = 0; kvs < 2; ++kvs) {
+                    const uint4* g = reinterpret_cast<const uint4*>((kvs ? a.node_v : a.node_k) + src);
+                    uint4 v[8];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) v[c] = ok ? g[c] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        *reinterpret_cast<uint4*>(st + kvs * 2 * KV_HALF + hh * KV_HALF + sw128(kr, c)) = v[c];
+                }
+                if constexpr (INT8) ssc[t] = 1.0f;  // ks[0..63], vs[0..63]: unscaled
+            } else if constexpr (INT8) {
+                const int r = j % RS;
+                if (!mbar_wait(&raw_full[r], (j / RS) & 1, a.err, kErrWait, abort_flag)) goto done;
+                const uint8_t* rs = sraw + r * RAW_STAGE;
+#pragma unroll
+                for (int kvs = 0; kvs < 2; ++kvs) {
+                    const uint4* src = reinterpret_cast<const uint4*>(rs + kvs * RAW_KV + kr * D + hh * 64);
+                    uint8_t* dst = st + kvs * 2 * KV_HALF + hh * KV_HALF;
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const uint4 raw = src[c4];  // 16 int8 -> two 16-byte f16 chunks
+                        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+                        uint32_t o[8];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int8_t* bb = reinterpret_cast<const int8_t*>(&wv[e]);
+                            __half2 h0 = __halves2half2(__int2half_rn(bb[0]), __int2half_rn(bb[1]));
+                            __half2 h1 = __halves2half2(__int2half_rn(bb[2]), __int2half_rn(bb[3]));
+                            o[2 * e] = *reinterpret_cast<uint32_t*>(&h0);
+                            o[2 * e + 1] = *reinterpret_cast<uint32_t*>(&h1);
+                        }
+                        *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                        *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                    }
+                }
+                const __half* sc = reinterpret_cast<const __half*>(rs + 2 * RAW_KV);
+                ssc[t] = __half2float(sc[t]);  // t < 64: K scales, t >= 64: V scales
+                mbar_arrive(&raw_empty[r]);    // after every read of the raw stage
+            }
+            fence_async_smem();
+            mbar_arrive(&kv_full[s]);
+        }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
+template <bool INT8>
+cudaError_t launch_impl(const TreeAttnArgs& a, cudaStream_t stream) {
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(tree_attn_kernel<INT8>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)AttnCfg<INT8>::kSmem);
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    CUtensorMap tk{}, tv{};
+    if (!INT8) {
+        const uint64_t rows = (uint64_t)a.pool_pages * a.Hkv * kKvPage;
+        cudaError_t e = make_tmap_f16_2d(&tk, a.k_pool, rows, D, D * 2, kKvPage);
+        if (e == cudaSuccess) e = make_tmap_f16_2d(&tv, a.v_pool, rows, D, D * 2, kKvPage);
+        if (e != cudaSuccess) return e;
+    }
+    const int G = a.Hq / a.Hkv;
+    const int MT = (a.N * G + BMQ - 1) / BMQ;
+    const long grid = (long)a.B * a.Hkv * MT;
+    tree_attn_kernel<INT8><<<(unsigned)grid, kThreads, AttnCfg<INT8>::kSmem, stream>>>(tk, tv, a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_tree_ancestors(const int32_t* parents, int B, int N, uint64_t* anc, int* err,
+                                  cudaStream_t stream) {
+    const int n = B * N;
+    tree_ancestors_kernel<<<(n + 127) / 128, 128, 0, stream>>>(parents, B, N, anc, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tree_attention(const TreeAttnArgs& a, bool kv_int8, cudaStream_t stream) {
+    return kv_int8 ? launch_impl<true>(a, stream) : launch_impl<false>(a, stream);
+}
+
+}  // namespace velo

@@ -134,6 +134,7 @@ void velo_cuda_destroy(velo_cuda_ctx* c) {
     c->workspace.release();
     c->counters.release();
     c->io.release();
+    c->attn_ws.release();
     if (c->err_flag) cudaFree(c->err_flag);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     delete c;

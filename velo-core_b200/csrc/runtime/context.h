@@ -50,5 +50,6 @@ struct velo_cuda_ctx {
     velo::DeviceBuffer workspace;  // per-launch scratch (tile statistics, partials)
     velo::DeviceBuffer counters;   // completion tickets, zero between launches
     velo::DeviceBuffer io;         // device copies for the host-buffer entries
+    velo::DeviceBuffer attn_ws;    // tree attention: ancestor masks
     int* err_flag = nullptr;       // device-side input flag
 };

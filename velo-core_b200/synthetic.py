@@ -81,3 +81,63 @@ def q4_0_weights(rows, cols, sigma=0.02, seed=0, stream=10):
     """Random-init weight N(0, sigma^2), quantised to q4_0."""
     w = rng(seed, stream).normal(0.0, sigma, (rows, cols)).astype(np.float32)
     return quantize_q4_0(w)
+
+
+def quantize_kv_int8(x):
+    """Per-row int8 quantisation of K/V rows [..., head_dim] (the reference's
+    kv_update_int8 rule, src/kernels.metal:783-801, with an fp16 scale):
+    scale = max|x| / 127, q = trunc(x * (127 / max|x|)), in f32 arithmetic.
+    Returns (int8 values, f16 scales [...])."""
+    x = np.ascontiguousarray(x, np.float32)
+    mx = np.abs(x).max(axis=-1)
+    sc = (mx / np.float32(127.0)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        inv = np.where(mx > 0, np.float32(127.0) / mx, np.float32(0.0)).astype(np.float32)
+    q = np.trunc((x * inv[..., None]).astype(np.float32)).astype(np.int8)
+    return q, sc.astype(np.float16)
+
+
+def random_tree(n_nodes, max_depth, g):
+    """Parents of a random draft tree: node 0 is the root (-1); node n picks a
+    parent uniformly among earlier nodes of depth < max_depth."""
+    parents = np.full(n_nodes, -1, np.int32)
+    depth = np.zeros(n_nodes, np.int32)
+    for n in range(1, n_nodes):
+        cand = np.nonzero(depth[:n] < max_depth - 1)[0]
+        p = int(cand[g.integers(0, len(cand))])
+        parents[n] = p
+        depth[n] = depth[p] + 1
+    return parents
+
+
+def tree_attention_inputs(B, n_nodes, n_head, n_kv, ctx_lens, kv_dtype=0, seed=0, max_depth=6,
+                          head_dim=128, page=16, spare_pages=3):
+    """Paged tree-attention inputs (BASELINE config 4 distributions): K/V and
+    queries ~ N(0,1); pages of all sequences are a random permutation of the
+    pool; int8 pools hold trunc-quantised values with f16 per-token scales.
+    Returns a dict of numpy arrays in the layouts of velo_cuda_tree_attention."""
+    ctx_lens = np.asarray(ctx_lens, np.int32)
+    npages = [(int(c) + page - 1) // page for c in ctx_lens]
+    max_pages = max(1, max(npages))
+    total = sum(npages) + spare_pages
+    perm = rng(seed, 30).permutation(total).astype(np.uint32)
+    page_table = np.zeros((B, max_pages), np.uint32)
+    off = 0
+    for b in range(B):
+        page_table[b, :npages[b]] = perm[off:off + npages[b]]
+        off += npages[b]
+    kv = rng(seed, 31).normal(0, 1, (2, total, n_kv, page, head_dim)).astype(np.float32)
+    out = {"page_table": page_table, "ctx_len": ctx_lens, "kv_dtype": kv_dtype}
+    if kv_dtype == 0:
+        out["k_pool"] = kv[0].astype(np.float16)
+        out["v_pool"] = kv[1].astype(np.float16)
+        out["k_scale"] = out["v_scale"] = None
+    else:
+        out["k_pool"], out["k_scale"] = quantize_kv_int8(kv[0])
+        out["v_pool"], out["v_scale"] = quantize_kv_int8(kv[1])
+    out["q"] = rng(seed, 32).normal(0, 1, (B, n_nodes, n_head, head_dim)).astype(np.float16)
+    out["node_k"] = rng(seed, 33).normal(0, 1, (B, n_nodes, n_kv, head_dim)).astype(np.float16)
+    out["node_v"] = rng(seed, 34).normal(0, 1, (B, n_nodes, n_kv, head_dim)).astype(np.float16)
+    g = rng(seed, 35)
+    out["parents"] = np.stack([random_tree(n_nodes, max_depth, g) for _ in range(B)])
+    return out

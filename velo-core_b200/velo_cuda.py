@@ -68,6 +68,8 @@ _SIGS = {
     "velo_cuda_q4_0_repacked_bytes": (ctypes.c_size_t, [_I32, _I32]),
     "velo_cuda_q4_0_repack": (_I32, [_P, _P, _P, _I32, _I32, _P]),
     "velo_cuda_gemm_q4_0": (_I32, [_P, _P, _P, _I32, _I32, _I32, _P, _I32, _I32]),
+    "velo_cuda_tree_attention": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _P, _I32, _P, _P, _P, _P,
+                                        _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32]),
 }
 
 EPI_STORE_F32, EPI_STORE_F16, EPI_ADD_F32, EPI_SWIGLU = 0, 1, 2, 3
@@ -185,6 +187,19 @@ class Context:
     def gemm_q4_0(self, w, x, M, N, K, y, ldy, mode):
         """y (+)= x[M][K] (f16) * W^T on the tensor cores; asynchronous."""
         check(lib().velo_cuda_gemm_q4_0(self._h, _ptr(w), _ptr(x), M, N, K, _ptr(y), ldy, mode))
+
+
+    # ------------------------------------------------------------ attention
+    def tree_attention(self, q, k_pool, v_pool, k_scale, v_scale, page_table, ctx_len, node_k,
+                       node_v, parents, n_kv, kv_dtype, out):
+        """Tree-masked paged attention on torch CUDA tensors (asynchronous).
+        q [B][N][Hq][128] f16; pools [P][n_kv][16][128]; out f32 or f16."""
+        B, N, Hq, hd = q.shape
+        out_f16 = 1 if out.dtype.itemsize == 2 else 0
+        check(lib().velo_cuda_tree_attention(
+            self._h, _ptr(q), _ptr(k_pool), _ptr(v_pool), _ptr(k_scale), _ptr(v_scale),
+            k_pool.shape[0], _ptr(page_table), page_table.shape[1], _ptr(ctx_len), _ptr(node_k),
+            _ptr(node_v), _ptr(parents), B, N, Hq, n_kv, hd, kv_dtype, _ptr(out), out_f16))
 
 
 def q4_0_repacked_bytes(N, K):
