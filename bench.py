@@ -400,6 +400,131 @@ def run_q4gemm(args):
     return 0
 
 
+# ---------------------------------------------------------------- tree attention workload
+def _attn_device_inputs(B, N, Hq, Hkv, ctx, kv_int8, seed, dev):
+    """Config-4 / config-3 attention inputs built on the device (seeded torch
+    generator): K/V ~ N(0,1) (int8: per-token-per-head trunc quantisation,
+    f16 scale), random page permutation, random draft trees of depth <= 6."""
+    import torch
+    import synthetic
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    npg = [(int(c) + 15) // 16 for c in ctx]
+    total = sum(npg) + 1
+    perm = torch.randperm(total, generator=g, device=dev).to(torch.int32)
+    max_pages = max(npg)
+    pt = torch.zeros((B, max_pages), dtype=torch.int32, device=dev)
+    off = 0
+    for b in range(B):
+        pt[b, :npg[b]] = perm[off:off + npg[b]]
+        off += npg[b]
+    pools, scales = [], []
+    for _ in range(2):
+        if kv_int8:
+            pool = torch.empty((total, Hkv, 16, 128), dtype=torch.int8, device=dev)
+            sc = torch.empty((total, Hkv, 16), dtype=torch.float16, device=dev)
+            step = 4096
+            for p0 in range(0, total, step):
+                x = torch.randn((min(step, total - p0), Hkv, 16, 128), generator=g, device=dev)
+                mx = x.abs().amax(-1)
+                inv = torch.where(mx > 0, 127.0 / mx, torch.zeros_like(mx))
+                pool[p0:p0 + x.shape[0]] = torch.trunc(x * inv[..., None]).to(torch.int8)
+                sc[p0:p0 + x.shape[0]] = (mx / 127.0).half()
+            pools.append(pool)
+            scales.append(sc.view(torch.int16))
+        else:
+            pools.append(torch.randn((total, Hkv, 16, 128), generator=g, device=dev).half())
+            scales.append(None)
+    q = torch.randn((B, N, Hq, 128), generator=g, device=dev).half()
+    nk = torch.randn((B, N, Hkv, 128), generator=g, device=dev).half()
+    nv = torch.randn((B, N, Hkv, 128), generator=g, device=dev).half()
+    gg = synthetic.rng(seed, 35)
+    par = torch.from_numpy(np.stack([synthetic.random_tree(N, 6, gg) for _ in range(B)])).to(dev)
+    ctx_t = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    depth_sum = 0
+    for row in par.cpu().numpy():
+        d = np.zeros(N, np.int64)
+        for n in range(1, N):
+            d[n] = d[row[n]] + 1
+        depth_sum += int((d + 1).sum())
+    return dict(q=q, k=pools[0], v=pools[1], ks=scales[0], vs=scales[1], pt=pt, ctx=ctx_t,
+                nk=nk, nv=nv, par=par, total=total, depth_sum=depth_sum)
+
+
+def run_attn(args):
+    """Tree-masked paged attention at BASELINE config 4 (INT8 KV, B=128, 64
+    nodes, 32/8 heads, ctx U{512..8192}) and one config-3 layer (f16 KV, B=32,
+    16 nodes, 32/32 heads, ctx 2048).  Pools total > L2, so launches stream
+    their KV from HBM."""
+    import torch
+    import velo_cuda
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    ctx = velo_cuda.Context(device=0)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    hbm = float(peaks.get("hbm_gbs", HBM_FALLBACK_GBS))
+    tfl = float(peaks.get("bf16_tflops", 1590.0))
+    res = []
+    cfgs = [("config4_int8", 128, 64, 32, 8, None, True),
+            ("config3_layer_f16", 32, 16, 32, 32, 2048, False)]
+    for name, B, N, Hq, Hkv, fixed_ctx, i8 in cfgs:
+        if args.case and args.case != name:
+            continue
+        if fixed_ctx is None:
+            ctx_l = [int(c) for c in synthetic_ctx(B)]
+        else:
+            ctx_l = [fixed_ctx] * B
+        d = _attn_device_inputs(B, N, Hq, Hkv, ctx_l, i8, 0, dev)
+        out = torch.empty((B, N, Hq, 128), dtype=torch.float16, device=dev)
+        call = lambda: ctx.tree_attention(d["q"], d["k"], d["v"], d["ks"], d["vs"], d["pt"],
+                                          d["ctx"], d["nk"], d["nv"], d["par"], Hkv,
+                                          1 if i8 else 0, out)
+        for _ in range(max(3, args.warmup)):
+            call()
+        torch.cuda.synchronize()
+        ctx.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(5, min(args.steps, 100))
+        e0.record(stream)
+        for _ in range(n):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ctx.sync()
+        us = e0.elapsed_time(e1) * 1e3 / n
+        tok = sum(ctx_l)
+        elt = 1 if i8 else 2
+        kv_bytes = tok * Hkv * 128 * elt * 2 + (tok * Hkv * 2 * 2 if i8 else 0)
+        io_bytes = B * N * Hq * 128 * 2 * 2 + B * N * Hkv * 128 * 2 * 2
+        alg_bytes = kv_bytes + io_bytes
+        flops = 2.0 * 2.0 * 128 * Hq * (N * tok + d["depth_sum"])
+        res.append({"case": name, "B": B, "nodes": N, "heads": f"{Hq}/{Hkv}",
+                    "kv": "int8" if i8 else "f16", "ctx_tokens": tok, "us": us,
+                    "alg_bytes": alg_bytes, "gbs": alg_bytes / us / 1e3,
+                    "hbm_frac": alg_bytes / us / 1e3 / hbm, "tflops": flops / us / 1e6,
+                    "tensor_frac": flops / us / 1e6 / tfl})
+        del d
+        torch.cuda.empty_cache()
+    ctx.close()
+    print(json.dumps({"workload": "tree-masked paged attention (BASELINE configs 4 and 3)",
+                      "per_case": res, "hbm_peak_gbs": hbm, "bf16_peak_tflops": tfl}), flush=True)
+    return 0
+
+
+def synthetic_ctx(B, seed=0):
+    """Per-sequence context lengths U{512..8192}."""
+    import synthetic
+    return synthetic.rng(seed, 36).integers(512, 8193, B)
+
+
 def cpu_baseline():
     """The CPU port (oracle) on this host, full C2 batch repeated ~10 s."""
     import vo
@@ -425,8 +550,9 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    ap.add_argument("--workload", default="accept", choices=["accept", "q4gemm"])
+    ap.add_argument("--workload", default="accept", choices=["accept", "q4gemm", "attn"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default="", help="one case of a multi-case workload")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -434,6 +560,8 @@ def main():
         return run_reference(args)
     if args.workload == "q4gemm":
         return run_q4gemm(args)
+    if args.workload == "attn":
+        return run_attn(args)
     return run_cuda(args)
 
 

@@ -63,13 +63,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity,
 
 // Waits until the phase with `parity` of `bar` has completed.  Returns false
 // (after recording `code` in *err) if that takes longer than kWaitLimitNs or
-// another role of the CTA already gave up (*abort != 0).
+// another role of the CTA already gave up (*abort != 0).  `sleep_ns` > 0 backs
+// off between tests, for waiters off the critical path whose spinning would
+// otherwise take issue slots from the warps doing the work.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
-                                          volatile int* abort) {
+                                          volatile int* abort, uint32_t sleep_ns = 0) {
     const uint32_t b = smem_u32(bar);
     if (mbar_try_wait(b, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
+        if (sleep_ns) __nanosleep(sleep_ns);
         if (mbar_try_wait(b, parity)) return true;
         if ((i & 15u) == 0) {
             if (*abort) return false;

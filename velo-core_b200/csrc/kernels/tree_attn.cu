@@ -17,11 +17,12 @@
 //   warp 1     one thread issues S = Q K^T (M=128, N=64) into a double-
 //              buffered TMEM tile and O += P V (M=128, N=128, V MN-major)
 //   warp 2     TMEM allocation (S0, S1: 64 columns each; O: 128 columns)
-//   warps 4-7  softmax, thread = query row: S from TMEM, exp2 on the SFU,
-//              P (f16) to shared memory for the PV MMA; O rescaled in TMEM
-//              only when the running max grows by more than 2^8
-//   warps 8-11 int8 -> f16 conversion of K/V tiles into the swizzled operand
-//              layout, and the tree tile (node K/V) for both pool types
+//   warps 4-11 softmax, two threads per query row (32 keys each): S from
+//              TMEM, exp2 on the SFU, P (f16) to shared memory for the PV MMA;
+//              O rescaled in TMEM only when the running max grows by > 2^8
+//   warps 12-15 the tree tile (node K/V) into its own buffer at the start,
+//              then (int8 pools) int8 -> f16 conversion of the K/V tiles into
+//              the swizzled operand layout
 #include <cuda_fp16.h>
 
 #include <mutex>
@@ -38,7 +39,7 @@ using namespace sm100;
 constexpr int D = kAttnHeadDim;        // 128
 constexpr int TK = 64;                 // keys per tile
 constexpr int BMQ = 128;               // query rows per CTA
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;
 constexpr int Q_BYTES = BMQ * D * 2;           // 32 KiB (two 64-wide halves)
 constexpr int KV_HALF = TK * 64 * 2;           // 8 KiB: 64 keys x 64 dims
 constexpr int KV_STAGE = 4 * KV_HALF;          // K halves + V halves: 32 KiB
@@ -51,16 +52,37 @@ constexpr int kErrPage = 0x5101, kErrWait = 0x5102;
 
 template <bool INT8>
 struct AttnCfg {
-    static constexpr int KS = INT8 ? 3 : 4;    // f16 operand ring
+    static constexpr int KS = INT8 ? 2 : 4;    // f16 operand ring (cached tokens)
     static constexpr int RS = INT8 ? 3 : 0;    // raw int8 ring
-    static constexpr size_t kSmem = (size_t)Q_BYTES + (size_t)KS * KV_STAGE + 2 * P_BYTES +
-                                    (size_t)RS * RAW_STAGE + (size_t)KS * 2 * TK * 4 + 1024 + 512;
+    // Q, the ring, the tree tile (its own buffer), P x 2, raw ring, scales
+    static constexpr size_t kSmem = (size_t)Q_BYTES + (size_t)(KS + 1) * KV_STAGE + 2 * P_BYTES +
+                                    (size_t)RS * RAW_STAGE + (INT8 ? (size_t)KS * 2 * TK * 4 : 0) +
+                                    1024 + 512 + 2 * BMQ * 4;
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
 };
 
 // swizzled byte offset of 16-byte chunk c of row r in a 128-byte-row tile
 __device__ __forceinline__ uint32_t sw128(int r, int c) {
     return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+// Named barrier of the two softmax warps that share TMEM lane quadrant q.
+__device__ __forceinline__ void pair_sync(int q) {
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + q) : "memory");
+}
+
+// Four int8 (little-endian in w) -> f16 pairs (b0,b1), (b2,b3), exactly:
+// flipping the sign bit gives u = x + 128, 0x6400 | u is 1024 + u in f16, and
+// subtracting 1152 leaves x.
+__device__ __forceinline__ void i8x4_to_f16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    const uint32_t r01 = __byte_perm(u, 0x64646464u, 0x5140);
+    const uint32_t r23 = __byte_perm(u, 0x64646464u, 0x5342);
+    const __half2 k = __half2half2(__ushort_as_half(0x6480));  // 1152
+    const __half2 a = __hsub2(*reinterpret_cast<const __half2*>(&r01), k);
+    const __half2 c = __hsub2(*reinterpret_cast<const __half2*>(&r23), k);
+    lo = *reinterpret_cast<const uint32_t*>(&a);
+    hi = *reinterpret_cast<const uint32_t*>(&c);
 }
 
 __global__ void tree_ancestors_kernel(const int32_t* __restrict__ parents, int B, int N,
@@ -92,10 +114,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sq = base;                                // Q: 2 halves x 16 KiB
     uint8_t* skv = sq + Q_BYTES;                       // KS x (K0 K1 V0 V1) 8 KiB each
-    uint8_t* sp = skv + KS * KV_STAGE;                 // P: 2 x 16 KiB
+    uint8_t* stree = skv + KS * KV_STAGE;              // tree tile (K0 K1 V0 V1)
+    uint8_t* sp = stree + KV_STAGE;                    // P: 2 x 16 KiB
     uint8_t* sraw = sp + 2 * P_BYTES;                  // RS x raw int8 stage
     float* sscale = reinterpret_cast<float*>(sraw + RS * RAW_STAGE);  // KS x (ks[64], vs[64])
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sscale + KS * 2 * TK);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sscale + (INT8 ? KS * 2 * TK : 0));
     uint64_t* kv_full = bars;
     uint64_t* kv_empty = kv_full + KS;
     uint64_t* raw_full = kv_empty + KS;                // RS entries (int8)
@@ -105,8 +128,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* p_full = s_free + 2;                     // 2
     uint64_t* pv_done = p_full + 2;                    // 1: phase j <-> PV_j done
     uint64_t* o_full = pv_done + 1;                    // 1: the last PV done
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
+    uint64_t* tree_full = o_full + 1;                  // 1: tree tile written
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tree_full + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* sxch = reinterpret_cast<float*>(tmem_slot + 4);  // [2][128] row exchange
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.Hq / a.Hkv;
@@ -121,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < KS; ++s) {
-            mbar_init(&kv_full[s], INT8 ? 128 : 1 + 128);
+            mbar_init(&kv_full[s], INT8 ? 128 : 1);
             mbar_init(&kv_empty[s], 1);
         }
         for (int s = 0; s < RS; ++s) {
@@ -130,11 +155,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 128);
-            mbar_init(&p_full[i], 128);
+            mbar_init(&s_free[i], 256);
+            mbar_init(&p_full[i], 256);
         }
         mbar_init(pv_done, 1);
         mbar_init(o_full, 1);
+        mbar_init(tree_full, 128);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -165,15 +191,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             const uint32_t* pt = a.page_table + (size_t)b * a.max_pages;
-            for (int j = 0; j < T; ++j) {
+            for (int j = 0; j < T_pre; ++j) {
                 if constexpr (!INT8) {
                     const int s = j % KS;
-                    if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag))
+                    if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag, 64))
                         goto done;
-                    if (j == T_pre) {  // tree tile: filled by the converter warps
-                        mbar_arrive(&kv_full[s]);
-                        continue;
-                    }
                     mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
                     uint8_t* st = skv + s * KV_STAGE;
                     for (int i = 0; i < TK / kKvPage; ++i) {
@@ -191,9 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 } else {
-                    if (j == T_pre) continue;  // tree tile: converters only
                     const int r = j % RS;
-                    if (!mbar_wait(&raw_empty[r], ((j / RS) & 1) ^ 1, a.err, kErrWait, abort_flag))
+                    if (!mbar_wait(&raw_empty[r], ((j / RS) & 1) ^ 1, a.err, kErrWait, abort_flag, 64))
                         goto done;
                     mbar_arrive_expect_tx(&raw_full[r], RAW_STAGE);
                     uint8_t* st = sraw + r * RAW_STAGE;
@@ -225,11 +246,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j <= T; ++j) {
                 if (j < T) {
                     const int s = j % KS, sb = j & 1;
-                    if (!mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag) ||
+                    const bool tree = j == T_pre;
+                    if (!(tree ? mbar_wait(tree_full, 0, a.err, kErrWait, abort_flag)
+                               : mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag)) ||
                         !mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, a.err, kErrWait, abort_flag))
                         goto done;
                     tc_fence_after();
-                    const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
+                    const uint32_t k_addr = smem_u32(tree ? stree : skv + s * KV_STAGE);
 #pragma unroll
                     for (int k = 0; k < D / 16; ++k) {
                         const uint64_t ad = desc_kmajor_sw128(q_addr + (k >> 2) * (Q_BYTES / 2)) + (k & 3) * 2;
@@ -243,61 +266,75 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait(&p_full[pb], (jj >> 1) & 1, a.err, kErrWait, abort_flag)) goto done;
                     tc_fence_after();
                     const uint32_t p_addr = smem_u32(sp + pb * P_BYTES);
-                    const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
+                    const bool tree = jj == T_pre;
+                    const uint32_t v_addr = smem_u32((tree ? stree : skv + sv * KV_STAGE) + 2 * KV_HALF);
 #pragma unroll
                     for (int kk = 0; kk < TK / 16; ++kk) {
                         const uint64_t ad = desc_kmajor_sw128(p_addr) + kk * 2;
                         const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
                         mma_f16_ss(tmem_o, ad, bd, id_pv, (jj | kk) != 0);
                     }
-                    mma_commit(&kv_empty[sv]);
+                    if (!tree) mma_commit(&kv_empty[sv]);
                     mma_commit(pv_done);
                     if (jj == T - 1) mma_commit(o_full);
                 }
             }
         }
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= 4 && warp < 12) {
         // ------------------------------------------------------------ softmax
-        const int r = threadIdx.x - 128;           // TMEM lane = query row
+        // warps w and w + 4 share TMEM lane quadrant q = w % 4 (query rows
+        // 32q..32q+31); half ch = 0 takes keys 0..31 and O columns 0..63, ch = 1
+        // keys 32..63 and O columns 64..127.  Row maxima and sums meet in
+        // shared memory behind a named barrier of the warp pair.
+        const int q = warp & 3, ch = (warp - 4) >> 2;
+        const int r = q * 32 + lane;               // TMEM lane = query row
         const int row = mt * BMQ + r;
         const bool row_ok = row < rows_total;
         const int node = row_ok ? row / G : 0;
         const uint64_t anc = row_ok ? a.anc[(size_t)b * a.N + node] : 0ull;
-        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        float m = -INFINITY, l = 0.0f;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        float* xch = sxch + ch * BMQ;              // this half's row values
+        const float* xoth = sxch + (ch ^ 1) * BMQ; // the partner's
+        const int kbase = ch * 32;
+        float m = -INFINITY, l = 0.0f;             // l: this half's partial sum
         for (int j = 0; j < T; ++j) {
             const int sb = j & 1, s = j % KS;
             const bool got = mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag);
             if (!__all_sync(0xffffffffu, got)) goto done;
             tc_fence_after();
-            uint32_t sr[64];
-            tmem_ld_32x32b_x32(tmem + lane_base + sb * TK, *reinterpret_cast<uint32_t(*)[32]>(sr));
-            tmem_ld_32x32b_x32(tmem + lane_base + sb * TK + 32, *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
+            uint32_t x32[32];
+            tmem_ld_32x32b_x32(tmem + lane_base + sb * TK + kbase, x32);
             tmem_ld_wait();
             tc_fence_before();
             mbar_arrive(&s_free[sb]);
             const bool tree = j == T_pre;
-            const float* ks = sscale + s * 2 * TK;
+            const float* ks = sscale + s * 2 * TK + kbase;
             if constexpr (INT8) {
                 // scales of this stage were written by the converter warps
-                const bool ok = mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag);
-                if (!__all_sync(0xffffffffu, ok)) goto done;
+                if (!tree) {
+                    const bool ok = mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag);
+                    if (!__all_sync(0xffffffffu, ok)) goto done;
+                }
             }
             // scaled scores (log2 domain) overwrite the raw ones in place
-            float* x = reinterpret_cast<float*>(sr);
-            float mx = -INFINITY;
+            float* x = reinterpret_cast<float*>(x32);
+            float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int t = 0; t < 64; ++t) {
-                const bool ok = tree ? ((anc >> t) & 1ull) != 0 : (j * TK + t < L);
+            for (int t = 0; t < 32; ++t) {
+                const int key = kbase + t;
+                const bool ok = tree ? ((anc >> key) & 1ull) != 0 : (j * TK + key < L);
                 float v = x[t] * a.scale_log2;
-                if constexpr (INT8) v *= ks[t];
+                if constexpr (INT8) v = tree ? v : v * ks[t];
                 v = ok ? v : -INFINITY;
                 x[t] = v;
-                mx = fmaxf(mx, v);
+                pm[t & 3] = fmaxf(pm[t & 3], v);
             }
-            // lazy rescale, decided per warp so the TMEM accesses stay convergent:
-            // a row whose max grew by more than 2^8 (or its first valid key)
-            // moves the whole warp to the new maxima
+            float mx = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
+            xch[r] = mx;
+            pair_sync(q);
+            mx = fmaxf(mx, xoth[r]);
+            // lazy rescale, decided per warp (identically in both warps of the
+            // pair) so the TMEM accesses stay convergent
             if (__any_sync(0xffffffffu, mx > m + kRescaleLog2)) {
                 const float m_new = fmaxf(m, mx);
                 const float f = m == -INFINITY ? 0.0f : ex2_approx(m - m_new);
@@ -311,111 +348,123 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!__all_sync(0xffffffffu, ok)) goto done;
                     tc_fence_after();
 #pragma unroll 1
-                    for (int c = 0; c < D / 32; ++c) {
+                    for (int c = 0; c < 2; ++c) {
                         uint32_t o[32];
-                        tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                        const uint32_t oc = tmem_o + lane_base + ch * 64 + c * 32;
+                        tmem_ld_32x32b_x32(oc, o);
                         tmem_ld_wait();
 #pragma unroll
                         for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-                        tmem_st_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                        tmem_st_32x32b_x32(oc, o);
                     }
                     tmem_st_wait();
                 }
                 m = m_new;
             }
-            // P (times the V scale for int8 pages) -> f16, row r of the P tile
+            // P (times the V scale for int8 pages) -> f16, this half of row r
             uint8_t* prow = sp + sb * P_BYTES;
             const float* vs = ks + TK;
-            float lsum = 0.0f;
+            const float ms = m == -INFINITY ? 0.0f : m;  // all keys masked so far: p = 0
+            float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
+            for (int c = 0; c < 4; ++c) {
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const int t = c * 8 + 2 * e;
-                    float p0 = x[t] == -INFINITY ? 0.0f : ex2_approx(x[t] - m);
-                    float p1 = x[t + 1] == -INFINITY ? 0.0f : ex2_approx(x[t + 1] - m);
-                    lsum += p0 + p1;
+                    float p0 = ex2_approx(x[t] - ms);      // masked (-inf) -> 0
+                    float p1 = ex2_approx(x[t + 1] - ms);
+                    ls[e] += p0 + p1;
                     if constexpr (INT8) {
-                        p0 *= vs[t];
-                        p1 *= vs[t + 1];
+                        if (!tree) {
+                            p0 *= vs[t];
+                            p1 *= vs[t + 1];
+                        }
                     }
                     __half2 hp = __floats2half2_rn(p0, p1);
                     w[e] = *reinterpret_cast<uint32_t*>(&hp);
                 }
-                *reinterpret_cast<uint4*>(prow + sw128(r, c)) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(prow + sw128(r, ch * 4 + c)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            l += lsum;
+            l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
             fence_async_smem();
             tc_fence_before();
             mbar_arrive(&p_full[sb]);
         }
-        // epilogue: O / l after the last PV
+        // epilogue: O / (both halves' sums) after the last PV
         {
             const bool ok = mbar_wait(o_full, 0, a.err, kErrWait, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) goto done;
         }
         tc_fence_after();
+        pair_sync(q);  // the partner finished reading xch for the last tile
+        xch[r] = l;
+        pair_sync(q);
         {
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            const float lt = l + xoth[r];
+            const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
             const int g = row_ok ? row % G : 0;
             const size_t obase = (((size_t)b * a.N + node) * a.Hq + h * G + g) * D;
 #pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < 2; ++c) {
                 uint32_t o[32];
-                tmem_ld_32x32b_x32(tmem_o + lane_base + c * 32, o);
+                const int col = ch * 64 + c * 32;
+                tmem_ld_32x32b_x32(tmem_o + lane_base + col, o);
                 tmem_ld_wait();
                 if (!row_ok) continue;
                 if (a.out_f16) {
-                    __half* dst = static_cast<__half*>(a.out) + obase + c * 32;
+                    __half* dst = static_cast<__half*>(a.out) + obase + col;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
+                    for (int qq = 0; qq < 4; ++qq) {
                         uint32_t w[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            __half2 hv = __floats2half2_rn(__uint_as_float(o[q * 8 + 2 * e]) * inv,
-                                                           __uint_as_float(o[q * 8 + 2 * e + 1]) * inv);
+                            __half2 hv = __floats2half2_rn(__uint_as_float(o[qq * 8 + 2 * e]) * inv,
+                                                           __uint_as_float(o[qq * 8 + 2 * e + 1]) * inv);
                             w[e] = *reinterpret_cast<uint32_t*>(&hv);
                         }
-                        reinterpret_cast<uint4*>(dst)[q] = make_uint4(w[0], w[1], w[2], w[3]);
+                        reinterpret_cast<uint4*>(dst)[qq] = make_uint4(w[0], w[1], w[2], w[3]);
                     }
                 } else {
-                    float* dst = static_cast<float*>(a.out) + obase + c * 32;
+                    float* dst = static_cast<float*>(a.out) + obase + col;
 #pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        reinterpret_cast<float4*>(dst)[q] =
-                            make_float4(__uint_as_float(o[4 * q]) * inv, __uint_as_float(o[4 * q + 1]) * inv,
-                                        __uint_as_float(o[4 * q + 2]) * inv, __uint_as_float(o[4 * q + 3]) * inv);
+                    for (int qq = 0; qq < 8; ++qq)
+                        reinterpret_cast<float4*>(dst)[qq] =
+                            make_float4(__uint_as_float(o[4 * qq]) * inv, __uint_as_float(o[4 * qq + 1]) * inv,
+                                        __uint_as_float(o[4 * qq + 2]) * inv, __uint_as_float(o[4 * qq + 3]) * inv);
                 }
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 12) {
         // ------------------------------------------------------------ converters
-        const int t = threadIdx.x - 256;  // 0..127
+        const int t = threadIdx.x - 384;  // 0..127
         const int kr = t >> 1, hh = t & 1;  // key row, 64-dim half
-        for (int j = 0; j < T; ++j) {
-            const int s = j % KS;
-            if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag)) goto done;
-            uint8_t* st = skv + s * KV_STAGE;
-            float* ssc = sscale + s * 2 * TK;
-            if (j == T_pre) {
-                // tree tile: node K/V rows (f16), zero past the last node
-                const bool ok = kr < a.N;
-                const size_t src = (((size_t)b * a.N + (ok ? kr : 0)) * a.Hkv + h) * D + hh * 64;
+        {
+            // tree tile into its own buffer: node K/V rows (f16), zero past
+            // the last node (masked keys still meet the tensor cores)
+            const bool ok = kr < a.N;
+            const size_t src = (((size_t)b * a.N + (ok ? kr : 0)) * a.Hkv + h) * D + hh * 64;
 #pragma unroll
-                for (int kvs = 0; kvs < 2; ++kvs) {
-                    const uint4* g = reinterpret_cast<const uint4*>((kvs ? a.node_v : a.node_k) + src);
-                    uint4 v[8];
+            for (int kvs = 0; kvs < 2; ++kvs) {
+                const uint4* g = reinterpret_cast<const uint4*>((kvs ? a.node_v : a.node_k) + src);
+                uint4 v[8];
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) v[c] = ok ? g[c] : make_uint4(0, 0, 0, 0);
+                for (int c = 0; c < 8; ++c) v[c] = ok ? g[c] : make_uint4(0, 0, 0, 0);
 #pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        *reinterpret_cast<uint4*>(st + kvs * 2 * KV_HALF + hh * KV_HALF + sw128(kr, c)) = v[c];
-                }
-                if constexpr (INT8) ssc[t] = 1.0f;  // ks[0..63], vs[0..63]: unscaled
-            } else if constexpr (INT8) {
-                const int r = j % RS;
-                if (!mbar_wait(&raw_full[r], (j / RS) & 1, a.err, kErrWait, abort_flag)) goto done;
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<uint4*>(stree + kvs * 2 * KV_HALF + hh * KV_HALF + sw128(kr, c)) = v[c];
+            }
+            fence_async_smem();
+            mbar_arrive(tree_full);
+        }
+        if constexpr (INT8) {
+            for (int j = 0; j < T_pre; ++j) {
+                const int s = j % KS, r = j % RS;
+                if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag) ||
+                    !mbar_wait(&raw_full[r], (j / RS) & 1, a.err, kErrWait, abort_flag))
+                    goto done;
+                uint8_t* st = skv + s * KV_STAGE;
+                float* ssc = sscale + s * 2 * TK;
                 const uint8_t* rs = sraw + r * RAW_STAGE;
 #pragma unroll
                 for (int kvs = 0; kvs < 2; ++kvs) {
@@ -424,16 +473,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int c4 = 0; c4 < 4; ++c4) {
                         const uint4 raw = src[c4];  // 16 int8 -> two 16-byte f16 chunks
-                        const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
                         uint32_t o[8];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int8_t* bb = reinterpret_cast<const int8_t*>(&wv[e]);
-                            __half2 h0 = __halves2half2(__int2half_rn(bb[0]), __int2half_rn(bb[1]));
-                            __half2 h1 = __halves2half2(__int2half_rn(bb[2]), __int2half_rn(bb[3]));
-                            o[2 * e] = *reinterpret_cast<uint32_t*>(&h0);
-                            o[2 * e + 1] = *reinterpret_cast<uint32_t*>(&h1);
-                        }
+                        i8x4_to_f16(raw.x, o[0], o[1]);
+                        i8x4_to_f16(raw.y, o[2], o[3]);
+                        i8x4_to_f16(raw.z, o[4], o[5]);
+                        i8x4_to_f16(raw.w, o[6], o[7]);
                         *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4)) = make_uint4(o[0], o[1], o[2], o[3]);
                         *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
                     }
@@ -441,9 +485,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const __half* sc = reinterpret_cast<const __half*>(rs + 2 * RAW_KV);
                 ssc[t] = __half2float(sc[t]);  // t < 64: K scales, t >= 64: V scales
                 mbar_arrive(&raw_empty[r]);    // after every read of the raw stage
+                fence_async_smem();
+                mbar_arrive(&kv_full[s]);
             }
-            fence_async_smem();
-            mbar_arrive(&kv_full[s]);
         }
     }
 done:
