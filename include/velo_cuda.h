@@ -218,6 +218,94 @@ VELO_API int32_t velo_cuda_tree_attention(velo_cuda_ctx *ctx, const void *q, con
                                           int32_t head_dim, int32_t kv_dtype, void *out,
                                           int32_t out_dtype);
 
+/* ---- model, KV pages and the verify step -------------------------------- */
+
+typedef enum velo_dtype { VELO_DT_F32 = 0, VELO_DT_F16 = 1, VELO_DT_Q4_0 = 2 } velo_dtype;
+
+/* The Llama hyper-parameters the verify step needs (ModelMeta,
+ * src/model_loader.rs:21-37).  head_dim must be 128. */
+typedef struct velo_model_desc {
+    uint32_t struct_size;  /* sizeof(velo_model_desc) */
+    uint32_t n_vocab, n_embd, n_layer, n_head, n_head_kv, n_ff, head_dim;
+    float rope_freq_base, norm_eps;
+} velo_model_desc;
+
+/* One named tensor of the WeightStore (src/model_loader.rs:192-234): names
+ * "token_embd.weight", "output_norm.weight", "output.weight" (optional: tied
+ * to token_embd), "layers.{l}.attention_norm.weight",
+ * "layers.{l}.attention.w{q,k,v,o}.weight", "layers.{l}.ffn_norm.weight",
+ * "layers.{l}.feed_forward.w{1,2,3}.weight".  data is host memory, rows x
+ * cols row-major (rows = output features; q4_0 rows are cols/32 blocks of 18
+ * bytes, quant.rs:50-64).  Matrices must be q4_0; embeddings and norms may be
+ * f32, f16 or q4_0. */
+typedef struct velo_weight_desc {
+    const char *name;
+    int32_t dtype; /* velo_dtype */
+    const void *data;
+    uint64_t rows, cols;
+} velo_weight_desc;
+
+/* Upload and repack a model (the context then owns the device copies) and
+ * allocate the zero-filled paged KV pool of the context's config (total_pages
+ * x n_layer, kv_dtype) and its page table (max_slots x max_pages_per_slot).
+ * Replaces LlamaCpuModel::from_weights / LlamaMetalModel::new and
+ * MetalMemoryRuntime::new (src/llama_cpu.rs:168-190, src/metal/runtime.rs). */
+VELO_API int32_t velo_cuda_load_model(velo_cuda_ctx *ctx, const velo_model_desc *desc,
+                                      const velo_weight_desc *weights, int32_t n_weights);
+
+/* Bind `slot` (a page-table row) to `pages` (n_pages ids < total_pages); the
+ * rest of the row is zeroed.  MemoryRuntime::bind_slot (src/runtime.rs:36,
+ * src/metal/runtime.rs:294-319).  VELO_ERR_OUT_OF_PAGES when n_pages exceeds
+ * the row or an id exceeds the pool. */
+VELO_API int32_t velo_cuda_bind_slot(velo_cuda_ctx *ctx, uint32_t slot, const uint32_t *pages,
+                                     size_t n_pages);
+
+/* Write n_tokens K/V rows (host f16 [n_tokens][n_head_kv][head_dim]) of one
+ * layer at positions pos0.. of `slot` (int8 pools quantise as kv_update_int8,
+ * src/kernels.metal:753-802).  The cache a prefill produced; synchronous. */
+VELO_API int32_t velo_cuda_write_kv(velo_cuda_ctx *ctx, uint32_t slot, int32_t layer, int32_t pos0,
+                                    int32_t n_tokens, const void *k_f16, const void *v_f16);
+
+/* Read back the pool bytes of positions pos0..pos0+n_tokens of `slot` and
+ * `layer`: k/v [n_tokens][n_head_kv][head_dim] (f16 or int8), scales
+ * [n_tokens][n_head_kv] f16 (int8 pools; may be NULL).  Synchronous. */
+VELO_API int32_t velo_cuda_read_kv(velo_cuda_ctx *ctx, uint32_t slot, int32_t layer, int32_t pos0,
+                                   int32_t n_tokens, void *k_out, void *v_out, void *k_scale_out,
+                                   void *v_scale_out);
+
+typedef struct velo_verify_batch {
+    uint32_t struct_size;     /* sizeof(velo_verify_batch) */
+    int32_t B, n_nodes;       /* sequences, draft-tree nodes per sequence (<= 64) */
+    const uint32_t *slots;    /* [B] page-table rows (host) */
+    const int32_t *ctx_len;   /* [B] cached tokens per sequence (host) */
+    const uint32_t *tokens;   /* [B][n_nodes]: node 0 is the last committed token */
+    const int32_t *parents;   /* [B][n_nodes]: -1 for node 0, parents[n] < n */
+    float temperature;        /* 0: greedy tree walk; > 0: rejection sampling (chains) */
+    const float *draft_logits;/* [B][n_nodes-1][V] host, sampling only */
+    const float *uniforms;    /* [B][n_nodes] host, sampling only */
+    int32_t commit;           /* 1: write the accepted path's K/V into the pages */
+} velo_verify_batch;
+
+typedef struct velo_verify_result {
+    int32_t *accepted_len;    /* [B] accepted draft tokens (path length - 1) */
+    int32_t *accepted_nodes;  /* [B][n_nodes] path root first, -1 padded (or NULL) */
+    uint32_t *bonus_token;    /* [B] token emitted after the accepted path */
+    float *logits;            /* [B][n_nodes][n_vocab] target logits (or NULL) */
+} velo_verify_result;
+
+/* One verify step for B sequences: the target forward over every draft-tree
+ * node (row n predicts the successor of node n; node n sits at position
+ * ctx_len + depth(n) - 1 and attends to the cache and its own root->n path),
+ * acceptance (greedy: GreedySampler argmax + find_best_path; sampling: the
+ * rejection rule of velo_cuda_accept on chains) and, with commit, the KV of
+ * the accepted path written at positions ctx_len.. on the device.  Host
+ * buffers; waits for the result.  Replaces TargetModel::verify_tree /
+ * verify_batch over CausalLmBackend::verify_logits and the commit of
+ * SpeculativeSession (src/speculative.rs:97-129, 217-254, 473-519;
+ * src/backend.rs:313-369; src/llama_cpu.rs:401-419). */
+VELO_API int32_t velo_cuda_verify_step(velo_cuda_ctx *ctx, const velo_verify_batch *batch,
+                                       velo_verify_result *result);
+
 #ifdef __cplusplus
 }
 #endif

@@ -59,6 +59,37 @@ void DeviceBuffer::release() {
 
 }  // namespace velo
 
+namespace velo {
+
+int32_t run_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
+                          const uint32_t* tok, const float* u, int32_t B, int32_t k, int32_t V,
+                          float temperature, int32_t* acc, uint32_t* bonus) {
+    const bool greedy = temperature == 0.0f;
+    int32_t st = c->workspace.ensure(velo::accept_workspace_bytes(B, k, V, greedy), c->stream);
+    if (st) return st;
+    // ticket block: zeroed when (re)allocated, then kept at zero by the kernel
+    st = c->counters.ensure(velo::accept_counter_bytes(B), c->stream, /*zero_new=*/true);
+    if (st) return st;
+    velo::AcceptParams p{};
+    p.tgt = tgt;
+    p.drf = drf;
+    p.tok = tok;
+    p.u = u;
+    p.acc_len = acc;
+    p.bonus = bonus;
+    p.err_flag = c->err_flag;
+    p.B = B;
+    p.k = k;
+    p.V = V;
+    p.inv_t = greedy ? 0.0f : 1.0f / temperature;
+    p.vec4 = (V % 4 == 0) && ((uintptr_t)tgt % 16 == 0) && (greedy || k == 0 || (uintptr_t)drf % 16 == 0);
+    velo::accept_bind_buffers(p, c->workspace.ptr, c->counters.ptr, greedy);
+    VELO_CUDA_TRY(velo::launch_accept(p, greedy, c->sm_count, c->stream));
+    return VELO_OK;
+}
+
+}  // namespace velo
+
 using velo::fail;
 
 extern "C" {
@@ -135,6 +166,8 @@ void velo_cuda_destroy(velo_cuda_ctx* c) {
     c->counters.release();
     c->io.release();
     c->attn_ws.release();
+    velo::destroy_model(c->model);
+    c->model = nullptr;
     if (c->err_flag) cudaFree(c->err_flag);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     delete c;
@@ -193,33 +226,6 @@ static int32_t check_accept_args(int32_t B, int32_t k, int32_t V, float temperat
     return VELO_OK;
 }
 
-static int32_t run_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
-                          const uint32_t* tok, const float* u, int32_t B, int32_t k, int32_t V,
-                          float temperature, int32_t* acc, uint32_t* bonus) {
-    const bool greedy = temperature == 0.0f;
-    int32_t st = c->workspace.ensure(velo::accept_workspace_bytes(B, k, V, greedy), c->stream);
-    if (st) return st;
-    // ticket block: zeroed when (re)allocated, then kept at zero by the kernel
-    st = c->counters.ensure(velo::accept_counter_bytes(B), c->stream, /*zero_new=*/true);
-    if (st) return st;
-    velo::AcceptParams p{};
-    p.tgt = tgt;
-    p.drf = drf;
-    p.tok = tok;
-    p.u = u;
-    p.acc_len = acc;
-    p.bonus = bonus;
-    p.err_flag = c->err_flag;
-    p.B = B;
-    p.k = k;
-    p.V = V;
-    p.inv_t = greedy ? 0.0f : 1.0f / temperature;
-    p.vec4 = (V % 4 == 0) && ((uintptr_t)tgt % 16 == 0) && (greedy || k == 0 || (uintptr_t)drf % 16 == 0);
-    velo::accept_bind_buffers(p, c->workspace.ptr, c->counters.ptr, greedy);
-    VELO_CUDA_TRY(velo::launch_accept(p, greedy, c->sm_count, c->stream));
-    return VELO_OK;
-}
-
 int32_t velo_cuda_accept_device(velo_cuda_ctx* c, const float* tgt, const float* drf,
                                 const uint32_t* tok, const float* u, int32_t B, int32_t k,
                                 int32_t V, float temperature, int32_t* acc, uint32_t* bonus) {
@@ -228,7 +234,7 @@ int32_t velo_cuda_accept_device(velo_cuda_ctx* c, const float* tgt, const float*
     int32_t st = check_accept_args(B, k, V, temperature, tgt, drf, tok, u, acc, bonus);
     if (st || B == 0) return st;
     VELO_CUDA_TRY(cudaSetDevice(c->device));
-    return run_accept(c, tgt, drf, tok, u, B, k, V, temperature, acc, bonus);
+    return velo::run_accept(c, tgt, drf, tok, u, B, k, V, temperature, acc, bonus);
 }
 
 int32_t velo_cuda_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
@@ -264,7 +270,7 @@ int32_t velo_cuda_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
     if (n_d) VELO_CUDA_TRY(cudaMemcpyAsync(d_d, drf, n_d, cudaMemcpyHostToDevice, c->stream));
     if (n_tok) VELO_CUDA_TRY(cudaMemcpyAsync(d_tok, tok, n_tok, cudaMemcpyHostToDevice, c->stream));
     if (n_u) VELO_CUDA_TRY(cudaMemcpyAsync(d_u, u, n_u, cudaMemcpyHostToDevice, c->stream));
-    st = run_accept(c, d_t, d_d, d_tok, d_u, B, k, V, temperature, d_acc, d_bonus);
+    st = velo::run_accept(c, d_t, d_d, d_tok, d_u, B, k, V, temperature, d_acc, d_bonus);
     if (st) return st;
     VELO_CUDA_TRY(cudaMemcpyAsync(acc, d_acc, (size_t)B * 4, cudaMemcpyDeviceToHost, c->stream));
     VELO_CUDA_TRY(cudaMemcpyAsync(bonus, d_bonus, (size_t)B * 4, cudaMemcpyDeviceToHost, c->stream));

@@ -39,6 +39,17 @@ struct DeviceBuffer {
 
 }  // namespace velo
 
+struct velo_cuda_ctx;
+namespace velo {
+struct Model;
+// Device-buffer acceptance on the context stream (velo_cuda_accept_device
+// without the argument checks).
+int32_t run_accept(velo_cuda_ctx* c, const float* tgt, const float* drf, const uint32_t* tok,
+                   const float* u, int32_t B, int32_t k, int32_t V, float temperature,
+                   int32_t* acc, uint32_t* bonus);
+void destroy_model(Model* m);
+}  // namespace velo
+
 struct velo_cuda_ctx {
     int device = 0;
     int tp_rank = 0, tp_size = 1;
@@ -52,4 +63,5 @@ struct velo_cuda_ctx {
     velo::DeviceBuffer io;         // device copies for the host-buffer entries
     velo::DeviceBuffer attn_ws;    // tree attention: ancestor masks
     int* err_flag = nullptr;       // device-side input flag
+    velo::Model* model = nullptr;  // weights, KV pool and verify buffers (velo_cuda_load_model)
 };

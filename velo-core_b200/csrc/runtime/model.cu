@@ -1,0 +1,653 @@
+// model.cu -- the target model on the device and the verify step of the C ABI
+// (include/velo_cuda.h): weight upload / repack, the paged KV pool and page
+// table, and the per-step launch sequence
+//   embed -> L x [rmsnorm -> QKV GEMM -> RoPE + split -> tree attention ->
+//   o_proj GEMM (+residual) -> rmsnorm -> w1/w3 GEMM (SwiGLU) -> w2 GEMM
+//   (+residual)] -> rmsnorm -> LM head GEMM -> acceptance -> KV commit,
+// all on the context stream.  The per-token loop of the reference
+// (LlamaCpuModel::forward_one, src/llama_cpu.rs:191-358, called k times by
+// verify_logits :401-419) becomes one pass over all B x N tree nodes.
+#include <cuda_fp16.h>
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "kernels/q4gemm.h"
+#include "kernels/tree_attn.h"
+#include "kernels/verify_ops.h"
+#include "runtime/context.h"
+
+namespace velo {
+
+struct Layer {
+    uint8_t* wqkv = nullptr;  // repacked q4_0 [(Hq + 2 Hkv) D][H]
+    uint8_t* wo = nullptr;    // [H][Hq D]
+    uint8_t* w13 = nullptr;   // SwiGLU pair [2F][H]
+    uint8_t* w2 = nullptr;    // [H][F]
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+};
+
+struct Model {
+    velo_model_desc meta{};
+    float* emb = nullptr;      // [V][H] f32
+    float* out_norm = nullptr; // [H]
+    uint8_t* lm_head = nullptr;
+    std::vector<Layer> layers;
+    std::vector<void*> allocs;
+    // KV pool [L][pages][Hkv][16][D] and page table [slots][max_pages]
+    void* k_pool = nullptr;
+    void* v_pool = nullptr;
+    __half* k_scale = nullptr;
+    __half* v_scale = nullptr;
+    int pool_pages = 0, kv_int8 = 0, max_slots = 0, max_pages = 0;
+    uint32_t* page_table = nullptr;
+    std::vector<uint32_t> page_table_host;
+    // per-step buffers, sized for cap_M rows
+    int cap_M = 0, cap_B = 0;
+    std::vector<void*> work;
+    float* x = nullptr;
+    __half* xn = nullptr;
+    float* qkv = nullptr;
+    __half* q = nullptr;
+    __half* nk = nullptr;  // [L][M][Hkv][D]
+    __half* nv = nullptr;
+    __half* attn = nullptr;
+    __half* hbuf = nullptr;
+    float* logits = nullptr;
+    uint32_t* tokens = nullptr;
+    int32_t* parents = nullptr;
+    int32_t* ctxlen = nullptr;
+    uint32_t* slots = nullptr;
+    uint32_t* pt_batch = nullptr;  // [B][max_pages] gathered rows
+    uint64_t* anc = nullptr;
+    uint32_t* expected = nullptr;
+    int32_t* path = nullptr;
+    int32_t* path_len = nullptr;
+    uint32_t* bonus = nullptr;
+    int32_t* acc = nullptr;
+    float* drf = nullptr;
+    float* uni = nullptr;
+    uint32_t* dtok = nullptr;
+    size_t drf_cap = 0;
+
+    int H() const { return (int)meta.n_embd; }
+    int Hq() const { return (int)meta.n_head; }
+    int Hkv() const { return (int)meta.n_head_kv; }
+    int F() const { return (int)meta.n_ff; }
+    int V() const { return (int)meta.n_vocab; }
+    int L() const { return (int)meta.n_layer; }
+    size_t kv_elt() const { return kv_int8 ? 1 : 2; }
+    size_t layer_pool_elems() const { return (size_t)pool_pages * Hkv() * 16 * 128; }
+    size_t layer_scale_elems() const { return (size_t)pool_pages * Hkv() * 16; }
+};
+
+void destroy_model(Model* m) {
+    if (!m) return;
+    for (void* p : m->allocs) cudaFree(p);
+    for (void* p : m->work) cudaFree(p);
+    if (m->drf) cudaFree(m->drf);
+    delete m;
+}
+
+namespace {
+
+float h2f(uint16_t h) {
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
+
+// dequant_row (src/quant.rs:181-191) for the dtypes accepted here
+void host_dequant_row(int dt, const uint8_t* src, float* out, size_t n) {
+    if (dt == VELO_DT_F32) {
+        std::memcpy(out, src, n * 4);
+    } else if (dt == VELO_DT_F16) {
+        for (size_t i = 0; i < n; ++i) out[i] = h2f((uint16_t)(src[2 * i] | (src[2 * i + 1] << 8)));
+    } else {  // q4_0, interleaved nibbles (quant.rs:50-64)
+        for (size_t b = 0; b < n / 32; ++b) {
+            const uint8_t* blk = src + b * 18;
+            const float d = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+            for (int i = 0; i < 16; ++i) {
+                out[b * 32 + 2 * i] = d * (float)((int)(blk[2 + i] & 15) - 8);
+                out[b * 32 + 2 * i + 1] = d * (float)((int)(blk[2 + i] >> 4) - 8);
+            }
+        }
+    }
+}
+
+size_t row_bytes(int dt, size_t cols) {
+    return dt == VELO_DT_F32 ? cols * 4 : dt == VELO_DT_F16 ? cols * 2 : cols / 32 * 18;
+}
+
+template <class T>
+int32_t dev_alloc(Model* m, T** p, size_t bytes, bool work = false) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+    if (e != cudaSuccess)
+        return fail(e == cudaErrorMemoryAllocation ? VELO_ERR_OUT_OF_MEMORY : VELO_ERR_CUDA,
+                    "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+    (work ? m->work : m->allocs).push_back(q);
+    *p = static_cast<T*>(q);
+    return VELO_OK;
+}
+
+using Index = std::map<std::string, const velo_weight_desc*>;
+
+const velo_weight_desc* find(const Index& ix, const std::string& name) {
+    auto it = ix.find(name);
+    return it == ix.end() ? nullptr : it->second;
+}
+
+// f32 vector (norm weight / embedding table) of rows x cols on the device
+int32_t upload_f32(Model* m, const velo_weight_desc* w, size_t rows, size_t cols, float** out,
+                   cudaStream_t s) {
+    if (!w) return fail(VELO_ERR_INVALID_ARGUMENT, "missing tensor");
+    if (w->rows * w->cols != rows * cols)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "tensor %s has %llu x %llu elements, expected %zu x %zu",
+                    w->name, (unsigned long long)w->rows, (unsigned long long)w->cols, rows, cols);
+    if (w->dtype < VELO_DT_F32 || w->dtype > VELO_DT_Q4_0 || !w->data ||
+        (w->dtype == VELO_DT_Q4_0 && cols % 32))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "tensor %s: bad dtype / data", w->name);
+    std::vector<float> host(rows * cols);
+    const size_t rb = row_bytes(w->dtype, cols);
+    for (size_t r = 0; r < rows; ++r)
+        host_dequant_row(w->dtype, static_cast<const uint8_t*>(w->data) + r * rb, host.data() + r * cols, cols);
+    int32_t st = dev_alloc(m, out, host.size() * 4);
+    if (st) return st;
+    VELO_CUDA_TRY(cudaMemcpyAsync(*out, host.data(), host.size() * 4, cudaMemcpyHostToDevice, s));
+    VELO_CUDA_TRY(cudaStreamSynchronize(s));
+    return VELO_OK;
+}
+
+// q4_0 matrices (concatenated by rows, or a gate/up pair) -> repacked device weight
+int32_t upload_q4(Model* m, const std::vector<const velo_weight_desc*>& parts, size_t cols, bool pair,
+                  uint8_t** out, cudaStream_t s) {
+    size_t rows = 0;
+    for (auto* w : parts) {
+        if (!w) return fail(VELO_ERR_INVALID_ARGUMENT, "missing matrix");
+        if (w->dtype != VELO_DT_Q4_0 || !w->data)
+            return fail(VELO_ERR_INVALID_ARGUMENT, "matrix %s must be q4_0 (dtype %d)", w->name, w->dtype);
+        if (w->cols != cols || cols % 32)
+            return fail(VELO_ERR_INVALID_ARGUMENT, "matrix %s: %llu columns, expected %zu", w->name,
+                        (unsigned long long)w->cols, cols);
+        rows += w->rows;
+    }
+    const size_t rb = cols / 32 * 18;
+    uint8_t* raw = nullptr;
+    VELO_CUDA_TRY(cudaMalloc(&raw, rows * rb));
+    size_t off = 0;
+    for (auto* w : parts) {
+        cudaError_t e = cudaMemcpy(raw + off, w->data, w->rows * rb, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            cudaFree(raw);
+            return fail(VELO_ERR_CUDA, "weight upload failed: %s", cudaGetErrorString(e));
+        }
+        off += w->rows * rb;
+    }
+    int32_t st = dev_alloc(m, out, q4_repacked_bytes((int)rows, (int)cols));
+    if (st) {
+        cudaFree(raw);
+        return st;
+    }
+    cudaError_t e = launch_q4_repack(raw, pair ? raw + parts[0]->rows * rb : nullptr, pair, (int)rows,
+                                     (int)cols, *out, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(raw);
+    if (e != cudaSuccess) return fail(VELO_ERR_CUDA, "q4_0 repack failed: %s", cudaGetErrorString(e));
+    return VELO_OK;
+}
+
+int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
+    const int M = B * N;
+    if (M <= m->cap_M && B <= m->cap_B) return VELO_OK;
+    VELO_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    for (void* p : m->work) cudaFree(p);
+    m->work.clear();
+    const int cM = M > m->cap_M ? M : m->cap_M, cB = B > m->cap_B ? B : m->cap_B;
+    const size_t H = m->H(), D = 128, Hq = m->Hq(), Hkv = m->Hkv(), F = m->F(), V = m->V();
+    const size_t L = m->L();
+    int32_t st = VELO_OK;
+    if (!st) st = dev_alloc(m, &m->x, (size_t)cM * H * 4, true);
+    if (!st) st = dev_alloc(m, &m->xn, (size_t)cM * (H > F ? H : F) * 2, true);
+    if (!st) st = dev_alloc(m, &m->qkv, (size_t)cM * (Hq + 2 * Hkv) * D * 4, true);
+    if (!st) st = dev_alloc(m, &m->q, (size_t)cM * Hq * D * 2, true);
+    if (!st) st = dev_alloc(m, &m->nk, L * cM * Hkv * D * 2, true);
+    if (!st) st = dev_alloc(m, &m->nv, L * cM * Hkv * D * 2, true);
+    if (!st) st = dev_alloc(m, &m->attn, (size_t)cM * Hq * D * 2, true);
+    if (!st) st = dev_alloc(m, &m->hbuf, (size_t)cM * F * 2, true);
+    if (!st) st = dev_alloc(m, &m->logits, (size_t)cM * V * 4, true);
+    if (!st) st = dev_alloc(m, &m->tokens, (size_t)cM * 4, true);
+    if (!st) st = dev_alloc(m, &m->parents, (size_t)cM * 4, true);
+    if (!st) st = dev_alloc(m, &m->anc, (size_t)cM * 8, true);
+    if (!st) st = dev_alloc(m, &m->expected, (size_t)cM * 4, true);
+    if (!st) st = dev_alloc(m, &m->path, (size_t)cM * 4, true);
+    if (!st) st = dev_alloc(m, &m->dtok, (size_t)cM * 4, true);
+    if (!st) st = dev_alloc(m, &m->uni, (size_t)cM * 4, true);
+    if (!st) st = dev_alloc(m, &m->ctxlen, (size_t)cB * 4, true);
+    if (!st) st = dev_alloc(m, &m->slots, (size_t)cB * 4, true);
+    if (!st) st = dev_alloc(m, &m->pt_batch, (size_t)cB * (m->max_pages ? m->max_pages : 1) * 4, true);
+    if (!st) st = dev_alloc(m, &m->path_len, (size_t)cB * 4, true);
+    if (!st) st = dev_alloc(m, &m->bonus, (size_t)cB * 4, true);
+    if (!st) st = dev_alloc(m, &m->acc, (size_t)cB * 4, true);
+    if (st) {
+        m->cap_M = m->cap_B = 0;
+        return st;
+    }
+    m->cap_M = cM;
+    m->cap_B = cB;
+    return VELO_OK;
+}
+
+int32_t gemm(velo_cuda_ctx* c, const uint8_t* w, const __half* x, int M, int N, int K, void* y,
+             int ldy, int mode) {
+    Q4GemmArgs a{};
+    a.w = w;
+    a.N = N;
+    a.K = K;
+    a.M = M;
+    a.y = y;
+    a.ldy = ldy;
+    a.mode = mode;
+    a.err = c->err_flag;
+    VELO_CUDA_TRY(launch_q4_gemm(a, x, c->sm_count, c->stream));
+    return VELO_OK;
+}
+
+int32_t check_model(velo_cuda_ctx* c) {
+    if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    if (!c->model) return fail(VELO_ERR_INVALID_ARGUMENT, "no model loaded (velo_cuda_load_model)");
+    return VELO_OK;
+}
+
+}  // namespace
+}  // namespace velo
+
+using velo::fail;
+using velo::Model;
+
+extern "C" {
+
+int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const velo_weight_desc* w,
+                             int32_t n) {
+    velo::clear_last_error();
+    if (!c || !d || (n > 0 && !w)) return fail(VELO_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (d->struct_size != 0 && d->struct_size != sizeof(velo_model_desc))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "velo_model_desc.struct_size %u != %zu", d->struct_size,
+                    sizeof(velo_model_desc));
+    if (d->head_dim != 128 || d->n_head == 0 || d->n_head_kv == 0 || d->n_head % d->n_head_kv ||
+        d->n_embd % 128 || d->n_ff % 32 || d->n_vocab == 0 || d->n_layer == 0 ||
+        (d->n_head * d->head_dim) % 32)
+        return fail(VELO_ERR_INVALID_ARGUMENT,
+                    "model shape unsupported: head_dim %u (128), heads %u/%u, n_embd %u, n_ff %u",
+                    d->head_dim, d->n_head, d->n_head_kv, d->n_embd, d->n_ff);
+    if (c->cfg.page_size != 16)
+        return fail(VELO_ERR_INVALID_BLOCK_SIZE, "page_size %u: the kernels use 16-token pages",
+                    c->cfg.page_size);
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    velo::destroy_model(c->model);
+    c->model = nullptr;
+    Model* m = new Model();
+    m->meta = *d;
+    m->meta.struct_size = sizeof(velo_model_desc);
+    velo::Index ix;
+    for (int i = 0; i < n; ++i)
+        if (w[i].name) ix[w[i].name] = &w[i];
+    const size_t H = d->n_embd, V = d->n_vocab, F = d->n_ff, Dq = (size_t)d->n_head * d->head_dim;
+    cudaStream_t s = c->stream;
+    int32_t st = VELO_OK;
+    const velo_weight_desc* emb = velo::find(ix, "token_embd.weight");
+    if (!emb) st = fail(VELO_ERR_INVALID_ARGUMENT, "missing token_embd.weight");
+    if (!st) st = velo::upload_f32(m, emb, V, H, &m->emb, s);
+    if (!st) st = velo::upload_f32(m, velo::find(ix, "output_norm.weight"), 1, H, &m->out_norm, s);
+    if (!st) {
+        const velo_weight_desc* out = velo::find(ix, "output.weight");
+        st = velo::upload_q4(m, {out ? out : emb}, H, false, &m->lm_head, s);  // tied fallback
+    }
+    for (uint32_t l = 0; !st && l < d->n_layer; ++l) {
+        const std::string p = "layers." + std::to_string(l) + ".";
+        velo::Layer ly;
+        st = velo::upload_f32(m, velo::find(ix, p + "attention_norm.weight"), 1, H, &ly.attn_norm, s);
+        if (!st) st = velo::upload_f32(m, velo::find(ix, p + "ffn_norm.weight"), 1, H, &ly.ffn_norm, s);
+        if (!st)
+            st = velo::upload_q4(m, {velo::find(ix, p + "attention.wq.weight"), velo::find(ix, p + "attention.wk.weight"),
+                                     velo::find(ix, p + "attention.wv.weight")},
+                                 H, false, &ly.wqkv, s);
+        if (!st) st = velo::upload_q4(m, {velo::find(ix, p + "attention.wo.weight")}, Dq, false, &ly.wo, s);
+        if (!st)
+            st = velo::upload_q4(m, {velo::find(ix, p + "feed_forward.w1.weight"), velo::find(ix, p + "feed_forward.w3.weight")},
+                                 H, true, &ly.w13, s);
+        if (!st) st = velo::upload_q4(m, {velo::find(ix, p + "feed_forward.w2.weight")}, F, false, &ly.w2, s);
+        m->layers.push_back(ly);
+    }
+    // paged KV pool of the context config
+    if (!st) {
+        m->pool_pages = (int)(c->cfg.total_pages ? c->cfg.total_pages : 1);
+        m->kv_int8 = c->cfg.kv_dtype == VELO_KV_INT8;
+        m->max_slots = (int)c->cfg.max_slots;
+        m->max_pages = (int)(c->cfg.max_pages_per_slot ? c->cfg.max_pages_per_slot : m->pool_pages);
+        const size_t pe = (size_t)d->n_layer * m->layer_pool_elems();
+        st = velo::dev_alloc(m, reinterpret_cast<uint8_t**>(&m->k_pool), pe * m->kv_elt());
+        if (!st) st = velo::dev_alloc(m, reinterpret_cast<uint8_t**>(&m->v_pool), pe * m->kv_elt());
+        if (!st && m->kv_int8) {
+            const size_t se = (size_t)d->n_layer * m->layer_scale_elems();
+            st = velo::dev_alloc(m, &m->k_scale, se * 2);
+            if (!st) st = velo::dev_alloc(m, &m->v_scale, se * 2);
+            if (!st) {
+                cudaMemsetAsync(m->k_scale, 0, se * 2, s);
+                cudaMemsetAsync(m->v_scale, 0, se * 2, s);
+            }
+        }
+        if (!st) {
+            cudaMemsetAsync(m->k_pool, 0, pe * m->kv_elt(), s);
+            cudaMemsetAsync(m->v_pool, 0, pe * m->kv_elt(), s);
+            m->page_table_host.assign((size_t)m->max_slots * m->max_pages, 0u);
+            st = velo::dev_alloc(m, &m->page_table, m->page_table_host.size() * 4);
+            if (!st) cudaMemsetAsync(m->page_table, 0, m->page_table_host.size() * 4, s);
+        }
+        if (!st) {
+            cudaError_t e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess) st = fail(VELO_ERR_CUDA, "pool init failed: %s", cudaGetErrorString(e));
+        }
+    }
+    if (st) {
+        velo::destroy_model(m);
+        return st;
+    }
+    c->model = m;
+    return VELO_OK;
+}
+
+int32_t velo_cuda_bind_slot(velo_cuda_ctx* c, uint32_t slot, const uint32_t* pages, size_t n) {
+    velo::clear_last_error();
+    int32_t st = velo::check_model(c);
+    if (st) return st;
+    Model* m = c->model;
+    if (slot >= (uint32_t)m->max_slots)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "slot %u >= max_slots %d", slot, m->max_slots);
+    if (n > (size_t)m->max_pages)
+        return fail(VELO_ERR_OUT_OF_PAGES, "OutOfPages { requested: %zu, available: %d }", n, m->max_pages);
+    if (n && !pages) return fail(VELO_ERR_INVALID_ARGUMENT, "pages is NULL");
+    for (size_t i = 0; i < n; ++i)
+        if (pages[i] >= (uint32_t)m->pool_pages)
+            return fail(VELO_ERR_OUT_OF_PAGES, "page id %u >= pool of %d pages", pages[i], m->pool_pages);
+    uint32_t* row = m->page_table_host.data() + (size_t)slot * m->max_pages;
+    for (int i = 0; i < m->max_pages; ++i) row[i] = (size_t)i < n ? pages[i] : 0u;
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    VELO_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    VELO_CUDA_TRY(cudaMemcpy(m->page_table + (size_t)slot * m->max_pages, row, (size_t)m->max_pages * 4,
+                             cudaMemcpyHostToDevice));
+    return VELO_OK;
+}
+
+int32_t velo_cuda_write_kv(velo_cuda_ctx* c, uint32_t slot, int32_t layer, int32_t pos0, int32_t n,
+                           const void* k, const void* v) {
+    velo::clear_last_error();
+    int32_t st = velo::check_model(c);
+    if (st) return st;
+    Model* m = c->model;
+    if (slot >= (uint32_t)m->max_slots || layer < 0 || layer >= m->L() || pos0 < 0 || n < 0 ||
+        n > velo::kAttnMaxNodes || (n && (!k || !v)))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "write_kv: slot %u layer %d pos0 %d n %d (n <= 64)", slot,
+                    layer, pos0, n);
+    if (n == 0) return VELO_OK;
+    if ((pos0 + n - 1) / 16 >= m->max_pages)
+        return fail(VELO_ERR_OUT_OF_PAGES, "write_kv: position %d beyond the page-table row", pos0 + n - 1);
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    const size_t rows = (size_t)n * m->Hkv() * 128;
+    __half* dk = nullptr;
+    VELO_CUDA_TRY(cudaMalloc(&dk, rows * 4 + 64 * 4 * 4));
+    __half* dv = dk + rows;
+    int32_t* meta = reinterpret_cast<int32_t*>(dv + rows);  // path[64], len, ctx, slot
+    std::vector<int32_t> hm(64 + 3);
+    for (int i = 0; i < 64; ++i) hm[i] = i < n ? i : -1;
+    hm[64] = n;
+    hm[65] = pos0;
+    hm[66] = (int32_t)slot;
+    cudaError_t e = cudaMemcpy(dk, k, rows * 2, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(dv, v, rows * 2, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(meta, hm.data(), hm.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        velo::KvCommitArgs a{};
+        a.node_k = dk;
+        a.node_v = dv;
+        a.path = meta;
+        a.path_len = meta + 64;
+        a.ctx_len = meta + 65;
+        a.slots = reinterpret_cast<const uint32_t*>(meta + 66);
+        a.page_table = m->page_table;
+        const size_t lo = (size_t)layer * m->layer_pool_elems() * m->kv_elt();
+        a.k_pool = static_cast<uint8_t*>(m->k_pool) + lo;
+        a.v_pool = static_cast<uint8_t*>(m->v_pool) + lo;
+        a.k_scale = m->kv_int8 ? m->k_scale + (size_t)layer * m->layer_scale_elems() : nullptr;
+        a.v_scale = m->kv_int8 ? m->v_scale + (size_t)layer * m->layer_scale_elems() : nullptr;
+        a.B = 1;
+        a.N = n;
+        a.L = 1;
+        a.Hkv = m->Hkv();
+        a.max_pages = m->max_pages;
+        a.pool_pages = m->pool_pages;
+        a.kv_int8 = m->kv_int8;
+        a.err = c->err_flag;
+        e = velo::launch_kv_commit(a, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    }
+    cudaFree(dk);
+    if (e != cudaSuccess) return fail(VELO_ERR_CUDA, "write_kv failed: %s", cudaGetErrorString(e));
+    return velo_cuda_sync(c, -1);
+}
+
+int32_t velo_cuda_read_kv(velo_cuda_ctx* c, uint32_t slot, int32_t layer, int32_t pos0, int32_t n,
+                          void* k_out, void* v_out, void* ks_out, void* vs_out) {
+    velo::clear_last_error();
+    int32_t st = velo::check_model(c);
+    if (st) return st;
+    Model* m = c->model;
+    if (slot >= (uint32_t)m->max_slots || layer < 0 || layer >= m->L() || pos0 < 0 || n < 0 ||
+        (n && (!k_out || !v_out)))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "read_kv: bad arguments");
+    if (n && (pos0 + n - 1) / 16 >= m->max_pages)
+        return fail(VELO_ERR_OUT_OF_PAGES, "read_kv: position beyond the page-table row");
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    VELO_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    const uint32_t* row = m->page_table_host.data() + (size_t)slot * m->max_pages;
+    const size_t hd = 128, tokb = hd * m->kv_elt();
+    for (int i = 0; i < n; ++i) {
+        const int pos = pos0 + i;
+        const uint32_t pg = row[pos / 16];
+        for (int h = 0; h < m->Hkv(); ++h) {
+            const size_t tok = (((size_t)layer * m->pool_pages + pg) * m->Hkv() + h) * 16 + pos % 16;
+            const size_t o = ((size_t)i * m->Hkv() + h);
+            VELO_CUDA_TRY(cudaMemcpy(static_cast<uint8_t*>(k_out) + o * tokb,
+                                     static_cast<uint8_t*>(m->k_pool) + tok * tokb, tokb, cudaMemcpyDeviceToHost));
+            VELO_CUDA_TRY(cudaMemcpy(static_cast<uint8_t*>(v_out) + o * tokb,
+                                     static_cast<uint8_t*>(m->v_pool) + tok * tokb, tokb, cudaMemcpyDeviceToHost));
+            if (m->kv_int8 && ks_out)
+                VELO_CUDA_TRY(cudaMemcpy(static_cast<uint16_t*>(ks_out) + o, m->k_scale + tok, 2, cudaMemcpyDeviceToHost));
+            if (m->kv_int8 && vs_out)
+                VELO_CUDA_TRY(cudaMemcpy(static_cast<uint16_t*>(vs_out) + o, m->v_scale + tok, 2, cudaMemcpyDeviceToHost));
+        }
+    }
+    return VELO_OK;
+}
+
+int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, velo_verify_result* out) {
+    velo::clear_last_error();
+    int32_t st = velo::check_model(c);
+    if (st) return st;
+    if (!in || !out) return fail(VELO_ERR_INVALID_ARGUMENT, "NULL batch / result");
+    if (in->struct_size != 0 && in->struct_size != sizeof(velo_verify_batch))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "velo_verify_batch.struct_size %u != %zu", in->struct_size,
+                    sizeof(velo_verify_batch));
+    Model* m = c->model;
+    const int B = in->B, N = in->n_nodes;
+    if (B < 0) return fail(VELO_ERR_INVALID_ARGUMENT, "B = %d", B);
+    if (N < 1) return fail(VELO_ERR_EMPTY_DRAFT_WINDOW, "n_nodes = %d: a verify step needs the root node", N);
+    if (N > velo::kAttnMaxNodes)
+        return fail(VELO_ERR_DRAFT_TOO_MANY, "n_nodes = %d > %d", N, velo::kAttnMaxNodes);
+    if (B == 0) return VELO_OK;
+    if (!in->slots || !in->ctx_len || !in->tokens || !in->parents || !out->accepted_len || !out->bonus_token)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "NULL batch array");
+    const bool sampling = in->temperature > 0.0f;
+    if (!(in->temperature >= 0.0f) || std::isinf(in->temperature))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "temperature must be finite and >= 0");
+    const int V = m->V();
+    for (int b = 0; b < B; ++b) {
+        if (in->slots[b] >= (uint32_t)m->max_slots)
+            return fail(VELO_ERR_INVALID_ARGUMENT, "slot %u >= max_slots", in->slots[b]);
+        if (in->ctx_len[b] < 0) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx_len[%d] < 0", b);
+        const int last = in->ctx_len[b] + N - 1;  // deepest possible position
+        if (in->ctx_len[b] > m->max_pages * 16 || (in->commit && last / 16 >= m->max_pages))
+            return fail(VELO_ERR_OUT_OF_PAGES, "OutOfPages: sequence %d needs position %d, row holds %d", b,
+                        last, m->max_pages * 16);
+        if (in->parents[(size_t)b * N] != -1)
+            return fail(VELO_ERR_INVALID_ARGUMENT, "node 0 of sequence %d must be the root (parent -1)", b);
+        for (int i = 1; i < N; ++i) {
+            const int p = in->parents[(size_t)b * N + i];
+            if (p < 0 || p >= i) return fail(VELO_ERR_INVALID_ARGUMENT, "parents[%d][%d] = %d", b, i, p);
+            if (sampling && p != i - 1)
+                return fail(VELO_ERR_INVALID_ARGUMENT, "sampling verifies chains only (parents[n] = n-1)");
+        }
+        for (int i = 0; i < N; ++i)
+            if (in->tokens[(size_t)b * N + i] >= (uint32_t)V)
+                return fail(VELO_ERR_INVALID_ARGUMENT, "token %u >= n_vocab", in->tokens[(size_t)b * N + i]);
+    }
+    if (sampling && N > 1 && (!in->draft_logits || !in->uniforms))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "sampling needs draft_logits and uniforms");
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    st = velo::ensure_work(c, m, B, N);
+    if (st) return st;
+    cudaStream_t s = c->stream;
+    const int M = B * N, H = m->H(), Hq = m->Hq(), Hkv = m->Hkv(), F = m->F(), L = m->L();
+    const int Nqkv = (Hq + 2 * Hkv) * 128;
+    // inputs and the batch's page-table rows
+    std::vector<uint32_t> ptb((size_t)B * m->max_pages);
+    for (int b = 0; b < B; ++b)
+        std::memcpy(ptb.data() + (size_t)b * m->max_pages,
+                    m->page_table_host.data() + (size_t)in->slots[b] * m->max_pages, (size_t)m->max_pages * 4);
+    VELO_CUDA_TRY(cudaMemcpyAsync(m->tokens, in->tokens, (size_t)M * 4, cudaMemcpyHostToDevice, s));
+    VELO_CUDA_TRY(cudaMemcpyAsync(m->parents, in->parents, (size_t)M * 4, cudaMemcpyHostToDevice, s));
+    VELO_CUDA_TRY(cudaMemcpyAsync(m->ctxlen, in->ctx_len, (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    VELO_CUDA_TRY(cudaMemcpyAsync(m->slots, in->slots, (size_t)B * 4, cudaMemcpyHostToDevice, s));
+    VELO_CUDA_TRY(cudaMemcpyAsync(m->pt_batch, ptb.data(), ptb.size() * 4, cudaMemcpyHostToDevice, s));
+    VELO_CUDA_TRY(velo::launch_tree_ancestors(m->parents, B, N, m->anc, c->err_flag, s));
+    VELO_CUDA_TRY(velo::launch_embed(m->emb, m->tokens, M, H, m->V(), m->x, c->err_flag, s));
+    const float eps = m->meta.norm_eps;
+    for (int l = 0; l < L; ++l) {
+        const velo::Layer& ly = m->layers[l];
+        __half* nk = m->nk + (size_t)l * M * Hkv * 128;
+        __half* nv = m->nv + (size_t)l * M * Hkv * 128;
+        VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, ly.attn_norm, M, H, eps, m->xn, s));
+        st = velo::gemm(c, ly.wqkv, m->xn, M, Nqkv, H, m->qkv, Nqkv, velo::kEpiStoreF32);
+        if (st) return st;
+        VELO_CUDA_TRY(velo::launch_rope_split(m->qkv, m->anc, m->ctxlen, B, N, Hq, Hkv, m->meta.rope_freq_base,
+                                              m->q, nk, nv, s));
+        velo::TreeAttnArgs a{};
+        const size_t lo = (size_t)l * m->layer_pool_elems() * m->kv_elt();
+        a.q = m->q;
+        a.k_pool = static_cast<uint8_t*>(m->k_pool) + lo;
+        a.v_pool = static_cast<uint8_t*>(m->v_pool) + lo;
+        a.k_scale = m->kv_int8 ? m->k_scale + (size_t)l * m->layer_scale_elems() : nullptr;
+        a.v_scale = m->kv_int8 ? m->v_scale + (size_t)l * m->layer_scale_elems() : nullptr;
+        a.page_table = m->pt_batch;
+        a.ctx_len = m->ctxlen;
+        a.node_k = nk;
+        a.node_v = nv;
+        a.anc = m->anc;
+        a.out = m->attn;
+        a.out_f16 = 1;
+        a.B = B;
+        a.N = N;
+        a.Hq = Hq;
+        a.Hkv = Hkv;
+        a.max_pages = m->max_pages;
+        a.pool_pages = m->pool_pages;
+        a.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+        a.err = c->err_flag;
+        VELO_CUDA_TRY(velo::launch_tree_attention(a, m->kv_int8 != 0, s));
+        st = velo::gemm(c, ly.wo, m->attn, M, H, Hq * 128, m->x, H, velo::kEpiAddF32);
+        if (!st) VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, ly.ffn_norm, M, H, eps, m->xn, s));
+        if (!st) st = velo::gemm(c, ly.w13, m->xn, M, 2 * F, H, m->hbuf, F, velo::kEpiSwiGLU);
+        if (!st) st = velo::gemm(c, ly.w2, m->hbuf, M, H, F, m->x, H, velo::kEpiAddF32);
+        if (st) return st;
+    }
+    VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, m->out_norm, M, H, eps, m->xn, s));
+    st = velo::gemm(c, m->lm_head, m->xn, M, V, H, m->logits, V, velo::kEpiStoreF32);
+    if (st) return st;
+    // acceptance
+    if (!sampling || N == 1) {
+        VELO_CUDA_TRY(velo::launch_tree_greedy(m->logits, m->tokens, m->parents, B, N, V, m->expected,
+                                               m->path, m->path_len, m->bonus, s));
+    } else {
+        const int k = N - 1;
+        const size_t need = (size_t)B * k * V;
+        if (need > m->drf_cap) {
+            VELO_CUDA_TRY(cudaStreamSynchronize(s));
+            if (m->drf) cudaFree(m->drf);
+            m->drf = nullptr;
+            m->drf_cap = 0;
+            VELO_CUDA_TRY(cudaMalloc(&m->drf, need * 4));
+            m->drf_cap = need;
+        }
+        std::vector<uint32_t> dt((size_t)B * k);
+        for (int b = 0; b < B; ++b)
+            for (int i = 0; i < k; ++i) dt[(size_t)b * k + i] = in->tokens[(size_t)b * N + i + 1];
+        VELO_CUDA_TRY(cudaMemcpyAsync(m->drf, in->draft_logits, need * 4, cudaMemcpyHostToDevice, s));
+        VELO_CUDA_TRY(cudaMemcpyAsync(m->uni, in->uniforms, (size_t)B * N * 4, cudaMemcpyHostToDevice, s));
+        VELO_CUDA_TRY(cudaMemcpyAsync(m->dtok, dt.data(), dt.size() * 4, cudaMemcpyHostToDevice, s));
+        VELO_CUDA_TRY(cudaStreamSynchronize(s));  // dt is host-stack memory
+        st = velo::run_accept(c, m->logits, m->drf, m->dtok, m->uni, B, k, V, in->temperature, m->acc, m->bonus);
+        if (st) return st;
+        // chain path: nodes 0..acc
+        std::vector<int32_t> acc(B);
+        VELO_CUDA_TRY(cudaMemcpyAsync(acc.data(), m->acc, (size_t)B * 4, cudaMemcpyDeviceToHost, s));
+        VELO_CUDA_TRY(cudaStreamSynchronize(s));
+        std::vector<int32_t> path((size_t)M, -1), plen(B);
+        for (int b = 0; b < B; ++b) {
+            plen[b] = acc[b] + 1;
+            for (int i = 0; i < plen[b]; ++i) path[(size_t)b * N + i] = i;
+        }
+        VELO_CUDA_TRY(cudaMemcpyAsync(m->path, path.data(), path.size() * 4, cudaMemcpyHostToDevice, s));
+        VELO_CUDA_TRY(cudaMemcpyAsync(m->path_len, plen.data(), plen.size() * 4, cudaMemcpyHostToDevice, s));
+        VELO_CUDA_TRY(cudaStreamSynchronize(s));
+    }
+    if (in->commit) {
+        velo::KvCommitArgs a{};
+        a.node_k = m->nk;
+        a.node_v = m->nv;
+        a.path = m->path;
+        a.path_len = m->path_len;
+        a.ctx_len = m->ctxlen;
+        a.slots = m->slots;
+        a.page_table = m->page_table;
+        a.k_pool = m->k_pool;
+        a.v_pool = m->v_pool;
+        a.k_scale = m->k_scale;
+        a.v_scale = m->v_scale;
+        a.B = B;
+        a.N = N;
+        a.L = L;
+        a.Hkv = Hkv;
+        a.max_pages = m->max_pages;
+        a.pool_pages = m->pool_pages;
+        a.kv_int8 = m->kv_int8;
+        a.err = c->err_flag;
+        VELO_CUDA_TRY(velo::launch_kv_commit(a, s));
+    }
+    std::vector<int32_t> plen(B);
+    VELO_CUDA_TRY(cudaMemcpyAsync(plen.data(), m->path_len, (size_t)B * 4, cudaMemcpyDeviceToHost, s));
+    VELO_CUDA_TRY(cudaMemcpyAsync(out->bonus_token, m->bonus, (size_t)B * 4, cudaMemcpyDeviceToHost, s));
+    if (out->accepted_nodes)
+        VELO_CUDA_TRY(cudaMemcpyAsync(out->accepted_nodes, m->path, (size_t)M * 4, cudaMemcpyDeviceToHost, s));
+    if (out->logits)
+        VELO_CUDA_TRY(cudaMemcpyAsync(out->logits, m->logits, (size_t)M * V * 4, cudaMemcpyDeviceToHost, s));
+    st = velo_cuda_sync(c, -1);
+    if (st) return st;
+    for (int b = 0; b < B; ++b) out->accepted_len[b] = plen[b] - 1;
+    return VELO_OK;
+}
+
+}  // extern "C"

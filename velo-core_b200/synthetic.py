@@ -141,3 +141,54 @@ def tree_attention_inputs(B, n_nodes, n_head, n_kv, ctx_lens, kv_dtype=0, seed=0
     g = rng(seed, 35)
     out["parents"] = np.stack([random_tree(n_nodes, max_depth, g) for _ in range(B)])
     return out
+
+
+LAYER_TENSORS = ("attention_norm", "attention.wq", "attention.wk", "attention.wv", "attention.wo",
+                 "ffn_norm", "feed_forward.w1", "feed_forward.w2", "feed_forward.w3")
+
+
+def llama_q4_model(n_vocab, n_embd, n_layer, n_head, n_head_kv, n_ff, seed=0, sigma=0.02,
+                   tied=False):
+    """Random-init Llama weights in the reference's WeightStore layout
+    (src/model_loader.rs:216-232; matrices [out][in]): q4_0 matrices and
+    embedding from N(0, sigma^2), f32 norm weights 1 + N(0, 0.1^2).
+    Returns (meta, {name: (dtype, array, rows, cols)})."""
+    hd = 128
+    meta = dict(n_vocab=n_vocab, n_embd=n_embd, n_layer=n_layer, n_head=n_head,
+                n_head_kv=n_head_kv, n_ff=n_ff, head_dim=hd, rope_freq_base=10000.0,
+                norm_eps=1e-5)
+    g = rng(seed, 50)
+
+    def q4(rows, cols):
+        return (2, quantize_q4_0(g.normal(0, sigma, (rows, cols)).astype(np.float32)), rows, cols)
+
+    def norm():
+        return (0, (1.0 + g.normal(0, 0.1, n_embd)).astype(np.float32), 1, n_embd)
+
+    t = {"token_embd.weight": q4(n_vocab, n_embd), "output_norm.weight": norm()}
+    if not tied:
+        t["output.weight"] = q4(n_vocab, n_embd)
+    for l in range(n_layer):
+        p = f"layers.{l}."
+        t[p + "attention_norm.weight"] = norm()
+        t[p + "attention.wq.weight"] = q4(n_head * hd, n_embd)
+        t[p + "attention.wk.weight"] = q4(n_head_kv * hd, n_embd)
+        t[p + "attention.wv.weight"] = q4(n_head_kv * hd, n_embd)
+        t[p + "attention.wo.weight"] = q4(n_embd, n_head * hd)
+        t[p + "ffn_norm.weight"] = norm()
+        t[p + "feed_forward.w1.weight"] = q4(n_ff, n_embd)
+        t[p + "feed_forward.w2.weight"] = q4(n_embd, n_ff)
+        t[p + "feed_forward.w3.weight"] = q4(n_ff, n_embd)
+    return meta, t
+
+
+def oracle_tensor_list(meta, tensors):
+    """The same tensors in the CPU oracle's order (token_embd, output_norm,
+    output|None, then per layer attention_norm, wq, wk, wv, wo, ffn_norm, w1,
+    w2, w3) as (dtype, array)."""
+    out = [tensors["token_embd.weight"][:2], tensors["output_norm.weight"][:2],
+           tensors["output.weight"][:2] if "output.weight" in tensors else None]
+    for l in range(meta["n_layer"]):
+        for nm in LAYER_TENSORS:
+            out.append(tensors[f"layers.{l}.{nm}.weight"][:2])
+    return out

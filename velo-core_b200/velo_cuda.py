@@ -70,7 +70,36 @@ _SIGS = {
     "velo_cuda_gemm_q4_0": (_I32, [_P, _P, _P, _I32, _I32, _I32, _P, _I32, _I32]),
     "velo_cuda_tree_attention": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _P, _I32, _P, _P, _P, _P,
                                         _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32]),
+    "velo_cuda_load_model": (_I32, [_P, _P, _P, _I32]),
+    "velo_cuda_bind_slot": (_I32, [_P, ctypes.c_uint32, _P, ctypes.c_size_t]),
+    "velo_cuda_write_kv": (_I32, [_P, ctypes.c_uint32, _I32, _I32, _I32, _P, _P]),
+    "velo_cuda_read_kv": (_I32, [_P, ctypes.c_uint32, _I32, _I32, _I32, _P, _P, _P, _P]),
+    "velo_cuda_verify_step": (_I32, [_P, _P, _P]),
 }
+
+DT_F32, DT_F16, DT_Q4_0 = 0, 1, 2
+
+
+class ModelDesc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in
+                ("struct_size", "n_vocab", "n_embd", "n_layer", "n_head", "n_head_kv", "n_ff",
+                 "head_dim")] + [("rope_freq_base", ctypes.c_float), ("norm_eps", ctypes.c_float)]
+
+
+class WeightDesc(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("dtype", ctypes.c_int32), ("data", ctypes.c_void_p),
+                ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64)]
+
+
+class VerifyBatch(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("B", ctypes.c_int32), ("n_nodes", ctypes.c_int32),
+                ("slots", _P), ("ctx_len", _P), ("tokens", _P), ("parents", _P),
+                ("temperature", ctypes.c_float), ("draft_logits", _P), ("uniforms", _P),
+                ("commit", ctypes.c_int32)]
+
+
+class VerifyResult(ctypes.Structure):
+    _fields_ = [("accepted_len", _P), ("accepted_nodes", _P), ("bonus_token", _P), ("logits", _P)]
 
 EPI_STORE_F32, EPI_STORE_F16, EPI_ADD_F32, EPI_SWIGLU = 0, 1, 2, 3
 
@@ -200,6 +229,62 @@ class Context:
             self._h, _ptr(q), _ptr(k_pool), _ptr(v_pool), _ptr(k_scale), _ptr(v_scale),
             k_pool.shape[0], _ptr(page_table), page_table.shape[1], _ptr(ctx_len), _ptr(node_k),
             _ptr(node_v), _ptr(parents), B, N, Hq, n_kv, hd, kv_dtype, _ptr(out), out_f16))
+
+
+    # ------------------------------------------------------------ model + verify
+    def load_model(self, meta, tensors):
+        """meta: dict of velo_model_desc fields; tensors: {name: (dtype, ndarray, rows, cols)}
+        with host arrays in the reference's WeightStore layout."""
+        d = ModelDesc(ctypes.sizeof(ModelDesc), *(int(meta[k]) for k in
+                      ("n_vocab", "n_embd", "n_layer", "n_head", "n_head_kv", "n_ff", "head_dim")),
+                      float(meta["rope_freq_base"]), float(meta["norm_eps"]))
+        keep, ws = [], (WeightDesc * len(tensors))()
+        for i, (name, (dt, arr, rows, cols)) in enumerate(tensors.items()):
+            a = np.ascontiguousarray(arr)
+            nm = name.encode()
+            keep += [a, nm]
+            ws[i] = WeightDesc(nm, dt, a.ctypes.data, rows, cols)
+        check(lib().velo_cuda_load_model(self._h, ctypes.byref(d), ws, len(tensors)))
+
+    def bind_slot(self, slot, pages):
+        p = np.ascontiguousarray(pages, np.uint32)
+        check(lib().velo_cuda_bind_slot(self._h, slot, _ptr(p), p.size))
+
+    def write_kv(self, slot, layer, pos0, k_f16, v_f16):
+        k = np.ascontiguousarray(k_f16, np.float16)
+        v = np.ascontiguousarray(v_f16, np.float16)
+        check(lib().velo_cuda_write_kv(self._h, slot, layer, pos0, k.shape[0], _ptr(k), _ptr(v)))
+
+    def read_kv(self, slot, layer, pos0, n, n_kv, int8=False):
+        dt = np.int8 if int8 else np.float16
+        k = np.zeros((n, n_kv, 128), dt)
+        v = np.zeros((n, n_kv, 128), dt)
+        ks = np.zeros((n, n_kv), np.uint16)
+        vs = np.zeros((n, n_kv), np.uint16)
+        check(lib().velo_cuda_read_kv(self._h, slot, layer, pos0, n, _ptr(k), _ptr(v), _ptr(ks),
+                                      _ptr(vs)))
+        return (k, v, ks, vs) if int8 else (k, v)
+
+    def verify_step(self, slots, ctx_len, tokens, parents, temperature=0.0, draft_logits=None,
+                    uniforms=None, commit=True, want_logits=False, n_vocab=None):
+        """One verify step (host buffers).  Returns dict(accepted_len, accepted_nodes, bonus,
+        logits)."""
+        tok = np.ascontiguousarray(tokens, np.uint32)
+        B, N = tok.shape
+        par = np.ascontiguousarray(parents, np.int32).reshape(B, N)
+        sl = np.ascontiguousarray(slots, np.uint32)
+        cl = np.ascontiguousarray(ctx_len, np.int32)
+        dl = None if draft_logits is None else np.ascontiguousarray(draft_logits, np.float32)
+        un = None if uniforms is None else np.ascontiguousarray(uniforms, np.float32)
+        acc = np.zeros(B, np.int32)
+        nodes = np.zeros((B, N), np.int32)
+        bonus = np.zeros(B, np.uint32)
+        logits = np.zeros((B, N, n_vocab), np.float32) if want_logits else None
+        bt = VerifyBatch(ctypes.sizeof(VerifyBatch), B, N, _ptr(sl), _ptr(cl), _ptr(tok), _ptr(par),
+                         float(temperature), _ptr(dl), _ptr(un), 1 if commit else 0)
+        rs = VerifyResult(_ptr(acc), _ptr(nodes), _ptr(bonus), _ptr(logits))
+        check(lib().velo_cuda_verify_step(self._h, ctypes.byref(bt), ctypes.byref(rs)))
+        return {"accepted_len": acc, "accepted_nodes": nodes, "bonus": bonus, "logits": logits}
 
 
 def q4_0_repacked_bytes(N, K):
