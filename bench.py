@@ -519,6 +519,136 @@ def run_attn(args):
     return 0
 
 
+# ---------------------------------------------------------------- full verify step
+C3_META = dict(n_vocab=32000, n_embd=4096, n_layer=32, n_head=32, n_head_kv=32, n_ff=11008,
+               head_dim=128, rope_freq_base=10000.0, norm_eps=1e-5)
+C3_TREE = [-1, 0, 0, 0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 5, 6]  # (4,2,2) breadth-first to 16 nodes
+
+
+def _q4_device(w):
+    """q4_0 bytes of a device f32 matrix [rows][cols] (the rule of
+    synthetic.quantize_q4_0, on the GPU): returns host uint8 [rows][cols/32*18]."""
+    import torch
+    rows, cols = w.shape
+    xb = w.view(rows, cols // 32, 32)
+    idx = xb.abs().argmax(-1, keepdim=True)
+    m = torch.gather(xb, -1, idx)[..., 0]
+    d = m / -8.0
+    inv = torch.where(d != 0, 1.0 / d, torch.zeros_like(d))
+    q = torch.clamp(torch.trunc(xb * inv[..., None] + 8.5), 0, 15).to(torch.uint8)
+    out = torch.empty((rows, cols // 32, 18), dtype=torch.uint8, device=w.device)
+    out[..., 0:2] = d.half().view(torch.uint8).view(rows, cols // 32, 2)
+    out[..., 2:] = q[..., 0::2] | (q[..., 1::2] << 4)
+    return out.view(rows, -1).cpu().numpy()
+
+
+def c3_model_tensors(meta, seed=0):
+    """Llama-2-7B-shape random-init weights N(0, 0.02^2) quantised to q4_0
+    generated and quantised on the GPU."""
+    import torch
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    H, V, F, L = meta["n_embd"], meta["n_vocab"], meta["n_ff"], meta["n_layer"]
+    Dq, Dk = meta["n_head"] * 128, meta["n_head_kv"] * 128
+
+    def q4(rows, cols):
+        return (2, _q4_device(torch.randn((rows, cols), generator=g, device="cuda") * 0.02), rows, cols)
+
+    def norm():
+        return (0, (1.0 + 0.1 * torch.randn(H, generator=g, device="cuda")).cpu().numpy(), 1, H)
+
+    t = {"token_embd.weight": q4(V, H), "output_norm.weight": norm(), "output.weight": q4(V, H)}
+    for l in range(L):
+        p = f"layers.{l}."
+        t[p + "attention_norm.weight"] = norm()
+        t[p + "attention.wq.weight"] = q4(Dq, H)
+        t[p + "attention.wk.weight"] = q4(Dk, H)
+        t[p + "attention.wv.weight"] = q4(Dk, H)
+        t[p + "attention.wo.weight"] = q4(H, Dq)
+        t[p + "ffn_norm.weight"] = norm()
+        t[p + "feed_forward.w1.weight"] = q4(F, H)
+        t[p + "feed_forward.w2.weight"] = q4(H, F)
+        t[p + "feed_forward.w3.weight"] = q4(F, H)
+    return t
+
+
+def run_verify(args):
+    """The whole verify step at BASELINE config 3: Llama-2-7B shape in q4_0,
+    B=32 sequences of context 2048 in 16-token fp16 pages, a 16-node draft
+    tree each: target forward over 512 rows, greedy tree acceptance and the KV
+    commit of the accepted paths, through velo_cuda_verify_step."""
+    import torch
+    import velo_cuda
+    torch.cuda.set_device(0)
+    meta = dict(C3_META)
+    B, ctx_len = 32, 2048
+    N = len(C3_TREE)
+    per_seq = (ctx_len + N + 15) // 16
+    t0 = time.time()
+    tensors = c3_model_tensors(meta)
+    gen_s = time.time() - t0
+    ctx = velo_cuda.Context(device=0, total_pages=B * per_seq, max_slots=B,
+                            max_pages_per_slot=per_seq)
+    t0 = time.time()
+    ctx.load_model(meta, tensors)
+    load_s = time.time() - t0
+    del tensors
+    for b in range(B):
+        ctx.bind_slot(b, np.arange(b * per_seq, (b + 1) * per_seq))
+    g = np.random.Generator(np.random.Philox(7))
+    tokens = g.integers(0, meta["n_vocab"], (B, N)).astype(np.uint32)
+    parents = np.tile(np.array(C3_TREE, np.int32), (B, 1))
+    slots = np.arange(B, dtype=np.uint32)
+    ctxl = np.full(B, ctx_len, np.int32)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    for _ in range(max(3, args.warmup)):
+        r = ctx.verify_step(slots, ctxl, tokens, parents, commit=True, n_vocab=meta["n_vocab"])
+    steps = max(3, min(args.steps, 30))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    acc_tok = 0
+    with ClockSampler(0) as clk:
+        w0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(steps):
+            r = ctx.verify_step(slots, ctxl, tokens, parents, commit=True, n_vocab=meta["n_vocab"])
+            acc_tok += int((r["accepted_len"] + 1).sum())
+        e1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - w0
+    ms = e0.elapsed_time(e1) / steps
+    params = 0
+    H, F, V = meta["n_embd"], meta["n_ff"], meta["n_vocab"]
+    Dq, Dk = meta["n_head"] * 128, meta["n_head_kv"] * 128
+    params = meta["n_layer"] * (H * (Dq + 2 * Dk) + Dq * H + 3 * H * F) + V * H
+    M = B * N
+    flops = 2.0 * M * params
+    kv_bytes = B * ctx_len * meta["n_layer"] * Dk * 2 * 2
+    w_bytes = params * 18 // 32
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    tfl = float(peaks.get("bf16_tflops_sustained", 1416.2))
+    hbm = float(peaks.get("hbm_gbs", HBM_FALLBACK_GBS))
+    floor_ms = flops / (tfl * 1e12) * 1e3 + kv_bytes / (hbm * 1e9) * 1e3
+    line = {"workload": "verify step, BASELINE config 3 (Llama-2-7B shape q4_0, B=32, "
+                        "16-node tree, ctx 2048 fp16 pages)",
+            "us_per_step": ms * 1e3, "accepted_tokens_per_s": acc_tok / steps / (ms / 1e3),
+            "e2e_ms_per_step": wall / steps * 1e3, "rows": M, "gemm_tflop": flops / 1e12,
+            "kv_gb": kv_bytes / 1e9, "weight_gb": w_bytes / 1e9,
+            "floor_ms_at_measured_peaks": floor_ms, "frac_of_floor": floor_ms / ms,
+            "accepted_per_step": acc_tok / steps, "clocks": clk.summary(),
+            "model_gen_s": gen_s, "load_s": load_s,
+            "data": "random-init N(0,0.02^2) weights quantised to q4_0 on the device; "
+                    "KV pages zero-filled (timing does not depend on their values)"}
+    ctx.close()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def synthetic_ctx(B, seed=0):
     """Per-sequence context lengths U{512..8192}."""
     import synthetic
@@ -550,7 +680,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    ap.add_argument("--workload", default="accept", choices=["accept", "q4gemm", "attn"])
+    ap.add_argument("--workload", default="accept", choices=["accept", "q4gemm", "attn", "verify"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default="", help="one case of a multi-case workload")
     args = ap.parse_args()
@@ -562,6 +692,8 @@ def main():
         return run_q4gemm(args)
     if args.workload == "attn":
         return run_attn(args)
+    if args.workload == "verify":
+        return run_verify(args)
     return run_cuda(args)
 
 
