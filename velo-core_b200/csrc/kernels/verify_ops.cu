@@ -56,39 +56,65 @@ __global__ void rmsnorm_f16_kernel(const float* __restrict__ x, const float* __r
     }
 }
 
-// one thread per (row, head of q/k/v, rotation pair i < 64)
+// one block per row m: the 64 rotation angles of the row's position are
+// computed once (theta = pos / base^(2i/128), llama_cpu.rs:121-123), then
+// every head of q / k / v is rotated (q, k) or copied (v), 8 values a thread
 __global__ void rope_split_kernel(const float* __restrict__ qkv, const uint64_t* __restrict__ anc,
                                   const int32_t* __restrict__ ctx_len, int B, int N, int Hq,
                                   int Hkv, float freq_base, __half* __restrict__ q,
                                   __half* __restrict__ nk, __half* __restrict__ nv) {
-    const int heads = Hq + 2 * Hkv;
-    const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (long)B * N * heads * (D / 2)) return;
-    const int i = (int)(idx % (D / 2));
-    const int hh = (int)((idx / (D / 2)) % heads);
-    const int m = (int)(idx / ((long)(D / 2) * heads));
+    __shared__ float cs[D / 2], sn[D / 2];
+    const int m = blockIdx.x;
     const int b = m / N;
-    const float* src = qkv + ((size_t)m * heads + hh) * D;
-    float x0 = src[i], x1 = src[i + D / 2];
-    if (hh < Hq + Hkv) {
-        const int pos = ctx_len[b] + __popcll(anc[m]) - 1;
+    const int pos = ctx_len[b] + __popcll(anc[m]) - 1;
+    if (threadIdx.x < D / 2) {
+        const int i = threadIdx.x;
         const float theta = (float)pos / powf(freq_base, (2.0f * (float)i) / (float)D);
-        float sn, cs;
-        sincosf(theta, &sn, &cs);
-        const float r0 = x0 * cs - x1 * sn;
-        const float r1 = x0 * sn + x1 * cs;
-        x0 = r0;
-        x1 = r1;
+        sincosf(theta, &sn[i], &cs[i]);
     }
-    __half* dst;
-    if (hh < Hq)
-        dst = q + ((size_t)m * Hq + hh) * D;
-    else if (hh < Hq + Hkv)
-        dst = nk + ((size_t)m * Hkv + (hh - Hq)) * D;
-    else
-        dst = nv + ((size_t)m * Hkv + (hh - Hq - Hkv)) * D;
-    dst[i] = __float2half_rn(x0);
-    dst[i + D / 2] = __float2half_rn(x1);
+    __syncthreads();
+    const int heads = Hq + 2 * Hkv;
+    // work item: (head, group of 8 rotation pairs)
+    for (int w = threadIdx.x; w < heads * (D / 16); w += blockDim.x) {
+        const int hh = w / (D / 16), i0 = (w % (D / 16)) * 8;
+        const float* src = qkv + ((size_t)m * heads + hh) * D;
+        float4 a0 = *reinterpret_cast<const float4*>(src + i0);
+        float4 a1 = *reinterpret_cast<const float4*>(src + i0 + 4);
+        float4 b0 = *reinterpret_cast<const float4*>(src + i0 + D / 2);
+        float4 b1 = *reinterpret_cast<const float4*>(src + i0 + D / 2 + 4);
+        float x0[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        float x1[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        if (hh < Hq + Hkv) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float c = cs[i0 + e], s = sn[i0 + e];
+                const float r0 = x0[e] * c - x1[e] * s;
+                const float r1 = x0[e] * s + x1[e] * c;
+                x0[e] = r0;
+                x1[e] = r1;
+            }
+        }
+        __half* dst;
+        if (hh < Hq)
+            dst = q + ((size_t)m * Hq + hh) * D;
+        else if (hh < Hq + Hkv)
+            dst = nk + ((size_t)m * Hkv + (hh - Hq)) * D;
+        else
+            dst = nv + ((size_t)m * Hkv + (hh - Hq - Hkv)) * D;
+        uint4 o0, o1;
+        __half2 h[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            h[e] = __floats2half2_rn(x0[2 * e], x0[2 * e + 1]);
+            h[4 + e] = __floats2half2_rn(x1[2 * e], x1[2 * e + 1]);
+        }
+        o0 = make_uint4(*reinterpret_cast<uint32_t*>(&h[0]), *reinterpret_cast<uint32_t*>(&h[1]),
+                        *reinterpret_cast<uint32_t*>(&h[2]), *reinterpret_cast<uint32_t*>(&h[3]));
+        o1 = make_uint4(*reinterpret_cast<uint32_t*>(&h[4]), *reinterpret_cast<uint32_t*>(&h[5]),
+                        *reinterpret_cast<uint32_t*>(&h[6]), *reinterpret_cast<uint32_t*>(&h[7]));
+        *reinterpret_cast<uint4*>(dst + i0) = o0;
+        *reinterpret_cast<uint4*>(dst + i0 + D / 2) = o1;
+    }
 }
 
 // argmax with the GreedySampler rule: candidates in increasing index order,
@@ -236,10 +262,8 @@ cudaError_t launch_rmsnorm_f16(const float* x, const float* w, int M, int H, flo
 cudaError_t launch_rope_split(const float* qkv, const uint64_t* anc, const int32_t* ctx_len,
                               int B, int N, int Hq, int Hkv, float freq_base, __half* q,
                               __half* nk, __half* nv, cudaStream_t s) {
-    const long total = (long)B * N * (Hq + 2 * Hkv) * (D / 2);
-    if (total == 0) return cudaSuccess;
-    rope_split_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(qkv, anc, ctx_len, B, N, Hq,
-                                                                      Hkv, freq_base, q, nk, nv);
+    if (B * N == 0) return cudaSuccess;
+    rope_split_kernel<<<B * N, 256, 0, s>>>(qkv, anc, ctx_len, B, N, Hq, Hkv, freq_base, q, nk, nv);
     return cudaGetLastError();
 }
 
