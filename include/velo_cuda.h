@@ -79,6 +79,13 @@ VELO_API int32_t velo_cuda_create(const velo_cuda_config *cfg, int32_t device, i
                          velo_cuda_ctx **out);
 VELO_API void velo_cuda_destroy(velo_cuda_ctx *ctx);
 
+/* Write a fresh NCCL unique id (128 bytes) to `out`: rank 0 of a tensor-
+ * parallel group makes one and hands it to every rank's velo_cuda_create,
+ * which all ranks call concurrently (one host thread or process per GPU).
+ * No counterpart in the reference, whose TP all-reduce runs on the CPU
+ * (src/metal/tp_model.rs:199-277). */
+VELO_API int32_t velo_cuda_nccl_unique_id(void *out);
+
 /* Message of the last failure on the calling thread ("" if none). */
 VELO_API const char *velo_cuda_last_error(void);
 VELO_API int32_t velo_cuda_abi_version(void);
@@ -245,9 +252,29 @@ typedef struct velo_weight_desc {
     uint64_t rows, cols;
 } velo_weight_desc;
 
+/* Tensor-parallel sharding on the host (src/metal/sharding.rs:28-126). */
+typedef enum velo_shard_strategy {
+    VELO_SHARD_REPLICATED = 0,
+    VELO_SHARD_COLUMN = 1, /* split the output rows */
+    VELO_SHARD_ROW = 2     /* split the input columns (q4_0: on 32-element blocks) */
+} velo_shard_strategy;
+
+/* get_shard_strategy (sharding.rs:112-126): q/k/v, w1/w3 and output.weight
+ * Column, wo and w2 Row, everything else Replicated. */
+VELO_API int32_t velo_cuda_shard_strategy(const char *name);
+
+/* shard_weight (sharding.rs:28-110) of a host tensor for `rank` of `tp`:
+ * copies the shard to `out` (out_bytes large enough) and writes its shape.
+ * Same divisibility errors as the reference (VELO_ERR_INVALID_ARGUMENT). */
+VELO_API int32_t velo_cuda_shard_weight(const velo_weight_desc *w, int32_t strategy, int32_t tp,
+                                        int32_t rank, void *out, size_t out_bytes,
+                                        uint64_t *out_rows, uint64_t *out_cols);
+
 /* Upload and repack a model (the context then owns the device copies) and
  * allocate the zero-filled paged KV pool of the context's config (total_pages
  * x n_layer, kv_dtype) and its page table (max_slots x max_pages_per_slot).
+ * With tp_size > 1 every rank passes the full tensors and keeps its shard
+ * (velo_cuda_shard_weight); its pool holds its n_head_kv / tp_size heads.
  * Replaces LlamaCpuModel::from_weights / LlamaMetalModel::new and
  * MetalMemoryRuntime::new (src/llama_cpu.rs:168-190, src/metal/runtime.rs). */
 VELO_API int32_t velo_cuda_load_model(velo_cuda_ctx *ctx, const velo_model_desc *desc,

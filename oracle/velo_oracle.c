@@ -974,3 +974,48 @@ int vo_kv_commit(int kv_dtype, void *pool, uint16_t *scale,
     free(tmp);
     return 0;
 }
+
+/* ------------------------------------------------------------------ */
+/* sharding.rs:112-126 get_shard_strategy                              */
+/* ------------------------------------------------------------------ */
+int vo_shard_strategy(const char *name) {
+    if (strstr(name, "attention.wq") || strstr(name, "attention.wk") || strstr(name, "attention.wv"))
+        return 1;
+    if (strstr(name, "attention.wo")) return 2;
+    if (strstr(name, "feed_forward.w1") || strstr(name, "feed_forward.w3")) return 1;
+    if (strstr(name, "feed_forward.w2")) return 2;
+    if (strcmp(name, "output.weight") == 0) return 1;
+    return 0;
+}
+
+/* sharding.rs:28-110 shard_weight.  The reference's shape is GGUF order
+ * [cols, rows]: Column divides shape[last] = rows and takes rows
+ * [rank*rows/tp, (rank+1)*rows/tp); Row divides shape[0] = cols, requires the
+ * shard width to be a multiple of the quant block, and takes the same byte
+ * slice of every row. */
+int vo_shard_weight(int dtype, const uint8_t *data, size_t rows, size_t cols, int strategy,
+                    int tp, int rank, uint8_t *out, size_t *rows_out, size_t *cols_out) {
+    size_t rb = vo_row_bytes(dtype, cols);
+    if (tp <= 1 || strategy == 0) {
+        memcpy(out, data, rb * rows);
+        *rows_out = rows;
+        *cols_out = cols;
+        return 0;
+    }
+    if (strategy == 1) {
+        if (rows % (size_t)tp) return 1;
+        size_t sr = rows / (size_t)tp;
+        memcpy(out, data + (size_t)rank * sr * rb, sr * rb);
+        *rows_out = sr;
+        *cols_out = cols;
+        return 0;
+    }
+    if (cols % (size_t)tp) return 1;
+    size_t sc = cols / (size_t)tp, block = dtype == VO_Q4_0 ? 32 : 1;
+    if (sc % block) return 1;
+    size_t srb = rb / (size_t)tp;
+    for (size_t r = 0; r < rows; ++r) memcpy(out + r * srb, data + r * rb + (size_t)rank * srb, srb);
+    *rows_out = rows;
+    *cols_out = sc;
+    return 0;
+}

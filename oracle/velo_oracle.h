@@ -152,6 +152,15 @@ int vo_kv_commit(int kv_dtype, void *pool, uint16_t *scale,
                  const uint16_t *node_kv, const int32_t *path, size_t len,
                  size_t n_kv, size_t hd, size_t page_size);
 
+/* ---- sharding.rs:28-126 (tensor parallelism) ----
+ * strategy: 0 replicated, 1 column (split rows = output features), 2 row
+ * (split cols = input features; q4_0 blocks of 32).  Returns 0, or 1 with the
+ * reference's divisibility errors.  out holds the shard, rows_out / cols_out
+ * its shape. */
+int vo_shard_strategy(const char *name);
+int vo_shard_weight(int dtype, const uint8_t *data, size_t rows, size_t cols, int strategy,
+                    int tp, int rank, uint8_t *out, size_t *rows_out, size_t *cols_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -75,6 +75,9 @@ def lib():
             "vo_quantize_kv_int8": (None, [_P, _SZ, _P, _P]),
             "vo_kv_commit": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _SZ, _SZ, _P, _P, _SZ,
                                             _SZ, _SZ, _SZ]),
+            "vo_shard_strategy": (ctypes.c_int, [ctypes.c_char_p]),
+            "vo_shard_weight": (ctypes.c_int, [ctypes.c_int, _P, _SZ, _SZ, ctypes.c_int,
+                                               ctypes.c_int, ctypes.c_int, _P, _P, _P]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -371,3 +374,24 @@ def kv_commit(kv_dtype, pool, scale, page_table, n_bound, n_cached, node_kv, pat
     p = c_arr(path, np.int32)
     return lib().vo_kv_commit(kv_dtype, ptr(pool), ptr(scale), ptr(pt), n_bound, n_cached,
                               ptr(nk), ptr(p), p.size, n_kv, hd, page_size)
+
+
+# ------------------------------------------------------------ sharding.rs
+def shard_strategy(name):
+    return lib().vo_shard_strategy(name.encode())
+
+
+def shard_weight(dtype, data, rows, cols, strategy, tp, rank):
+    """sharding.rs:28-110.  Returns (bytes, rows, cols) or raises ValueError."""
+    d = np.ascontiguousarray(data).view(np.uint8).reshape(-1)  # raw bytes of any dtype
+    out = np.zeros(d.size, np.uint8)
+    r, c = ctypes.c_size_t(), ctypes.c_size_t()
+    rc = lib().vo_shard_weight(dtype, ptr(d), rows, cols, strategy, tp, rank, ptr(out),
+                               ctypes.byref(r), ctypes.byref(c))
+    if rc:
+        raise ValueError("shard_weight: not divisible")
+    return out[:r.value * row_bytes(dtype, c.value)], r.value, c.value
+
+
+def row_bytes(dtype, cols):
+    return lib().vo_row_bytes(dtype, cols)

@@ -1,0 +1,84 @@
+"""Tensor-parallel verify step on 2 GPUs (one process per GPU, NCCL over
+NVLink): q/k/v/w1/w3/LM head column-split, wo/w2 row-split with an
+all-reduce after each (src/metal/sharding.rs:112-126, tp_model.rs:92-277),
+vocabulary-sharded greedy acceptance.  The all-gathered logits must match the
+CPU oracle of the unsharded model within 2e-2 and the decisions must be
+bit-exact on those logits.  Skipped on a machine with fewer than 2 GPUs."""
+import os
+
+import numpy as np
+import pytest
+
+import synthetic
+import vo
+
+pytestmark = pytest.mark.gpu
+
+SHAPE = dict(n_vocab=1000, n_embd=512, n_layer=2, n_head=4, n_head_kv=2, n_ff=1024)
+
+
+def _rank(rank, tp, nid, meta, tensors, kv, tokens, parents, P, q):
+    try:
+        import velo_cuda
+        ctx = velo_cuda.Context(device=rank, total_pages=32, max_slots=2, max_pages_per_slot=16,
+                                tp_rank=rank, tp_size=tp, nccl_id=nid)
+        ctx.load_model(meta, tensors)
+        ctx.bind_slot(1, np.arange(16) + 7)
+        hk = meta["n_head_kv"] // tp
+        for l, (K, V) in enumerate(kv):
+            ks = K[:, rank * hk:(rank + 1) * hk]
+            vs = V[:, rank * hk:(rank + 1) * hk]
+            for p0 in range(0, P, 64):
+                ctx.write_kv(1, l, p0, ks[p0:p0 + 64], vs[p0:p0 + 64])
+        res = ctx.verify_step([1], [P], tokens[None], parents[None], commit=True,
+                              want_logits=True, n_vocab=meta["n_vocab"])
+        ctx.close()
+        q.put((rank, res["logits"][0], int(res["accepted_len"][0]),
+               list(res["accepted_nodes"][0]), int(res["bonus"][0]), None))
+    except Exception as e:  # report instead of hanging the peer
+        q.put((rank, None, 0, [], 0, repr(e)))
+
+
+def test_tp2_verify_matches_oracle():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    import velo_cuda
+    meta, tensors = synthetic.llama_q4_model(**SHAPE, seed=21)
+    g = synthetic.rng(22, 80)
+    P = 50
+    prompt = g.integers(0, meta["n_vocab"], P).astype(np.uint32)
+    ora = vo.Model(dict(meta, n_ctx=512), synthetic.oracle_tensor_list(meta, tensors))
+    ora.forward_sequence(prompt)
+    Hkv = meta["n_head_kv"]
+    kv = [(ora.read_kv(0, l, P).reshape(P, Hkv, 128).astype(np.float16),
+           ora.read_kv(1, l, P).reshape(P, Hkv, 128).astype(np.float16))
+          for l in range(meta["n_layer"])]
+    parents = synthetic.random_tree(10, 4, g)
+    tokens = g.integers(0, meta["n_vocab"], 10).astype(np.uint32)
+    ref = ora.verify_tree(tokens, parents, P)
+    nid = velo_cuda.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank, args=(r, 2, nid, meta, tensors, kv, tokens, parents, P, q))
+          for r in range(2)]
+    for p in ps:
+        p.start()
+    out = {}
+    for _ in ps:
+        r = q.get(timeout=300)
+        out[r[0]] = r
+    for p in ps:
+        p.join(timeout=60)
+    for r in range(2):
+        assert out[r][5] is None, out[r][5]
+    lg = out[0][1]
+    assert np.array_equal(lg, out[1][1])
+    assert np.abs(lg - ref).max() <= 2e-2
+    exp = np.array([vo.greedy(lg[n])[0] for n in range(10)], np.uint32)
+    path, bonus = vo.find_best_path(parents, tokens, exp)
+    for r in range(2):
+        assert out[r][2] == len(path) - 1
+        assert out[r][3][:len(path)] == path
+        assert out[r][4] == bonus

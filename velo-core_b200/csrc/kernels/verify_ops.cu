@@ -159,6 +159,59 @@ __global__ void row_argmax_kernel(const float* __restrict__ logits, int V,
     }
 }
 
+// per row: (value, global index) of this shard's GreedySampler maximum
+__global__ void row_argmax_pairs_kernel(const float* __restrict__ logits, int v_loc, int v_ofs,
+                                        int2* __restrict__ pairs) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float* row = logits + (size_t)blockIdx.x * v_loc;
+    ArgMax best{-INFINITY, -1};
+    for (int i = threadIdx.x; i < v_loc; i += blockDim.x) {
+        const float x = row[i];
+        if (x >= best.v) best = ArgMax{x, i};
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        ArgMax other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+        best = am_combine(best, other);
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        sv[w] = best.v;
+        si[w] = best.i;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        ArgMax r{-INFINITY, -1};
+        for (int k = 0; k < (int)(blockDim.x >> 5); ++k) r = am_combine(r, ArgMax{sv[k], si[k]});
+        pairs[blockIdx.x] = make_int2(__float_as_int(r.v), r.i < 0 ? -1 : r.i + v_ofs);
+    }
+}
+
+__global__ void argmax_combine_kernel(const int2* __restrict__ pairs, int tp, int M,
+                                      uint32_t* __restrict__ expected) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= M) return;
+    ArgMax r{-INFINITY, -1};
+    for (int t = 0; t < tp; ++t) {
+        const int2 p = pairs[(size_t)t * M + m];
+        r = am_combine(r, ArgMax{__int_as_float(p.x), p.y});
+    }
+    expected[m] = r.i < 0 ? 0u : (uint32_t)r.i;
+}
+
+__global__ void add_f32_kernel(float* __restrict__ x, const float* __restrict__ y, size_t n4) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    float4 a = reinterpret_cast<float4*>(x)[i];
+    const float4 b = reinterpret_cast<const float4*>(y)[i];
+    a.x += b.x;
+    a.y += b.y;
+    a.z += b.z;
+    a.w += b.w;
+    reinterpret_cast<float4*>(x)[i] = a;
+}
+
 // one thread per sequence: find_best_path on the expected tokens
 __global__ void tree_walk_kernel(const uint32_t* __restrict__ tokens, const int32_t* __restrict__ parents,
                                  const uint32_t* __restrict__ expected, int B, int N,
@@ -274,6 +327,34 @@ cudaError_t launch_tree_greedy(const float* logits, const uint32_t* tokens, cons
     row_argmax_kernel<<<B * N, 512, 0, s>>>(logits, V, expected);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    tree_walk_kernel<<<(B + 63) / 64, 64, 0, s>>>(tokens, parents, expected, B, N, path, path_len, bonus);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add_f32(float* x, const float* y, size_t n, cudaStream_t s) {
+    const size_t n4 = n / 4;  // n is a multiple of 128 here
+    if (n4 == 0) return cudaSuccess;
+    add_f32_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(x, y, n4);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_row_argmax_pairs(const float* logits, int M, int v_loc, int v_ofs, int2* pairs,
+                                    cudaStream_t s) {
+    if (M == 0) return cudaSuccess;
+    row_argmax_pairs_kernel<<<M, 512, 0, s>>>(logits, v_loc, v_ofs, pairs);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_combine(const int2* pairs, int tp, int M, uint32_t* expected, cudaStream_t s) {
+    if (M == 0) return cudaSuccess;
+    argmax_combine_kernel<<<(M + 127) / 128, 128, 0, s>>>(pairs, tp, M, expected);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tree_walk(const uint32_t* tokens, const int32_t* parents, const uint32_t* expected,
+                             int B, int N, int32_t* path, int32_t* path_len, uint32_t* bonus,
+                             cudaStream_t s) {
+    if (B == 0) return cudaSuccess;
     tree_walk_kernel<<<(B + 63) / 64, 64, 0, s>>>(tokens, parents, expected, B, N, path, path_len, bonus);
     return cudaGetLastError();
 }

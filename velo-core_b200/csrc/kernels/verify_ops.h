@@ -33,6 +33,23 @@ cudaError_t launch_tree_greedy(const float* logits, const uint32_t* tokens, cons
                                int B, int N, int V, uint32_t* expected, int32_t* path,
                                int32_t* path_len, uint32_t* bonus, cudaStream_t s);
 
+// Tensor parallelism: x += y (the all-reduced partial of a row-split GEMM).
+cudaError_t launch_add_f32(float* x, const float* y, size_t n, cudaStream_t s);
+
+// Tensor parallelism, vocabulary-sharded LM head: per row the GreedySampler
+// maximum of this rank's logits [M][v_loc] as (value, global index) pairs
+// (index -1 when the shard has no non-NaN value) ...
+cudaError_t launch_row_argmax_pairs(const float* logits, int M, int v_loc, int v_ofs, int2* pairs,
+                                    cudaStream_t s);
+// ... and the winner over the tp gathered shards [tp][M] (larger value, ties
+// to the larger index = the later shard, as one pass over the whole row).
+cudaError_t launch_argmax_combine(const int2* pairs, int tp, int M, uint32_t* expected, cudaStream_t s);
+
+// Greedy tree walk alone, on precomputed expected tokens.
+cudaError_t launch_tree_walk(const uint32_t* tokens, const int32_t* parents, const uint32_t* expected,
+                             int B, int N, int32_t* path, int32_t* path_len, uint32_t* bonus,
+                             cudaStream_t s);
+
 // KV commit: node rows path[b][0..path_len[b]) of every layer's tree scratch
 // (f16 [L][B*N][Hkv][128], stride layer_rows) are written to the paged pool
 // at positions ctx_len[b] + i.  INT8 pools quantise per token and head as

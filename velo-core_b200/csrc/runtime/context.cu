@@ -10,6 +10,7 @@
 #include <thread>
 
 #include "kernels/accept.h"
+#include "runtime/nccl_dyn.h"
 
 namespace velo {
 
@@ -153,7 +154,38 @@ int32_t velo_cuda_create(const velo_cuda_config* cfg, int32_t device, int32_t tp
         return st;
     }
     c->stream = c->own_stream;
+    if (tp_size > 1) {
+        // tensor-parallel group: every rank calls velo_cuda_create with the
+        // same id at the same time (ncclCommInitRank is collective)
+        const velo::NcclApi* nc = velo::nccl_api();
+        if (!nc) {
+            velo_cuda_destroy(c);
+            return VELO_ERR_NCCL;
+        }
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_unique_id, sizeof(id));
+        ncclComm_t comm = nullptr;
+        ncclResult_t r = nc->CommInitRank(&comm, tp_size, id, tp_rank);
+        if (r != ncclSuccess) {
+            const char* msg = nc->GetErrorString(r);
+            velo_cuda_destroy(c);
+            return fail(VELO_ERR_NCCL, "ncclCommInitRank(rank %d of %d) failed: %s", tp_rank, tp_size, msg);
+        }
+        c->nccl_comm = comm;
+    }
     *out = c;
+    return VELO_OK;
+}
+
+int32_t velo_cuda_nccl_unique_id(void* out) {
+    velo::clear_last_error();
+    if (!out) return fail(VELO_ERR_INVALID_ARGUMENT, "out is NULL");
+    const velo::NcclApi* nc = velo::nccl_api();
+    if (!nc) return VELO_ERR_NCCL;
+    ncclUniqueId id;
+    ncclResult_t r = nc->GetUniqueId(&id);
+    if (r != ncclSuccess) return fail(VELO_ERR_NCCL, "ncclGetUniqueId failed: %s", nc->GetErrorString(r));
+    std::memcpy(out, &id, sizeof(id));
     return VELO_OK;
 }
 
@@ -168,6 +200,10 @@ void velo_cuda_destroy(velo_cuda_ctx* c) {
     c->attn_ws.release();
     velo::destroy_model(c->model);
     c->model = nullptr;
+    if (c->nccl_comm) {
+        if (const velo::NcclApi* nc = velo::nccl_api()) nc->CommDestroy(static_cast<ncclComm_t>(c->nccl_comm));
+        c->nccl_comm = nullptr;
+    }
     if (c->err_flag) cudaFree(c->err_flag);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     delete c;

@@ -64,4 +64,5 @@ struct velo_cuda_ctx {
     velo::DeviceBuffer attn_ws;    // tree attention: ancestor masks
     int* err_flag = nullptr;       // device-side input flag
     velo::Model* model = nullptr;  // weights, KV pool and verify buffers (velo_cuda_load_model)
+    void* nccl_comm = nullptr;     // ncclComm_t of the tensor-parallel group (tp_size > 1)
 };

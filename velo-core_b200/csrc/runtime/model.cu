@@ -19,6 +19,10 @@
 #include "kernels/tree_attn.h"
 #include "kernels/verify_ops.h"
 #include "runtime/context.h"
+#include "runtime/nccl_dyn.h"
+#include "runtime/shard.h"
+
+#include <deque>
 
 namespace velo {
 
@@ -32,7 +36,9 @@ struct Layer {
 };
 
 struct Model {
-    velo_model_desc meta{};
+    velo_model_desc meta{};    // head / kv-head / ffn counts of this rank's shard
+    int tp = 1, rank = 0;      // tensor-parallel position
+    int V_loc = 0, v_ofs = 0;  // this rank's vocabulary shard of the LM head
     float* emb = nullptr;      // [V][H] f32
     float* out_norm = nullptr; // [H]
     uint8_t* lm_head = nullptr;
@@ -57,7 +63,12 @@ struct Model {
     __half* nv = nullptr;
     __half* attn = nullptr;
     __half* hbuf = nullptr;
-    float* logits = nullptr;
+    float* logits = nullptr;   // [M][V_loc]
+    float* y = nullptr;        // [M][H] partial of a row-split GEMM (tp > 1)
+    int2* pairs = nullptr;     // [M] this shard's argmax
+    int2* pairs_all = nullptr; // [tp][M]
+    float* logits_all = nullptr;  // [tp][M][V_loc] (logits requested, tp > 1)
+    size_t logits_all_cap = 0;
     uint32_t* tokens = nullptr;
     int32_t* parents = nullptr;
     int32_t* ctxlen = nullptr;
@@ -90,6 +101,7 @@ void destroy_model(Model* m) {
     for (void* p : m->allocs) cudaFree(p);
     for (void* p : m->work) cudaFree(p);
     if (m->drf) cudaFree(m->drf);
+    if (m->logits_all) cudaFree(m->logits_all);
     delete m;
 }
 
@@ -208,7 +220,7 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
     for (void* p : m->work) cudaFree(p);
     m->work.clear();
     const int cM = M > m->cap_M ? M : m->cap_M, cB = B > m->cap_B ? B : m->cap_B;
-    const size_t H = m->H(), D = 128, Hq = m->Hq(), Hkv = m->Hkv(), F = m->F(), V = m->V();
+    const size_t H = m->H(), D = 128, Hq = m->Hq(), Hkv = m->Hkv(), F = m->F();
     const size_t L = m->L();
     int32_t st = VELO_OK;
     if (!st) st = dev_alloc(m, &m->x, (size_t)cM * H * 4, true);
@@ -219,7 +231,10 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
     if (!st) st = dev_alloc(m, &m->nv, L * cM * Hkv * D * 2, true);
     if (!st) st = dev_alloc(m, &m->attn, (size_t)cM * Hq * D * 2, true);
     if (!st) st = dev_alloc(m, &m->hbuf, (size_t)cM * F * 2, true);
-    if (!st) st = dev_alloc(m, &m->logits, (size_t)cM * V * 4, true);
+    if (!st) st = dev_alloc(m, &m->logits, (size_t)cM * m->V_loc * 4, true);
+    if (!st && m->tp > 1) st = dev_alloc(m, &m->y, (size_t)cM * H * 4, true);
+    if (!st) st = dev_alloc(m, &m->pairs, (size_t)cM * 8, true);
+    if (!st) st = dev_alloc(m, &m->pairs_all, (size_t)cM * 8 * m->tp, true);
     if (!st) st = dev_alloc(m, &m->tokens, (size_t)cM * 4, true);
     if (!st) st = dev_alloc(m, &m->parents, (size_t)cM * 4, true);
     if (!st) st = dev_alloc(m, &m->anc, (size_t)cM * 8, true);
@@ -257,6 +272,24 @@ int32_t gemm(velo_cuda_ctx* c, const uint8_t* w, const __half* x, int M, int N, 
     return VELO_OK;
 }
 
+int32_t nccl_check(ncclResult_t r, const NcclApi* nc, const char* what) {
+    if (r == ncclSuccess) return VELO_OK;
+    return fail(VELO_ERR_NCCL, "%s failed: %s", what, nc->GetErrorString(r));
+}
+
+// y (the partial of this rank's row-split GEMM) summed over the group, added to x
+int32_t allreduce_add(velo_cuda_ctx* c, Model* m, int M) {
+    const NcclApi* nc = nccl_api();
+    if (!nc) return VELO_ERR_NCCL;
+    const size_t n = (size_t)M * m->H();
+    int32_t st = nccl_check(nc->AllReduce(m->y, m->y, n, ncclFloat32, ncclSum,
+                                          static_cast<ncclComm_t>(c->nccl_comm), c->stream),
+                            nc, "ncclAllReduce");
+    if (st) return st;
+    VELO_CUDA_TRY(launch_add_f32(m->x, m->y, n, c->stream));
+    return VELO_OK;
+}
+
 int32_t check_model(velo_cuda_ctx* c) {
     if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
     if (!c->model) return fail(VELO_ERR_INVALID_ARGUMENT, "no model loaded (velo_cuda_load_model)");
@@ -287,41 +320,84 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
     if (c->cfg.page_size != 16)
         return fail(VELO_ERR_INVALID_BLOCK_SIZE, "page_size %u: the kernels use 16-token pages",
                     c->cfg.page_size);
+    const int tp = c->tp_size, rank = c->tp_rank;
+    if (tp > 1 && (d->n_head % tp || d->n_head_kv % tp || d->n_ff % tp || d->n_vocab % tp ||
+                   (d->n_ff / tp) % 32))
+        return fail(VELO_ERR_INVALID_ARGUMENT,
+                    "heads %u/%u, n_ff %u and n_vocab %u must divide by tp %d (n_ff/tp by 32)",
+                    d->n_head, d->n_head_kv, d->n_ff, d->n_vocab, tp);
     VELO_CUDA_TRY(cudaSetDevice(c->device));
     velo::destroy_model(c->model);
     c->model = nullptr;
     Model* m = new Model();
     m->meta = *d;
     m->meta.struct_size = sizeof(velo_model_desc);
+    m->tp = tp;
+    m->rank = rank;
+    m->meta.n_head = d->n_head / tp;
+    m->meta.n_head_kv = d->n_head_kv / tp;
+    m->meta.n_ff = d->n_ff / tp;
+    m->V_loc = (int)(d->n_vocab / tp);
+    m->v_ofs = rank * m->V_loc;
     velo::Index ix;
     for (int i = 0; i < n; ++i)
         if (w[i].name) ix[w[i].name] = &w[i];
-    const size_t H = d->n_embd, V = d->n_vocab, F = d->n_ff, Dq = (size_t)d->n_head * d->head_dim;
-    cudaStream_t s = c->stream;
+    // this rank's shard of a tensor (sharding.rs), kept alive until uploaded
+    std::deque<std::vector<uint8_t>> bufs;
+    std::deque<velo_weight_desc> descs;
     int32_t st = VELO_OK;
+    auto shard = [&](const velo_weight_desc* wd, int32_t strategy) -> const velo_weight_desc* {
+        if (!wd || st || tp == 1 || strategy == VELO_SHARD_REPLICATED) return wd;
+        if (!wd->data || wd->dtype < VELO_DT_F32 || wd->dtype > VELO_DT_Q4_0) return wd;
+        bufs.emplace_back();
+        velo_weight_desc out = *wd;
+        st = velo::shard_weight(*wd, strategy, tp, rank, bufs.back(), out.rows, out.cols);
+        out.data = bufs.back().data();
+        descs.push_back(out);
+        return st ? nullptr : &descs.back();
+    };
+    auto get = [&](const std::string& name) {
+        return shard(velo::find(ix, name), velo::shard_strategy(name.c_str()));
+    };
+    const size_t H = d->n_embd, V = d->n_vocab, F = m->meta.n_ff;
+    const size_t Dq = (size_t)m->meta.n_head * d->head_dim;
+    cudaStream_t s = c->stream;
     const velo_weight_desc* emb = velo::find(ix, "token_embd.weight");
     if (!emb) st = fail(VELO_ERR_INVALID_ARGUMENT, "missing token_embd.weight");
     if (!st) st = velo::upload_f32(m, emb, V, H, &m->emb, s);
     if (!st) st = velo::upload_f32(m, velo::find(ix, "output_norm.weight"), 1, H, &m->out_norm, s);
     if (!st) {
         const velo_weight_desc* out = velo::find(ix, "output.weight");
-        st = velo::upload_q4(m, {out ? out : emb}, H, false, &m->lm_head, s);  // tied fallback
+        const velo_weight_desc* lm = shard(out ? out : emb, VELO_SHARD_COLUMN);  // tied fallback
+        if (!st) st = velo::upload_q4(m, {lm}, H, false, &m->lm_head, s);
     }
     for (uint32_t l = 0; !st && l < d->n_layer; ++l) {
         const std::string p = "layers." + std::to_string(l) + ".";
         velo::Layer ly;
         st = velo::upload_f32(m, velo::find(ix, p + "attention_norm.weight"), 1, H, &ly.attn_norm, s);
         if (!st) st = velo::upload_f32(m, velo::find(ix, p + "ffn_norm.weight"), 1, H, &ly.ffn_norm, s);
-        if (!st)
-            st = velo::upload_q4(m, {velo::find(ix, p + "attention.wq.weight"), velo::find(ix, p + "attention.wk.weight"),
-                                     velo::find(ix, p + "attention.wv.weight")},
-                                 H, false, &ly.wqkv, s);
-        if (!st) st = velo::upload_q4(m, {velo::find(ix, p + "attention.wo.weight")}, Dq, false, &ly.wo, s);
-        if (!st)
-            st = velo::upload_q4(m, {velo::find(ix, p + "feed_forward.w1.weight"), velo::find(ix, p + "feed_forward.w3.weight")},
-                                 H, true, &ly.w13, s);
-        if (!st) st = velo::upload_q4(m, {velo::find(ix, p + "feed_forward.w2.weight")}, F, false, &ly.w2, s);
+        if (!st) {
+            auto* wq = get(p + "attention.wq.weight");
+            auto* wk = get(p + "attention.wk.weight");
+            auto* wv = get(p + "attention.wv.weight");
+            if (!st) st = velo::upload_q4(m, {wq, wk, wv}, H, false, &ly.wqkv, s);
+        }
+        if (!st) {
+            auto* wo = get(p + "attention.wo.weight");
+            if (!st) st = velo::upload_q4(m, {wo}, Dq, false, &ly.wo, s);
+        }
+        if (!st) {
+            auto* w1 = get(p + "feed_forward.w1.weight");
+            auto* w3 = get(p + "feed_forward.w3.weight");
+            if (!st) st = velo::upload_q4(m, {w1, w3}, H, true, &ly.w13, s);
+        }
+        if (!st) {
+            auto* w2 = get(p + "feed_forward.w2.weight");
+            if (!st) st = velo::upload_q4(m, {w2}, F, false, &ly.w2, s);
+        }
         m->layers.push_back(ly);
+        bufs.clear();
+        descs.clear();
     }
     // paged KV pool of the context config
     if (!st) {
@@ -568,19 +644,46 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         a.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
         a.err = c->err_flag;
         VELO_CUDA_TRY(velo::launch_tree_attention(a, m->kv_int8 != 0, s));
-        st = velo::gemm(c, ly.wo, m->attn, M, H, Hq * 128, m->x, H, velo::kEpiAddF32);
+        if (m->tp == 1) {
+            st = velo::gemm(c, ly.wo, m->attn, M, H, Hq * 128, m->x, H, velo::kEpiAddF32);
+        } else {  // row-split o_proj: partial, all-reduce, residual add
+            st = velo::gemm(c, ly.wo, m->attn, M, H, Hq * 128, m->y, H, velo::kEpiStoreF32);
+            if (!st) st = velo::allreduce_add(c, m, M);
+        }
         if (!st) VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, ly.ffn_norm, M, H, eps, m->xn, s));
         if (!st) st = velo::gemm(c, ly.w13, m->xn, M, 2 * F, H, m->hbuf, F, velo::kEpiSwiGLU);
-        if (!st) st = velo::gemm(c, ly.w2, m->hbuf, M, H, F, m->x, H, velo::kEpiAddF32);
+        if (!st) {
+            if (m->tp == 1) {
+                st = velo::gemm(c, ly.w2, m->hbuf, M, H, F, m->x, H, velo::kEpiAddF32);
+            } else {  // row-split down_proj
+                st = velo::gemm(c, ly.w2, m->hbuf, M, H, F, m->y, H, velo::kEpiStoreF32);
+                if (!st) st = velo::allreduce_add(c, m, M);
+            }
+        }
         if (st) return st;
     }
     VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, m->out_norm, M, H, eps, m->xn, s));
-    st = velo::gemm(c, m->lm_head, m->xn, M, V, H, m->logits, V, velo::kEpiStoreF32);
+    const int Vl = m->V_loc;
+    st = velo::gemm(c, m->lm_head, m->xn, M, Vl, H, m->logits, Vl, velo::kEpiStoreF32);
     if (st) return st;
     // acceptance
-    if (!sampling || N == 1) {
+    if (m->tp > 1 && (!sampling || N == 1)) {
+        // vocabulary-sharded greedy: per-shard maxima, gathered, combined
+        const velo::NcclApi* nc = velo::nccl_api();
+        if (!nc) return VELO_ERR_NCCL;
+        VELO_CUDA_TRY(velo::launch_row_argmax_pairs(m->logits, M, Vl, m->v_ofs, m->pairs, s));
+        st = velo::nccl_check(nc->AllGather(m->pairs, m->pairs_all, (size_t)M * 2, ncclInt32,
+                                            static_cast<ncclComm_t>(c->nccl_comm), s),
+                              nc, "ncclAllGather");
+        if (st) return st;
+        VELO_CUDA_TRY(velo::launch_argmax_combine(m->pairs_all, m->tp, M, m->expected, s));
+        VELO_CUDA_TRY(velo::launch_tree_walk(m->tokens, m->parents, m->expected, B, N, m->path,
+                                             m->path_len, m->bonus, s));
+    } else if (!sampling || N == 1) {
         VELO_CUDA_TRY(velo::launch_tree_greedy(m->logits, m->tokens, m->parents, B, N, V, m->expected,
                                                m->path, m->path_len, m->bonus, s));
+    } else if (m->tp > 1) {
+        return fail(VELO_ERR_INVALID_ARGUMENT, "sampling acceptance with tp_size > 1 is not supported");
     } else {
         const int k = N - 1;
         const size_t need = (size_t)B * k * V;
@@ -642,10 +745,35 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     VELO_CUDA_TRY(cudaMemcpyAsync(out->bonus_token, m->bonus, (size_t)B * 4, cudaMemcpyDeviceToHost, s));
     if (out->accepted_nodes)
         VELO_CUDA_TRY(cudaMemcpyAsync(out->accepted_nodes, m->path, (size_t)M * 4, cudaMemcpyDeviceToHost, s));
-    if (out->logits)
+    std::vector<float> gathered;
+    if (out->logits && m->tp == 1)
         VELO_CUDA_TRY(cudaMemcpyAsync(out->logits, m->logits, (size_t)M * V * 4, cudaMemcpyDeviceToHost, s));
+    if (out->logits && m->tp > 1) {
+        const size_t per = (size_t)M * Vl;
+        if (per * m->tp > m->logits_all_cap) {
+            VELO_CUDA_TRY(cudaStreamSynchronize(s));
+            if (m->logits_all) cudaFree(m->logits_all);
+            m->logits_all = nullptr;
+            m->logits_all_cap = 0;
+            VELO_CUDA_TRY(cudaMalloc(&m->logits_all, per * m->tp * 4));
+            m->logits_all_cap = per * m->tp;
+        }
+        const velo::NcclApi* nc = velo::nccl_api();
+        if (!nc) return VELO_ERR_NCCL;
+        st = velo::nccl_check(nc->AllGather(m->logits, m->logits_all, per, ncclFloat32,
+                                            static_cast<ncclComm_t>(c->nccl_comm), s),
+                              nc, "ncclAllGather");
+        if (st) return st;
+        gathered.resize(per * m->tp);
+        VELO_CUDA_TRY(cudaMemcpyAsync(gathered.data(), m->logits_all, per * m->tp * 4, cudaMemcpyDeviceToHost, s));
+    }
     st = velo_cuda_sync(c, -1);
     if (st) return st;
+    if (!gathered.empty())  // [tp][M][Vl] -> [M][V]
+        for (int r = 0; r < m->tp; ++r)
+            for (int i = 0; i < M; ++i)
+                std::memcpy(out->logits + (size_t)i * V + (size_t)r * Vl,
+                            gathered.data() + ((size_t)r * M + i) * Vl, (size_t)Vl * 4);
     for (int b = 0; b < B; ++b) out->accepted_len[b] = plen[b] - 1;
     return VELO_OK;
 }

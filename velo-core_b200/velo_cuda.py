@@ -75,6 +75,11 @@ _SIGS = {
     "velo_cuda_write_kv": (_I32, [_P, ctypes.c_uint32, _I32, _I32, _I32, _P, _P]),
     "velo_cuda_read_kv": (_I32, [_P, ctypes.c_uint32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "velo_cuda_verify_step": (_I32, [_P, _P, _P]),
+    "velo_cuda_nccl_unique_id": (_I32, [_P]),
+    "velo_cuda_shard_strategy": (_I32, [ctypes.c_char_p]),
+    "velo_cuda_shard_weight": (_I32, [_P, _I32, _I32, _I32, _P, ctypes.c_size_t,
+                                      ctypes.POINTER(ctypes.c_uint64),
+                                      ctypes.POINTER(ctypes.c_uint64)]),
 }
 
 DT_F32, DT_F16, DT_Q4_0 = 0, 1, 2
@@ -285,6 +290,30 @@ class Context:
         rs = VerifyResult(_ptr(acc), _ptr(nodes), _ptr(bonus), _ptr(logits))
         check(lib().velo_cuda_verify_step(self._h, ctypes.byref(bt), ctypes.byref(rs)))
         return {"accepted_len": acc, "accepted_nodes": nodes, "bonus": bonus, "logits": logits}
+
+
+def nccl_unique_id():
+    """128-byte NCCL unique id for a tensor-parallel group (rank 0 makes it)."""
+    buf = (ctypes.c_char * 128)()
+    check(lib().velo_cuda_nccl_unique_id(buf))
+    return bytes(buf)
+
+
+def shard_strategy(name):
+    return int(lib().velo_cuda_shard_strategy(name.encode()))
+
+
+def shard_weight(name, dtype, data, rows, cols, strategy, tp, rank):
+    """velo_cuda_shard_weight on a host tensor: returns (bytes, rows, cols)."""
+    a = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
+    w = WeightDesc(name.encode(), dtype, a.ctypes.data, rows, cols)
+    out = np.zeros(a.size, np.uint8)
+    r, c = ctypes.c_uint64(), ctypes.c_uint64()
+    check(lib().velo_cuda_shard_weight(ctypes.byref(w), strategy, tp, rank, _ptr(out), out.size,
+                                       ctypes.byref(r), ctypes.byref(c)))
+    rb = cols * 4 if dtype == DT_F32 else cols * 2 if dtype == DT_F16 else cols // 32 * 18
+    n = r.value * (rb if strategy != 2 else rb // tp)
+    return out[:n], r.value, c.value
 
 
 def q4_0_repacked_bytes(N, K):
