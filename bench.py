@@ -576,10 +576,21 @@ def run_verify(args):
     """The whole verify step at BASELINE config 3: Llama-2-7B shape in q4_0,
     B=32 sequences of context 2048 in 16-token fp16 pages, a 16-node draft
     tree each: target forward over 512 rows, greedy tree acceptance and the KV
-    commit of the accepted paths, through velo_cuda_verify_step."""
+    commit of the accepted paths, through velo_cuda_verify_step.  Under
+    torchrun the ranks form one tensor-parallel group (NCCL all-reduce after
+    o_proj / down_proj, vocabulary-sharded LM head): strong scaling."""
     import torch
+    import torch.distributed as dist
     import velo_cuda
-    torch.cuda.set_device(0)
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    nid = None
+    if ws > 1:
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+        box = [velo_cuda.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        nid = box[0]
     meta = dict(C3_META)
     B, ctx_len = 32, 2048
     N = len(C3_TREE)
@@ -587,8 +598,8 @@ def run_verify(args):
     t0 = time.time()
     tensors = c3_model_tensors(meta)
     gen_s = time.time() - t0
-    ctx = velo_cuda.Context(device=0, total_pages=B * per_seq, max_slots=B,
-                            max_pages_per_slot=per_seq)
+    ctx = velo_cuda.Context(device=local, total_pages=B * per_seq, max_slots=B,
+                            max_pages_per_slot=per_seq, tp_rank=rank, tp_size=ws, nccl_id=nid)
     t0 = time.time()
     ctx.load_model(meta, tensors)
     load_s = time.time() - t0
@@ -607,7 +618,9 @@ def run_verify(args):
     steps = max(3, min(args.steps, 30))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     acc_tok = 0
-    with ClockSampler(0) as clk:
+    if ws > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
         w0 = time.perf_counter()
         e0.record(stream)
         for _ in range(steps):
@@ -617,7 +630,10 @@ def run_verify(args):
         torch.cuda.synchronize()
         wall = time.perf_counter() - w0
     ms = e0.elapsed_time(e1) / steps
-    params = 0
+    if ws > 1:
+        t = torch.tensor([ms, wall], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, wall = float(t[0]), float(t[1])
     H, F, V = meta["n_embd"], meta["n_ff"], meta["n_vocab"]
     Dq, Dk = meta["n_head"] * 128, meta["n_head_kv"] * 128
     params = meta["n_layer"] * (H * (Dq + 2 * Dk) + Dq * H + 3 * H * F) + V * H
@@ -633,10 +649,12 @@ def run_verify(args):
         pass
     tfl = float(peaks.get("bf16_tflops_sustained", 1416.2))
     hbm = float(peaks.get("hbm_gbs", HBM_FALLBACK_GBS))
-    floor_ms = flops / (tfl * 1e12) * 1e3 + kv_bytes / (hbm * 1e9) * 1e3
+    floor_ms = (flops / (tfl * 1e12) + kv_bytes / (hbm * 1e9)) * 1e3 / ws
     line = {"workload": "verify step, BASELINE config 3 (Llama-2-7B shape q4_0, B=32, "
                         "16-node tree, ctx 2048 fp16 pages)",
-            "us_per_step": ms * 1e3, "accepted_tokens_per_s": acc_tok / steps / (ms / 1e3),
+            "n_gpus": ws, "parallelism": f"tp{ws}" if ws > 1 else "single GPU",
+            "scaling": "strong", "us_per_step": ms * 1e3,
+            "accepted_tokens_per_s": acc_tok / steps / (ms / 1e3),
             "e2e_ms_per_step": wall / steps * 1e3, "rows": M, "gemm_tflop": flops / 1e12,
             "kv_gb": kv_bytes / 1e9, "weight_gb": w_bytes / 1e9,
             "floor_ms_at_measured_peaks": floor_ms, "frac_of_floor": floor_ms / ms,
@@ -645,7 +663,11 @@ def run_verify(args):
             "data": "random-init N(0,0.02^2) weights quantised to q4_0 on the device; "
                     "KV pages zero-filled (timing does not depend on their values)"}
     ctx.close()
-    print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     return 0
 
 
