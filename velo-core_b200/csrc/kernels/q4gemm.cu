@@ -465,6 +465,23 @@ cudaError_t make_tmap_f16_2d(CUtensorMap* map, const void* base, uint64_t rows, 
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+cudaError_t make_tmap_f16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                             uint32_t box2) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    if (((uintptr_t)base & 15) || (stride1_bytes & 15) || (stride2_bytes & 15))
+        return cudaErrorMisalignedAddress;
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+    const cuuint32_t box[3] = {64, 1, box2};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 cudaError_t launch_q4_repack(const uint8_t* src_a, const uint8_t* src_b, bool pair, int N, int K,
                              uint8_t* dst, cudaStream_t stream) {
     const int n_rows = q4_n_tiles(N) * kQ4TileN;

@@ -64,4 +64,10 @@ cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
 cudaError_t make_tmap_f16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
                              uint64_t row_stride_bytes, uint32_t box_rows);
 
+// 3-D f16 tensor [d2][d1][d0] (d0 contiguous) with a box of 64 x 1 x box2
+// elements and 128-byte swizzle (one 128-byte row per (d1, d2) index).
+cudaError_t make_tmap_f16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                             uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                             uint32_t box2);
+
 }  // namespace velo

@@ -20,9 +20,9 @@
 //   warps 4-11 softmax, two threads per query row (32 keys each): S from
 //              TMEM, exp2 on the SFU, P (f16) to shared memory for the PV MMA;
 //              O rescaled in TMEM only when the running max grows by > 2^8
-//   warps 12-15 the tree tile (node K/V) into its own buffer at the start,
-//              then (int8 pools) int8 -> f16 conversion of the K/V tiles into
-//              the swizzled operand layout
+//   warps 12-15 (int8 pools) int8 -> f16 conversion of every K/V tile into
+//              the swizzled operand layout, and the tree tile from the node K/V
+//              (f16 pools: the producer loads the tree tile with a 3-D TMA)
 #include <cuda_fp16.h>
 
 #include <mutex>
@@ -52,10 +52,10 @@ constexpr int kErrPage = 0x5101, kErrWait = 0x5102;
 
 template <bool INT8>
 struct AttnCfg {
-    static constexpr int KS = INT8 ? 2 : 4;    // f16 operand ring (cached tokens)
+    static constexpr int KS = INT8 ? 3 : 5;    // f16 operand ring (cached tokens + tree tile)
     static constexpr int RS = INT8 ? 3 : 0;    // raw int8 ring
-    // Q, the ring, the tree tile (its own buffer), P x 2, raw ring, scales
-    static constexpr size_t kSmem = (size_t)Q_BYTES + (size_t)(KS + 1) * KV_STAGE + 2 * P_BYTES +
+    // Q, the ring, P x 2, raw ring, scales, alignment, barriers, row exchange
+    static constexpr size_t kSmem = (size_t)Q_BYTES + (size_t)KS * KV_STAGE + 2 * P_BYTES +
                                     (size_t)RS * RAW_STAGE + (INT8 ? (size_t)KS * 2 * TK * 4 : 0) +
                                     1024 + 512 + 2 * BMQ * 4;
     static_assert(kSmem <= 227 * 1024, "shared memory budget");
@@ -107,6 +107,7 @@ __global__ void tree_ancestors_kernel(const int32_t* __restrict__ parents, int B
 template <bool INT8>
 __global__ void __launch_bounds__(kThreads, 1)
     tree_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                     const __grid_constant__ CUtensorMap tnk, const __grid_constant__ CUtensorMap tnv,
                      const TreeAttnArgs a) {
     using C = AttnCfg<INT8>;
     constexpr int KS = C::KS, RS = C::RS;
@@ -114,8 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sq = base;                                // Q: 2 halves x 16 KiB
     uint8_t* skv = sq + Q_BYTES;                       // KS x (K0 K1 V0 V1) 8 KiB each
-    uint8_t* stree = skv + KS * KV_STAGE;              // tree tile (K0 K1 V0 V1)
-    uint8_t* sp = stree + KV_STAGE;                    // P: 2 x 16 KiB
+    uint8_t* sp = skv + KS * KV_STAGE;                 // P: 2 x 16 KiB
     uint8_t* sraw = sp + 2 * P_BYTES;                  // RS x raw int8 stage
     float* sscale = reinterpret_cast<float*>(sraw + RS * RAW_STAGE);  // KS x (ks[64], vs[64])
     uint64_t* bars = reinterpret_cast<uint64_t*>(sscale + (INT8 ? KS * 2 * TK : 0));
@@ -128,8 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* p_full = s_free + 2;                     // 2
     uint64_t* pv_done = p_full + 2;                    // 1: phase j <-> PV_j done
     uint64_t* o_full = pv_done + 1;                    // 1: the last PV done
-    uint64_t* tree_full = o_full + 1;                  // 1: tree tile written
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tree_full + 1);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     float* sxch = reinterpret_cast<float*>(tmem_slot + 4);  // [2][128] row exchange
 
@@ -160,7 +159,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(pv_done, 1);
         mbar_init(o_full, 1);
-        mbar_init(tree_full, 128);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -191,11 +189,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             const uint32_t* pt = a.page_table + (size_t)b * a.max_pages;
-            for (int j = 0; j < T_pre; ++j) {
+            for (int j = 0; j < (INT8 ? T_pre : T); ++j) {
                 if constexpr (!INT8) {
                     const int s = j % KS;
                     if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag, 64))
                         goto done;
+                    if (j == T_pre) {
+                        // tree tile: node K/V rows b*N .. b*N+63 of KV head h (3-D
+                        // maps [B*N][Hkv][128]); rows past this sequence's nodes are
+                        // masked, rows past the tensor read as zero
+                        mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
+                        uint8_t* st = skv + s * KV_STAGE;
+                        for (int dh = 0; dh < 2; ++dh) {
+                            tma_load_3d(st + dh * KV_HALF, &tnk, &kv_full[s], dh * 64, h, b * a.N);
+                            tma_load_3d(st + 2 * KV_HALF + dh * KV_HALF, &tnv, &kv_full[s], dh * 64, h, b * a.N);
+                        }
+                        continue;
+                    }
                     mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
                     uint8_t* st = skv + s * KV_STAGE;
                     for (int i = 0; i < TK / kKvPage; ++i) {
@@ -246,13 +256,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j <= T; ++j) {
                 if (j < T) {
                     const int s = j % KS, sb = j & 1;
-                    const bool tree = j == T_pre;
-                    if (!(tree ? mbar_wait(tree_full, 0, a.err, kErrWait, abort_flag)
-                               : mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag)) ||
+                    if (!mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag) ||
                         !mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, a.err, kErrWait, abort_flag))
                         goto done;
                     tc_fence_after();
-                    const uint32_t k_addr = smem_u32(tree ? stree : skv + s * KV_STAGE);
+                    const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
 #pragma unroll
                     for (int k = 0; k < D / 16; ++k) {
                         const uint64_t ad = desc_kmajor_sw128(q_addr + (k >> 2) * (Q_BYTES / 2)) + (k & 3) * 2;
@@ -266,15 +274,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait(&p_full[pb], (jj >> 1) & 1, a.err, kErrWait, abort_flag)) goto done;
                     tc_fence_after();
                     const uint32_t p_addr = smem_u32(sp + pb * P_BYTES);
-                    const bool tree = jj == T_pre;
-                    const uint32_t v_addr = smem_u32((tree ? stree : skv + sv * KV_STAGE) + 2 * KV_HALF);
+                    const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
 #pragma unroll
                     for (int kk = 0; kk < TK / 16; ++kk) {
                         const uint64_t ad = desc_kmajor_sw128(p_addr) + kk * 2;
                         const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
                         mma_f16_ss(tmem_o, ad, bd, id_pv, (jj | kk) != 0);
                     }
-                    if (!tree) mma_commit(&kv_empty[sv]);
+                    mma_commit(&kv_empty[sv]);
                     mma_commit(pv_done);
                     if (jj == T - 1) mma_commit(o_full);
                 }
@@ -297,6 +304,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float* xoth = sxch + (ch ^ 1) * BMQ; // the partner's
         const int kbase = ch * 32;
         float m = -INFINITY, l = 0.0f;             // l: this half's partial sum
+        if (!__any_sync(0xffffffffu, row_ok)) {
+            // no query row of this warp exists (few nodes x heads, e.g. 16 rows
+            // of 128): its P rows stay zero and it only keeps the barrier
+            // counts, leaving the SFU and issue slots to the warps with rows
+#pragma unroll
+            for (int pb = 0; pb < 2; ++pb)
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    *reinterpret_cast<uint4*>(sp + pb * P_BYTES + sw128(r, ch * 4 + c)) = make_uint4(0, 0, 0, 0);
+            fence_async_smem();
+            for (int j = 0; j < T; ++j) {
+                const int sb = j & 1;
+                const bool got = mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag, 32);
+                if (!__all_sync(0xffffffffu, got)) goto done;
+                mbar_arrive(&s_free[sb]);
+                mbar_arrive(&p_full[sb]);
+            }
+            goto done;
+        }
         for (int j = 0; j < T; ++j) {
             const int sb = j & 1, s = j % KS;
             const bool got = mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag);
@@ -311,21 +337,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* ks = sscale + s * 2 * TK + kbase;
             if constexpr (INT8) {
                 // scales of this stage were written by the converter warps
-                if (!tree) {
-                    const bool ok = mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag);
-                    if (!__all_sync(0xffffffffu, ok)) goto done;
-                }
+                const bool ok = mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+            }
+            // this thread's 32 keys as a bit mask: the node's ancestors in the
+            // tree tile, the cached tokens below ctx_len otherwise
+            uint32_t kmask;
+            if (tree) {
+                kmask = (uint32_t)(anc >> kbase);
+            } else {
+                const int nvalid = L - (j * TK + kbase);
+                kmask = nvalid >= 32 ? 0xffffffffu : nvalid <= 0 ? 0u : (1u << nvalid) - 1u;
             }
             // scaled scores (log2 domain) overwrite the raw ones in place
             float* x = reinterpret_cast<float*>(x32);
             float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int t = 0; t < 32; ++t) {
-                const int key = kbase + t;
-                const bool ok = tree ? ((anc >> key) & 1ull) != 0 : (j * TK + key < L);
                 float v = x[t] * a.scale_log2;
-                if constexpr (INT8) v = tree ? v : v * ks[t];
-                v = ok ? v : -INFINITY;
+                if constexpr (INT8) v *= ks[t];
+                v = ((kmask >> t) & 1u) ? v : -INFINITY;
                 x[t] = v;
                 pm[t & 3] = fmaxf(pm[t & 3], v);
             }
@@ -376,10 +407,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float p1 = ex2_approx(x[t + 1] - ms);
                     ls[e] += p0 + p1;
                     if constexpr (INT8) {
-                        if (!tree) {
-                            p0 *= vs[t];
-                            p1 *= vs[t + 1];
-                        }
+                        p0 *= vs[t];
+                        p1 *= vs[t + 1];
                     }
                     __half2 hp = __floats2half2_rn(p0, p1);
                     w[e] = *reinterpret_cast<uint32_t*>(&hp);
@@ -437,54 +466,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 12) {
         // ------------------------------------------------------------ converters
-        const int t = threadIdx.x - 384;  // 0..127
-        const int kr = t >> 1, hh = t & 1;  // key row, 64-dim half
-        {
-            // tree tile into its own buffer: node K/V rows (f16), zero past
-            // the last node (masked keys still meet the tensor cores)
-            const bool ok = kr < a.N;
-            const size_t src = (((size_t)b * a.N + (ok ? kr : 0)) * a.Hkv + h) * D + hh * 64;
-#pragma unroll
-            for (int kvs = 0; kvs < 2; ++kvs) {
-                const uint4* g = reinterpret_cast<const uint4*>((kvs ? a.node_v : a.node_k) + src);
-                uint4 v[8];
-#pragma unroll
-                for (int c = 0; c < 8; ++c) v[c] = ok ? g[c] : make_uint4(0, 0, 0, 0);
-#pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    *reinterpret_cast<uint4*>(stree + kvs * 2 * KV_HALF + hh * KV_HALF + sw128(kr, c)) = v[c];
-            }
-            fence_async_smem();
-            mbar_arrive(tree_full);
-        }
+        // int8 pools only: every tile of the ring (the cached tokens converted
+        // from the raw stage, the tree tile from the node K/V rows)
         if constexpr (INT8) {
-            for (int j = 0; j < T_pre; ++j) {
-                const int s = j % KS, r = j % RS;
-                if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag) ||
-                    !mbar_wait(&raw_full[r], (j / RS) & 1, a.err, kErrWait, abort_flag))
-                    goto done;
+            const int t = threadIdx.x - 384;    // 0..127
+            const int kr = t >> 1, hh = t & 1;  // key row, 64-dim half
+            for (int j = 0; j < T; ++j) {
+                const int s = j % KS;
+                if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag)) goto done;
                 uint8_t* st = skv + s * KV_STAGE;
                 float* ssc = sscale + s * 2 * TK;
-                const uint8_t* rs = sraw + r * RAW_STAGE;
+                if (j == T_pre) {
+                    // node K/V rows (f16), zero past the last node
+                    const bool ok = kr < a.N;
+                    const size_t src = (((size_t)b * a.N + (ok ? kr : 0)) * a.Hkv + h) * D + hh * 64;
 #pragma unroll
-                for (int kvs = 0; kvs < 2; ++kvs) {
-                    const uint4* src = reinterpret_cast<const uint4*>(rs + kvs * RAW_KV + kr * D + hh * 64);
-                    uint8_t* dst = st + kvs * 2 * KV_HALF + hh * KV_HALF;
+                    for (int kvs = 0; kvs < 2; ++kvs) {
+                        const uint4* g = reinterpret_cast<const uint4*>((kvs ? a.node_v : a.node_k) + src);
+                        uint4 v[8];
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        const uint4 raw = src[c4];  // 16 int8 -> two 16-byte f16 chunks
-                        uint32_t o[8];
-                        i8x4_to_f16(raw.x, o[0], o[1]);
-                        i8x4_to_f16(raw.y, o[2], o[3]);
-                        i8x4_to_f16(raw.z, o[4], o[5]);
-                        i8x4_to_f16(raw.w, o[6], o[7]);
-                        *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4)) = make_uint4(o[0], o[1], o[2], o[3]);
-                        *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                        for (int c = 0; c < 8; ++c) v[c] = ok ? g[c] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                        for (int c = 0; c < 8; ++c)
+                            *reinterpret_cast<uint4*>(st + kvs * 2 * KV_HALF + hh * KV_HALF + sw128(kr, c)) = v[c];
                     }
+                    ssc[t] = 1.0f;  // node K/V are not scaled
+                } else {
+                    const int r = j % RS;
+                    if (!mbar_wait(&raw_full[r], (j / RS) & 1, a.err, kErrWait, abort_flag)) goto done;
+                    const uint8_t* rs = sraw + r * RAW_STAGE;
+#pragma unroll
+                    for (int kvs = 0; kvs < 2; ++kvs) {
+                        const uint4* src = reinterpret_cast<const uint4*>(rs + kvs * RAW_KV + kr * D + hh * 64);
+                        uint8_t* dst = st + kvs * 2 * KV_HALF + hh * KV_HALF;
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            const uint4 raw = src[c4];  // 16 int8 -> two 16-byte f16 chunks
+                            uint32_t o[8];
+                            i8x4_to_f16(raw.x, o[0], o[1]);
+                            i8x4_to_f16(raw.y, o[2], o[3]);
+                            i8x4_to_f16(raw.z, o[4], o[5]);
+                            i8x4_to_f16(raw.w, o[6], o[7]);
+                            *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                            *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                        }
+                    }
+                    const __half* sc = reinterpret_cast<const __half*>(rs + 2 * RAW_KV);
+                    ssc[t] = __half2float(sc[t]);  // t < 64: K scales, t >= 64: V scales
+                    mbar_arrive(&raw_empty[r]);    // after every read of the raw stage
                 }
-                const __half* sc = reinterpret_cast<const __half*>(rs + 2 * RAW_KV);
-                ssc[t] = __half2float(sc[t]);  // t < 64: K scales, t >= 64: V scales
-                mbar_arrive(&raw_empty[r]);    // after every read of the raw stage
                 fence_async_smem();
                 mbar_arrive(&kv_full[s]);
             }
@@ -509,17 +539,22 @@ cudaError_t launch_impl(const TreeAttnArgs& a, cudaStream_t stream) {
                                         (int)AttnCfg<INT8>::kSmem);
     });
     if (attr_err != cudaSuccess) return attr_err;
-    CUtensorMap tk{}, tv{};
+    CUtensorMap tk{}, tv{}, tnk{}, tnv{};
     if (!INT8) {
         const uint64_t rows = (uint64_t)a.pool_pages * a.Hkv * kKvPage;
         cudaError_t e = make_tmap_f16_2d(&tk, a.k_pool, rows, D, D * 2, kKvPage);
         if (e == cudaSuccess) e = make_tmap_f16_2d(&tv, a.v_pool, rows, D, D * 2, kKvPage);
+        const uint64_t nodes = (uint64_t)a.B * a.N;
+        if (e == cudaSuccess)
+            e = make_tmap_f16_3d(&tnk, a.node_k, D, a.Hkv, nodes, D * 2, (uint64_t)a.Hkv * D * 2, TK);
+        if (e == cudaSuccess)
+            e = make_tmap_f16_3d(&tnv, a.node_v, D, a.Hkv, nodes, D * 2, (uint64_t)a.Hkv * D * 2, TK);
         if (e != cudaSuccess) return e;
     }
     const int G = a.Hq / a.Hkv;
     const int MT = (a.N * G + BMQ - 1) / BMQ;
     const long grid = (long)a.B * a.Hkv * MT;
-    tree_attn_kernel<INT8><<<(unsigned)grid, kThreads, AttnCfg<INT8>::kSmem, stream>>>(tk, tv, a);
+    tree_attn_kernel<INT8><<<(unsigned)grid, kThreads, AttnCfg<INT8>::kSmem, stream>>>(tk, tv, tnk, tnv, a);
     return cudaGetLastError();
 }
 
