@@ -61,6 +61,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity,
     return ok != 0;
 }
 
+// Non-blocking test of the phase with `parity`.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits until the phase with `parity` of `bar` has completed.  Returns false
 // (after recording `code` in *err) if that takes longer than kWaitLimitNs or
 // another role of the CTA already gave up (*abort != 0).  `sleep_ns` > 0 backs
@@ -69,6 +82,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity,
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
                                           volatile int* abort, uint32_t sleep_ns = 0) {
     const uint32_t b = smem_u32(bar);
+#ifdef VELO_SPIN_TEST_WAIT
+    for (int i = 0; i < VELO_SPIN_TEST_WAIT; ++i)
+        if (mbar_test_wait(b, parity)) return true;
+#endif
     if (mbar_try_wait(b, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {

@@ -189,7 +189,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ producer
         if (lane == 0) {
             const uint32_t* pt = a.page_table + (size_t)b * a.max_pages;
+            // page ids of the next tile are read one iteration early, so the
+            // global-memory latency hides behind the wait for a free slot
+            uint32_t pg_next[TK / kKvPage];
+            auto fetch = [&](int j, uint32_t (&dst)[TK / kKvPage]) {
+#pragma unroll
+                for (int i = 0; i < TK / kKvPage; ++i) {
+                    const int pi = j * (TK / kKvPage) + i;
+                    dst[i] = (j < T_pre && pi < a.max_pages) ? pt[pi] : 0u;
+                }
+            };
+            fetch(0, pg_next);
             for (int j = 0; j < (INT8 ? T_pre : T); ++j) {
+                uint32_t pg_cur[TK / kKvPage];
+#pragma unroll
+                for (int i = 0; i < TK / kKvPage; ++i) pg_cur[i] = pg_next[i];
+                fetch(j + 1, pg_next);
                 if constexpr (!INT8) {
                     const int s = j % KS;
                     if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag, 64))
@@ -209,8 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
                     uint8_t* st = skv + s * KV_STAGE;
                     for (int i = 0; i < TK / kKvPage; ++i) {
-                        const int pi = j * (TK / kKvPage) + i;
-                        uint32_t pg = pi < a.max_pages ? pt[pi] : 0u;
+                        uint32_t pg = pg_cur[i];
                         if (pg >= (uint32_t)a.pool_pages) {
                             atomicCAS(a.err, 0, kErrPage);
                             pg = 0;
@@ -229,8 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(&raw_full[r], RAW_STAGE);
                     uint8_t* st = sraw + r * RAW_STAGE;
                     for (int i = 0; i < TK / kKvPage; ++i) {
-                        const int pi = j * (TK / kKvPage) + i;
-                        uint32_t pg = pi < a.max_pages ? pt[pi] : 0u;
+                        uint32_t pg = pg_cur[i];
                         if (pg >= (uint32_t)a.pool_pages) {
                             atomicCAS(a.err, 0, kErrPage);
                             pg = 0;
@@ -253,37 +266,59 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t id_s = idesc_f16_f32(BMQ, TK);
             const uint32_t id_pv = idesc_f16_f32(BMQ, D, /*b_mn_major=*/true);
             const uint32_t q_addr = smem_u32(sq);
-            for (int j = 0; j <= T; ++j) {
-                if (j < T) {
-                    const int s = j % KS, sb = j & 1;
-                    if (!mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag) ||
-                        !mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, a.err, kErrWait, abort_flag))
-                        goto done;
-                    tc_fence_after();
-                    const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
+            // Issue S_j and PV_j in whichever order their inputs arrive: S_j
+            // needs its K tile and a free S buffer, PV_j the softmax's P_j.
+            // S_j also waits until PV_{j-2} is issued, so that when S_j
+            // completes every PV before j-1 has completed (the softmax relies
+            // on that to wait for PV_{j-1} by parity alone).
+            int ns = 0, npv = 0;
+            const uint64_t t0 = global_ns();
+            uint32_t spins = 0;
+            while (npv < T) {
+                bool progressed = false;
+                if (ns < T && npv >= ns - 1) {
+                    const int s = ns % KS, sb = ns & 1;
+                    if (mbar_test_wait(smem_u32(&kv_full[s]), (ns / KS) & 1) &&
+                        mbar_test_wait(smem_u32(&s_free[sb]), ((ns >> 1) & 1) ^ 1)) {
+                        tc_fence_after();
+                        const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
 #pragma unroll
-                    for (int k = 0; k < D / 16; ++k) {
-                        const uint64_t ad = desc_kmajor_sw128(q_addr + (k >> 2) * (Q_BYTES / 2)) + (k & 3) * 2;
-                        const uint64_t bd = desc_kmajor_sw128(k_addr + (k >> 2) * KV_HALF) + (k & 3) * 2;
-                        mma_f16_ss(tmem + sb * TK, ad, bd, id_s, k > 0);
+                        for (int k = 0; k < D / 16; ++k) {
+                            const uint64_t ad = desc_kmajor_sw128(q_addr + (k >> 2) * (Q_BYTES / 2)) + (k & 3) * 2;
+                            const uint64_t bd = desc_kmajor_sw128(k_addr + (k >> 2) * KV_HALF) + (k & 3) * 2;
+                            mma_f16_ss(tmem + sb * TK, ad, bd, id_s, k > 0);
+                        }
+                        mma_commit(&s_full[sb]);
+                        ++ns;
+                        progressed = true;
                     }
-                    mma_commit(&s_full[sb]);
                 }
-                if (j >= 1) {
-                    const int jj = j - 1, pb = jj & 1, sv = jj % KS;
-                    if (!mbar_wait(&p_full[pb], (jj >> 1) & 1, a.err, kErrWait, abort_flag)) goto done;
-                    tc_fence_after();
-                    const uint32_t p_addr = smem_u32(sp + pb * P_BYTES);
-                    const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
+                if (npv < ns) {
+                    const int jj = npv, pb = jj & 1, sv = jj % KS;
+                    if (mbar_test_wait(smem_u32(&p_full[pb]), (jj >> 1) & 1)) {
+                        tc_fence_after();
+                        const uint32_t p_addr = smem_u32(sp + pb * P_BYTES);
+                        const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
 #pragma unroll
-                    for (int kk = 0; kk < TK / 16; ++kk) {
-                        const uint64_t ad = desc_kmajor_sw128(p_addr) + kk * 2;
-                        const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
-                        mma_f16_ss(tmem_o, ad, bd, id_pv, (jj | kk) != 0);
+                        for (int kk = 0; kk < TK / 16; ++kk) {
+                            const uint64_t ad = desc_kmajor_sw128(p_addr) + kk * 2;
+                            const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
+                            mma_f16_ss(tmem_o, ad, bd, id_pv, (jj | kk) != 0);
+                        }
+                        mma_commit(&kv_empty[sv]);
+                        mma_commit(pv_done);
+                        if (jj == T - 1) mma_commit(o_full);
+                        ++npv;
+                        progressed = true;
                     }
-                    mma_commit(&kv_empty[sv]);
-                    mma_commit(pv_done);
-                    if (jj == T - 1) mma_commit(o_full);
+                }
+                if (!progressed && (++spins & 255u) == 0) {
+                    if (*abort_flag) goto done;
+                    if (global_ns() - t0 > kWaitLimitNs * 8) {  // a whole item, not one wait
+                        atomicCAS(a.err, 0, kErrWait);
+                        *abort_flag = 1;
+                        goto done;
+                    }
                 }
             }
         }
