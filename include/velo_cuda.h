@@ -310,7 +310,10 @@ typedef struct velo_verify_batch {
     float temperature;        /* 0: greedy tree walk; > 0: rejection sampling (chains) */
     const float *draft_logits;/* [B][n_nodes-1][V] host, sampling only */
     const float *uniforms;    /* [B][n_nodes] host, sampling only */
-    int32_t commit;           /* 1: write the accepted path's K/V into the pages */
+    int32_t commit;           /* 0: no KV write; 1: the accepted path's K/V; 2 (greedy
+                                 chains): every node's K/V, accepted_len = n_nodes - 1
+                                 and bonus = argmax after the last node (prefill in
+                                 chunks of <= 64 tokens, or one draft decode step) */
 } velo_verify_batch;
 
 typedef struct velo_verify_result {

@@ -185,3 +185,40 @@ def test_write_kv_matches_oracle_commit_bit_exact(int8):
                     assert np.array_equal(got[2 + which][i], scale[pg, :, sl])
     finally:
         ctx.close()
+
+
+def test_prefill_and_decode_through_the_step_match_oracle():
+    """Prefill by chained steps that commit every node (chunks of 64) and greedy
+    decoding one token per step (the draft model's loop) reproduce the oracle's
+    forward_sequence / forward_one: same next tokens, cache within f16 rounding."""
+    shape = dict(n_vocab=512, n_embd=256, n_layer=2, n_head=2, n_head_kv=1, n_ff=512)
+    meta, tensors = synthetic.llama_q4_model(**shape, seed=31)
+    g = synthetic.rng(32, 90)
+    P = 150
+    prompt = g.integers(0, meta["n_vocab"], P).astype(np.uint32)
+    ora = vo.Model(dict(meta, n_ctx=512), synthetic.oracle_tensor_list(meta, tensors))
+    lg = ora.forward_sequence(prompt)
+    ctx = velo_cuda.Context(device=0, total_pages=32, max_slots=1, max_pages_per_slot=16)
+    try:
+        ctx.load_model(meta, tensors)
+        ctx.bind_slot(0, np.arange(16)[::-1].copy())
+        nxt = velo_cuda.prefill(ctx, 0, prompt, n_vocab=meta["n_vocab"])
+        k, _ = ctx.read_kv(0, 1, 0, P, 1)
+        assert np.abs(k.astype(np.float32) - ora.read_kv(0, 1, P).reshape(P, 1, 128)).max() <= 2e-2
+        # greedy decode 8 tokens: GPU step on its own last token vs oracle forward_one
+        ref_tok = vo.greedy(lg)[0]
+        pos = P
+        agree = 0
+        for _ in range(8):
+            r = ctx.verify_step([0], [pos], np.array([[nxt]], np.uint32), np.array([[-1]], np.int32),
+                                commit="all", want_logits=True, n_vocab=meta["n_vocab"])
+            ref = ora.forward_one(int(nxt), pos)
+            assert np.abs(r["logits"][0, 0] - ref).max() <= 2e-2
+            agree += int(nxt == ref_tok)
+            ref_tok = vo.greedy(ref)[0]
+            nxt = int(r["bonus"][0])
+            assert nxt == vo.greedy(r["logits"][0, 0])[0]
+            pos += 1
+        assert agree >= 1
+    finally:
+        ctx.close()

@@ -570,6 +570,8 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     const bool sampling = in->temperature > 0.0f;
     if (!(in->temperature >= 0.0f) || std::isinf(in->temperature))
         return fail(VELO_ERR_INVALID_ARGUMENT, "temperature must be finite and >= 0");
+    if (in->commit < 0 || in->commit > 2 || (in->commit == 2 && sampling))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "commit mode %d (0, 1 or 2; 2 is greedy only)", in->commit);
     const int V = m->V();
     for (int b = 0; b < B; ++b) {
         if (in->slots[b] >= (uint32_t)m->max_slots)
@@ -584,8 +586,9 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         for (int i = 1; i < N; ++i) {
             const int p = in->parents[(size_t)b * N + i];
             if (p < 0 || p >= i) return fail(VELO_ERR_INVALID_ARGUMENT, "parents[%d][%d] = %d", b, i, p);
-            if (sampling && p != i - 1)
-                return fail(VELO_ERR_INVALID_ARGUMENT, "sampling verifies chains only (parents[n] = n-1)");
+            if ((sampling || in->commit == 2) && p != i - 1)
+                return fail(VELO_ERR_INVALID_ARGUMENT,
+                            "sampling and commit of every node take chains only (parents[n] = n-1)");
         }
         for (int i = 0; i < N; ++i)
             if (in->tokens[(size_t)b * N + i] >= (uint32_t)V)
@@ -716,6 +719,19 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         VELO_CUDA_TRY(cudaMemcpyAsync(m->path, path.data(), path.size() * 4, cudaMemcpyHostToDevice, s));
         VELO_CUDA_TRY(cudaMemcpyAsync(m->path_len, plen.data(), plen.size() * 4, cudaMemcpyHostToDevice, s));
         VELO_CUDA_TRY(cudaStreamSynchronize(s));
+    }
+    if (in->commit == 2) {
+        // prefill / draft decode: the whole chain is committed and reported as
+        // accepted; the bonus is the argmax after the last node
+        VELO_CUDA_TRY(cudaMemcpy2DAsync(m->bonus, sizeof(uint32_t), m->expected + (N - 1),
+                                        (size_t)N * sizeof(uint32_t), sizeof(uint32_t), (size_t)B,
+                                        cudaMemcpyDeviceToDevice, s));
+        std::vector<int32_t> path((size_t)M), plen(B, N);
+        for (int b = 0; b < B; ++b)
+            for (int i = 0; i < N; ++i) path[(size_t)b * N + i] = i;
+        VELO_CUDA_TRY(cudaMemcpyAsync(m->path, path.data(), path.size() * 4, cudaMemcpyHostToDevice, s));
+        VELO_CUDA_TRY(cudaMemcpyAsync(m->path_len, plen.data(), plen.size() * 4, cudaMemcpyHostToDevice, s));
+        VELO_CUDA_TRY(cudaStreamSynchronize(s));  // host vectors go out of scope
     }
     if (in->commit) {
         velo::KvCommitArgs a{};

@@ -272,8 +272,9 @@ class Context:
 
     def verify_step(self, slots, ctx_len, tokens, parents, temperature=0.0, draft_logits=None,
                     uniforms=None, commit=True, want_logits=False, n_vocab=None):
-        """One verify step (host buffers).  Returns dict(accepted_len, accepted_nodes, bonus,
-        logits)."""
+        """One verify step (host buffers).  commit: True (the accepted path),
+        False, or "all" (every node of a chain: prefill / draft decode).
+        Returns dict(accepted_len, accepted_nodes, bonus, logits)."""
         tok = np.ascontiguousarray(tokens, np.uint32)
         B, N = tok.shape
         par = np.ascontiguousarray(parents, np.int32).reshape(B, N)
@@ -285,11 +286,27 @@ class Context:
         nodes = np.zeros((B, N), np.int32)
         bonus = np.zeros(B, np.uint32)
         logits = np.zeros((B, N, n_vocab), np.float32) if want_logits else None
+        cm = 2 if commit == "all" else (1 if commit else 0)
         bt = VerifyBatch(ctypes.sizeof(VerifyBatch), B, N, _ptr(sl), _ptr(cl), _ptr(tok), _ptr(par),
-                         float(temperature), _ptr(dl), _ptr(un), 1 if commit else 0)
+                         float(temperature), _ptr(dl), _ptr(un), cm)
         rs = VerifyResult(_ptr(acc), _ptr(nodes), _ptr(bonus), _ptr(logits))
         check(lib().velo_cuda_verify_step(self._h, ctypes.byref(bt), ctypes.byref(rs)))
         return {"accepted_len": acc, "accepted_nodes": nodes, "bonus": bonus, "logits": logits}
+
+
+def prefill(ctx, slot, tokens, pos0=0, chunk=64, n_vocab=None):
+    """Fill `slot`'s pages with the K/V of `tokens` at positions pos0.. by
+    chained verify steps that commit every node (chunks of <= 64 tokens).
+    Returns the greedy next token after the last one."""
+    toks = np.asarray(tokens, np.uint32)
+    nxt = None
+    for c0 in range(0, len(toks), chunk):
+        part = toks[c0:c0 + chunk]
+        par = np.arange(-1, len(part) - 1, dtype=np.int32)
+        r = ctx.verify_step([slot], [pos0 + c0], part[None], par[None], commit="all",
+                            n_vocab=n_vocab)
+        nxt = int(r["bonus"][0])
+    return nxt
 
 
 def nccl_unique_id():
