@@ -1,0 +1,255 @@
+"""The speculative-decoding session over the B200 verify step.
+
+A host-side restatement of velo-core's session loop (src/speculative.rs):
+SpeculativeDecoder (:255-361), SpeculativeSession::draft / commit (:400-519),
+adjust_window (:529-537), SpeculativeStats and SpeculativeError (:280-305),
+driving device models through the TargetModel / DraftModel shape
+(:133-254):
+
+- CudaTarget.verify runs one velo_cuda_verify_step over a chain whose root is
+  the last context token (the trait contract: step i holds the target's token
+  for drafted[i]) and commits the accepted path's K/V into the slot's pages;
+- CudaDraft.draft decodes greedily one token per step through the same call
+  (commit of every node), rewinding its cache to the prefix it shares with the
+  session's context, so rejected drafts are rolled back by length.
+
+The session logic itself is plain Python; every model call is the C ABI.
+"""
+from dataclasses import dataclass, field
+
+import numpy as np
+
+import velo_cuda
+
+
+class SpeculativeError(Exception):
+    """SpeculativeError (speculative.rs:294-305)."""
+
+
+class EmptyDraftWindow(SpeculativeError):
+    def __str__(self):
+        return "draft window must be greater than zero"
+
+
+class DraftReturnedTooMany(SpeculativeError):
+    def __init__(self, requested, returned):
+        super().__init__(requested, returned)
+        self.requested, self.returned = requested, returned
+
+    def __str__(self):
+        return f"draft model returned {self.returned} tokens, requested at most {self.requested}"
+
+
+class TargetReturnedWrongLength(SpeculativeError):
+    def __init__(self, drafted, returned):
+        super().__init__(drafted, returned)
+        self.drafted, self.returned = drafted, returned
+
+    def __str__(self):
+        return (f"target model returned {self.returned} verification steps "
+                f"for {self.drafted} drafted tokens")
+
+
+@dataclass
+class SpeculativeStats:
+    draft_calls: int = 0
+    target_calls: int = 0
+    drafted_tokens: int = 0
+    accepted_tokens: int = 0
+    rejected_tokens: int = 0
+
+
+@dataclass
+class SpeculativeOutput:
+    tokens: list
+    stats: SpeculativeStats
+
+
+@dataclass
+class NextTokenPrediction:
+    token: int
+    confidence: float = 1.0
+
+
+@dataclass
+class VerifyStep:
+    expected: int
+
+
+class SpeculativeDecoder:
+    """SpeculativeDecoder::new / with_max_window / generate / begin."""
+
+    def __init__(self, draft_window, max_window=None):
+        if draft_window == 0 or (max_window is not None and max_window < draft_window):
+            raise EmptyDraftWindow()
+        self.draft_window = draft_window
+        self.max_window = draft_window * 2 if max_window is None else max_window
+
+    def begin(self, prompt):
+        return SpeculativeSession(self.draft_window, self.max_window, list(prompt))
+
+    def generate(self, draft_model, target_model, prompt, max_new_tokens):
+        session = self.begin(prompt)
+        generated = []
+        while len(generated) < max_new_tokens:
+            remaining = max_new_tokens - len(generated)
+            drafted = session.draft(draft_model, target_model, remaining)
+            if not drafted and not session.has_pending_rejection():
+                break
+            generated.extend(drafted)
+            if not session.has_pending_rejection():
+                continue
+            token = session.take_rejected_token()
+            if token is not None:
+                generated.append(token)
+        return SpeculativeOutput(generated, session.stats)
+
+
+@dataclass
+class SpeculativeSession:
+    draft_window: int
+    max_window: int
+    prompt: list
+    context: list = field(default=None)
+    stats: SpeculativeStats = field(default_factory=SpeculativeStats)
+    rejected_token: object = None
+
+    def __post_init__(self):
+        if self.context is None:
+            self.context = list(self.prompt)
+
+    def has_pending_rejection(self):
+        return self.rejected_token is not None
+
+    def take_rejected_token(self):
+        t, self.rejected_token = self.rejected_token, None
+        return t
+
+    def current_window(self):
+        return self.draft_window
+
+    def record_draft_call(self):
+        self.stats.draft_calls += 1
+
+    def record_target_call(self):
+        self.stats.target_calls += 1
+
+    def draft(self, draft_model, target_model, max_new_tokens):
+        """SpeculativeSession::draft (speculative.rs:400-471)."""
+        requested = min(max_new_tokens, self.draft_window)
+        predictions = draft_model.draft(self.context, requested)
+        self.stats.draft_calls += 1
+        if len(predictions) > requested:
+            raise DraftReturnedTooMany(requested, len(predictions))
+        if not predictions:
+            return []
+        drafted = [p.token for p in predictions]
+        self.stats.drafted_tokens += len(drafted)
+        verified = target_model.verify(self.context, drafted)
+        self.stats.target_calls += 1
+        if len(verified) != len(drafted):
+            raise TargetReturnedWrongLength(len(drafted), len(verified))
+        return self._accept(drafted, verified)
+
+    def commit(self, drafted, verified):
+        """SpeculativeSession::commit (speculative.rs:473-519)."""
+        if len(verified) != len(drafted):
+            raise TargetReturnedWrongLength(len(drafted), len(verified))
+        self.stats.drafted_tokens += len(drafted)
+        return self._accept([p.token for p in drafted], verified)
+
+    def _accept(self, drafted, verified):
+        accepted_this_round, rejected = 0, None
+        for index, (tok, step) in enumerate(zip(drafted, verified)):
+            if tok == step.expected:
+                accepted_this_round += 1
+                continue
+            rejected = (index, step.expected)
+            break
+        accepted = list(drafted[:accepted_this_round])
+        if accepted:
+            self.context.extend(accepted)
+            self.stats.accepted_tokens += accepted_this_round
+        if rejected is not None:
+            self.context.append(rejected[1])
+            self.rejected_token = rejected[1]
+            self.stats.rejected_tokens += len(drafted) - rejected[0]
+        else:
+            self.rejected_token = None
+        self._adjust_window(accepted_this_round, len(drafted))
+        return accepted
+
+    def _adjust_window(self, accepted_count, drafted_count):
+        """adjust_window (speculative.rs:529-537)."""
+        if accepted_count == drafted_count:
+            if self.draft_window < self.max_window:
+                self.draft_window += 1
+        else:
+            self.draft_window = max(accepted_count + 1, 1)
+
+
+# ---------------------------------------------------------------- device models
+class CudaTarget:
+    """TargetModel over velo_cuda_verify_step for one sequence (`slot`).
+
+    The slot's pages hold the K/V of context[:-1]; verify() runs the chain
+    [context[-1]] + drafted and commits the accepted path, so the invariant
+    holds for the session's next context.  Rows past the first mismatch are
+    not needed by the session and repeat the target's token there."""
+
+    def __init__(self, ctx, slot, n_vocab, temperature=0.0):
+        self.ctx, self.slot, self.n_vocab, self.T = ctx, slot, n_vocab, temperature
+        self.cached = 0  # tokens of the context whose K/V are in the pages
+
+    def prefill(self, context):
+        n = len(context) - 1
+        if n > self.cached:
+            velo_cuda.prefill(self.ctx, self.slot, context[self.cached:n], pos0=self.cached,
+                              n_vocab=self.n_vocab)
+            self.cached = n
+
+    def verify(self, context, drafted):
+        self.prefill(context)
+        pos = len(context) - 1
+        nodes = np.array([context[-1]] + list(drafted), np.uint32)
+        parents = np.arange(-1, len(nodes) - 1, dtype=np.int32)
+        r = self.ctx.verify_step([self.slot], [pos], nodes[None], parents[None], commit=True,
+                                 n_vocab=self.n_vocab)
+        acc, bonus = int(r["accepted_len"][0]), int(r["bonus"][0])
+        self.cached = pos + acc + 1
+        return ([VerifyStep(t) for t in drafted[:acc]] +
+                [VerifyStep(bonus)] * (len(drafted) - acc))
+
+
+class CudaDraft:
+    """DraftModel: greedy decoding on the device, one verify step per token
+    (commit of every node), cache rewound to the prefix it shares with the
+    session's context."""
+
+    def __init__(self, ctx, slot, n_vocab):
+        self.ctx, self.slot, self.n_vocab = ctx, slot, n_vocab
+        self.tokens = []  # tokens whose K/V are in the draft's pages
+
+    def draft(self, context, max_tokens):
+        if max_tokens <= 0:
+            return []
+        common = 0
+        for a, b in zip(self.tokens, context[:-1]):
+            if a != b:
+                break
+            common += 1
+        self.tokens = self.tokens[:common]
+        if len(context) - 1 > common:
+            velo_cuda.prefill(self.ctx, self.slot, context[common:-1], pos0=common,
+                              n_vocab=self.n_vocab)
+            self.tokens = list(context[:-1])
+        out, last = [], context[-1]
+        for _ in range(max_tokens):
+            pos = len(self.tokens)
+            r = self.ctx.verify_step([self.slot], [pos], np.array([[last]], np.uint32),
+                                     np.array([[-1]], np.int32), commit="all",
+                                     n_vocab=self.n_vocab)
+            self.tokens.append(last)
+            last = int(r["bonus"][0])
+            out.append(NextTokenPrediction(last))
+        return out
