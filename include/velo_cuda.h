@@ -65,7 +65,11 @@ typedef struct velo_cuda_config {
     uint32_t max_pages_per_slot; /* page-table width [total_pages] */
 } velo_cuda_config;
 
-typedef enum velo_kv_dtype { VELO_KV_F16 = 0, VELO_KV_INT8 = 1 } velo_kv_dtype;
+/* KV page element type.  VELO_KV_F32 selects the fp32 path of the model: f32
+ * pages (the reference's f32 KvCache, src/llama_cpu.rs:22-50), weights of any
+ * dtype dequantised to f32 at load, every op in f32 (logits within 1e-4 of
+ * LlamaCpuModel); F16 / INT8 pages run q4_0 weights on the tensor cores. */
+typedef enum velo_kv_dtype { VELO_KV_F16 = 0, VELO_KV_INT8 = 1, VELO_KV_F32 = 2 } velo_kv_dtype;
 
 /* ---- lifecycle ---------------------------------------------------------- */
 
@@ -230,7 +234,7 @@ VELO_API int32_t velo_cuda_tree_attention(velo_cuda_ctx *ctx, const void *q, con
 typedef enum velo_dtype { VELO_DT_F32 = 0, VELO_DT_F16 = 1, VELO_DT_Q4_0 = 2 } velo_dtype;
 
 /* The Llama hyper-parameters the verify step needs (ModelMeta,
- * src/model_loader.rs:21-37).  head_dim must be 128. */
+ * src/model_loader.rs:21-37).  head_dim 128 (64 or 128 on the fp32 path). */
 typedef struct velo_model_desc {
     uint32_t struct_size;  /* sizeof(velo_model_desc) */
     uint32_t n_vocab, n_embd, n_layer, n_head, n_head_kv, n_ff, head_dim;
@@ -287,14 +291,15 @@ VELO_API int32_t velo_cuda_load_model(velo_cuda_ctx *ctx, const velo_model_desc 
 VELO_API int32_t velo_cuda_bind_slot(velo_cuda_ctx *ctx, uint32_t slot, const uint32_t *pages,
                                      size_t n_pages);
 
-/* Write n_tokens K/V rows (host f16 [n_tokens][n_head_kv][head_dim]) of one
- * layer at positions pos0.. of `slot` (int8 pools quantise as kv_update_int8,
- * src/kernels.metal:753-802).  The cache a prefill produced; synchronous. */
+/* Write n_tokens K/V rows (host [n_tokens][n_head_kv][head_dim], f16 for f16 /
+ * int8 pools, f32 for f32 pools) of one layer at positions pos0.. of `slot`
+ * (int8 pools quantise as kv_update_int8, src/kernels.metal:753-802).  The
+ * cache a prefill produced; synchronous. */
 VELO_API int32_t velo_cuda_write_kv(velo_cuda_ctx *ctx, uint32_t slot, int32_t layer, int32_t pos0,
-                                    int32_t n_tokens, const void *k_f16, const void *v_f16);
+                                    int32_t n_tokens, const void *k, const void *v);
 
 /* Read back the pool bytes of positions pos0..pos0+n_tokens of `slot` and
- * `layer`: k/v [n_tokens][n_head_kv][head_dim] (f16 or int8), scales
+ * `layer`: k/v [n_tokens][n_head_kv][head_dim] (pool dtype), scales
  * [n_tokens][n_head_kv] f16 (int8 pools; may be NULL).  Synchronous. */
 VELO_API int32_t velo_cuda_read_kv(velo_cuda_ctx *ctx, uint32_t slot, int32_t layer, int32_t pos0,
                                    int32_t n_tokens, void *k_out, void *v_out, void *k_scale_out,

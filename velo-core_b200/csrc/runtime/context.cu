@@ -138,7 +138,7 @@ int32_t velo_cuda_create(const velo_cuda_config* cfg, int32_t device, int32_t tp
     if (c->cfg.page_size == 0) c->cfg.page_size = 16;
     if (c->cfg.max_slots == 0) c->cfg.max_slots = 1;
     if (c->cfg.max_pages_per_slot == 0) c->cfg.max_pages_per_slot = c->cfg.total_pages;
-    if (c->cfg.kv_dtype > VELO_KV_INT8) {
+    if (c->cfg.kv_dtype > VELO_KV_F32) {
         const unsigned kd = c->cfg.kv_dtype;
         delete c;
         return fail(VELO_ERR_INVALID_ARGUMENT, "kv_dtype %u unknown", kd);

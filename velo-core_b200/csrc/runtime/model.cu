@@ -15,6 +15,7 @@
 #include <string>
 #include <vector>
 
+#include "kernels/f32_path.h"
 #include "kernels/q4gemm.h"
 #include "kernels/tree_attn.h"
 #include "kernels/verify_ops.h"
@@ -26,10 +27,12 @@
 
 namespace velo {
 
+// Matrices are repacked q4_0 (the tensor-core path) or, on the fp32 path, f32
+// rows (cast from the same pointers).
 struct Layer {
-    uint8_t* wqkv = nullptr;  // repacked q4_0 [(Hq + 2 Hkv) D][H]
+    uint8_t* wqkv = nullptr;  // [(Hq + 2 Hkv) D][H]
     uint8_t* wo = nullptr;    // [H][Hq D]
-    uint8_t* w13 = nullptr;   // SwiGLU pair [2F][H]
+    uint8_t* w13 = nullptr;   // SwiGLU pair [2F][H] (f32: w1 rows, then w3 rows)
     uint8_t* w2 = nullptr;    // [H][F]
     float* attn_norm = nullptr;
     float* ffn_norm = nullptr;
@@ -38,6 +41,11 @@ struct Layer {
 struct Model {
     velo_model_desc meta{};    // head / kv-head / ffn counts of this rank's shard
     int tp = 1, rank = 0;      // tensor-parallel position
+    // fp32 path (f32 KV pool): weights dequantised to f32 at load (dequant_row,
+    // quant.rs:181-191) and every op in f32 on the CUDA cores, the precision of
+    // LlamaCpuModel; otherwise q4_0 weights on the tensor cores, f16 / int8 pages
+    bool f32 = false;
+    int D = 128;               // head_dim
     int V_loc = 0, v_ofs = 0;  // this rank's vocabulary shard of the LM head
     float* emb = nullptr;      // [V][H] f32
     float* out_norm = nullptr; // [H]
@@ -49,7 +57,7 @@ struct Model {
     void* v_pool = nullptr;
     __half* k_scale = nullptr;
     __half* v_scale = nullptr;
-    int pool_pages = 0, kv_int8 = 0, max_slots = 0, max_pages = 0;
+    int pool_pages = 0, kv_int8 = 0, max_slots = 0, max_pages = 0;  // kv_int8: int8 pages
     uint32_t* page_table = nullptr;
     std::vector<uint32_t> page_table_host;
     // per-step buffers, sized for cap_M rows
@@ -63,6 +71,12 @@ struct Model {
     __half* nv = nullptr;
     __half* attn = nullptr;
     __half* hbuf = nullptr;
+    float* xn32 = nullptr;     // fp32 path: normed rows / SwiGLU rows [M][max(H, F)]
+    float* q32 = nullptr;      // [M][Hq][D]
+    float* nk32 = nullptr;     // [L][M][Hkv][D]
+    float* nv32 = nullptr;
+    float* attn32 = nullptr;   // [M][Hq D]
+    float* h32 = nullptr;      // [M][F]
     float* logits = nullptr;   // [M][V_loc]
     float* y = nullptr;        // [M][H] partial of a row-split GEMM (tp > 1)
     int2* pairs = nullptr;     // [M] this shard's argmax
@@ -91,8 +105,8 @@ struct Model {
     int F() const { return (int)meta.n_ff; }
     int V() const { return (int)meta.n_vocab; }
     int L() const { return (int)meta.n_layer; }
-    size_t kv_elt() const { return kv_int8 ? 1 : 2; }
-    size_t layer_pool_elems() const { return (size_t)pool_pages * Hkv() * 16 * 128; }
+    size_t kv_elt() const { return f32 ? 4 : kv_int8 ? 1 : 2; }
+    size_t layer_pool_elems() const { return (size_t)pool_pages * Hkv() * 16 * D; }
     size_t layer_scale_elems() const { return (size_t)pool_pages * Hkv() * 16; }
 };
 
@@ -175,6 +189,37 @@ int32_t upload_f32(Model* m, const velo_weight_desc* w, size_t rows, size_t cols
     return VELO_OK;
 }
 
+// fp32 path: matrices of any dtype (concatenated by rows) dequantised to f32
+// rows on the device, as LlamaCpuModel reads them (matvec_quant over
+// dequant_row, llama_cpu.rs:75-90)
+int32_t upload_f32_rows(Model* m, const std::vector<const velo_weight_desc*>& parts, size_t cols,
+                        uint8_t** out, cudaStream_t s) {
+    size_t rows = 0;
+    for (auto* w : parts) {
+        if (!w) return fail(VELO_ERR_INVALID_ARGUMENT, "missing matrix");
+        if (w->dtype < VELO_DT_F32 || w->dtype > VELO_DT_Q4_0 || !w->data)
+            return fail(VELO_ERR_INVALID_ARGUMENT, "matrix %s: bad dtype / data", w->name);
+        if (w->cols != cols || (w->dtype == VELO_DT_Q4_0 && cols % 32))
+            return fail(VELO_ERR_INVALID_ARGUMENT, "matrix %s: %llu columns, expected %zu", w->name,
+                        (unsigned long long)w->cols, cols);
+        rows += w->rows;
+    }
+    std::vector<float> host(rows * cols);
+    size_t r0 = 0;
+    for (auto* w : parts) {
+        const size_t rb = row_bytes(w->dtype, cols);
+        for (size_t r = 0; r < w->rows; ++r)
+            host_dequant_row(w->dtype, static_cast<const uint8_t*>(w->data) + r * rb,
+                             host.data() + (r0 + r) * cols, cols);
+        r0 += w->rows;
+    }
+    int32_t st = dev_alloc(m, out, host.size() * 4);
+    if (st) return st;
+    VELO_CUDA_TRY(cudaMemcpyAsync(*out, host.data(), host.size() * 4, cudaMemcpyHostToDevice, s));
+    VELO_CUDA_TRY(cudaStreamSynchronize(s));
+    return VELO_OK;
+}
+
 // q4_0 matrices (concatenated by rows, or a gate/up pair) -> repacked device weight
 int32_t upload_q4(Model* m, const std::vector<const velo_weight_desc*>& parts, size_t cols, bool pair,
                   uint8_t** out, cudaStream_t s) {
@@ -220,17 +265,26 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
     for (void* p : m->work) cudaFree(p);
     m->work.clear();
     const int cM = M > m->cap_M ? M : m->cap_M, cB = B > m->cap_B ? B : m->cap_B;
-    const size_t H = m->H(), D = 128, Hq = m->Hq(), Hkv = m->Hkv(), F = m->F();
+    const size_t H = m->H(), D = m->D, Hq = m->Hq(), Hkv = m->Hkv(), F = m->F();
     const size_t L = m->L();
     int32_t st = VELO_OK;
     if (!st) st = dev_alloc(m, &m->x, (size_t)cM * H * 4, true);
-    if (!st) st = dev_alloc(m, &m->xn, (size_t)cM * (H > F ? H : F) * 2, true);
     if (!st) st = dev_alloc(m, &m->qkv, (size_t)cM * (Hq + 2 * Hkv) * D * 4, true);
-    if (!st) st = dev_alloc(m, &m->q, (size_t)cM * Hq * D * 2, true);
-    if (!st) st = dev_alloc(m, &m->nk, L * cM * Hkv * D * 2, true);
-    if (!st) st = dev_alloc(m, &m->nv, L * cM * Hkv * D * 2, true);
-    if (!st) st = dev_alloc(m, &m->attn, (size_t)cM * Hq * D * 2, true);
-    if (!st) st = dev_alloc(m, &m->hbuf, (size_t)cM * F * 2, true);
+    if (m->f32) {
+        if (!st) st = dev_alloc(m, &m->xn32, (size_t)cM * H * 4, true);
+        if (!st) st = dev_alloc(m, &m->q32, (size_t)cM * Hq * D * 4, true);
+        if (!st) st = dev_alloc(m, &m->nk32, L * cM * Hkv * D * 4, true);
+        if (!st) st = dev_alloc(m, &m->nv32, L * cM * Hkv * D * 4, true);
+        if (!st) st = dev_alloc(m, &m->attn32, (size_t)cM * Hq * D * 4, true);
+        if (!st) st = dev_alloc(m, &m->h32, (size_t)cM * F * 4, true);
+    } else {
+        if (!st) st = dev_alloc(m, &m->xn, (size_t)cM * (H > F ? H : F) * 2, true);
+        if (!st) st = dev_alloc(m, &m->q, (size_t)cM * Hq * D * 2, true);
+        if (!st) st = dev_alloc(m, &m->nk, L * cM * Hkv * D * 2, true);
+        if (!st) st = dev_alloc(m, &m->nv, L * cM * Hkv * D * 2, true);
+        if (!st) st = dev_alloc(m, &m->attn, (size_t)cM * Hq * D * 2, true);
+        if (!st) st = dev_alloc(m, &m->hbuf, (size_t)cM * F * 2, true);
+    }
     if (!st) st = dev_alloc(m, &m->logits, (size_t)cM * m->V_loc * 4, true);
     if (!st && m->tp > 1) st = dev_alloc(m, &m->y, (size_t)cM * H * 4, true);
     if (!st) st = dev_alloc(m, &m->pairs, (size_t)cM * 8, true);
@@ -290,6 +344,64 @@ int32_t allreduce_add(velo_cuda_ctx* c, Model* m, int M) {
     return VELO_OK;
 }
 
+// The fp32 path's layer loop and LM head (f32_path.cu), on rows x = the
+// embedded tree nodes; logits [M][V_loc] out.
+int32_t forward_f32(velo_cuda_ctx* c, Model* m, int B, int N) {
+    cudaStream_t s = c->stream;
+    const int M = B * N, H = m->H(), Hq = m->Hq(), Hkv = m->Hkv(), F = m->F(), L = m->L(), D = m->D;
+    const int Nqkv = (Hq + 2 * Hkv) * D;
+    const float eps = m->meta.norm_eps;
+    auto mat = [](const uint8_t* p) { return reinterpret_cast<const float*>(p); };
+    int32_t st = VELO_OK;
+    for (int l = 0; l < L; ++l) {
+        const Layer& ly = m->layers[l];
+        float* nk = m->nk32 + (size_t)l * M * Hkv * D;
+        float* nv = m->nv32 + (size_t)l * M * Hkv * D;
+        VELO_CUDA_TRY(launch_rmsnorm_f32(m->x, ly.attn_norm, M, H, eps, m->xn32, s));
+        VELO_CUDA_TRY(launch_gemm_f32(mat(ly.wqkv), m->xn32, M, Nqkv, H, m->qkv, Nqkv, kF32Store, s));
+        VELO_CUDA_TRY(launch_rope_split_f32(m->qkv, m->anc, m->ctxlen, B, N, Hq, Hkv, D,
+                                            m->meta.rope_freq_base, m->q32, nk, nv, s));
+        TreeAttnF32Args a{};
+        const size_t lo = (size_t)l * m->layer_pool_elems();
+        a.q = m->q32;
+        a.k_pool = static_cast<const float*>(m->k_pool) + lo;
+        a.v_pool = static_cast<const float*>(m->v_pool) + lo;
+        a.page_table = m->pt_batch;
+        a.ctx_len = m->ctxlen;
+        a.node_k = nk;
+        a.node_v = nv;
+        a.anc = m->anc;
+        a.out = m->attn32;
+        a.B = B;
+        a.N = N;
+        a.Hq = Hq;
+        a.Hkv = Hkv;
+        a.D = D;
+        a.max_pages = m->max_pages;
+        a.pool_pages = m->pool_pages;
+        a.err = c->err_flag;
+        VELO_CUDA_TRY(launch_tree_attention_f32(a, s));
+        if (m->tp == 1) {
+            VELO_CUDA_TRY(launch_gemm_f32(mat(ly.wo), m->attn32, M, H, Hq * D, m->x, H, kF32Add, s));
+        } else {  // row-split o_proj: partial, all-reduce, residual add
+            VELO_CUDA_TRY(launch_gemm_f32(mat(ly.wo), m->attn32, M, H, Hq * D, m->y, H, kF32Store, s));
+            if ((st = allreduce_add(c, m, M))) return st;
+        }
+        VELO_CUDA_TRY(launch_rmsnorm_f32(m->x, ly.ffn_norm, M, H, eps, m->xn32, s));
+        VELO_CUDA_TRY(launch_gemm_f32(mat(ly.w13), m->xn32, M, F, H, m->h32, F, kF32SwiGLU, s));
+        if (m->tp == 1) {
+            VELO_CUDA_TRY(launch_gemm_f32(mat(ly.w2), m->h32, M, H, F, m->x, H, kF32Add, s));
+        } else {  // row-split down_proj
+            VELO_CUDA_TRY(launch_gemm_f32(mat(ly.w2), m->h32, M, H, F, m->y, H, kF32Store, s));
+            if ((st = allreduce_add(c, m, M))) return st;
+        }
+    }
+    VELO_CUDA_TRY(launch_rmsnorm_f32(m->x, m->out_norm, M, H, eps, m->xn32, s));
+    VELO_CUDA_TRY(launch_gemm_f32(mat(m->lm_head), m->xn32, M, m->V_loc, H, m->logits, m->V_loc,
+                                  kF32Store, s));
+    return VELO_OK;
+}
+
 int32_t check_model(velo_cuda_ctx* c) {
     if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
     if (!c->model) return fail(VELO_ERR_INVALID_ARGUMENT, "no model loaded (velo_cuda_load_model)");
@@ -311,21 +423,30 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
     if (d->struct_size != 0 && d->struct_size != sizeof(velo_model_desc))
         return fail(VELO_ERR_INVALID_ARGUMENT, "velo_model_desc.struct_size %u != %zu", d->struct_size,
                     sizeof(velo_model_desc));
-    if (d->head_dim != 128 || d->n_head == 0 || d->n_head_kv == 0 || d->n_head % d->n_head_kv ||
-        d->n_embd % 128 || d->n_ff % 32 || d->n_vocab == 0 || d->n_layer == 0 ||
-        (d->n_head * d->head_dim) % 32)
+    // an f32 KV pool selects the fp32 path (any weight dtype, dequantised at load)
+    const bool f32 = c->cfg.kv_dtype == VELO_KV_F32;
+    if (d->n_head == 0 || d->n_head_kv == 0 || d->n_head % d->n_head_kv || d->n_vocab == 0 ||
+        d->n_layer == 0)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "model shape unsupported: heads %u/%u, n_vocab %u, %u layers",
+                    d->n_head, d->n_head_kv, d->n_vocab, d->n_layer);
+    if (f32 && ((d->head_dim != 64 && d->head_dim != 128) || d->n_embd % 4 || d->n_ff % 4))
         return fail(VELO_ERR_INVALID_ARGUMENT,
-                    "model shape unsupported: head_dim %u (128), heads %u/%u, n_embd %u, n_ff %u",
-                    d->head_dim, d->n_head, d->n_head_kv, d->n_embd, d->n_ff);
+                    "fp32 model shape unsupported: head_dim %u (64 or 128), n_embd %u and n_ff %u (by 4)",
+                    d->head_dim, d->n_embd, d->n_ff);
+    if (!f32 && (d->head_dim != 128 || d->n_embd % 128 || d->n_ff % 32))
+        return fail(VELO_ERR_INVALID_ARGUMENT,
+                    "q4_0 model shape unsupported: head_dim %u (128), n_embd %u (by 128), n_ff %u (by 32)",
+                    d->head_dim, d->n_embd, d->n_ff);
     if (c->cfg.page_size != 16)
         return fail(VELO_ERR_INVALID_BLOCK_SIZE, "page_size %u: the kernels use 16-token pages",
                     c->cfg.page_size);
     const int tp = c->tp_size, rank = c->tp_rank;
+    const uint32_t ff_align = f32 ? 4 : 32;
     if (tp > 1 && (d->n_head % tp || d->n_head_kv % tp || d->n_ff % tp || d->n_vocab % tp ||
-                   (d->n_ff / tp) % 32))
+                   (d->n_ff / tp) % ff_align))
         return fail(VELO_ERR_INVALID_ARGUMENT,
-                    "heads %u/%u, n_ff %u and n_vocab %u must divide by tp %d (n_ff/tp by 32)",
-                    d->n_head, d->n_head_kv, d->n_ff, d->n_vocab, tp);
+                    "heads %u/%u, n_ff %u and n_vocab %u must divide by tp %d (n_ff/tp by %u)",
+                    d->n_head, d->n_head_kv, d->n_ff, d->n_vocab, tp, ff_align);
     VELO_CUDA_TRY(cudaSetDevice(c->device));
     velo::destroy_model(c->model);
     c->model = nullptr;
@@ -334,6 +455,8 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
     m->meta.struct_size = sizeof(velo_model_desc);
     m->tp = tp;
     m->rank = rank;
+    m->f32 = f32;
+    m->D = (int)d->head_dim;
     m->meta.n_head = d->n_head / tp;
     m->meta.n_head_kv = d->n_head_kv / tp;
     m->meta.n_ff = d->n_ff / tp;
@@ -369,8 +492,14 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
     if (!st) {
         const velo_weight_desc* out = velo::find(ix, "output.weight");
         const velo_weight_desc* lm = shard(out ? out : emb, VELO_SHARD_COLUMN);  // tied fallback
-        if (!st) st = velo::upload_q4(m, {lm}, H, false, &m->lm_head, s);
+        if (!st) st = f32 ? velo::upload_f32_rows(m, {lm}, H, &m->lm_head, s)
+                          : velo::upload_q4(m, {lm}, H, false, &m->lm_head, s);
     }
+    auto upload = [&](const std::vector<const velo_weight_desc*>& parts, size_t cols, bool pair,
+                      uint8_t** dst) {
+        return f32 ? velo::upload_f32_rows(m, parts, cols, dst, s)
+                   : velo::upload_q4(m, parts, cols, pair, dst, s);
+    };
     for (uint32_t l = 0; !st && l < d->n_layer; ++l) {
         const std::string p = "layers." + std::to_string(l) + ".";
         velo::Layer ly;
@@ -380,20 +509,20 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
             auto* wq = get(p + "attention.wq.weight");
             auto* wk = get(p + "attention.wk.weight");
             auto* wv = get(p + "attention.wv.weight");
-            if (!st) st = velo::upload_q4(m, {wq, wk, wv}, H, false, &ly.wqkv, s);
+            if (!st) st = upload({wq, wk, wv}, H, false, &ly.wqkv);
         }
         if (!st) {
             auto* wo = get(p + "attention.wo.weight");
-            if (!st) st = velo::upload_q4(m, {wo}, Dq, false, &ly.wo, s);
+            if (!st) st = upload({wo}, Dq, false, &ly.wo);
         }
         if (!st) {
             auto* w1 = get(p + "feed_forward.w1.weight");
             auto* w3 = get(p + "feed_forward.w3.weight");
-            if (!st) st = velo::upload_q4(m, {w1, w3}, H, true, &ly.w13, s);
+            if (!st) st = upload({w1, w3}, H, true, &ly.w13);
         }
         if (!st) {
             auto* w2 = get(p + "feed_forward.w2.weight");
-            if (!st) st = velo::upload_q4(m, {w2}, F, false, &ly.w2, s);
+            if (!st) st = upload({w2}, F, false, &ly.w2);
         }
         m->layers.push_back(ly);
         bufs.clear();
@@ -473,29 +602,51 @@ int32_t velo_cuda_write_kv(velo_cuda_ctx* c, uint32_t slot, int32_t layer, int32
     if ((pos0 + n - 1) / 16 >= m->max_pages)
         return fail(VELO_ERR_OUT_OF_PAGES, "write_kv: position %d beyond the page-table row", pos0 + n - 1);
     VELO_CUDA_TRY(cudaSetDevice(c->device));
-    const size_t rows = (size_t)n * m->Hkv() * 128;
-    __half* dk = nullptr;
-    VELO_CUDA_TRY(cudaMalloc(&dk, rows * 4 + 64 * 4 * 4));
-    __half* dv = dk + rows;
-    int32_t* meta = reinterpret_cast<int32_t*>(dv + rows);  // path[64], len, ctx, slot
+    const size_t rows = (size_t)n * m->Hkv() * m->D;
+    const size_t in_elt = m->f32 ? 4 : 2;  // host rows: f32 for f32 pools, else f16
+    uint8_t* dk = nullptr;
+    VELO_CUDA_TRY(cudaMalloc(&dk, rows * in_elt * 2 + 64 * 4 * 4));
+    uint8_t* dv = dk + rows * in_elt;
+    int32_t* meta = reinterpret_cast<int32_t*>(dv + rows * in_elt);  // path[64], len, ctx, slot
     std::vector<int32_t> hm(64 + 3);
     for (int i = 0; i < 64; ++i) hm[i] = i < n ? i : -1;
     hm[64] = n;
     hm[65] = pos0;
     hm[66] = (int32_t)slot;
-    cudaError_t e = cudaMemcpy(dk, k, rows * 2, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(dv, v, rows * 2, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMemcpy(dk, k, rows * in_elt, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(dv, v, rows * in_elt, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(meta, hm.data(), hm.size() * 4, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) {
-        velo::KvCommitArgs a{};
-        a.node_k = dk;
-        a.node_v = dv;
+    const size_t lo = (size_t)layer * m->layer_pool_elems() * m->kv_elt();
+    if (e == cudaSuccess && m->f32) {
+        velo::KvCommitF32Args a{};
+        a.node_k = reinterpret_cast<const float*>(dk);
+        a.node_v = reinterpret_cast<const float*>(dv);
         a.path = meta;
         a.path_len = meta + 64;
         a.ctx_len = meta + 65;
         a.slots = reinterpret_cast<const uint32_t*>(meta + 66);
         a.page_table = m->page_table;
-        const size_t lo = (size_t)layer * m->layer_pool_elems() * m->kv_elt();
+        a.k_pool = reinterpret_cast<float*>(static_cast<uint8_t*>(m->k_pool) + lo);
+        a.v_pool = reinterpret_cast<float*>(static_cast<uint8_t*>(m->v_pool) + lo);
+        a.B = 1;
+        a.N = n;
+        a.L = 1;
+        a.Hkv = m->Hkv();
+        a.D = m->D;
+        a.max_pages = m->max_pages;
+        a.pool_pages = m->pool_pages;
+        a.err = c->err_flag;
+        e = velo::launch_kv_commit_f32(a, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    } else if (e == cudaSuccess) {
+        velo::KvCommitArgs a{};
+        a.node_k = reinterpret_cast<const __half*>(dk);
+        a.node_v = reinterpret_cast<const __half*>(dv);
+        a.path = meta;
+        a.path_len = meta + 64;
+        a.ctx_len = meta + 65;
+        a.slots = reinterpret_cast<const uint32_t*>(meta + 66);
+        a.page_table = m->page_table;
         a.k_pool = static_cast<uint8_t*>(m->k_pool) + lo;
         a.v_pool = static_cast<uint8_t*>(m->v_pool) + lo;
         a.k_scale = m->kv_int8 ? m->k_scale + (size_t)layer * m->layer_scale_elems() : nullptr;
@@ -530,7 +681,7 @@ int32_t velo_cuda_read_kv(velo_cuda_ctx* c, uint32_t slot, int32_t layer, int32_
     VELO_CUDA_TRY(cudaSetDevice(c->device));
     VELO_CUDA_TRY(cudaStreamSynchronize(c->stream));
     const uint32_t* row = m->page_table_host.data() + (size_t)slot * m->max_pages;
-    const size_t hd = 128, tokb = hd * m->kv_elt();
+    const size_t hd = m->D, tokb = hd * m->kv_elt();
     for (int i = 0; i < n; ++i) {
         const int pos = pos0 + i;
         const uint32_t pg = row[pos / 16];
@@ -615,7 +766,11 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     VELO_CUDA_TRY(velo::launch_tree_ancestors(m->parents, B, N, m->anc, c->err_flag, s));
     VELO_CUDA_TRY(velo::launch_embed(m->emb, m->tokens, M, H, m->V(), m->x, c->err_flag, s));
     const float eps = m->meta.norm_eps;
-    for (int l = 0; l < L; ++l) {
+    if (m->f32) {
+        st = velo::forward_f32(c, m, B, N);
+        if (st) return st;
+    }
+    for (int l = 0; !m->f32 && l < L; ++l) {
         const velo::Layer& ly = m->layers[l];
         __half* nk = m->nk + (size_t)l * M * Hkv * 128;
         __half* nv = m->nv + (size_t)l * M * Hkv * 128;
@@ -665,10 +820,12 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         }
         if (st) return st;
     }
-    VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, m->out_norm, M, H, eps, m->xn, s));
     const int Vl = m->V_loc;
-    st = velo::gemm(c, m->lm_head, m->xn, M, Vl, H, m->logits, Vl, velo::kEpiStoreF32);
-    if (st) return st;
+    if (!m->f32) {
+        VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, m->out_norm, M, H, eps, m->xn, s));
+        st = velo::gemm(c, m->lm_head, m->xn, M, Vl, H, m->logits, Vl, velo::kEpiStoreF32);
+        if (st) return st;
+    }
     // acceptance
     if (m->tp > 1 && (!sampling || N == 1)) {
         // vocabulary-sharded greedy: per-shard maxima, gathered, combined
@@ -733,7 +890,27 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         VELO_CUDA_TRY(cudaMemcpyAsync(m->path_len, plen.data(), plen.size() * 4, cudaMemcpyHostToDevice, s));
         VELO_CUDA_TRY(cudaStreamSynchronize(s));  // host vectors go out of scope
     }
-    if (in->commit) {
+    if (in->commit && m->f32) {
+        velo::KvCommitF32Args a{};
+        a.node_k = m->nk32;
+        a.node_v = m->nv32;
+        a.path = m->path;
+        a.path_len = m->path_len;
+        a.ctx_len = m->ctxlen;
+        a.slots = m->slots;
+        a.page_table = m->page_table;
+        a.k_pool = static_cast<float*>(m->k_pool);
+        a.v_pool = static_cast<float*>(m->v_pool);
+        a.B = B;
+        a.N = N;
+        a.L = L;
+        a.Hkv = Hkv;
+        a.D = m->D;
+        a.max_pages = m->max_pages;
+        a.pool_pages = m->pool_pages;
+        a.err = c->err_flag;
+        VELO_CUDA_TRY(velo::launch_kv_commit_f32(a, s));
+    } else if (in->commit) {
         velo::KvCommitArgs a{};
         a.node_k = m->nk;
         a.node_v = m->nv;

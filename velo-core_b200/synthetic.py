@@ -147,39 +147,62 @@ LAYER_TENSORS = ("attention_norm", "attention.wq", "attention.wk", "attention.wv
                  "ffn_norm", "feed_forward.w1", "feed_forward.w2", "feed_forward.w3")
 
 
-def llama_q4_model(n_vocab, n_embd, n_layer, n_head, n_head_kv, n_ff, seed=0, sigma=0.02,
-                   tied=False):
+def llama_model(n_vocab, n_embd, n_layer, n_head, n_head_kv, n_ff, seed=0, sigma=0.02,
+                tied=False, dtype=2, head_dim=128, norm_sigma=0.1):
     """Random-init Llama weights in the reference's WeightStore layout
-    (src/model_loader.rs:216-232; matrices [out][in]): q4_0 matrices and
-    embedding from N(0, sigma^2), f32 norm weights 1 + N(0, 0.1^2).
-    Returns (meta, {name: (dtype, array, rows, cols)})."""
-    hd = 128
+    (src/model_loader.rs:216-232; matrices [out][in]): matrices and embedding
+    from N(0, sigma^2) as q4_0 (dtype 2) or f32 (dtype 0), f32 norm weights
+    1 + N(0, norm_sigma^2).  Returns (meta, {name: (dtype, array, rows, cols)})."""
+    hd = head_dim
     meta = dict(n_vocab=n_vocab, n_embd=n_embd, n_layer=n_layer, n_head=n_head,
                 n_head_kv=n_head_kv, n_ff=n_ff, head_dim=hd, rope_freq_base=10000.0,
                 norm_eps=1e-5)
     g = rng(seed, 50)
 
-    def q4(rows, cols):
-        return (2, quantize_q4_0(g.normal(0, sigma, (rows, cols)).astype(np.float32)), rows, cols)
+    def mat(rows, cols):
+        w = g.normal(0, sigma, (rows, cols)).astype(np.float32)
+        return (2, quantize_q4_0(w), rows, cols) if dtype == 2 else (0, w, rows, cols)
 
     def norm():
-        return (0, (1.0 + g.normal(0, 0.1, n_embd)).astype(np.float32), 1, n_embd)
+        w = np.ones(n_embd, np.float32)
+        if norm_sigma:
+            w = (1.0 + g.normal(0, norm_sigma, n_embd)).astype(np.float32)
+        return (0, w, 1, n_embd)
 
-    t = {"token_embd.weight": q4(n_vocab, n_embd), "output_norm.weight": norm()}
+    t = {"token_embd.weight": mat(n_vocab, n_embd), "output_norm.weight": norm()}
     if not tied:
-        t["output.weight"] = q4(n_vocab, n_embd)
+        t["output.weight"] = mat(n_vocab, n_embd)
     for l in range(n_layer):
         p = f"layers.{l}."
         t[p + "attention_norm.weight"] = norm()
-        t[p + "attention.wq.weight"] = q4(n_head * hd, n_embd)
-        t[p + "attention.wk.weight"] = q4(n_head_kv * hd, n_embd)
-        t[p + "attention.wv.weight"] = q4(n_head_kv * hd, n_embd)
-        t[p + "attention.wo.weight"] = q4(n_embd, n_head * hd)
+        t[p + "attention.wq.weight"] = mat(n_head * hd, n_embd)
+        t[p + "attention.wk.weight"] = mat(n_head_kv * hd, n_embd)
+        t[p + "attention.wv.weight"] = mat(n_head_kv * hd, n_embd)
+        t[p + "attention.wo.weight"] = mat(n_embd, n_head * hd)
         t[p + "ffn_norm.weight"] = norm()
-        t[p + "feed_forward.w1.weight"] = q4(n_ff, n_embd)
-        t[p + "feed_forward.w2.weight"] = q4(n_embd, n_ff)
-        t[p + "feed_forward.w3.weight"] = q4(n_ff, n_embd)
+        t[p + "feed_forward.w1.weight"] = mat(n_ff, n_embd)
+        t[p + "feed_forward.w2.weight"] = mat(n_embd, n_ff)
+        t[p + "feed_forward.w3.weight"] = mat(n_ff, n_embd)
     return meta, t
+
+
+def llama_q4_model(n_vocab, n_embd, n_layer, n_head, n_head_kv, n_ff, seed=0, sigma=0.02,
+                   tied=False):
+    """q4_0 weights, head_dim 128 (the tensor-core path)."""
+    return llama_model(n_vocab, n_embd, n_layer, n_head, n_head_kv, n_ff, seed, sigma, tied)
+
+
+def c1_pair(seed=0):
+    """The CPU-runnable tiny fp32 Llama pair: target 2 layers, hidden 256,
+    4 heads x 64, SwiGLU FFN 688, vocab 4096, RMSNorm eps 1e-5, RoPE theta 1e4;
+    draft 1 layer of the same dims.  Weights N(0, 0.02^2) f32, norm weights 1,
+    both from `seed` (so the draft shares the target's embedding, LM head and
+    first layer).  Returns (target_meta, target_tensors, draft_meta, draft_tensors)."""
+    kw = dict(n_vocab=4096, n_embd=256, n_head=4, n_head_kv=4, n_ff=688, sigma=0.02, dtype=0,
+              head_dim=64, norm_sigma=0.0, seed=seed)
+    tm, tw = llama_model(n_layer=2, **kw)
+    dm, dw = llama_model(n_layer=1, **kw)
+    return tm, tw, dm, dw
 
 
 def oracle_tensor_list(meta, tensors):

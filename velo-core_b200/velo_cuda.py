@@ -33,7 +33,7 @@ ERR_OUT_OF_MEMORY = 11
 ERR_NCCL = 12
 ERR_DEVICE_FLAG = 13
 
-KV_F16, KV_INT8 = 0, 1
+KV_F16, KV_INT8, KV_F32 = 0, 1, 2  # KV_F32: the fp32 path of the model
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -157,6 +157,7 @@ class Context:
                  max_pages_per_slot=0, tp_rank=0, tp_size=1, nccl_id=None):
         cfg = Config(ctypes.sizeof(Config), page_size, kv_dtype, max_slots, total_pages,
                      max_pages_per_slot)
+        self.kv_dtype = kv_dtype
         h = _P()
         nid = None if nccl_id is None else ctypes.c_char_p(bytes(nccl_id))
         check(lib().velo_cuda_create(ctypes.byref(cfg), device, tp_rank, tp_size, nid,
@@ -255,15 +256,17 @@ class Context:
         p = np.ascontiguousarray(pages, np.uint32)
         check(lib().velo_cuda_bind_slot(self._h, slot, _ptr(p), p.size))
 
-    def write_kv(self, slot, layer, pos0, k_f16, v_f16):
-        k = np.ascontiguousarray(k_f16, np.float16)
-        v = np.ascontiguousarray(v_f16, np.float16)
+    def write_kv(self, slot, layer, pos0, k, v):
+        """k, v [n][n_kv][head_dim]: f32 for an f32 pool, else f16."""
+        dt = np.float32 if self.kv_dtype == KV_F32 else np.float16
+        k = np.ascontiguousarray(k, dt)
+        v = np.ascontiguousarray(v, dt)
         check(lib().velo_cuda_write_kv(self._h, slot, layer, pos0, k.shape[0], _ptr(k), _ptr(v)))
 
-    def read_kv(self, slot, layer, pos0, n, n_kv, int8=False):
-        dt = np.int8 if int8 else np.float16
-        k = np.zeros((n, n_kv, 128), dt)
-        v = np.zeros((n, n_kv, 128), dt)
+    def read_kv(self, slot, layer, pos0, n, n_kv, int8=False, head_dim=128):
+        dt = np.int8 if int8 else np.float32 if self.kv_dtype == KV_F32 else np.float16
+        k = np.zeros((n, n_kv, head_dim), dt)
+        v = np.zeros((n, n_kv, head_dim), dt)
         ks = np.zeros((n, n_kv), np.uint16)
         vs = np.zeros((n, n_kv), np.uint16)
         check(lib().velo_cuda_read_kv(self._h, slot, layer, pos0, n, _ptr(k), _ptr(v), _ptr(ks),
