@@ -671,6 +671,239 @@ def run_verify(args):
     return 0
 
 
+# ---------------------------------------------------------------- tiny fp32 pair (config 1)
+C1_K, C1_PROMPT, C1_NEW = 4, 64, 128
+
+
+class _Timed:
+    """A draft / target model whose every call is bracketed by CUDA events on
+    the contexts' stream (device time of the call, host gaps inside it
+    included)."""
+
+    def __init__(self, model, stream):
+        import torch
+        self.m, self.stream, self.ev, self.torch = model, stream, [], torch
+
+    def _call(self, fn, *a):
+        e0 = self.torch.cuda.Event(enable_timing=True)
+        e1 = self.torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        out = fn(*a)
+        e1.record(self.stream)
+        self.ev.append((e0, e1))
+        return out
+
+    def draft(self, context, n):
+        return self._call(self.m.draft, context, n)
+
+    def verify(self, context, drafted):
+        return self._call(self.m.verify, context, drafted)
+
+
+class _OracleGreedyTarget:
+    """The CPU port's target for the session baseline (chain verify, commit)."""
+
+    def __init__(self, model):
+        self.m, self.cached = model, 0
+
+    def verify(self, context, drafted):
+        import vo
+        from speculative import VerifyStep
+        for i in range(self.cached, len(context) - 1):
+            self.m.forward_one(int(context[i]), i)
+        pos = len(context) - 1
+        nodes = np.array([context[-1]] + list(drafted), np.uint32)
+        lg = self.m.verify_tree(nodes, np.arange(-1, len(nodes) - 1, dtype=np.int32), pos)
+        exp = [vo.greedy(lg[i])[0] for i in range(len(drafted))]
+        acc = 0
+        while acc < len(drafted) and drafted[acc] == exp[acc]:
+            acc += 1
+        self.m.commit_path(list(range(acc + 1)), pos)
+        self.cached = pos + acc + 1
+        return [VerifyStep(e) for e in exp]
+
+
+class _OracleGreedyDraft:
+    def __init__(self, model):
+        self.m, self.tokens = model, []
+
+    def draft(self, context, n):
+        import vo
+        from speculative import NextTokenPrediction
+        common = 0
+        for a, b in zip(self.tokens, context[:-1]):
+            if a != b:
+                break
+            common += 1
+        self.tokens = self.tokens[:common]
+        for i in range(common, len(context) - 1):
+            self.m.forward_one(int(context[i]), i)
+            self.tokens.append(int(context[i]))
+        out, last = [], int(context[-1])
+        for _ in range(n):
+            lg = self.m.forward_one(last, len(self.tokens))
+            self.tokens.append(last)
+            last = vo.greedy(lg)[0]
+            out.append(NextTokenPrediction(last))
+        return out
+
+
+def c1_cpu_baseline():
+    """The CPU port (oracle restatement of llama_cpu.rs, one thread) running the
+    whole greedy session of config 1: accepted tokens/s."""
+    import synthetic
+    import vo
+    from speculative import SpeculativeDecoder
+    tm, tw, dm, dw = synthetic.c1_pair(0)
+    prompt = [int(t) for t in synthetic.rng(0, 91).integers(0, tm["n_vocab"], C1_PROMPT)]
+    dl, tl = synthetic.oracle_tensor_list(dm, dw), synthetic.oracle_tensor_list(tm, tw)
+    secs, toks, reps = 0.0, 0, 0
+    while secs < 10.0:
+        t0 = time.perf_counter()
+        out = SpeculativeDecoder(C1_K, C1_K).generate(
+            _OracleGreedyDraft(vo.Model(dict(dm, n_ctx=512), dl)),
+            _OracleGreedyTarget(vo.Model(dict(tm, n_ctx=512), tl)), prompt, C1_NEW)
+        secs += time.perf_counter() - t0
+        toks += len(out.tokens)
+        reps += 1
+    return {"value": toks / secs, "unit": "accepted tokens/s", "cores": 1, "kind": "port",
+            "sample": f"{reps} whole greedy sessions ({C1_PROMPT}-token prompt incl. prefill, "
+                      f"k={C1_K}, {C1_NEW} new tokens), single-threaded like llama_cpu.rs, "
+                      f"{secs:.1f} s"}
+
+
+def run_c1(args):
+    """BASELINE config 1 on the fp32 path: the tiny Llama pair (target 2 layers,
+    draft 1 layer; hidden 256, 4 x 64 heads, FFN 688, vocab 4096, f32 weights
+    N(0, 0.02^2)), batch 1, 64-token prompt, linear speculation k = 4, sessions
+    of 128 new tokens, greedy and T = 1.0.  A step is one session round: the
+    draft's k one-token decode steps and the target's verify step (forward over
+    k + 1 nodes, acceptance, KV commit), every call through the host-buffer C
+    ABI.  Independent replicas under torchrun."""
+    import torch
+    import torch.distributed as dist
+    import synthetic
+    import velo_cuda
+    from speculative import CudaDraft, CudaTarget, SpeculativeDecoder
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+    tm, tw, dm, dw = synthetic.c1_pair(0)
+    V = tm["n_vocab"]
+    prompt = [int(t) for t in synthetic.rng(0, 91).integers(0, V, C1_PROMPT)]
+    pages = (C1_PROMPT + C1_NEW + C1_K + 16) // 16 + 1
+    stream = torch.cuda.Stream()
+    ctxs = []
+    for meta, w in ((tm, tw), (dm, dw)):
+        c = velo_cuda.Context(device=local, kv_dtype=velo_cuda.KV_F32, total_pages=pages,
+                              max_slots=1, max_pages_per_slot=pages)
+        c.load_model(meta, w)
+        c.bind_slot(0, np.arange(pages))
+        c.set_stream(stream.cuda_stream)
+        ctxs.append(c)
+    tctx, dctx = ctxs
+    rounds = max(3, min(args.steps, 400))
+
+    def run_mode(T):
+        rng = np.random.Generator(np.random.Philox(5))
+        rec = []  # per round: (new tokens, drafted, accepted, draft event, verify event)
+        wall = 0.0
+        while len(rec) < args.warmup + rounds:
+            draft = CudaDraft(dctx, 0, V, T, rng)
+            target = CudaTarget(tctx, 0, V, T, draft, rng)
+            td, tt = _Timed(draft, stream), _Timed(target, stream)
+            sess = SpeculativeDecoder(C1_K, C1_K).begin(prompt)
+            target.prefill(sess.context)
+            draft.prefill(sess.context)
+            generated = 0
+            while generated < C1_NEW and len(rec) < args.warmup + rounds:
+                s0, d0 = sess.stats.accepted_tokens, sess.stats.drafted_tokens
+                w0 = time.perf_counter()
+                got = sess.draft(td, tt, C1_NEW - generated)
+                new = len(got) + (1 if sess.take_rejected_token() is not None else 0)
+                wall_r = time.perf_counter() - w0
+                if len(rec) >= args.warmup:
+                    wall += wall_r
+                generated += new
+                rec.append((new, sess.stats.drafted_tokens - d0, sess.stats.accepted_tokens - s0,
+                            td.ev[-1], tt.ev[-1]))
+        torch.cuda.synchronize()
+        timed = rec[args.warmup:]
+        d_ms = [r[3][0].elapsed_time(r[3][1]) for r in timed]
+        v_ms = [r[4][0].elapsed_time(r[4][1]) for r in timed]
+        toks = sum(r[0] for r in timed)
+        acc = sum(r[2] for r in timed)
+        drafted = sum(r[1] for r in timed)
+        return dict(tokens=toks, draft_ms=sum(d_ms), verify_ms=sum(v_ms), wall=wall,
+                    acceptance_rate=acc / max(drafted, 1), rounds=len(timed),
+                    us_per_verify=statistics.mean(v_ms) * 1e3, us_per_draft=statistics.mean(d_ms) * 1e3)
+
+    if ws > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        g = run_mode(0.0)
+        t1 = run_mode(1.0)
+    dev_s = (g["draft_ms"] + g["verify_ms"]) / 1e3
+    vals = [g["tokens"] / dev_s, g["tokens"] / g["wall"], dev_s, g["wall"]]
+    if ws > 1:
+        t = torch.tensor([dev_s, g["wall"]], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_s, wall = float(t[0]), float(t[1])
+        vals = [ws * g["tokens"] / dev_s, ws * g["tokens"] / wall, dev_s, wall]
+    L, Ld, H, F, D = tm["n_layer"], dm["n_layer"], tm["n_embd"], tm["n_ff"], tm["head_dim"]
+    Hq = tm["n_head"]
+    layer_w = (H * (Hq + 2 * tm["n_head_kv"]) * D + Hq * D * H + 3 * H * F) * 4
+    step_bytes = L * layer_w + V * H * 4  # every f32 weight of the target read once per verify
+    ctx_mean = C1_PROMPT + C1_NEW / 2
+    step_bytes += L * ctx_mean * tm["n_head_kv"] * D * 4 * 2
+    hbm, peak_kind = load_peaks()
+    v_s = g["verify_ms"] / 1e3 / g["rounds"]
+    # launches per round: verify step (tree ancestors, embed, 8 per layer, norm + head,
+    # argmax + walk, commit) and k draft decode steps (the same sequence at L = 1)
+    launches_round = (2 + 8 * L + 2 + 2 + 1) + C1_K * (2 + 8 * Ld + 2 + 2 + 1)
+    N = C1_K + 1
+    h2d = (N * 8 + 8 + pages * 4) + C1_K * (8 + 8 + pages * 4)
+    d2h = (8 + N * 4) + C1_K * (8 + 4)
+    line = {
+        "metric": BASELINE_METRIC, "value": vals[0], "unit": "accepted tokens/s",
+        "n_gpus": ws, "steps": g["rounds"], "warmup": args.warmup,
+        "ms_per_step": dev_s * 1e3 / g["rounds"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "BASELINE config 1: tiny fp32 Llama pair (target 2 layers, draft 1; "
+                               "hidden 256, 4x64 heads, FFN 688, vocab 4096), batch 1, 64-token "
+                               "prompt, k=4, sessions of 128 new tokens",
+                   "parallelism": f"{ws} replicas" if ws > 1 else "single GPU",
+                   "l2": "weights (10.5 MB) are L2-resident by design: latency-bound"},
+        "us_per_verify_step": g["us_per_verify"], "us_per_draft_k4": g["us_per_draft"],
+        "acceptance_rate": g["acceptance_rate"],
+        "t1": {"accepted_tokens_per_s": t1["tokens"] / ((t1["draft_ms"] + t1["verify_ms"]) / 1e3),
+               "us_per_verify_step": t1["us_per_verify"], "us_per_draft_k4": t1["us_per_draft"],
+               "acceptance_rate": t1["acceptance_rate"], "rounds": t1["rounds"]},
+        "e2e": {"value": vals[1], "unit": "accepted tokens/s (wall clock of the Python session "
+                                          "loop over the host-buffer C ABI)",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "achieved": step_bytes / v_s / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": step_bytes / v_s / 1e9 / hbm, "traffic": None,
+                     "peak_kind": peak_kind,
+                     "note": "verify step: target f32 weights + mean-context KV bytes / step time; "
+                             "the step is launch-latency-bound (weights live in L2)"},
+        "gpu_launches": launches_round * g["rounds"],
+        "clocks": clk.summary(),
+    }
+    for c in ctxs:
+        c.close()
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = c1_cpu_baseline()
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def synthetic_ctx(B, seed=0):
     """Per-sequence context lengths U{512..8192}."""
     import synthetic
@@ -702,7 +935,7 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    ap.add_argument("--workload", default="accept", choices=["accept", "q4gemm", "attn", "verify"])
+    ap.add_argument("--workload", default="accept", choices=["accept", "q4gemm", "attn", "verify", "c1"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default="", help="one case of a multi-case workload")
     args = ap.parse_args()
@@ -716,6 +949,8 @@ def main():
         return run_attn(args)
     if args.workload == "verify":
         return run_verify(args)
+    if args.workload == "c1":
+        return run_c1(args)
     return run_cuda(args)
 
 

@@ -16,7 +16,8 @@ import pytest
 import synthetic
 import velo_cuda
 import vo
-from speculative import CudaDraft, CudaTarget, SpeculativeDecoder
+from speculative import (CudaDraft, CudaTarget, NextTokenPrediction, SpeculativeDecoder,
+                         VerifyStep, sample_token)
 from test_speculative_gpu import OracleDraft, OracleTarget
 
 pytestmark = pytest.mark.gpu
@@ -121,5 +122,78 @@ def test_f32_session_matches_oracle():
         dctx.bind_slot(0, np.arange(16))
         out = dec.generate(CudaDraft(dctx, 0, V), CudaTarget(tctx, 0, V), prompt, 128)
     assert out.stats.accepted_tokens > 0
+    assert out.tokens == ref.tokens
+    assert out.stats == ref.stats
+
+
+class _OracleSamplingDraft:
+    """The oracle's draft at T > 0: the same host sampler as CudaDraft."""
+
+    def __init__(self, model, T, rng):
+        self.m, self.T, self.rng, self.tokens, self.last_logits = model, T, rng, [], None
+
+    def draft(self, context, n):
+        common = 0
+        for a, b in zip(self.tokens, context[:-1]):
+            if a != b:
+                break
+            common += 1
+        self.tokens = self.tokens[:common]
+        for i in range(common, len(context) - 1):
+            self.m.forward_one(int(context[i]), i)
+            self.tokens.append(int(context[i]))
+        out, last, lgs = [], int(context[-1]), []
+        for _ in range(n):
+            lg = self.m.forward_one(last, len(self.tokens))
+            self.tokens.append(last)
+            lgs.append(lg)
+            last = sample_token(lg, self.T, self.rng.random())
+            out.append(NextTokenPrediction(last))
+        self.last_logits = np.stack(lgs)
+        return out
+
+
+class _OracleSamplingTarget:
+    def __init__(self, model, T, draft, rng):
+        self.m, self.T, self.draft, self.rng, self.cached = model, T, draft, rng, 0
+
+    def verify(self, context, drafted):
+        for i in range(self.cached, len(context) - 1):
+            self.m.forward_one(int(context[i]), i)
+        pos = len(context) - 1
+        nodes = np.array([context[-1]] + list(drafted), np.uint32)
+        lg = self.m.verify_tree(nodes, np.arange(-1, len(nodes) - 1, dtype=np.int32), pos)
+        u = self.rng.random((1, len(nodes))).astype(np.float32)
+        acc, bonus = vo.accept(lg[None], self.draft.last_logits[None, :len(drafted)],
+                               np.array([drafted], np.uint32), u, self.T)
+        acc, bonus = int(acc[0]), int(bonus[0])
+        self.m.commit_path(list(range(acc + 1)), pos)
+        self.cached = pos + acc + 1
+        return [VerifyStep(t) for t in drafted[:acc]] + [VerifyStep(bonus)] * (len(drafted) - acc)
+
+
+def test_f32_session_sampling_matches_oracle():
+    """The same workload at T = 1.0: the draft samples from its logits, the
+    verify step runs rejection sampling (seeded uniforms shared by both sides).
+    Device and oracle logits differ by <= 1e-4, so the sampled tokens agree
+    unless a uniform lands within that distance of a CDF step."""
+    tm, tw, dm, dw = synthetic.c1_pair()
+    V = tm["n_vocab"]
+    prompt = [int(t) for t in synthetic.rng(0, 91).integers(0, V, 64)]
+    dec = SpeculativeDecoder(4, 4)
+    g = np.random.Generator(np.random.Philox(5))
+    od = _OracleSamplingDraft(vo.Model(dict(dm, n_ctx=512), synthetic.oracle_tensor_list(dm, dw)), 1.0, g)
+    ot = _OracleSamplingTarget(vo.Model(dict(tm, n_ctx=512), synthetic.oracle_tensor_list(tm, tw)),
+                               1.0, od, g)
+    ref = dec.generate(od, ot, prompt, 64)
+    g = np.random.Generator(np.random.Philox(5))
+    with _ctx(pages=16, slots=1) as tctx, _ctx(pages=16, slots=1) as dctx:
+        tctx.load_model(tm, tw)
+        dctx.load_model(dm, dw)
+        tctx.bind_slot(0, np.arange(16))
+        dctx.bind_slot(0, np.arange(16))
+        d = CudaDraft(dctx, 0, V, 1.0, g)
+        out = dec.generate(d, CudaTarget(tctx, 0, V, 1.0, d, g), prompt, 64)
+    assert out.stats.accepted_tokens > 0 and out.stats.rejected_tokens > 0
     assert out.tokens == ref.tokens
     assert out.stats == ref.stats

@@ -189,16 +189,30 @@ class SpeculativeSession:
 
 
 # ---------------------------------------------------------------- device models
+def sample_token(logits, temperature, u):
+    """Inverse-CDF draw from softmax(logits / T) with the uniform u (the draft
+    model's sampler at T > 0; float64 on the host)."""
+    z = np.asarray(logits, np.float64) / temperature
+    p = np.exp(z - z.max())
+    c = np.cumsum(p)
+    return min(int(np.searchsorted(c, u * c[-1], side="right")), len(c) - 1)
+
+
 class CudaTarget:
     """TargetModel over velo_cuda_verify_step for one sequence (`slot`).
 
     The slot's pages hold the K/V of context[:-1]; verify() runs the chain
     [context[-1]] + drafted and commits the accepted path, so the invariant
     holds for the session's next context.  Rows past the first mismatch are
-    not needed by the session and repeat the target's token there."""
+    not needed by the session and repeat the target's token there.
 
-    def __init__(self, ctx, slot, n_vocab, temperature=0.0):
+    temperature > 0: rejection sampling against the draft's distributions
+    (`draft.last_logits`) with uniforms from `rng`; the residual / bonus draw
+    stands at the first rejected position."""
+
+    def __init__(self, ctx, slot, n_vocab, temperature=0.0, draft=None, rng=None):
         self.ctx, self.slot, self.n_vocab, self.T = ctx, slot, n_vocab, temperature
+        self.draft, self.rng = draft, rng
         self.cached = 0  # tokens of the context whose K/V are in the pages
 
     def prefill(self, context):
@@ -213,8 +227,12 @@ class CudaTarget:
         pos = len(context) - 1
         nodes = np.array([context[-1]] + list(drafted), np.uint32)
         parents = np.arange(-1, len(nodes) - 1, dtype=np.int32)
+        kw = {}
+        if self.T > 0 and drafted:
+            kw = dict(temperature=self.T, draft_logits=self.draft.last_logits[None, :len(drafted)],
+                      uniforms=self.rng.random((1, len(nodes))).astype(np.float32))
         r = self.ctx.verify_step([self.slot], [pos], nodes[None], parents[None], commit=True,
-                                 n_vocab=self.n_vocab)
+                                 n_vocab=self.n_vocab, **kw)
         acc, bonus = int(r["accepted_len"][0]), int(r["bonus"][0])
         self.cached = pos + acc + 1
         return ([VerifyStep(t) for t in drafted[:acc]] +
@@ -222,17 +240,19 @@ class CudaTarget:
 
 
 class CudaDraft:
-    """DraftModel: greedy decoding on the device, one verify step per token
-    (commit of every node), cache rewound to the prefix it shares with the
-    session's context."""
+    """DraftModel: decoding on the device, one verify step per token (commit
+    of every node), cache rewound to the prefix it shares with the session's
+    context.  Greedy at temperature 0, else each token drawn from the step's
+    logits (sample_token) and the logits kept in `last_logits` for the
+    target's rejection sampling."""
 
-    def __init__(self, ctx, slot, n_vocab):
-        self.ctx, self.slot, self.n_vocab = ctx, slot, n_vocab
+    def __init__(self, ctx, slot, n_vocab, temperature=0.0, rng=None):
+        self.ctx, self.slot, self.n_vocab, self.T, self.rng = ctx, slot, n_vocab, temperature, rng
         self.tokens = []  # tokens whose K/V are in the draft's pages
+        self.last_logits = None
 
-    def draft(self, context, max_tokens):
-        if max_tokens <= 0:
-            return []
+    def prefill(self, context):
+        """Rewind to the prefix shared with context[:-1], then fill the rest."""
         common = 0
         for a, b in zip(self.tokens, context[:-1]):
             if a != b:
@@ -243,13 +263,25 @@ class CudaDraft:
             velo_cuda.prefill(self.ctx, self.slot, context[common:-1], pos0=common,
                               n_vocab=self.n_vocab)
             self.tokens = list(context[:-1])
-        out, last = [], context[-1]
+
+    def draft(self, context, max_tokens):
+        if max_tokens <= 0:
+            return []
+        self.prefill(context)
+        out, last, logits = [], context[-1], []
         for _ in range(max_tokens):
             pos = len(self.tokens)
             r = self.ctx.verify_step([self.slot], [pos], np.array([[last]], np.uint32),
                                      np.array([[-1]], np.int32), commit="all",
-                                     n_vocab=self.n_vocab)
+                                     want_logits=self.T > 0, n_vocab=self.n_vocab)
             self.tokens.append(last)
-            last = int(r["bonus"][0])
+            if self.T > 0:
+                lg = r["logits"][0, 0]
+                logits.append(lg)
+                last = sample_token(lg, self.T, self.rng.random())
+            else:
+                last = int(r["bonus"][0])
             out.append(NextTokenPrediction(last))
+        if self.T > 0:
+            self.last_logits = np.stack(logits)
         return out
