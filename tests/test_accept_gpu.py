@@ -90,3 +90,17 @@ def test_invalid_token_is_rejected_on_host(ctx):
     with pytest.raises(velo_cuda.VeloError) as e:
         ctx.accept(tgt, drf, tok, u, 0.8)
     assert e.value.status == velo_cuda.ERR_INVALID_ARGUMENT
+
+
+def test_shape_changes_reuse_tag_block(ctx):
+    """One context, launches of changing shapes (the fused kernel's tag block
+    holds words of earlier launches at other offsets) and the one-kernel /
+    two-kernel boundary (2k+1 rows <= 32 vs more): every launch bit-exact."""
+    shapes = [(64, 8, 32000), (3, 15, 4096), (9, 16, 4096), (64, 8, 32000), (2, 1, 64000),
+              (17, 7, 2048), (3, 15, 4096)]
+    for n, (B, k, V) in enumerate(shapes):
+        for T in (0.9, 0.0):
+            tgt, drf, tok, u = synthetic.acceptance_inputs(B, k, V, temperature=T or 0.9, seed=n)
+            (ag, bg), (ar, br) = _both(ctx, tgt, drf, tok, u, T)
+            assert np.array_equal(ag, ar), (B, k, V, T)
+            assert np.array_equal(bg, br), (B, k, V, T)

@@ -76,10 +76,14 @@ __device__ __forceinline__ bool elem_valid(int V, int t, int lane, int i, int c)
 // (m_t, z_t) of the spec for one tile.
 template <bool kFullTile>
 __device__ __forceinline__ float2 tile_stats(const float* x, int V, int t, int lane, float inv_t) {
-    float mx = max3(x[0], x[1], x[2]);
+    // maximum as a tree (max is exact in any order): 32 -> 11 -> 4 -> 1
+    float m1[11];
 #pragma unroll
-    for (int j = 3; j + 1 < 32; j += 2) mx = max3(mx, x[j], x[j + 1]);
-    mx = fmaxf(mx, x[31]);
+    for (int j = 0; j < 10; ++j) m1[j] = max3(x[3 * j], x[3 * j + 1], x[3 * j + 2]);
+    m1[10] = fmaxf(x[30], x[31]);
+    const float m2a = max3(m1[0], m1[1], m1[2]), m2b = max3(m1[3], m1[4], m1[5]);
+    const float m2c = max3(m1[6], m1[7], m1[8]), m2d = fmaxf(m1[9], m1[10]);
+    float mx = fmaxf(max3(m2a, m2b, m2c), m2d);
     mx = warp_max(mx);
     const float m = __fmul_rn(mx, inv_t);
     const float2 it = f2(inv_t), nm = f2(-m);
@@ -206,32 +210,29 @@ __device__ __forceinline__ float2 elem_weight2(const Draw& d, float inv_t, float
 }
 
 // Weigh tile t of the draw row pair: lane weight -> lane_w[t*32 + lane],
-// tile weight (warp butterfly) -> tile_w[t].
+// tile weight (warp butterfly) -> tile_w[t].  Both rows' tile is loaded up
+// front (one round trip to memory).
 __device__ void weigh_tile(const AcceptParams& p, const float* trow, const float* drow,
                            const Draw& d, int t, int lane, float* lane_w, float* tile_w) {
     const bool full = (t + 1) * kTile <= p.V;
+    float tx[32], dx[32];
+    load_groups<8>(trow, p.V, t, lane, 0, p.vec4, tx);
+    if (d.resid) load_groups<8>(drow, p.V, t, lane, 0, p.vec4, dx);
     float2 a01 = f2(0.0f), a23 = f2(0.0f);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {  // halves (i < 4, i >= 4) bound the registers
-        float tx[16], dx[16];
-        load_groups<4>(trow, p.V, t, lane, 4 * h, p.vec4, tx);
-        if (d.resid) load_groups<4>(drow, p.V, t, lane, 4 * h, p.vec4, dx);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int i = 4 * h + q;
-            float2 w01 = elem_weight2(d, p.inv_t, make_float2(tx[4 * q], tx[4 * q + 1]),
-                                      d.resid ? make_float2(dx[4 * q], dx[4 * q + 1]) : f2(0.0f));
-            float2 w23 = elem_weight2(d, p.inv_t, make_float2(tx[4 * q + 2], tx[4 * q + 3]),
-                                      d.resid ? make_float2(dx[4 * q + 2], dx[4 * q + 3]) : f2(0.0f));
-            if (!full) {
-                if (!elem_valid(p.V, t, lane, i, 0)) w01.x = 0.0f;
-                if (!elem_valid(p.V, t, lane, i, 1)) w01.y = 0.0f;
-                if (!elem_valid(p.V, t, lane, i, 2)) w23.x = 0.0f;
-                if (!elem_valid(p.V, t, lane, i, 3)) w23.y = 0.0f;
-            }
-            a01 = __fadd2_rn(a01, w01);
-            a23 = __fadd2_rn(a23, w23);
+    for (int i = 0; i < 8; ++i) {
+        float2 w01 = elem_weight2(d, p.inv_t, make_float2(tx[4 * i], tx[4 * i + 1]),
+                                  d.resid ? make_float2(dx[4 * i], dx[4 * i + 1]) : f2(0.0f));
+        float2 w23 = elem_weight2(d, p.inv_t, make_float2(tx[4 * i + 2], tx[4 * i + 3]),
+                                  d.resid ? make_float2(dx[4 * i + 2], dx[4 * i + 3]) : f2(0.0f));
+        if (!full) {
+            if (!elem_valid(p.V, t, lane, i, 0)) w01.x = 0.0f;
+            if (!elem_valid(p.V, t, lane, i, 1)) w01.y = 0.0f;
+            if (!elem_valid(p.V, t, lane, i, 2)) w23.x = 0.0f;
+            if (!elem_valid(p.V, t, lane, i, 3)) w23.y = 0.0f;
         }
+        a01 = __fadd2_rn(a01, w01);
+        a23 = __fadd2_rn(a23, w23);
     }
     const float lw = lane_combine(a01, a23);
     lane_w[t * 32 + lane] = lw;
