@@ -572,6 +572,18 @@ def c3_model_tensors(meta, seed=0):
     return t
 
 
+def verify_cpu_token_seconds(meta, tensors, ctx_len):
+    """Seconds of one forward_one of the CPU port (oracle, one thread) at
+    position ctx_len - 1 of the config-3 model: matvecs of every layer plus
+    attention over ctx_len cached positions (zero K/V: same arithmetic)."""
+    import synthetic
+    import vo
+    m = vo.Model(dict(meta, n_ctx=ctx_len), synthetic.oracle_tensor_list(meta, tensors))
+    t0 = time.perf_counter()
+    m.forward_one(1, ctx_len - 1)
+    return time.perf_counter() - t0
+
+
 def run_verify(args):
     """The whole verify step at BASELINE config 3: Llama-2-7B shape in q4_0,
     B=32 sequences of context 2048 in 16-token fp16 pages, a 16-node draft
@@ -603,6 +615,9 @@ def run_verify(args):
     t0 = time.time()
     ctx.load_model(meta, tensors)
     load_s = time.time() - t0
+    cpu_token_s = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu_token_s = verify_cpu_token_seconds(meta, tensors, ctx_len)
     del tensors
     for b in range(B):
         ctx.bind_slot(b, np.arange(b * per_seq, (b + 1) * per_seq))
@@ -662,6 +677,15 @@ def run_verify(args):
             "model_gen_s": gen_s, "load_s": load_s,
             "data": "random-init N(0,0.02^2) weights quantised to q4_0 on the device; "
                     "KV pages zero-filled (timing does not depend on their values)"}
+    if cpu_token_s is not None:
+        cpu_step = cpu_token_s * M  # the reference runs forward_one once per tree node
+        line["cpu_baseline"] = {
+            "value": (acc_tok / steps) / cpu_step, "unit": "accepted tokens/s", "cores": 1,
+            "kind": "port", "us_per_step": cpu_step * 1e6,
+            "sample": f"one forward_one of the CPU port (llama_cpu.rs restatement, single thread) at "
+                      f"position {ctx_len - 1} over all {meta['n_layer']} layers took "
+                      f"{cpu_token_s:.2f} s; a verify step is {M} such calls (B x nodes), "
+                      f"extrapolated linearly"}
     ctx.close()
     if ws > 1:
         dist.barrier()

@@ -296,7 +296,27 @@ __global__ void kv_commit_kernel(const KvCommitArgs a) {
     }
 }
 
+__global__ void chain_commit_kernel(const uint32_t* __restrict__ expected, int B, int N,
+                                    int32_t* __restrict__ path, int32_t* __restrict__ path_len,
+                                    uint32_t* __restrict__ bonus) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * N) return;
+    const int b = i / N, n = i - b * N;
+    path[i] = n;
+    if (n == N - 1) {
+        path_len[b] = N;
+        bonus[b] = expected[i];
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_chain_commit(const uint32_t* expected, int B, int N, int32_t* path,
+                                int32_t* path_len, uint32_t* bonus, cudaStream_t s) {
+    if (B * N == 0) return cudaSuccess;
+    chain_commit_kernel<<<(B * N + 127) / 128, 128, 0, s>>>(expected, B, N, path, path_len, bonus);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_embed(const float* emb, const uint32_t* tokens, int M, int H, int V, float* x,
                          int* err, cudaStream_t s) {

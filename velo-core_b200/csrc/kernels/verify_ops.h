@@ -45,6 +45,11 @@ cudaError_t launch_row_argmax_pairs(const float* logits, int M, int v_loc, int v
 // to the larger index = the later shard, as one pass over the whole row).
 cudaError_t launch_argmax_combine(const int2* pairs, int tp, int M, uint32_t* expected, cudaStream_t s);
 
+// Commit of whole chains (prefill / draft decode): path[b] = 0..N-1,
+// path_len[b] = N, bonus[b] = expected[b][N-1].
+cudaError_t launch_chain_commit(const uint32_t* expected, int B, int N, int32_t* path,
+                                int32_t* path_len, uint32_t* bonus, cudaStream_t s);
+
 // Greedy tree walk alone, on precomputed expected tokens.
 cudaError_t launch_tree_walk(const uint32_t* tokens, const int32_t* parents, const uint32_t* expected,
                              int B, int N, int32_t* path, int32_t* path_len, uint32_t* bonus,

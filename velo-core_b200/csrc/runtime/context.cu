@@ -146,6 +146,8 @@ int32_t velo_cuda_create(const velo_cuda_config* cfg, int32_t device, int32_t tp
     cudaError_t e = cudaSetDevice(device);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&c->err_flag, sizeof(int));
+    if (e == cudaSuccess) e = cudaMallocHost(&c->err_host, sizeof(int));
+    if (e == cudaSuccess) *c->err_host = 0;
     if (e == cudaSuccess) e = cudaMemsetAsync(c->err_flag, 0, sizeof(int), c->own_stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->own_stream);
     if (e != cudaSuccess) {
@@ -205,6 +207,7 @@ void velo_cuda_destroy(velo_cuda_ctx* c) {
         c->nccl_comm = nullptr;
     }
     if (c->err_flag) cudaFree(c->err_flag);
+    if (c->err_host) cudaFreeHost(c->err_host);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     delete c;
 }
@@ -218,24 +221,34 @@ int32_t velo_cuda_set_stream(velo_cuda_ctx* c, void* stream) {
 int32_t velo_cuda_sync(velo_cuda_ctx* c, int64_t timeout_ns) {
     if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
     cudaSetDevice(c->device);
-    const auto start = std::chrono::steady_clock::now();
-    for (;;) {
-        cudaError_t e = cudaStreamQuery(c->stream);
-        if (e == cudaSuccess) break;
-        if (e != cudaErrorNotReady)
-            return fail(VELO_ERR_CUDA, "stream error: %s", cudaGetErrorString(e));
-        if (timeout_ns >= 0) {
+    // the device error word rides along with the stream's work
+    VELO_CUDA_TRY(cudaMemcpyAsync(c->err_host, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost,
+                                  c->stream));
+    if (timeout_ns < 0) {
+        cudaError_t e = cudaStreamSynchronize(c->stream);
+        if (e != cudaSuccess) return fail(VELO_ERR_CUDA, "stream error: %s", cudaGetErrorString(e));
+    } else {
+        // poll: yield for the first 200 us (short steps finish here), then sleep
+        const auto start = std::chrono::steady_clock::now();
+        for (;;) {
+            cudaError_t e = cudaStreamQuery(c->stream);
+            if (e == cudaSuccess) break;
+            if (e != cudaErrorNotReady)
+                return fail(VELO_ERR_CUDA, "stream error: %s", cudaGetErrorString(e));
             auto el = std::chrono::duration_cast<std::chrono::nanoseconds>(
                           std::chrono::steady_clock::now() - start).count();
             if (el > timeout_ns)
                 return fail(VELO_ERR_TIMEOUT, "velo_cuda_sync: work still running after %lld ns",
                             (long long)timeout_ns);
+            if (el < 200000)
+                std::this_thread::yield();
+            else
+                std::this_thread::sleep_for(std::chrono::microseconds(20));
         }
-        std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
-    int flag = 0;
-    VELO_CUDA_TRY(cudaMemcpy(&flag, c->err_flag, sizeof(int), cudaMemcpyDeviceToHost));
+    const int flag = *c->err_host;
     if (flag) {
+        *c->err_host = 0;
         VELO_CUDA_TRY(cudaMemset(c->err_flag, 0, sizeof(int)));
         return fail(VELO_ERR_DEVICE_FLAG, "a kernel flagged invalid input (code %d)", flag);
     }

@@ -63,6 +63,7 @@ struct velo_cuda_ctx {
     velo::DeviceBuffer io;         // device copies for the host-buffer entries
     velo::DeviceBuffer attn_ws;    // tree attention: ancestor masks
     int* err_flag = nullptr;       // device-side input flag
+    int* err_host = nullptr;       // pinned host copy of err_flag (read at sync)
     velo::Model* model = nullptr;  // weights, KV pool and verify buffers (velo_cuda_load_model)
     void* nccl_comm = nullptr;     // ncclComm_t of the tensor-parallel group (tp_size > 1)
 };

@@ -83,11 +83,25 @@ struct Model {
     int2* pairs_all = nullptr; // [tp][M]
     float* logits_all = nullptr;  // [tp][M][V_loc] (logits requested, tp > 1)
     size_t logits_all_cap = 0;
+    // per-step inputs, one device block filled by one copy from a pinned
+    // host mirror: tokens [M] | parents [M] | ctxlen [B] | slots [B] | pt_batch [B][max_pages]
+    uint8_t* din = nullptr;
+    uint8_t* hin = nullptr;
+    size_t in_bytes = 0;
     uint32_t* tokens = nullptr;
     int32_t* parents = nullptr;
     int32_t* ctxlen = nullptr;
     uint32_t* slots = nullptr;
     uint32_t* pt_batch = nullptr;  // [B][max_pages] gathered rows
+    // per-step outputs, one device block read back by one copy into pinned
+    // memory: path_len [B] | bonus [B] | path [M]
+    uint8_t* dout = nullptr;
+    uint8_t* hout = nullptr;
+    bool staging_busy = false;  // a step's copies may still use hin / hout
+    // CUDA graphs of the step's launch sequence, one per (B, N, commit mode),
+    // valid while the work buffers keep their addresses
+    std::map<uint64_t, cudaGraphExec_t> graphs;
+    bool graphs_off = false;    // capture refused on the stream in use
     uint64_t* anc = nullptr;
     uint32_t* expected = nullptr;
     int32_t* path = nullptr;
@@ -114,6 +128,9 @@ void destroy_model(Model* m) {
     if (!m) return;
     for (void* p : m->allocs) cudaFree(p);
     for (void* p : m->work) cudaFree(p);
+    if (m->hin) cudaFreeHost(m->hin);
+    if (m->hout) cudaFreeHost(m->hout);
+    for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     if (m->drf) cudaFree(m->drf);
     if (m->logits_all) cudaFree(m->logits_all);
     delete m;
@@ -262,6 +279,8 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
     const int M = B * N;
     if (M <= m->cap_M && B <= m->cap_B) return VELO_OK;
     VELO_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);  // they name the old buffers
+    m->graphs.clear();
     for (void* p : m->work) cudaFree(p);
     m->work.clear();
     const int cM = M > m->cap_M ? M : m->cap_M, cB = B > m->cap_B ? B : m->cap_B;
@@ -289,18 +308,26 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
     if (!st && m->tp > 1) st = dev_alloc(m, &m->y, (size_t)cM * H * 4, true);
     if (!st) st = dev_alloc(m, &m->pairs, (size_t)cM * 8, true);
     if (!st) st = dev_alloc(m, &m->pairs_all, (size_t)cM * 8 * m->tp, true);
-    if (!st) st = dev_alloc(m, &m->tokens, (size_t)cM * 4, true);
-    if (!st) st = dev_alloc(m, &m->parents, (size_t)cM * 4, true);
+
     if (!st) st = dev_alloc(m, &m->anc, (size_t)cM * 8, true);
     if (!st) st = dev_alloc(m, &m->expected, (size_t)cM * 4, true);
-    if (!st) st = dev_alloc(m, &m->path, (size_t)cM * 4, true);
+
     if (!st) st = dev_alloc(m, &m->dtok, (size_t)cM * 4, true);
     if (!st) st = dev_alloc(m, &m->uni, (size_t)cM * 4, true);
-    if (!st) st = dev_alloc(m, &m->ctxlen, (size_t)cB * 4, true);
-    if (!st) st = dev_alloc(m, &m->slots, (size_t)cB * 4, true);
-    if (!st) st = dev_alloc(m, &m->pt_batch, (size_t)cB * (m->max_pages ? m->max_pages : 1) * 4, true);
-    if (!st) st = dev_alloc(m, &m->path_len, (size_t)cB * 4, true);
-    if (!st) st = dev_alloc(m, &m->bonus, (size_t)cB * 4, true);
+    // packed step I/O (4-byte words)
+    const size_t mp = m->max_pages ? m->max_pages : 1;
+    m->in_bytes = ((size_t)2 * cM + 2 * cB + cB * mp) * 4;
+    const size_t out_bytes = ((size_t)2 * cB + cM) * 4;
+    if (!st) st = dev_alloc(m, &m->din, m->in_bytes, true);
+    if (!st) st = dev_alloc(m, &m->dout, out_bytes, true);
+    if (!st) {
+        if (m->hin) cudaFreeHost(m->hin);
+        if (m->hout) cudaFreeHost(m->hout);
+        m->hin = m->hout = nullptr;
+        cudaError_t e = cudaMallocHost(&m->hin, m->in_bytes);
+        if (e == cudaSuccess) e = cudaMallocHost(&m->hout, out_bytes);
+        if (e != cudaSuccess) st = fail(VELO_ERR_OUT_OF_MEMORY, "pinned staging: %s", cudaGetErrorString(e));
+    }
     if (!st) st = dev_alloc(m, &m->acc, (size_t)cB * 4, true);
     if (st) {
         m->cap_M = m->cap_B = 0;
@@ -753,16 +780,34 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     cudaStream_t s = c->stream;
     const int M = B * N, H = m->H(), Hq = m->Hq(), Hkv = m->Hkv(), F = m->F(), L = m->L();
     const int Nqkv = (Hq + 2 * Hkv) * 128;
-    // inputs and the batch's page-table rows
-    std::vector<uint32_t> ptb((size_t)B * m->max_pages);
-    for (int b = 0; b < B; ++b)
-        std::memcpy(ptb.data() + (size_t)b * m->max_pages,
-                    m->page_table_host.data() + (size_t)in->slots[b] * m->max_pages, (size_t)m->max_pages * 4);
-    VELO_CUDA_TRY(cudaMemcpyAsync(m->tokens, in->tokens, (size_t)M * 4, cudaMemcpyHostToDevice, s));
-    VELO_CUDA_TRY(cudaMemcpyAsync(m->parents, in->parents, (size_t)M * 4, cudaMemcpyHostToDevice, s));
-    VELO_CUDA_TRY(cudaMemcpyAsync(m->ctxlen, in->ctx_len, (size_t)B * 4, cudaMemcpyHostToDevice, s));
-    VELO_CUDA_TRY(cudaMemcpyAsync(m->slots, in->slots, (size_t)B * 4, cudaMemcpyHostToDevice, s));
-    VELO_CUDA_TRY(cudaMemcpyAsync(m->pt_batch, ptb.data(), ptb.size() * 4, cudaMemcpyHostToDevice, s));
+    // inputs and the batch's page-table rows: packed into pinned memory, one copy
+    const size_t mp = (size_t)m->max_pages;
+    m->tokens = reinterpret_cast<uint32_t*>(m->din);
+    m->parents = reinterpret_cast<int32_t*>(m->tokens + M);
+    m->ctxlen = m->parents + M;
+    m->slots = reinterpret_cast<uint32_t*>(m->ctxlen + B);
+    m->pt_batch = m->slots + B;
+    m->path_len = reinterpret_cast<int32_t*>(m->dout);
+    m->bonus = reinterpret_cast<uint32_t*>(m->path_len + B);
+    m->path = reinterpret_cast<int32_t*>(m->bonus + B);
+    if (m->staging_busy) VELO_CUDA_TRY(cudaStreamSynchronize(s));  // an earlier step ended early
+    m->staging_busy = true;
+    {
+        uint32_t* h = reinterpret_cast<uint32_t*>(m->hin);
+        std::memcpy(h, in->tokens, (size_t)M * 4);
+        std::memcpy(h + M, in->parents, (size_t)M * 4);
+        std::memcpy(h + 2 * M, in->ctx_len, (size_t)B * 4);
+        std::memcpy(h + 2 * M + B, in->slots, (size_t)B * 4);
+        for (int b = 0; b < B; ++b)
+            std::memcpy(h + 2 * M + 2 * B + (size_t)b * mp,
+                        m->page_table_host.data() + (size_t)in->slots[b] * mp, mp * 4);
+        VELO_CUDA_TRY(cudaMemcpyAsync(m->din, m->hin, ((size_t)2 * M + 2 * B + B * mp) * 4,
+                                      cudaMemcpyHostToDevice, s));
+    }
+    const int Vl = m->V_loc;
+    // the launch sequence of the step, from the ancestor masks to the KV commit
+    auto body = [&]() -> int32_t {
+    int32_t st = VELO_OK;
     VELO_CUDA_TRY(velo::launch_tree_ancestors(m->parents, B, N, m->anc, c->err_flag, s));
     VELO_CUDA_TRY(velo::launch_embed(m->emb, m->tokens, M, H, m->V(), m->x, c->err_flag, s));
     const float eps = m->meta.norm_eps;
@@ -820,7 +865,6 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         }
         if (st) return st;
     }
-    const int Vl = m->V_loc;
     if (!m->f32) {
         VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, m->out_norm, M, H, eps, m->xn, s));
         st = velo::gemm(c, m->lm_head, m->xn, M, Vl, H, m->logits, Vl, velo::kEpiStoreF32);
@@ -880,15 +924,7 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     if (in->commit == 2) {
         // prefill / draft decode: the whole chain is committed and reported as
         // accepted; the bonus is the argmax after the last node
-        VELO_CUDA_TRY(cudaMemcpy2DAsync(m->bonus, sizeof(uint32_t), m->expected + (N - 1),
-                                        (size_t)N * sizeof(uint32_t), sizeof(uint32_t), (size_t)B,
-                                        cudaMemcpyDeviceToDevice, s));
-        std::vector<int32_t> path((size_t)M), plen(B, N);
-        for (int b = 0; b < B; ++b)
-            for (int i = 0; i < N; ++i) path[(size_t)b * N + i] = i;
-        VELO_CUDA_TRY(cudaMemcpyAsync(m->path, path.data(), path.size() * 4, cudaMemcpyHostToDevice, s));
-        VELO_CUDA_TRY(cudaMemcpyAsync(m->path_len, plen.data(), plen.size() * 4, cudaMemcpyHostToDevice, s));
-        VELO_CUDA_TRY(cudaStreamSynchronize(s));  // host vectors go out of scope
+        VELO_CUDA_TRY(velo::launch_chain_commit(m->expected, B, N, m->path, m->path_len, m->bonus, s));
     }
     if (in->commit && m->f32) {
         velo::KvCommitF32Args a{};
@@ -933,11 +969,45 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         a.err = c->err_flag;
         VELO_CUDA_TRY(velo::launch_kv_commit(a, s));
     }
-    std::vector<int32_t> plen(B);
-    VELO_CUDA_TRY(cudaMemcpyAsync(plen.data(), m->path_len, (size_t)B * 4, cudaMemcpyDeviceToHost, s));
-    VELO_CUDA_TRY(cudaMemcpyAsync(out->bonus_token, m->bonus, (size_t)B * 4, cudaMemcpyDeviceToHost, s));
-    if (out->accepted_nodes)
-        VELO_CUDA_TRY(cudaMemcpyAsync(out->accepted_nodes, m->path, (size_t)M * 4, cudaMemcpyDeviceToHost, s));
+    return st;
+    };  // body
+
+    // Greedy single-GPU steps replay a captured graph of the body (one
+    // launch instead of ~25); sampling (host round trip) and tensor-parallel
+    // steps run it directly.
+    const bool graphable = m->tp == 1 && !(sampling && N > 1) && !m->graphs_off;
+    if (graphable) {
+        const uint64_t key = ((uint64_t)B << 32) | ((uint64_t)N << 8) | (uint64_t)in->commit;
+        auto it = m->graphs.find(key);
+        if (it == m->graphs.end()) {
+            if (cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+                cudaGetLastError();
+                m->graphs_off = true;  // e.g. the legacy default stream: launch directly
+                st = body();
+                if (st) return st;
+            } else {
+                const int32_t bst = body();
+                cudaGraph_t g = nullptr;
+                const cudaError_t e = cudaStreamEndCapture(s, &g);
+                if (bst) {
+                    if (g) cudaGraphDestroy(g);
+                    return bst;
+                }
+                if (e != cudaSuccess) return fail(VELO_ERR_CUDA, "graph capture: %s", cudaGetErrorString(e));
+                cudaGraphExec_t exec = nullptr;
+                const cudaError_t ei = cudaGraphInstantiate(&exec, g, 0);
+                cudaGraphDestroy(g);
+                if (ei != cudaSuccess) return fail(VELO_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ei));
+                it = m->graphs.emplace(key, exec).first;
+            }
+        }
+        if (it != m->graphs.end()) VELO_CUDA_TRY(cudaGraphLaunch(it->second, s));
+    } else {
+        st = body();
+        if (st) return st;
+    }
+    // path_len | bonus | path: one copy into pinned memory
+    VELO_CUDA_TRY(cudaMemcpyAsync(m->hout, m->dout, ((size_t)2 * B + M) * 4, cudaMemcpyDeviceToHost, s));
     std::vector<float> gathered;
     if (out->logits && m->tp == 1)
         VELO_CUDA_TRY(cudaMemcpyAsync(out->logits, m->logits, (size_t)M * V * 4, cudaMemcpyDeviceToHost, s));
@@ -962,12 +1032,16 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     }
     st = velo_cuda_sync(c, -1);
     if (st) return st;
+    m->staging_busy = false;
     if (!gathered.empty())  // [tp][M][Vl] -> [M][V]
         for (int r = 0; r < m->tp; ++r)
             for (int i = 0; i < M; ++i)
                 std::memcpy(out->logits + (size_t)i * V + (size_t)r * Vl,
                             gathered.data() + ((size_t)r * M + i) * Vl, (size_t)Vl * 4);
-    for (int b = 0; b < B; ++b) out->accepted_len[b] = plen[b] - 1;
+    const int32_t* hp = reinterpret_cast<const int32_t*>(m->hout);
+    for (int b = 0; b < B; ++b) out->accepted_len[b] = hp[b] - 1;
+    std::memcpy(out->bonus_token, hp + B, (size_t)B * 4);
+    if (out->accepted_nodes) std::memcpy(out->accepted_nodes, hp + 2 * B, (size_t)M * 4);
     return VELO_OK;
 }
 
