@@ -525,9 +525,17 @@ C3_META = dict(n_vocab=32000, n_embd=4096, n_layer=32, n_head=32, n_head_kv=32, 
 C3_TREE = [-1, 0, 0, 0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 5, 6]  # (4,2,2) breadth-first to 16 nodes
 
 
-def _q4_device(w):
+C5_META = dict(n_vocab=128256, n_embd=8192, n_layer=80, n_head=64, n_head_kv=8, n_ff=28672,
+               head_dim=128, rope_freq_base=500000.0, norm_eps=1e-5)
+# branching (4, 2, 2, 2, ...) filled breadth-first to 32 nodes
+C5_TREE = ([-1, 0, 0, 0, 0] + [1 + i // 2 for i in range(8)] + [5 + i // 2 for i in range(16)]
+           + [13 + i // 2 for i in range(3)])
+
+
+def _q4_device(w, keep_on_device=False):
     """q4_0 bytes of a device f32 matrix [rows][cols] (the rule of
-    synthetic.quantize_q4_0, on the GPU): returns host uint8 [rows][cols/32*18]."""
+    synthetic.quantize_q4_0, on the GPU): uint8 [rows][cols/32*18], on the host
+    (numpy) or left on the device."""
     import torch
     rows, cols = w.shape
     xb = w.view(rows, cols // 32, 32)
@@ -539,7 +547,45 @@ def _q4_device(w):
     out = torch.empty((rows, cols // 32, 18), dtype=torch.uint8, device=w.device)
     out[..., 0:2] = d.half().view(torch.uint8).view(rows, cols // 32, 2)
     out[..., 2:] = q[..., 0::2] | (q[..., 1::2] << 4)
-    return out.view(rows, -1).cpu().numpy()
+    out = out.view(rows, -1)
+    return out if keep_on_device else out.cpu().numpy()
+
+
+def c5_shard_tensors(meta, tp, rank, seed=0):
+    """This rank's shards of a Llama-3-70B-shape model:
+    random N(0, 0.02^2) matrices quantised to q4_0 and an f32 embedding, all
+    generated on the device and handed to the loader as device tensors (no
+    host copy of the 39 GB of weights).  Shard shapes follow sharding.rs
+    (column split of q/k/v/w1/w3/output, row split of wo/w2)."""
+    import torch
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed * 1000 + rank)
+    H, V, F, L = meta["n_embd"], meta["n_vocab"], meta["n_ff"] // tp, meta["n_layer"]
+    Dq, Dk, Vl = meta["n_head"] // tp * 128, meta["n_head_kv"] // tp * 128, V // tp
+
+    def q4(rows, cols):
+        w = torch.randn((rows, cols), generator=g, device="cuda") * 0.02
+        q = _q4_device(w, keep_on_device=True)
+        del w
+        return (2, q, rows, cols)
+
+    def norm():
+        return (0, 1.0 + 0.1 * torch.randn(H, generator=g, device="cuda"), 1, H)
+
+    t = {"token_embd.weight": (0, torch.randn((V, H), generator=g, device="cuda") * 0.02, V, H),
+         "output_norm.weight": norm(), "output.weight": q4(Vl, H)}
+    for l in range(L):
+        p = f"layers.{l}."
+        t[p + "attention_norm.weight"] = norm()
+        t[p + "attention.wq.weight"] = q4(Dq, H)
+        t[p + "attention.wk.weight"] = q4(Dk, H)
+        t[p + "attention.wv.weight"] = q4(Dk, H)
+        t[p + "attention.wo.weight"] = q4(H, Dq)
+        t[p + "ffn_norm.weight"] = norm()
+        t[p + "feed_forward.w1.weight"] = q4(F, H)
+        t[p + "feed_forward.w2.weight"] = q4(H, F)
+        t[p + "feed_forward.w3.weight"] = q4(F, H)
+    return t
 
 
 def c3_model_tensors(meta, seed=0):
@@ -603,27 +649,31 @@ def run_verify(args):
         box = [velo_cuda.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         nid = box[0]
-    meta = dict(C3_META)
-    B, ctx_len = 32, 2048
-    N = len(C3_TREE)
+    c5 = args.case == "c5"
+    meta = dict(C5_META if c5 else C3_META)
+    tree = C5_TREE if c5 else C3_TREE
+    B, ctx_len = (64, 4096) if c5 else (32, 2048)
+    N = len(tree)
     per_seq = (ctx_len + N + 15) // 16
     t0 = time.time()
-    tensors = c3_model_tensors(meta)
+    tensors = c5_shard_tensors(meta, ws, rank) if c5 else c3_model_tensors(meta)
+    torch.cuda.synchronize()
     gen_s = time.time() - t0
     ctx = velo_cuda.Context(device=local, total_pages=B * per_seq, max_slots=B,
                             max_pages_per_slot=per_seq, tp_rank=rank, tp_size=ws, nccl_id=nid)
     t0 = time.time()
-    ctx.load_model(meta, tensors)
+    ctx.load_model(meta, tensors, shards=c5)
     load_s = time.time() - t0
     cpu_token_s = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and not args.no_cpu_baseline and not c5:
         cpu_token_s = verify_cpu_token_seconds(meta, tensors, ctx_len)
     del tensors
+    torch.cuda.empty_cache()
     for b in range(B):
         ctx.bind_slot(b, np.arange(b * per_seq, (b + 1) * per_seq))
     g = np.random.Generator(np.random.Philox(7))
     tokens = g.integers(0, meta["n_vocab"], (B, N)).astype(np.uint32)
-    parents = np.tile(np.array(C3_TREE, np.int32), (B, 1))
+    parents = np.tile(np.array(tree, np.int32), (B, 1))
     slots = np.arange(B, dtype=np.uint32)
     ctxl = np.full(B, ctx_len, np.int32)
     stream = torch.cuda.Stream()
@@ -665,8 +715,10 @@ def run_verify(args):
     tfl = float(peaks.get("bf16_tflops_sustained", 1416.2))
     hbm = float(peaks.get("hbm_gbs", HBM_FALLBACK_GBS))
     floor_ms = (flops / (tfl * 1e12) + kv_bytes / (hbm * 1e9)) * 1e3 / ws
-    line = {"workload": "verify step, BASELINE config 3 (Llama-2-7B shape q4_0, B=32, "
-                        "16-node tree, ctx 2048 fp16 pages)",
+    wl = ("verify step, BASELINE config 5 (Llama-3-70B shape q4_0, B=64, 32-node tree, ctx 4096 "
+          "fp16 pages)" if c5 else
+          "verify step, BASELINE config 3 (Llama-2-7B shape q4_0, B=32, 16-node tree, ctx 2048 fp16 pages)")
+    line = {"workload": wl,
             "n_gpus": ws, "parallelism": f"tp{ws}" if ws > 1 else "single GPU",
             "scaling": "strong", "us_per_step": ms * 1e3,
             "accepted_tokens_per_s": acc_tok / steps / (ms / 1e3),
@@ -675,8 +727,9 @@ def run_verify(args):
             "floor_ms_at_measured_peaks": floor_ms, "frac_of_floor": floor_ms / ms,
             "accepted_per_step": acc_tok / steps, "clocks": clk.summary(),
             "model_gen_s": gen_s, "load_s": load_s,
-            "data": "random-init N(0,0.02^2) weights quantised to q4_0 on the device; "
-                    "KV pages zero-filled (timing does not depend on their values)"}
+            "data": "random-init N(0,0.02^2) weights quantised to q4_0 on the device"
+                    + ("; each rank generates its own shards, passed as device tensors" if c5 else "")
+                    + "; KV pages zero-filled (timing does not depend on their values)"}
     if cpu_token_s is not None:
         cpu_step = cpu_token_s * M  # the reference runs forward_one once per tree node
         line["cpu_baseline"] = {

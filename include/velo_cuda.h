@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define VELO_CUDA_ABI_VERSION 1
+#define VELO_CUDA_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define VELO_API __attribute__((visibility("default")))
@@ -249,9 +249,15 @@ typedef struct velo_model_desc {
  * cols row-major (rows = output features; q4_0 rows are cols/32 blocks of 18
  * bytes, quant.rs:50-64).  Matrices must be q4_0; embeddings and norms may be
  * f32, f16 or q4_0. */
+typedef enum velo_weight_flags {
+    VELO_WEIGHT_DEVICE = 1, /* data is device memory of the context's GPU (else host memory) */
+    VELO_WEIGHT_SHARD = 2   /* the tensor is already this rank's shard (sharding.rs applied) */
+} velo_weight_flags;
+
 typedef struct velo_weight_desc {
     const char *name;
-    int32_t dtype; /* velo_dtype */
+    int32_t dtype;   /* velo_dtype */
+    uint32_t flags;  /* velo_weight_flags (0: a host tensor, sharded by the context) */
     const void *data;
     uint64_t rows, cols;
 } velo_weight_desc;
@@ -278,7 +284,9 @@ VELO_API int32_t velo_cuda_shard_weight(const velo_weight_desc *w, int32_t strat
  * allocate the zero-filled paged KV pool of the context's config (total_pages
  * x n_layer, kv_dtype) and its page table (max_slots x max_pages_per_slot).
  * With tp_size > 1 every rank passes the full tensors and keeps its shard
- * (velo_cuda_shard_weight); its pool holds its n_head_kv / tp_size heads.
+ * (velo_cuda_shard_weight), or passes its shards (VELO_WEIGHT_SHARD); its pool
+ * holds its n_head_kv / tp_size heads.  Device tensors (VELO_WEIGHT_DEVICE)
+ * are repacked in place of a host upload; with tp_size > 1 they must be shards.
  * Replaces LlamaCpuModel::from_weights / LlamaMetalModel::new and
  * MetalMemoryRuntime::new (src/llama_cpu.rs:168-190, src/metal/runtime.rs). */
 VELO_API int32_t velo_cuda_load_model(velo_cuda_ctx *ctx, const velo_model_desc *desc,

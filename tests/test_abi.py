@@ -20,7 +20,7 @@ def test_wrapper_binds_every_declared_symbol():
 
 
 def test_abi_version():
-    assert velo_cuda.lib().velo_cuda_abi_version() == 1
+    assert velo_cuda.lib().velo_cuda_abi_version() == 2
 
 
 def test_create_rejects_bad_arguments():

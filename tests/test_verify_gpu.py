@@ -222,3 +222,26 @@ def test_prefill_and_decode_through_the_step_match_oracle():
         assert agree >= 1
     finally:
         ctx.close()
+
+
+def test_device_tensors_load_like_host():
+    """Weights handed over as device tensors (VELO_WEIGHT_DEVICE, here also
+    flagged as this rank's shards) give the same repacked model as host
+    tensors: identical logits and decisions."""
+    import torch
+    meta, tensors = synthetic.llama_q4_model(512, 256, 2, 2, 1, 512, seed=5)
+    dev = {k: (dt, torch.from_numpy(np.ascontiguousarray(a)).cuda(), r, c)
+           for k, (dt, a, r, c) in tensors.items()}
+    tokens = np.array([[7, 300, 41, 9]], np.uint32)
+    parents = np.array([[-1, 0, 1, 1]], np.int32)
+    out = []
+    for src, shards in ((tensors, False), (dev, True)):
+        with velo_cuda.Context(device=0, total_pages=8, max_slots=1, max_pages_per_slot=8) as ctx:
+            ctx.load_model(meta, src, shards=shards)
+            ctx.bind_slot(0, np.arange(8))
+            velo_cuda.prefill(ctx, 0, [3, 1, 4, 1, 5, 9, 2, 6], n_vocab=512)
+            out.append(ctx.verify_step([0], [8], tokens, parents, commit=False, want_logits=True,
+                                       n_vocab=512))
+    assert np.array_equal(out[0]["logits"], out[1]["logits"])
+    assert np.array_equal(out[0]["accepted_len"], out[1]["accepted_len"])
+    assert np.array_equal(out[0]["bonus"], out[1]["bonus"])

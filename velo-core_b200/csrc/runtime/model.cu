@@ -185,6 +185,21 @@ const velo_weight_desc* find(const Index& ix, const std::string& name) {
     return it == ix.end() ? nullptr : it->second;
 }
 
+bool on_device(const velo_weight_desc* w) { return (w->flags & VELO_WEIGHT_DEVICE) != 0; }
+
+// A tensor's bytes in host memory: the caller's buffer, or a copy of a device
+// tensor in `tmp`.  Null (error recorded) when the copy fails.
+const uint8_t* host_view(const velo_weight_desc* w, size_t bytes, std::vector<uint8_t>& tmp) {
+    if (!on_device(w)) return static_cast<const uint8_t*>(w->data);
+    tmp.resize(bytes);
+    const cudaError_t e = cudaMemcpy(tmp.data(), w->data, bytes, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) {
+        fail(VELO_ERR_CUDA, "reading device tensor %s: %s", w->name, cudaGetErrorString(e));
+        return nullptr;
+    }
+    return tmp.data();
+}
+
 // f32 vector (norm weight / embedding table) of rows x cols on the device
 int32_t upload_f32(Model* m, const velo_weight_desc* w, size_t rows, size_t cols, float** out,
                    cudaStream_t s) {
@@ -195,10 +210,19 @@ int32_t upload_f32(Model* m, const velo_weight_desc* w, size_t rows, size_t cols
     if (w->dtype < VELO_DT_F32 || w->dtype > VELO_DT_Q4_0 || !w->data ||
         (w->dtype == VELO_DT_Q4_0 && cols % 32))
         return fail(VELO_ERR_INVALID_ARGUMENT, "tensor %s: bad dtype / data", w->name);
+    if (on_device(w) && w->dtype == VELO_DT_F32) {  // device f32: a device copy
+        int32_t st = dev_alloc(m, out, rows * cols * 4);
+        if (st) return st;
+        VELO_CUDA_TRY(cudaMemcpyAsync(*out, w->data, rows * cols * 4, cudaMemcpyDeviceToDevice, s));
+        VELO_CUDA_TRY(cudaStreamSynchronize(s));
+        return VELO_OK;
+    }
     std::vector<float> host(rows * cols);
     const size_t rb = row_bytes(w->dtype, cols);
-    for (size_t r = 0; r < rows; ++r)
-        host_dequant_row(w->dtype, static_cast<const uint8_t*>(w->data) + r * rb, host.data() + r * cols, cols);
+    std::vector<uint8_t> tmp;
+    const uint8_t* src = host_view(w, rows * rb, tmp);
+    if (!src) return VELO_ERR_CUDA;
+    for (size_t r = 0; r < rows; ++r) host_dequant_row(w->dtype, src + r * rb, host.data() + r * cols, cols);
     int32_t st = dev_alloc(m, out, host.size() * 4);
     if (st) return st;
     VELO_CUDA_TRY(cudaMemcpyAsync(*out, host.data(), host.size() * 4, cudaMemcpyHostToDevice, s));
@@ -225,9 +249,10 @@ int32_t upload_f32_rows(Model* m, const std::vector<const velo_weight_desc*>& pa
     size_t r0 = 0;
     for (auto* w : parts) {
         const size_t rb = row_bytes(w->dtype, cols);
-        for (size_t r = 0; r < w->rows; ++r)
-            host_dequant_row(w->dtype, static_cast<const uint8_t*>(w->data) + r * rb,
-                             host.data() + (r0 + r) * cols, cols);
+        std::vector<uint8_t> tmp;
+        const uint8_t* src = host_view(w, w->rows * rb, tmp);
+        if (!src) return VELO_ERR_CUDA;
+        for (size_t r = 0; r < w->rows; ++r) host_dequant_row(w->dtype, src + r * rb, host.data() + (r0 + r) * cols, cols);
         r0 += w->rows;
     }
     int32_t st = dev_alloc(m, out, host.size() * 4);
@@ -255,7 +280,8 @@ int32_t upload_q4(Model* m, const std::vector<const velo_weight_desc*>& parts, s
     VELO_CUDA_TRY(cudaMalloc(&raw, rows * rb));
     size_t off = 0;
     for (auto* w : parts) {
-        cudaError_t e = cudaMemcpy(raw + off, w->data, w->rows * rb, cudaMemcpyHostToDevice);
+        cudaError_t e = cudaMemcpy(raw + off, w->data, w->rows * rb,
+                                   on_device(w) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice);
         if (e != cudaSuccess) {
             cudaFree(raw);
             return fail(VELO_ERR_CUDA, "weight upload failed: %s", cudaGetErrorString(e));
@@ -498,6 +524,12 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
     int32_t st = VELO_OK;
     auto shard = [&](const velo_weight_desc* wd, int32_t strategy) -> const velo_weight_desc* {
         if (!wd || st || tp == 1 || strategy == VELO_SHARD_REPLICATED) return wd;
+        if (wd->flags & VELO_WEIGHT_SHARD) return wd;  // the caller's shard
+        if (velo::on_device(wd)) {
+            st = fail(VELO_ERR_INVALID_ARGUMENT, "device tensor %s must be passed as this rank's shard",
+                      wd->name);
+            return nullptr;
+        }
         if (!wd->data || wd->dtype < VELO_DT_F32 || wd->dtype > VELO_DT_Q4_0) return wd;
         bufs.emplace_back();
         velo_weight_desc out = *wd;
@@ -506,8 +538,15 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
         descs.push_back(out);
         return st ? nullptr : &descs.back();
     };
-    auto get = [&](const std::string& name) {
-        return shard(velo::find(ix, name), velo::shard_strategy(name.c_str()));
+    // this rank's matrix `name`, which must have `rows` rows (after sharding)
+    auto get_rows = [&](const std::string& name, uint64_t rows) -> const velo_weight_desc* {
+        const velo_weight_desc* w = shard(velo::find(ix, name), velo::shard_strategy(name.c_str()));
+        if (w && !st && w->rows != rows) {
+            st = fail(VELO_ERR_INVALID_ARGUMENT, "matrix %s has %llu rows, this rank expects %llu",
+                      name.c_str(), (unsigned long long)w->rows, (unsigned long long)rows);
+            return nullptr;
+        }
+        return w;
     };
     const size_t H = d->n_embd, V = d->n_vocab, F = m->meta.n_ff;
     const size_t Dq = (size_t)m->meta.n_head * d->head_dim;
@@ -519,6 +558,9 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
     if (!st) {
         const velo_weight_desc* out = velo::find(ix, "output.weight");
         const velo_weight_desc* lm = shard(out ? out : emb, VELO_SHARD_COLUMN);  // tied fallback
+        if (!st && lm && lm->rows != (uint64_t)m->V_loc)
+            st = fail(VELO_ERR_INVALID_ARGUMENT, "LM head has %llu rows, this rank expects %d",
+                      (unsigned long long)lm->rows, m->V_loc);
         if (!st) st = f32 ? velo::upload_f32_rows(m, {lm}, H, &m->lm_head, s)
                           : velo::upload_q4(m, {lm}, H, false, &m->lm_head, s);
     }
@@ -533,22 +575,23 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
         st = velo::upload_f32(m, velo::find(ix, p + "attention_norm.weight"), 1, H, &ly.attn_norm, s);
         if (!st) st = velo::upload_f32(m, velo::find(ix, p + "ffn_norm.weight"), 1, H, &ly.ffn_norm, s);
         if (!st) {
-            auto* wq = get(p + "attention.wq.weight");
-            auto* wk = get(p + "attention.wk.weight");
-            auto* wv = get(p + "attention.wv.weight");
+            const uint64_t Dk = (uint64_t)m->meta.n_head_kv * d->head_dim;
+            auto* wq = get_rows(p + "attention.wq.weight", Dq);
+            auto* wk = get_rows(p + "attention.wk.weight", Dk);
+            auto* wv = get_rows(p + "attention.wv.weight", Dk);
             if (!st) st = upload({wq, wk, wv}, H, false, &ly.wqkv);
         }
         if (!st) {
-            auto* wo = get(p + "attention.wo.weight");
+            auto* wo = get_rows(p + "attention.wo.weight", H);
             if (!st) st = upload({wo}, Dq, false, &ly.wo);
         }
         if (!st) {
-            auto* w1 = get(p + "feed_forward.w1.weight");
-            auto* w3 = get(p + "feed_forward.w3.weight");
+            auto* w1 = get_rows(p + "feed_forward.w1.weight", F);
+            auto* w3 = get_rows(p + "feed_forward.w3.weight", F);
             if (!st) st = upload({w1, w3}, H, true, &ly.w13);
         }
         if (!st) {
-            auto* w2 = get(p + "feed_forward.w2.weight");
+            auto* w2 = get_rows(p + "feed_forward.w2.weight", H);
             if (!st) st = upload({w2}, F, false, &ly.w2);
         }
         m->layers.push_back(ly);

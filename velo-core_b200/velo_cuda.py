@@ -92,8 +92,11 @@ class ModelDesc(ctypes.Structure):
 
 
 class WeightDesc(ctypes.Structure):
-    _fields_ = [("name", ctypes.c_char_p), ("dtype", ctypes.c_int32), ("data", ctypes.c_void_p),
-                ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64)]
+    _fields_ = [("name", ctypes.c_char_p), ("dtype", ctypes.c_int32), ("flags", ctypes.c_uint32),
+                ("data", ctypes.c_void_p), ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64)]
+
+
+WEIGHT_DEVICE, WEIGHT_SHARD = 1, 2
 
 
 class VerifyBatch(ctypes.Structure):
@@ -238,18 +241,26 @@ class Context:
 
 
     # ------------------------------------------------------------ model + verify
-    def load_model(self, meta, tensors):
-        """meta: dict of velo_model_desc fields; tensors: {name: (dtype, ndarray, rows, cols)}
-        with host arrays in the reference's WeightStore layout."""
+    def load_model(self, meta, tensors, shards=False):
+        """meta: dict of velo_model_desc fields; tensors: {name: (dtype, array, rows, cols)}
+        in the reference's WeightStore layout.  An array is a host ndarray or a
+        CUDA torch tensor on the context's device (VELO_WEIGHT_DEVICE);
+        shards=True: the tensors are already this rank's shards."""
         d = ModelDesc(ctypes.sizeof(ModelDesc), *(int(meta[k]) for k in
                       ("n_vocab", "n_embd", "n_layer", "n_head", "n_head_kv", "n_ff", "head_dim")),
                       float(meta["rope_freq_base"]), float(meta["norm_eps"]))
         keep, ws = [], (WeightDesc * len(tensors))()
         for i, (name, (dt, arr, rows, cols)) in enumerate(tensors.items()):
-            a = np.ascontiguousarray(arr)
+            flags = WEIGHT_SHARD if shards else 0
+            if hasattr(arr, "data_ptr") and getattr(arr, "is_cuda", False):
+                a = arr.contiguous()
+                ptr, flags = a.data_ptr(), flags | WEIGHT_DEVICE
+            else:
+                a = np.ascontiguousarray(arr)
+                ptr = a.ctypes.data
             nm = name.encode()
             keep += [a, nm]
-            ws[i] = WeightDesc(nm, dt, a.ctypes.data, rows, cols)
+            ws[i] = WeightDesc(nm, dt, flags, ptr, rows, cols)
         check(lib().velo_cuda_load_model(self._h, ctypes.byref(d), ws, len(tensors)))
 
     def bind_slot(self, slot, pages):
@@ -326,7 +337,7 @@ def shard_strategy(name):
 def shard_weight(name, dtype, data, rows, cols, strategy, tp, rank):
     """velo_cuda_shard_weight on a host tensor: returns (bytes, rows, cols)."""
     a = np.ascontiguousarray(data).view(np.uint8).reshape(-1)
-    w = WeightDesc(name.encode(), dtype, a.ctypes.data, rows, cols)
+    w = WeightDesc(name.encode(), dtype, 0, a.ctypes.data, rows, cols)
     out = np.zeros(a.size, np.uint8)
     r, c = ctypes.c_uint64(), ctypes.c_uint64()
     check(lib().velo_cuda_shard_weight(ctypes.byref(w), strategy, tp, rank, _ptr(out), out.size,
