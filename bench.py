@@ -333,25 +333,31 @@ def run_cuda(args):
 Q4_SHAPES_C3 = [  # (name, N, K, mode) of one Llama-2-7B layer + LM head at M = 32 x 16 nodes
     ("wqkv", 3 * 4096, 4096, 1), ("wo", 4096, 4096, 2), ("w1w3", 2 * 11008, 4096, 3),
     ("w2", 4096, 11008, 2), ("output", 32000, 4096, 0)]
+Q4_SHAPES_C5 = [  # one Llama-3-70B layer (GQA 64/8) + LM head at M = 64 x 32 nodes, one GPU
+    ("wqkv", 8192 + 2 * 1024, 8192, 1), ("wo", 8192, 8192, 2), ("w1w3", 2 * 28672, 8192, 3),
+    ("w2", 8192, 28672, 2), ("output", 128256, 8192, 0)]
 
 
 def run_q4gemm(args):
-    """tcgen05 q4_0 GEMMs at BASELINE config 3 shapes (M = 512 verify rows).
-    Weights of `layers` distinct layers (> L2 in total) are cycled so no launch
-    finds its weight tile in L2."""
+    """tcgen05 q4_0 GEMMs at BASELINE config 3 shapes (M = 512 verify rows), or
+    config 5 shapes with --case c5 (M = 2048).  Weights of `layers` distinct
+    layers (> L2 in total) are cycled so no launch finds its weight tile in L2."""
     import torch
     import synthetic
     import velo_cuda
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
-    M, layers = 512, 8
+    c5 = args.case == "c5"
+    shapes = Q4_SHAPES_C5 if c5 else Q4_SHAPES_C3
+    M, layers = (2048, 4) if c5 else (512, 8)
     ctx = velo_cuda.Context(device=0)
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     ctx.set_stream(stream.cuda_stream)
-    x = torch.from_numpy(synthetic.rng(0, 20).normal(0, 1, (M, 11008)).astype(np.float16)).to(dev)
+    kmax = max(K for _, _, K, _ in shapes)
+    x = torch.from_numpy(synthetic.rng(0, 20).normal(0, 1, (M, kmax)).astype(np.float16)).to(dev)
     res = []
-    for name, N, K, mode in Q4_SHAPES_C3:
+    for name, N, K, mode in shapes:
         ws = []
         for l in range(layers if name != "output" else 2):
             raw = torch.randint(0, 256, (N, K // 32, 18), dtype=torch.uint8, device=dev)
@@ -390,7 +396,7 @@ def run_q4gemm(args):
         pass
     tot_us = sum(r["us"] for r in res[:-1])
     tot_fl = sum(2.0 * r["M"] * r["N"] * r["K"] for r in res[:-1])
-    line = {"workload": "q4_0 tcgen05 GEMM at BASELINE config 3 shapes (M=512)",
+    line = {"workload": f"q4_0 tcgen05 GEMM at BASELINE config {'5' if c5 else '3'} shapes (M={M})",
             "per_gemm": res, "layer_us": tot_us, "layer_tflops": tot_fl / tot_us / 1e6,
             "roofline": {"bound": "tensor", "achieved": tot_fl / tot_us / 1e6, "peak": peak,
                          "unit": "TFLOP/s", "frac": tot_fl / tot_us / 1e6 / peak,

@@ -179,27 +179,37 @@ __global__ void rope_split_f32_kernel(const float* __restrict__ qkv, const uint6
 }
 
 // -------------------------------------------------------- tree attention
-// One warp per query row (b, n, head).  Keys come 32 at a time, one per
-// lane: the cached prefix [0, ctx_len) through the page table, then the
-// tree nodes j whose bit is set in anc[b][n].  Each lane scores its key
-// against the whole q row (broadcast from shared memory); the warp keeps an
-// online softmax and accumulates P V with lane-owned dimensions (d = lane +
-// 32 i), so every V row is read with coalesced 128-byte accesses.
-constexpr int kAttnWarps = 8;
+// One CTA (4 warps) per query row (b, n, head).  The keys -- the cached prefix
+// [0, ctx_len) through the page table, then the tree nodes j whose bit is set
+// in anc[b][n] -- come in chunks of 32, one key per lane; warp w takes chunks
+// w, w + 4, ...  A lane scores its key against the q row (broadcast from
+// shared memory) while cp.async copies its V row into the warp's staging
+// rows; P V then runs with lane-owned dimensions (d = lane + 32 i) over the
+// staged rows, so every load of a chunk is in flight at once.  Each warp
+// keeps an online softmax; the four states are merged at the end.
+constexpr int kAttnWarps = 4;
+
+__host__ __device__ constexpr int attn_f32_smem(int D) {
+    return (D + kAttnWarps * 32 * D + kAttnWarps * (D + 2)) * 4;
+}
 
 template <int DW>
 __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_f32_kernel(const TreeAttnF32Args a) {
     constexpr int D = DW * 32;
-    __shared__ __align__(16) float qs[kAttnWarps][D];
+    extern __shared__ __align__(16) float sm[];
+    float* qs = sm;                                 // [D]
+    float* vs = qs + D;                             // [warps][32][D]
+    float* os = vs + kAttnWarps * 32 * D;           // [warps][D]
+    float* ms = os + kAttnWarps * D;                // [warps]
+    float* ls = ms + kAttnWarps;                    // [warps]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x * kAttnWarps + warp;
-    if (row >= a.B * a.N * a.Hq) return;
+    const int row = blockIdx.x;
     const int hq = row % a.Hq, bn = row / a.Hq, b = bn / a.N;
     const int hkv = hq / (a.Hq / a.Hkv);
-#pragma unroll
-    for (int i = 0; i < DW; ++i) qs[warp][lane + 32 * i] = a.q[(size_t)row * D + lane + 32 * i];
-    __syncwarp();
-    const float4* q4 = reinterpret_cast<const float4*>(qs[warp]);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) qs[d] = a.q[(size_t)row * D + d];
+    __syncthreads();
+    const float4* q4 = reinterpret_cast<const float4*>(qs);
+    float* vw = vs + warp * 32 * D;
     const float inv_sqrt_d = 1.0f / sqrtf((float)D);
     const int ctx = a.ctx_len[b];
     const uint64_t amask = a.anc[bn];
@@ -208,7 +218,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_f32_kernel(const Tr
     float m_run = -INFINITY, l_run = 0.0f, o[DW];
 #pragma unroll
     for (int i = 0; i < DW; ++i) o[i] = 0.0f;
-    for (int c0 = 0; c0 < total; c0 += 32) {
+    for (int c0 = 32 * warp; c0 < total; c0 += 32 * kAttnWarps) {
         const int t = c0 + lane;
         const float* kp = nullptr;
         const float* vp = nullptr;
@@ -230,6 +240,15 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_f32_kernel(const Tr
                 vp = a.node_v + r;
             }
         }
+        if (vp) {  // V row -> this lane's staging row, asynchronously
+            const unsigned dst = (unsigned)__cvta_generic_to_shared(vw + lane * D);
+#pragma unroll
+            for (int d4 = 0; d4 < D / 4; ++d4)
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(dst + 16 * d4),
+                             "l"(vp + 4 * d4)
+                             : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
         float s = -INFINITY;
         if (kp) {
             const float4* k4 = reinterpret_cast<const float4*>(kp);
@@ -244,29 +263,53 @@ __global__ void __launch_bounds__(kAttnWarps * 32) tree_attn_f32_kernel(const Tr
             }
             s = dot * inv_sqrt_d;
         }
-        const float cmax = warp_max(s);
-        if (cmax == -INFINITY) continue;  // no key of this chunk is visible (warp-uniform)
-        const float m_new = fmaxf(m_run, cmax);
-        const float corr = expf(m_run - m_new);  // 0 on the first visible chunk
-        const float p = kp ? expf(s - m_new) : 0.0f;
-        l_run = l_run * corr + warp_sum(p);
+        const unsigned live = __ballot_sync(0xffffffffu, kp != nullptr);
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncwarp();
+        if (live) {
+            const float cmax = warp_max(s);
+            const float m_new = fmaxf(m_run, cmax);
+            const float corr = expf(m_run - m_new);  // 0 on the first visible chunk
+            const float p = kp ? expf(s - m_new) : 0.0f;
+            l_run = l_run * corr + warp_sum(p);
 #pragma unroll
-        for (int i = 0; i < DW; ++i) o[i] *= corr;
-        unsigned live = __ballot_sync(0xffffffffu, kp != nullptr);
-        while (live) {
-            const int jj = __ffs(live) - 1;
-            live &= live - 1;
-            const float pj = __shfl_sync(0xffffffffu, p, jj);
-            const float* vj = reinterpret_cast<const float*>(
-                __shfl_sync(0xffffffffu, reinterpret_cast<unsigned long long>(vp), jj));
+            for (int i = 0; i < DW; ++i) o[i] *= corr;
+#pragma unroll 8
+            for (int j = 0; j < 32; ++j) {
+                const float pj = __shfl_sync(0xffffffffu, p, j);
+                if ((live >> j) & 1u) {
 #pragma unroll
-            for (int i = 0; i < DW; ++i) o[i] = fmaf(pj, __ldg(vj + lane + 32 * i), o[i]);
+                    for (int i = 0; i < DW; ++i) o[i] = fmaf(pj, vw[j * D + lane + 32 * i], o[i]);
+                }
+            }
+            m_run = m_new;
         }
-        m_run = m_new;
+        __syncwarp();  // the staging rows are rewritten by the next chunk
     }
-    const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+    // merge the warps' states
 #pragma unroll
-    for (int i = 0; i < DW; ++i) a.out[(size_t)row * D + lane + 32 * i] = o[i] * inv_l;
+    for (int i = 0; i < DW; ++i) os[warp * D + lane + 32 * i] = o[i];
+    if (lane == 0) {
+        ms[warp] = m_run;
+        ls[warp] = l_run;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        float M = -INFINITY;
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, ms[w]);
+        float L = 0.0f, acc[DW];
+#pragma unroll
+        for (int i = 0; i < DW; ++i) acc[i] = 0.0f;
+        for (int w = 0; w < kAttnWarps; ++w) {
+            const float f = ls[w] > 0.0f ? expf(ms[w] - M) : 0.0f;
+            L += ls[w] * f;
+#pragma unroll
+            for (int i = 0; i < DW; ++i) acc[i] = fmaf(os[w * D + lane + 32 * i], f, acc[i]);
+        }
+        const float inv_l = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+        for (int i = 0; i < DW; ++i) a.out[(size_t)row * D + lane + 32 * i] = acc[i] * inv_l;
+    }
 }
 
 // -------------------------------------------------------------- KV commit
@@ -337,18 +380,27 @@ cudaError_t launch_rope_split_f32(const float* qkv, const uint64_t* anc, const i
     return cudaGetLastError();
 }
 
+template <int DW>
+cudaError_t attn_f32_launch(const TreeAttnF32Args& a, unsigned grid, cudaStream_t s) {
+    constexpr int smem = attn_f32_smem(DW * 32);
+    static bool configured = false;
+    if (smem > 48 * 1024 && !configured) {
+        cudaError_t e = cudaFuncSetAttribute(tree_attn_f32_kernel<DW>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    tree_attn_f32_kernel<DW><<<grid, kAttnWarps * 32, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_tree_attention_f32(const TreeAttnF32Args& a, cudaStream_t s) {
     const long rows = (long)a.B * a.N * a.Hq;
     if (rows == 0) return cudaSuccess;
     if (a.N > 64 || a.Hkv <= 0 || a.Hq % a.Hkv) return cudaErrorInvalidValue;
-    const unsigned grid = (unsigned)((rows + kAttnWarps - 1) / kAttnWarps);
-    if (a.D == 64)
-        tree_attn_f32_kernel<2><<<grid, kAttnWarps * 32, 0, s>>>(a);
-    else if (a.D == 128)
-        tree_attn_f32_kernel<4><<<grid, kAttnWarps * 32, 0, s>>>(a);
-    else
-        return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    if (a.D == 64) return attn_f32_launch<2>(a, (unsigned)rows, s);
+    if (a.D == 128) return attn_f32_launch<4>(a, (unsigned)rows, s);
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_kv_commit_f32(const KvCommitF32Args& a, cudaStream_t s) {
