@@ -334,6 +334,8 @@ typedef struct velo_verify_result {
     int32_t *accepted_nodes;  /* [B][n_nodes] path root first, -1 padded (or NULL) */
     uint32_t *bonus_token;    /* [B] token emitted after the accepted path */
     float *logits;            /* [B][n_nodes][n_vocab] target logits (or NULL) */
+    uint32_t *expected;       /* [B][n_nodes] the target's greedy token after each node
+                                 (TreeVerifyResult::expected; greedy steps; or NULL) */
 } velo_verify_result;
 
 /* One verify step for B sequences: the target forward over every draft-tree

@@ -94,7 +94,7 @@ struct Model {
     uint32_t* slots = nullptr;
     uint32_t* pt_batch = nullptr;  // [B][max_pages] gathered rows
     // per-step outputs, one device block read back by one copy into pinned
-    // memory: path_len [B] | bonus [B] | path [M]
+    // memory: path_len [B] | bonus [B] | path [M] | expected [M]
     uint8_t* dout = nullptr;
     uint8_t* hout = nullptr;
     bool staging_busy = false;  // a step's copies may still use hin / hout
@@ -336,14 +336,14 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
     if (!st) st = dev_alloc(m, &m->pairs_all, (size_t)cM * 8 * m->tp, true);
 
     if (!st) st = dev_alloc(m, &m->anc, (size_t)cM * 8, true);
-    if (!st) st = dev_alloc(m, &m->expected, (size_t)cM * 4, true);
+
 
     if (!st) st = dev_alloc(m, &m->dtok, (size_t)cM * 4, true);
     if (!st) st = dev_alloc(m, &m->uni, (size_t)cM * 4, true);
     // packed step I/O (4-byte words)
     const size_t mp = m->max_pages ? m->max_pages : 1;
     m->in_bytes = ((size_t)2 * cM + 2 * cB + cB * mp) * 4;
-    const size_t out_bytes = ((size_t)2 * cB + cM) * 4;
+    const size_t out_bytes = ((size_t)2 * cB + 2 * cM) * 4;
     if (!st) st = dev_alloc(m, &m->din, m->in_bytes, true);
     if (!st) st = dev_alloc(m, &m->dout, out_bytes, true);
     if (!st) {
@@ -833,6 +833,7 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     m->path_len = reinterpret_cast<int32_t*>(m->dout);
     m->bonus = reinterpret_cast<uint32_t*>(m->path_len + B);
     m->path = reinterpret_cast<int32_t*>(m->bonus + B);
+    m->expected = reinterpret_cast<uint32_t*>(m->path + M);
     if (m->staging_busy) VELO_CUDA_TRY(cudaStreamSynchronize(s));  // an earlier step ended early
     m->staging_busy = true;
     {
@@ -1049,8 +1050,10 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         st = body();
         if (st) return st;
     }
-    // path_len | bonus | path: one copy into pinned memory
-    VELO_CUDA_TRY(cudaMemcpyAsync(m->hout, m->dout, ((size_t)2 * B + M) * 4, cudaMemcpyDeviceToHost, s));
+    // path_len | bonus | path | expected: one copy into pinned memory
+    const bool want_expected = out->expected && (!sampling || N == 1);
+    VELO_CUDA_TRY(cudaMemcpyAsync(m->hout, m->dout, ((size_t)2 * B + (want_expected ? 2 : 1) * M) * 4,
+                                  cudaMemcpyDeviceToHost, s));
     std::vector<float> gathered;
     if (out->logits && m->tp == 1)
         VELO_CUDA_TRY(cudaMemcpyAsync(out->logits, m->logits, (size_t)M * V * 4, cudaMemcpyDeviceToHost, s));
@@ -1085,6 +1088,7 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     for (int b = 0; b < B; ++b) out->accepted_len[b] = hp[b] - 1;
     std::memcpy(out->bonus_token, hp + B, (size_t)B * 4);
     if (out->accepted_nodes) std::memcpy(out->accepted_nodes, hp + 2 * B, (size_t)M * 4);
+    if (want_expected) std::memcpy(out->expected, hp + 2 * B + M, (size_t)M * 4);
     return VELO_OK;
 }
 

@@ -76,6 +76,57 @@ class VerifyStep:
     expected: int
 
 
+class SpeculativeTree:
+    """SpeculativeTree / TreeNode (speculative.rs:47-96): drafted tokens with
+    parent links; node 0 is the root (parent None)."""
+
+    def __init__(self, token):
+        self.tokens, self.parents = [int(token)], [None]
+
+    def add_child(self, parent_idx, token):
+        self.tokens.append(int(token))
+        self.parents.append(int(parent_idx))
+        return len(self.tokens) - 1
+
+    def get_path(self, idx):
+        path = []
+        while idx is not None:
+            path.append(self.tokens[idx])
+            idx = self.parents[idx]
+        return path[::-1]
+
+    def find_best_path(self, expected):
+        """find_best_path (speculative.rs:97-129): valid[0]; valid[n] =
+        valid[parent] and token[n] == expected[parent]; the deepest valid node
+        wins (ties to the later index); returns (path tokens, expected[best])."""
+        n = len(self.tokens)
+        valid, depth = [False] * n, [0] * n
+        valid[0], depth[0] = True, 1
+        best = 0
+        for i in range(1, n):
+            p = self.parents[i]
+            if valid[p] and self.tokens[i] == expected[p]:
+                valid[i], depth[i] = True, depth[p] + 1
+            if valid[i] and depth[i] >= depth[best]:
+                best = i
+        return self.get_path(best), expected[best]
+
+
+@dataclass
+class TreeVerifyResult:
+    expected: list
+
+
+def top_k(logits, k):
+    """TopKSampler::sample_top_k (sampling.rs:105-131): the k largest logits
+    by a stable descending sort (equal logits keep ascending token order).
+    TopKSampler::sample (sampling.rs:76-100) is its first entry.  Finite
+    logits only (the reference's NaN placement depends on its sort)."""
+    x = np.asarray(logits, np.float32)
+    order = np.argsort(-x, kind="stable")[:k]
+    return [NextTokenPrediction(int(i), float(x[i])) for i in order]
+
+
 class SpeculativeDecoder:
     """SpeculativeDecoder::new / with_max_window / generate / begin."""
 
@@ -285,3 +336,56 @@ class CudaDraft:
         if self.T > 0:
             self.last_logits = np.stack(logits)
         return out
+
+
+class CudaTreeDraft(CudaDraft):
+    """TreeDraftModel::draft_tree (backend.rs:255-294) on the device: the
+    draft's top-`width` tokens after the context form the root and its
+    children, then the primary branch is extended greedily (TopKSampler) to
+    max_tokens nodes, one decode step per node."""
+
+    def _decode(self, token):
+        pos = len(self.tokens)
+        r = self.ctx.verify_step([self.slot], [pos], np.array([[token]], np.uint32),
+                                 np.array([[-1]], np.int32), commit="all", want_logits=True,
+                                 n_vocab=self.n_vocab)
+        self.tokens.append(int(token))
+        return r["logits"][0, 0]
+
+    def draft_tree(self, context, max_tokens, width):
+        self.prefill(context)
+        top = top_k(self._decode(context[-1]), width)
+        if not top:
+            raise SpeculativeError("Draft model returned no tokens")
+        tree = SpeculativeTree(top[0].token)
+        for pred in top[1:]:
+            tree.add_child(0, pred.token)
+        curr = 0
+        for _ in range(1, max_tokens):
+            nxt = top_k(self._decode(tree.tokens[curr]), 1)[0].token
+            curr = tree.add_child(curr, nxt)
+        return tree
+
+
+def rooted_tree(context, tree):
+    """The tree the device verifies: the last context token as root, the draft
+    tree under it (its root a child of node 0).  find_best_path over this tree
+    checks the first drafted token as well (the trait contract), where the
+    reference's draft_tree root would be taken unchecked."""
+    t = SpeculativeTree(context[-1])
+    for tok, p in zip(tree.tokens, tree.parents):
+        t.add_child(0 if p is None else p + 1, tok)
+    return t
+
+
+def verify_tree_on_device(ctx, slot, n_vocab, context, tree, commit=True):
+    """TargetModel::verify_tree (speculative.rs:217-242) over the whole tree in
+    one verify step.  Returns (the rooted tree, TreeVerifyResult with the
+    target's token after each of its nodes, the step's result); with commit
+    the accepted path's K/V are written at len(context) - 1 onwards."""
+    rt = rooted_tree(context, tree)
+    nodes = np.array(rt.tokens, np.uint32)
+    parents = np.array([-1] + rt.parents[1:], np.int32)
+    r = ctx.verify_step([slot], [len(context) - 1], nodes[None], parents[None], commit=commit,
+                        n_vocab=n_vocab)
+    return rt, TreeVerifyResult([int(e) for e in r["expected"][0]]), r

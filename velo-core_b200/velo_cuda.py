@@ -107,7 +107,8 @@ class VerifyBatch(ctypes.Structure):
 
 
 class VerifyResult(ctypes.Structure):
-    _fields_ = [("accepted_len", _P), ("accepted_nodes", _P), ("bonus_token", _P), ("logits", _P)]
+    _fields_ = [("accepted_len", _P), ("accepted_nodes", _P), ("bonus_token", _P), ("logits", _P),
+                ("expected", _P)]
 
 EPI_STORE_F32, EPI_STORE_F16, EPI_ADD_F32, EPI_SWIGLU = 0, 1, 2, 3
 
@@ -303,9 +304,11 @@ class Context:
         cm = 2 if commit == "all" else (1 if commit else 0)
         bt = VerifyBatch(ctypes.sizeof(VerifyBatch), B, N, _ptr(sl), _ptr(cl), _ptr(tok), _ptr(par),
                          float(temperature), _ptr(dl), _ptr(un), cm)
-        rs = VerifyResult(_ptr(acc), _ptr(nodes), _ptr(bonus), _ptr(logits))
+        expected = np.zeros((B, N), np.uint32)
+        rs = VerifyResult(_ptr(acc), _ptr(nodes), _ptr(bonus), _ptr(logits), _ptr(expected))
         check(lib().velo_cuda_verify_step(self._h, ctypes.byref(bt), ctypes.byref(rs)))
-        return {"accepted_len": acc, "accepted_nodes": nodes, "bonus": bonus, "logits": logits}
+        return {"accepted_len": acc, "accepted_nodes": nodes, "bonus": bonus, "logits": logits,
+                "expected": expected}
 
 
 def prefill(ctx, slot, tokens, pos0=0, chunk=64, n_vocab=None):
