@@ -58,7 +58,9 @@ def _oracle(d, n_head, n_kv):
     (2, 64, 32, 8, [600, 1500]),           # config-4 head shape: 256 rows, 2 CTAs per head
     (2, 16, 4, 4, [64, 2048]),             # config-3 head shape (no GQA), exact tiles
     (1, 1, 8, 1, [333]),                   # single node, GQA 8
-    (2, 33, 16, 2, [17, 4099])])           # odd node count, 264 rows -> 3 row tiles
+    (2, 33, 16, 2, [17, 4099]),            # odd node count, 264 rows -> 3 row tiles
+    (2, 40, 32, 8, [0, 1000]),             # 160 rows: second query tile a quarter full
+    (1, 64, 64, 8, [2500])])               # 512 rows: two CTAs of two query tiles
 def test_tree_attention_matches_oracle(ctx, kv_dtype, B, N, Hq, Hkv, ctx_lens):
     d = synthetic.tree_attention_inputs(B, N, Hq, Hkv, ctx_lens, kv_dtype=kv_dtype, seed=B * 7 + N)
     got = _gpu(ctx, d, Hkv)
@@ -66,6 +68,20 @@ def test_tree_attention_matches_oracle(ctx, kv_dtype, B, N, Hq, Hkv, ctx_lens):
     assert np.isfinite(got).all()
     err = np.abs(got - ref).max()
     assert err <= TOL, err
+
+
+@pytest.mark.parametrize("kv_dtype", [0, 1])
+def test_one_and_two_query_tiles_agree(ctx, monkeypatch, kv_dtype):
+    # 256 rows per KV head: two query tiles per CTA by default, one per CTA
+    # with VELO_ATTN_QUERY_TILES=1; both layouts meet the oracle
+    d = synthetic.tree_attention_inputs(2, 64, 32, 8, [700, 2100], kv_dtype=kv_dtype, seed=11)
+    two = _gpu(ctx, d, 8)
+    monkeypatch.setenv("VELO_ATTN_QUERY_TILES", "1")
+    one = _gpu(ctx, d, 8)
+    ref = _oracle(d, 32, 8)
+    assert np.abs(two - ref).max() <= TOL
+    assert np.abs(one - ref).max() <= TOL
+    assert np.abs(two - one).max() <= TOL
 
 
 def test_tree_attention_f16_output_and_repeat(ctx):

@@ -9,25 +9,33 @@
 // probability-weighted V.  INT8 pages carry one fp16 scale per token and
 // head (value = q * scale).  GQA: query head hq reads KV head hq / (Hq/Hkv).
 //
-// One CTA = one (sequence, KV head, 128 query rows) item.  Query rows are the
-// (node, group head) pairs of the KV head, node-major.  Keys stream in tiles
-// of 64 (4 pages), the tree nodes form a final tile with an ancestor mask.
+// One CTA = one (sequence, KV head, QT x 128 query rows) item, QT = 1 or 2
+// query tiles.  Query rows are the (node, group head) pairs of the KV head,
+// node-major.  Keys stream in tiles of 64 (4 pages), the tree nodes form a
+// final tile with an ancestor mask.  With QT = 2 (more than 128 rows per KV
+// head) both query tiles share every K/V tile: it is read from HBM, and for
+// int8 pools converted, once.
 //   warp 0     producer: TMA (f16 pools, 128-byte swizzle straight into the
 //              operand tiles) or bulk copies of the raw int8 pages + scales
-//   warp 1     one thread issues S = Q K^T (M=128, N=64) into a double-
-//              buffered TMEM tile and O += P V (M=128, N=128, V MN-major)
-//   warp 2     TMEM allocation (S0, S1: 64 columns each; O: 128 columns)
-//   warps 4-11 softmax, two threads per query row (32 keys each): S from
-//              TMEM, exp2 on the SFU, P (f16) to shared memory for the PV MMA;
-//              O rescaled in TMEM only when the running max grows by > 2^8
+//   warp 1     one thread issues, per query tile, S = Q K^T (M=128, N=64)
+//              into a double-buffered TMEM tile and O += P V (M=128, N=128,
+//              V MN-major), in the order their inputs arrive
+//   warp 2     TMEM allocation (per query tile S0, S1: 64 columns each; O: 128)
+//   warps 4-11 softmax: S from TMEM, exp2 on the SFU, P (f16) to shared
+//              memory for the PV MMA; O rescaled in TMEM only when the running
+//              max grows by > 2^8.  QT = 1: two threads per query row (32 keys
+//              each); QT = 2: warps 4-7 own query tile 0 and warps 8-11 tile 1,
+//              one thread per row (all 64 keys)
 //   warps 12-15 (int8 pools) int8 -> f16 conversion of every K/V tile into
 //              the swizzled operand layout, and the tree tile from the node K/V
 //              (f16 pools: the producer loads the tree tile with a 3-D TMA)
 #include <cuda_fp16.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "common/sm100.cuh"
+#include "common/spec_math.cuh"  // max3
 #include "kernels/q4gemm.h"  // make_tmap_f16_2d
 #include "kernels/tree_attn.h"
 
@@ -50,15 +58,23 @@ constexpr float kRescaleLog2 = 8.0f;           // lazy O rescale threshold
 
 constexpr int kErrPage = 0x5101, kErrWait = 0x5102;
 
-template <bool INT8>
+template <bool INT8, int QT>
 struct AttnCfg {
-    static constexpr int KS = INT8 ? 3 : 5;    // f16 operand ring (cached tokens + tree tile)
-    static constexpr int RS = INT8 ? 3 : 0;    // raw int8 ring
-    // Q, the ring, P x 2, raw ring, scales, alignment, barriers, row exchange
-    static constexpr size_t kSmem = (size_t)Q_BYTES + (size_t)KS * KV_STAGE + 2 * P_BYTES +
-                                    (size_t)RS * RAW_STAGE + (INT8 ? (size_t)KS * 2 * TK * 4 : 0) +
-                                    1024 + 512 + 2 * BMQ * 4;
-    static_assert(kSmem <= 227 * 1024, "shared memory budget");
+    static_assert(QT == 1 || QT == 2, "one or two query tiles per CTA");
+    // f16 operand ring (cached tokens + tree tile) and raw int8 ring
+    static constexpr int KS = QT == 1 ? (INT8 ? 3 : 5) : (INT8 ? 2 : 4);
+    static constexpr int RS = INT8 ? 3 : 0;
+    // P buffers per query tile: two let the softmax write P_j while PV_{j-1}
+    // still reads P_{j-1}; with two query tiles the budget holds one each
+    static constexpr int PB = QT == 1 ? 2 : 1;
+    static constexpr int kSoftmaxPerQt = QT == 1 ? 256 : 128;  // softmax threads per tile
+    static constexpr uint32_t kTmemCols = QT * 256;
+    // Q, the ring, P, raw ring, scales, alignment, barriers, row exchange (QT = 1)
+    static constexpr size_t kSmem = (size_t)QT * Q_BYTES + (size_t)KS * KV_STAGE +
+                                    (size_t)QT * PB * P_BYTES + (size_t)RS * RAW_STAGE +
+                                    (INT8 ? (size_t)KS * 2 * TK * 4 : 0) + 1024 + 512 +
+                                    (QT == 1 ? 2 * BMQ * 4 : 0);
+    static_assert(kSmem <= 232448, "shared memory budget (227 KiB per block)");
 };
 
 // swizzled byte offset of 16-byte chunk c of row r in a 128-byte-row tile
@@ -85,6 +101,217 @@ __device__ __forceinline__ void i8x4_to_f16(uint32_t w, uint32_t& lo, uint32_t& 
     hi = *reinterpret_cast<const uint32_t*>(&c);
 }
 
+// Maximum of 32 raw scores of a query row.  Int8 pages: each score is first
+// multiplied by its key's scale, in place.  kMasked: scores of keys without
+// a bit in kmask become -inf (the tree tile and a ragged last tile only).
+template <bool INT8, bool kMasked>
+__device__ __forceinline__ float raw_max32(uint32_t (&x32)[32], uint32_t kmask, const float* ks) {
+    if constexpr (INT8) {
+#pragma unroll
+        for (int t4 = 0; t4 < 8; ++t4) {
+            const float4 k4 = *reinterpret_cast<const float4*>(ks + 4 * t4);  // broadcast
+            x32[4 * t4 + 0] = __float_as_uint(__uint_as_float(x32[4 * t4 + 0]) * k4.x);
+            x32[4 * t4 + 1] = __float_as_uint(__uint_as_float(x32[4 * t4 + 1]) * k4.y);
+            x32[4 * t4 + 2] = __float_as_uint(__uint_as_float(x32[4 * t4 + 2]) * k4.z);
+            x32[4 * t4 + 3] = __float_as_uint(__uint_as_float(x32[4 * t4 + 3]) * k4.w);
+        }
+    }
+    if constexpr (kMasked) {
+#pragma unroll
+        for (int t = 0; t < 32; ++t)
+            if (!((kmask >> t) & 1u)) x32[t] = __float_as_uint(-INFINITY);
+    }
+    // 32 -> 11 -> 4 -> 1 with three-input maxima (exact in any order)
+    float m1[11];
+#pragma unroll
+    for (int i = 0; i < 10; ++i)
+        m1[i] = max3(__uint_as_float(x32[3 * i]), __uint_as_float(x32[3 * i + 1]), __uint_as_float(x32[3 * i + 2]));
+    m1[10] = fmaxf(__uint_as_float(x32[30]), __uint_as_float(x32[31]));
+    return fmaxf(max3(max3(m1[0], m1[1], m1[2]), max3(m1[3], m1[4], m1[5]), max3(m1[6], m1[7], m1[8])),
+                 fmaxf(m1[9], m1[10]));
+}
+
+// p = 2^(x * sl2 - ms) of 32 keys (one packed FMA per pair), times the V
+// scale for int8 pages, as f16 into chunks c0 .. c0+3 of P row r; returns the
+// pairwise sums of the unscaled p.
+template <bool INT8>
+__device__ __forceinline__ float2 exp_pack_store(const uint32_t (&x32)[32], float sl2, float ms,
+                                                 const float* vs, uint8_t* pbuf, int r, int c0) {
+    float2 acc = make_float2(0.0f, 0.0f);
+    const float2 s2 = make_float2(sl2, sl2), nm = make_float2(-ms, -ms);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int t = c * 8 + 2 * e;
+            const float2 y = __ffma2_rn(make_float2(__uint_as_float(x32[t]), __uint_as_float(x32[t + 1])), s2, nm);
+            float2 pp = make_float2(ex2_approx(y.x), ex2_approx(y.y));  // masked (-inf) -> 0
+            acc = __fadd2_rn(acc, pp);
+            if constexpr (INT8) pp = __fmul2_rn(pp, *reinterpret_cast<const float2*>(vs + t));
+            __half2 hp = __floats2half2_rn(pp.x, pp.y);
+            w[e] = *reinterpret_cast<uint32_t*>(&hp);
+        }
+        *reinterpret_cast<uint4*>(pbuf + sw128(r, c0 + c)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    return acc;
+}
+
+// Softmax of a CTA with two query tiles: warps 4-7 own tile 0, warps 8-11
+// tile 1, one thread per query row over all 64 keys of every K tile (no
+// exchange between threads).  Each tile has one P buffer, so P_j is written
+// only after PV_{j-1} completed.  Returns early (the CTA then exits) when a
+// wait runs out or another role aborted.
+template <bool INT8, int KS>
+__device__ __forceinline__ void softmax_rows(const TreeAttnArgs& a, int warp, int lane, int mt, int b,
+                                             int h, int L, int T_pre, int T, int G, int rows_total,
+                                             uint32_t tmem, uint64_t* qbars, uint8_t* sp,
+                                             const float* sscale, uint64_t* kv_full,
+                                             volatile int* abort_flag) {
+    const int qt = (warp - 4) >> 2, q = warp & 3;
+    const int r = q * 32 + lane;                       // TMEM lane = query row of tile qt
+    const int row = mt * (2 * BMQ) + qt * BMQ + r;
+    const bool row_ok = row < rows_total;
+    const int node = row_ok ? row / G : 0;
+    const uint64_t anc = row_ok ? a.anc[(size_t)b * a.N + node] : 0ull;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const uint32_t tq = tmem + qt * 256;               // S0, S1, O of tile qt
+    uint64_t* qb = qbars + qt * 8;                     // s_full, s_free, p_full, pv_done, o_full
+    uint8_t* pbuf = sp + qt * P_BYTES;
+    if (!__any_sync(0xffffffffu, row_ok)) {
+        // no query row of this warp exists: its P rows stay zero and it only
+        // keeps the barrier counts (arriving on P_j after PV_{j-1} completed,
+        // as the other warps of its tile do)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(pbuf + sw128(r, c)) = make_uint4(0, 0, 0, 0);
+        fence_async_smem();
+        for (int j = 0; j < T; ++j) {
+            const int sb = j & 1;
+            bool got = mbar_wait(&qb[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag, 32);
+            if (!__all_sync(0xffffffffu, got)) return;
+            mbar_arrive(&qb[2 + sb]);
+            if (j > 0) {
+                got = mbar_wait(&qb[6], (j - 1) & 1, a.err, kErrWait, abort_flag, 32);
+                if (!__all_sync(0xffffffffu, got)) return;
+            }
+            mbar_arrive(&qb[4]);
+        }
+        return;
+    }
+    float m = -INFINITY, l = 0.0f;
+    for (int j = 0; j < T; ++j) {
+        const int sb = j & 1, s = j % KS;
+        bool got = mbar_wait(&qb[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag);
+        if (!__all_sync(0xffffffffu, got)) return;
+        tc_fence_after();
+        uint32_t xa[32], xb[32];
+        tmem_ld_32x32b_x32(tq + lane_base + sb * TK, xa);
+        tmem_ld_32x32b_x32(tq + lane_base + sb * TK + 32, xb);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&qb[2 + sb]);
+        const float* ks = sscale + s * 2 * TK;
+        if constexpr (INT8) {
+            // scales of this stage were written by the converter warps
+            got = mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag);
+            if (!__all_sync(0xffffffffu, got)) return;
+        }
+        // maximum of the row's raw scores (scale_log2 > 0 commutes with max):
+        // full tiles of cached tokens need no mask; the tree tile keeps the
+        // node's ancestors, a ragged last tile the tokens below ctx_len
+        float mx;
+        if (j < T_pre && L - j * TK >= TK) {
+            mx = fmaxf(raw_max32<INT8, false>(xa, 0u, ks), raw_max32<INT8, false>(xb, 0u, ks + 32));
+        } else {
+            uint64_t kmask;
+            if (j == T_pre) {
+                kmask = anc;
+            } else {
+                const int nvalid = L - j * TK;
+                kmask = nvalid <= 0 ? 0ull : (1ull << nvalid) - 1ull;  // nvalid < 64 here
+            }
+            mx = fmaxf(raw_max32<INT8, true>(xa, (uint32_t)kmask, ks),
+                       raw_max32<INT8, true>(xb, (uint32_t)(kmask >> 32), ks + 32));
+        }
+        mx *= a.scale_log2;  // the scaled maximum, exactly (rounding is monotonic)
+        // P_j replaces P_{j-1} and O may be rescaled: PV_{j-1} must be done.
+        // Its phase is the only one in doubt: S_j was issued after PV_{j-2}
+        // (so phase j-2 is complete) and PV_j needs this tile's P (so phase j
+        // is not), hence a parity wait is exact here.
+        if (j > 0) {
+            got = mbar_wait(&qb[6], (j - 1) & 1, a.err, kErrWait, abort_flag);
+            if (!__all_sync(0xffffffffu, got)) return;
+            tc_fence_after();
+        }
+        // lazy rescale, decided per warp so the TMEM accesses stay convergent
+        if (__any_sync(0xffffffffu, mx > m + kRescaleLog2)) {
+            const float m_new = fmaxf(m, mx);
+            const float f = m == -INFINITY ? 0.0f : ex2_approx(m - m_new);
+            l *= f;
+            if (j > 0) {
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {  // 16 columns at a time: xa, xb stay in registers
+                    uint32_t o[16];
+                    const uint32_t oc = tq + 128 + lane_base + c * 16;
+                    tmem_ld_32x32b_x16(oc, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+                    tmem_st_32x32b_x16(oc, o);
+                }
+                tmem_st_wait();
+            }
+            m = m_new;
+        }
+        const float ms = m == -INFINITY ? 0.0f : m;  // all keys masked so far: p = 0
+        const float* vs = ks + TK;
+        const float2 sa = exp_pack_store<INT8>(xa, a.scale_log2, ms, vs, pbuf, r, 0);
+        const float2 sb2 = exp_pack_store<INT8>(xb, a.scale_log2, ms, vs + 32, pbuf, r, 4);
+        l += (sa.x + sa.y) + (sb2.x + sb2.y);
+        fence_async_smem();
+        tc_fence_before();
+        mbar_arrive(&qb[4]);
+    }
+    // epilogue: O / l after the last PV
+    {
+        const bool ok = mbar_wait(&qb[7], 0, a.err, kErrWait, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) return;
+    }
+    tc_fence_after();
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    const int g = row_ok ? row % G : 0;
+    const size_t obase = (((size_t)b * a.N + node) * a.Hq + h * G + g) * D;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        const int col = c * 32;
+        tmem_ld_32x32b_x32(tq + 128 + lane_base + col, o);
+        tmem_ld_wait();
+        if (!row_ok) continue;
+        if (a.out_f16) {
+            __half* dst = static_cast<__half*>(a.out) + obase + col;
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) {
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    __half2 hv = __floats2half2_rn(__uint_as_float(o[qq * 8 + 2 * e]) * inv,
+                                                   __uint_as_float(o[qq * 8 + 2 * e + 1]) * inv);
+                    w[e] = *reinterpret_cast<uint32_t*>(&hv);
+                }
+                reinterpret_cast<uint4*>(dst)[qq] = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        } else {
+            float* dst = static_cast<float*>(a.out) + obase + col;
+#pragma unroll
+            for (int qq = 0; qq < 8; ++qq)
+                reinterpret_cast<float4*>(dst)[qq] =
+                    make_float4(__uint_as_float(o[4 * qq]) * inv, __uint_as_float(o[4 * qq + 1]) * inv,
+                                __uint_as_float(o[4 * qq + 2]) * inv, __uint_as_float(o[4 * qq + 3]) * inv);
+        }
+    }
+}
+
 __global__ void tree_ancestors_kernel(const int32_t* __restrict__ parents, int B, int N,
                                       uint64_t* __restrict__ anc, int* err) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -104,38 +331,36 @@ __global__ void tree_ancestors_kernel(const int32_t* __restrict__ parents, int B
     anc[i] = m;
 }
 
-template <bool INT8>
+template <bool INT8, int QT>
 __global__ void __launch_bounds__(kThreads, 1)
     tree_attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                      const __grid_constant__ CUtensorMap tnk, const __grid_constant__ CUtensorMap tnv,
                      const TreeAttnArgs a) {
-    using C = AttnCfg<INT8>;
-    constexpr int KS = C::KS, RS = C::RS;
+    using C = AttnCfg<INT8, QT>;
+    constexpr int KS = C::KS, RS = C::RS, PB = C::PB;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* sq = base;                                // Q: 2 halves x 16 KiB
-    uint8_t* skv = sq + Q_BYTES;                       // KS x (K0 K1 V0 V1) 8 KiB each
-    uint8_t* sp = skv + KS * KV_STAGE;                 // P: 2 x 16 KiB
-    uint8_t* sraw = sp + 2 * P_BYTES;                  // RS x raw int8 stage
+    uint8_t* sq = base;                                // Q: per tile 2 halves x 16 KiB
+    uint8_t* skv = sq + QT * Q_BYTES;                  // KS x (K0 K1 V0 V1) 8 KiB each
+    uint8_t* sp = skv + KS * KV_STAGE;                 // P: [QT][PB] x 16 KiB
+    uint8_t* sraw = sp + QT * PB * P_BYTES;            // RS x raw int8 stage
     float* sscale = reinterpret_cast<float*>(sraw + RS * RAW_STAGE);  // KS x (ks[64], vs[64])
     uint64_t* bars = reinterpret_cast<uint64_t*>(sscale + (INT8 ? KS * 2 * TK : 0));
     uint64_t* kv_full = bars;
     uint64_t* kv_empty = kv_full + KS;
     uint64_t* raw_full = kv_empty + KS;                // RS entries (int8)
     uint64_t* raw_empty = raw_full + (RS ? RS : 1);
-    uint64_t* s_full = raw_empty + (RS ? RS : 1);      // 2
-    uint64_t* s_free = s_full + 2;                     // 2
-    uint64_t* p_full = s_free + 2;                     // 2
-    uint64_t* pv_done = p_full + 2;                    // 1: phase j <-> PV_j done
-    uint64_t* o_full = pv_done + 1;                    // 1: the last PV done
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 1);
+    // per query tile qt, at qt * 8: s_full[2], s_free[2], p_full[2] (PB used),
+    // pv_done (phase j <-> PV_j done), o_full (the last PV done)
+    uint64_t* qbars = raw_empty + (RS ? RS : 1);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qbars + QT * 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    float* sxch = reinterpret_cast<float*>(tmem_slot + 4);  // [2][128] row exchange
+    float* sxch = reinterpret_cast<float*>(tmem_slot + 4);  // [2][128] row exchange (QT = 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.Hq / a.Hkv;
     const int rows_total = a.N * G;
-    const int MT = (rows_total + BMQ - 1) / BMQ;
+    const int MT = (rows_total + QT * BMQ - 1) / (QT * BMQ);
     const int mt = blockIdx.x % MT;
     const int h = (blockIdx.x / MT) % a.Hkv;
     const int b = blockIdx.x / (MT * a.Hkv);
@@ -152,38 +377,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&raw_full[s], 1);
             mbar_init(&raw_empty[s], 128);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 256);
-            mbar_init(&p_full[i], 256);
+        for (int qt = 0; qt < QT; ++qt) {
+            uint64_t* qb = qbars + qt * 8;
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&qb[i], 1);                      // s_full
+                mbar_init(&qb[2 + i], C::kSoftmaxPerQt);   // s_free
+                mbar_init(&qb[4 + i], C::kSoftmaxPerQt);   // p_full
+            }
+            mbar_init(&qb[6], 1);
+            mbar_init(&qb[7], 1);
         }
-        mbar_init(pv_done, 1);
-        mbar_init(o_full, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (warp == 2) {
-        tmem_alloc(tmem_slot, 256);
+        tmem_alloc(tmem_slot, C::kTmemCols);
         tmem_relinquish();
     }
-    // Q tile (all threads): row r = node-major (node, group head), 16 chunks
-    for (int idx = threadIdx.x; idx < BMQ * 16; idx += kThreads) {
-        const int r = idx >> 4, c = idx & 15;
-        const int row = mt * BMQ + r;
+    // Q tiles (all threads): row r = node-major (node, group head), 16 chunks
+    for (int idx = threadIdx.x; idx < QT * BMQ * 16; idx += kThreads) {
+        const int rr = idx >> 4, c = idx & 15;
+        const int qt = rr / BMQ, r = rr % BMQ;
+        const int row = mt * (QT * BMQ) + rr;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (row < rows_total) {
             const int node = row / G, g = row % G;
             const __half* src = a.q + (((size_t)b * a.N + node) * a.Hq + h * G + g) * D + c * 8;
             v = *reinterpret_cast<const uint4*>(src);
         }
-        *reinterpret_cast<uint4*>(sq + (c >> 3) * (Q_BYTES / 2) + sw128(r, c & 7)) = v;
+        *reinterpret_cast<uint4*>(sq + qt * Q_BYTES + (c >> 3) * (Q_BYTES / 2) + sw128(r, c & 7)) = v;
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-    const uint32_t tmem_o = tmem + 128;
+    const uint32_t tmem = *tmem_slot;  // query tile qt: S0, S1, O at qt * 256 + 0, 64, 128
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -265,53 +493,69 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const uint32_t id_s = idesc_f16_f32(BMQ, TK);
             const uint32_t id_pv = idesc_f16_f32(BMQ, D, /*b_mn_major=*/true);
-            const uint32_t q_addr = smem_u32(sq);
-            // Issue S_j and PV_j in whichever order their inputs arrive: S_j
-            // needs its K tile and a free S buffer, PV_j the softmax's P_j.
-            // S_j also waits until PV_{j-2} is issued, so that when S_j
-            // completes every PV before j-1 has completed (the softmax relies
-            // on that to wait for PV_{j-1} by parity alone).
-            int ns = 0, npv = 0;
+            // Per query tile, issue S_j and PV_j in whichever order their
+            // inputs arrive: S_j needs its K tile and a free S buffer, PV_j the
+            // softmax's P_j.  S_j also waits until PV_{j-2} is issued, so that
+            // when S_j completes every PV before j-1 has completed (the softmax
+            // relies on that to wait for PV_{j-1} by parity alone).  A K/V
+            // stage is released after the last query tile's PV of it.
+            int ns[QT], npv[QT];
+#pragma unroll
+            for (int qt = 0; qt < QT; ++qt) ns[qt] = npv[qt] = 0;
             const uint64_t t0 = global_ns();
             uint32_t spins = 0;
-            while (npv < T) {
-                bool progressed = false;
-                if (ns < T && npv >= ns - 1) {
-                    const int s = ns % KS, sb = ns & 1;
-                    if (mbar_test_wait(smem_u32(&kv_full[s]), (ns / KS) & 1) &&
-                        mbar_test_wait(smem_u32(&s_free[sb]), ((ns >> 1) & 1) ^ 1)) {
-                        tc_fence_after();
-                        const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
+            for (;;) {
+                bool progressed = false, all_done = true;
 #pragma unroll
-                        for (int k = 0; k < D / 16; ++k) {
-                            const uint64_t ad = desc_kmajor_sw128(q_addr + (k >> 2) * (Q_BYTES / 2)) + (k & 3) * 2;
-                            const uint64_t bd = desc_kmajor_sw128(k_addr + (k >> 2) * KV_HALF) + (k & 3) * 2;
-                            mma_f16_ss(tmem + sb * TK, ad, bd, id_s, k > 0);
-                        }
-                        mma_commit(&s_full[sb]);
-                        ++ns;
-                        progressed = true;
-                    }
-                }
-                if (npv < ns) {
-                    const int jj = npv, pb = jj & 1, sv = jj % KS;
-                    if (mbar_test_wait(smem_u32(&p_full[pb]), (jj >> 1) & 1)) {
-                        tc_fence_after();
-                        const uint32_t p_addr = smem_u32(sp + pb * P_BYTES);
-                        const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
+                for (int qt = 0; qt < QT; ++qt) {
+                    uint64_t* qb = qbars + qt * 8;
+                    const uint32_t tq = tmem + qt * 256;
+                    if (ns[qt] < T && npv[qt] >= ns[qt] - 1) {
+                        const int j = ns[qt], s = j % KS, sb = j & 1;
+                        if (mbar_test_wait(smem_u32(&kv_full[s]), (j / KS) & 1) &&
+                            mbar_test_wait(smem_u32(&qb[2 + sb]), ((j >> 1) & 1) ^ 1)) {
+                            tc_fence_after();
+                            const uint32_t q_addr = smem_u32(sq + qt * Q_BYTES);
+                            const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
 #pragma unroll
-                        for (int kk = 0; kk < TK / 16; ++kk) {
-                            const uint64_t ad = desc_kmajor_sw128(p_addr) + kk * 2;
-                            const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
-                            mma_f16_ss(tmem_o, ad, bd, id_pv, (jj | kk) != 0);
+                            for (int k = 0; k < D / 16; ++k) {
+                                const uint64_t ad = desc_kmajor_sw128(q_addr + (k >> 2) * (Q_BYTES / 2)) + (k & 3) * 2;
+                                const uint64_t bd = desc_kmajor_sw128(k_addr + (k >> 2) * KV_HALF) + (k & 3) * 2;
+                                mma_f16_ss(tq + sb * TK, ad, bd, id_s, k > 0);
+                            }
+                            mma_commit(&qb[sb]);
+                            ++ns[qt];
+                            progressed = true;
                         }
-                        mma_commit(&kv_empty[sv]);
-                        mma_commit(pv_done);
-                        if (jj == T - 1) mma_commit(o_full);
-                        ++npv;
-                        progressed = true;
                     }
+                    if (npv[qt] < ns[qt]) {
+                        const int jj = npv[qt], sv = jj % KS;
+                        const int pb = PB == 2 ? (jj & 1) : 0;
+                        const uint32_t par = PB == 2 ? ((jj >> 1) & 1) : (jj & 1);
+                        if (mbar_test_wait(smem_u32(&qb[4 + pb]), par)) {
+                            tc_fence_after();
+                            const uint32_t p_addr = smem_u32(sp + (qt * PB + pb) * P_BYTES);
+                            const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
+#pragma unroll
+                            for (int kk = 0; kk < TK / 16; ++kk) {
+                                const uint64_t ad = desc_kmajor_sw128(p_addr) + kk * 2;
+                                const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
+                                mma_f16_ss(tq + 128, ad, bd, id_pv, (jj | kk) != 0);
+                            }
+                            bool last_of_stage = true;
+#pragma unroll
+                            for (int o = 0; o < QT; ++o)
+                                if (o != qt && npv[o] <= jj) last_of_stage = false;
+                            if (last_of_stage) mma_commit(&kv_empty[sv]);
+                            mma_commit(&qb[6]);
+                            if (jj == T - 1) mma_commit(&qb[7]);
+                            ++npv[qt];
+                            progressed = true;
+                        }
+                    }
+                    if (npv[qt] < T) all_done = false;
                 }
+                if (all_done) break;
                 if (!progressed && (++spins & 255u) == 0) {
                     if (*abort_flag) goto done;
                     if (global_ns() - t0 > kWaitLimitNs * 8) {  // a whole item, not one wait
@@ -324,180 +568,191 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= 4 && warp < 12) {
         // ------------------------------------------------------------ softmax
-        // warps w and w + 4 share TMEM lane quadrant q = w % 4 (query rows
-        // 32q..32q+31); half ch = 0 takes keys 0..31 and O columns 0..63, ch = 1
-        // keys 32..63 and O columns 64..127.  Row maxima and sums meet in
-        // shared memory behind a named barrier of the warp pair.
-        const int q = warp & 3, ch = (warp - 4) >> 2;
-        const int r = q * 32 + lane;               // TMEM lane = query row
-        const int row = mt * BMQ + r;
-        const bool row_ok = row < rows_total;
-        const int node = row_ok ? row / G : 0;
-        const uint64_t anc = row_ok ? a.anc[(size_t)b * a.N + node] : 0ull;
-        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        float* xch = sxch + ch * BMQ;              // this half's row values
-        const float* xoth = sxch + (ch ^ 1) * BMQ; // the partner's
-        const int kbase = ch * 32;
-        float m = -INFINITY, l = 0.0f;             // l: this half's partial sum
-        if (!__any_sync(0xffffffffu, row_ok)) {
-            // no query row of this warp exists (few nodes x heads, e.g. 16 rows
-            // of 128): its P rows stay zero and it only keeps the barrier
-            // counts, leaving the SFU and issue slots to the warps with rows
+        if constexpr (QT == 1) {
+            uint64_t* s_full = qbars;
+            uint64_t* s_free = qbars + 2;
+            uint64_t* p_full = qbars + 4;
+            uint64_t* pv_done = qbars + 6;
+            uint64_t* o_full = qbars + 7;
+            const uint32_t tmem_o = tmem + 128;
+            // warps w and w + 4 share TMEM lane quadrant q = w % 4 (query rows
+            // 32q..32q+31); half ch = 0 takes keys 0..31 and O columns 0..63, ch = 1
+            // keys 32..63 and O columns 64..127.  Row maxima and sums meet in
+            // shared memory behind a named barrier of the warp pair.
+            const int q = warp & 3, ch = (warp - 4) >> 2;
+            const int r = q * 32 + lane;               // TMEM lane = query row
+            const int row = mt * BMQ + r;
+            const bool row_ok = row < rows_total;
+            const int node = row_ok ? row / G : 0;
+            const uint64_t anc = row_ok ? a.anc[(size_t)b * a.N + node] : 0ull;
+            const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+            float* xch = sxch + ch * BMQ;              // this half's row values
+            const float* xoth = sxch + (ch ^ 1) * BMQ; // the partner's
+            const int kbase = ch * 32;
+            float m = -INFINITY, l = 0.0f;             // l: this half's partial sum
+            if (!__any_sync(0xffffffffu, row_ok)) {
+                // no query row of this warp exists (few nodes x heads, e.g. 16 rows
+                // of 128): its P rows stay zero and it only keeps the barrier
+                // counts, leaving the SFU and issue slots to the warps with rows
 #pragma unroll
-            for (int pb = 0; pb < 2; ++pb)
+                for (int pb = 0; pb < 2; ++pb)
 #pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    *reinterpret_cast<uint4*>(sp + pb * P_BYTES + sw128(r, ch * 4 + c)) = make_uint4(0, 0, 0, 0);
-            fence_async_smem();
+                    for (int c = 0; c < 4; ++c)
+                        *reinterpret_cast<uint4*>(sp + pb * P_BYTES + sw128(r, ch * 4 + c)) = make_uint4(0, 0, 0, 0);
+                fence_async_smem();
+                for (int j = 0; j < T; ++j) {
+                    const int sb = j & 1;
+                    const bool got = mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag, 32);
+                    if (!__all_sync(0xffffffffu, got)) goto done;
+                    mbar_arrive(&s_free[sb]);
+                    mbar_arrive(&p_full[sb]);
+                }
+                goto done;
+            }
             for (int j = 0; j < T; ++j) {
-                const int sb = j & 1;
-                const bool got = mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag, 32);
+                const int sb = j & 1, s = j % KS;
+                const bool got = mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag);
                 if (!__all_sync(0xffffffffu, got)) goto done;
+                tc_fence_after();
+                uint32_t x32[32];
+                tmem_ld_32x32b_x32(tmem + lane_base + sb * TK + kbase, x32);
+                tmem_ld_wait();
+                tc_fence_before();
                 mbar_arrive(&s_free[sb]);
+                const bool tree = j == T_pre;
+                const float* ks = sscale + s * 2 * TK + kbase;
+                if constexpr (INT8) {
+                    // scales of this stage were written by the converter warps
+                    const bool ok = mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag);
+                    if (!__all_sync(0xffffffffu, ok)) goto done;
+                }
+                // this thread's 32 keys as a bit mask: the node's ancestors in the
+                // tree tile, the cached tokens below ctx_len otherwise
+                uint32_t kmask;
+                if (tree) {
+                    kmask = (uint32_t)(anc >> kbase);
+                } else {
+                    const int nvalid = L - (j * TK + kbase);
+                    kmask = nvalid >= 32 ? 0xffffffffu : nvalid <= 0 ? 0u : (1u << nvalid) - 1u;
+                }
+                // scaled scores (log2 domain) overwrite the raw ones in place
+                float* x = reinterpret_cast<float*>(x32);
+                float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int t = 0; t < 32; ++t) {
+                    float v = x[t] * a.scale_log2;
+                    if constexpr (INT8) v *= ks[t];
+                    v = ((kmask >> t) & 1u) ? v : -INFINITY;
+                    x[t] = v;
+                    pm[t & 3] = fmaxf(pm[t & 3], v);
+                }
+                float mx = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
+                xch[r] = mx;
+                pair_sync(q);
+                mx = fmaxf(mx, xoth[r]);
+                // lazy rescale, decided per warp (identically in both warps of the
+                // pair) so the TMEM accesses stay convergent
+                if (__any_sync(0xffffffffu, mx > m + kRescaleLog2)) {
+                    const float m_new = fmaxf(m, mx);
+                    const float f = m == -INFINITY ? 0.0f : ex2_approx(m - m_new);
+                    l *= f;
+                    if (j > 0) {
+                        // O holds PV_0..PV_{j-1}; wait for PV_{j-1}.  Its phase is the
+                        // only one in doubt: S_j was issued after PV_{j-2} (so phase
+                        // j-2 is complete) and PV_j needs this tile's P (so phase j
+                        // is not), hence a parity wait is exact here.
+                        const bool ok = mbar_wait(pv_done, (j - 1) & 1, a.err, kErrWait, abort_flag);
+                        if (!__all_sync(0xffffffffu, ok)) goto done;
+                        tc_fence_after();
+#pragma unroll 1
+                        for (int c = 0; c < 2; ++c) {
+                            uint32_t o[32];
+                            const uint32_t oc = tmem_o + lane_base + ch * 64 + c * 32;
+                            tmem_ld_32x32b_x32(oc, o);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+                            tmem_st_32x32b_x32(oc, o);
+                        }
+                        tmem_st_wait();
+                    }
+                    m = m_new;
+                }
+                // P (times the V scale for int8 pages) -> f16, this half of row r
+                uint8_t* prow = sp + sb * P_BYTES;
+                const float* vs = ks + TK;
+                const float ms = m == -INFINITY ? 0.0f : m;  // all keys masked so far: p = 0
+                float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int t = c * 8 + 2 * e;
+                        float p0 = ex2_approx(x[t] - ms);      // masked (-inf) -> 0
+                        float p1 = ex2_approx(x[t + 1] - ms);
+                        ls[e] += p0 + p1;
+                        if constexpr (INT8) {
+                            p0 *= vs[t];
+                            p1 *= vs[t + 1];
+                        }
+                        __half2 hp = __floats2half2_rn(p0, p1);
+                        w[e] = *reinterpret_cast<uint32_t*>(&hp);
+                    }
+                    *reinterpret_cast<uint4*>(prow + sw128(r, ch * 4 + c)) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+                fence_async_smem();
+                tc_fence_before();
                 mbar_arrive(&p_full[sb]);
             }
-            goto done;
-        }
-        for (int j = 0; j < T; ++j) {
-            const int sb = j & 1, s = j % KS;
-            const bool got = mbar_wait(&s_full[sb], (j >> 1) & 1, a.err, kErrWait, abort_flag);
-            if (!__all_sync(0xffffffffu, got)) goto done;
-            tc_fence_after();
-            uint32_t x32[32];
-            tmem_ld_32x32b_x32(tmem + lane_base + sb * TK + kbase, x32);
-            tmem_ld_wait();
-            tc_fence_before();
-            mbar_arrive(&s_free[sb]);
-            const bool tree = j == T_pre;
-            const float* ks = sscale + s * 2 * TK + kbase;
-            if constexpr (INT8) {
-                // scales of this stage were written by the converter warps
-                const bool ok = mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag);
+            // epilogue: O / (both halves' sums) after the last PV
+            {
+                const bool ok = mbar_wait(o_full, 0, a.err, kErrWait, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) goto done;
             }
-            // this thread's 32 keys as a bit mask: the node's ancestors in the
-            // tree tile, the cached tokens below ctx_len otherwise
-            uint32_t kmask;
-            if (tree) {
-                kmask = (uint32_t)(anc >> kbase);
-            } else {
-                const int nvalid = L - (j * TK + kbase);
-                kmask = nvalid >= 32 ? 0xffffffffu : nvalid <= 0 ? 0u : (1u << nvalid) - 1u;
-            }
-            // scaled scores (log2 domain) overwrite the raw ones in place
-            float* x = reinterpret_cast<float*>(x32);
-            float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-                float v = x[t] * a.scale_log2;
-                if constexpr (INT8) v *= ks[t];
-                v = ((kmask >> t) & 1u) ? v : -INFINITY;
-                x[t] = v;
-                pm[t & 3] = fmaxf(pm[t & 3], v);
-            }
-            float mx = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
-            xch[r] = mx;
+            tc_fence_after();
+            pair_sync(q);  // the partner finished reading xch for the last tile
+            xch[r] = l;
             pair_sync(q);
-            mx = fmaxf(mx, xoth[r]);
-            // lazy rescale, decided per warp (identically in both warps of the
-            // pair) so the TMEM accesses stay convergent
-            if (__any_sync(0xffffffffu, mx > m + kRescaleLog2)) {
-                const float m_new = fmaxf(m, mx);
-                const float f = m == -INFINITY ? 0.0f : ex2_approx(m - m_new);
-                l *= f;
-                if (j > 0) {
-                    // O holds PV_0..PV_{j-1}; wait for PV_{j-1}.  Its phase is the
-                    // only one in doubt: S_j was issued after PV_{j-2} (so phase
-                    // j-2 is complete) and PV_j needs this tile's P (so phase j
-                    // is not), hence a parity wait is exact here.
-                    const bool ok = mbar_wait(pv_done, (j - 1) & 1, a.err, kErrWait, abort_flag);
-                    if (!__all_sync(0xffffffffu, ok)) goto done;
-                    tc_fence_after();
+            {
+                const float lt = l + xoth[r];
+                const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+                const int g = row_ok ? row % G : 0;
+                const size_t obase = (((size_t)b * a.N + node) * a.Hq + h * G + g) * D;
 #pragma unroll 1
-                    for (int c = 0; c < 2; ++c) {
-                        uint32_t o[32];
-                        const uint32_t oc = tmem_o + lane_base + ch * 64 + c * 32;
-                        tmem_ld_32x32b_x32(oc, o);
-                        tmem_ld_wait();
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t o[32];
+                    const int col = ch * 64 + c * 32;
+                    tmem_ld_32x32b_x32(tmem_o + lane_base + col, o);
+                    tmem_ld_wait();
+                    if (!row_ok) continue;
+                    if (a.out_f16) {
+                        __half* dst = static_cast<__half*>(a.out) + obase + col;
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-                        tmem_st_32x32b_x32(oc, o);
-                    }
-                    tmem_st_wait();
-                }
-                m = m_new;
-            }
-            // P (times the V scale for int8 pages) -> f16, this half of row r
-            uint8_t* prow = sp + sb * P_BYTES;
-            const float* vs = ks + TK;
-            const float ms = m == -INFINITY ? 0.0f : m;  // all keys masked so far: p = 0
-            float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                        for (int qq = 0; qq < 4; ++qq) {
+                            uint32_t w[4];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int t = c * 8 + 2 * e;
-                    float p0 = ex2_approx(x[t] - ms);      // masked (-inf) -> 0
-                    float p1 = ex2_approx(x[t + 1] - ms);
-                    ls[e] += p0 + p1;
-                    if constexpr (INT8) {
-                        p0 *= vs[t];
-                        p1 *= vs[t + 1];
-                    }
-                    __half2 hp = __floats2half2_rn(p0, p1);
-                    w[e] = *reinterpret_cast<uint32_t*>(&hp);
-                }
-                *reinterpret_cast<uint4*>(prow + sw128(r, ch * 4 + c)) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-            l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-            fence_async_smem();
-            tc_fence_before();
-            mbar_arrive(&p_full[sb]);
-        }
-        // epilogue: O / (both halves' sums) after the last PV
-        {
-            const bool ok = mbar_wait(o_full, 0, a.err, kErrWait, abort_flag);
-            if (!__all_sync(0xffffffffu, ok)) goto done;
-        }
-        tc_fence_after();
-        pair_sync(q);  // the partner finished reading xch for the last tile
-        xch[r] = l;
-        pair_sync(q);
-        {
-            const float lt = l + xoth[r];
-            const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
-            const int g = row_ok ? row % G : 0;
-            const size_t obase = (((size_t)b * a.N + node) * a.Hq + h * G + g) * D;
-#pragma unroll 1
-            for (int c = 0; c < 2; ++c) {
-                uint32_t o[32];
-                const int col = ch * 64 + c * 32;
-                tmem_ld_32x32b_x32(tmem_o + lane_base + col, o);
-                tmem_ld_wait();
-                if (!row_ok) continue;
-                if (a.out_f16) {
-                    __half* dst = static_cast<__half*>(a.out) + obase + col;
-#pragma unroll
-                    for (int qq = 0; qq < 4; ++qq) {
-                        uint32_t w[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            __half2 hv = __floats2half2_rn(__uint_as_float(o[qq * 8 + 2 * e]) * inv,
-                                                           __uint_as_float(o[qq * 8 + 2 * e + 1]) * inv);
-                            w[e] = *reinterpret_cast<uint32_t*>(&hv);
+                            for (int e = 0; e < 4; ++e) {
+                                __half2 hv = __floats2half2_rn(__uint_as_float(o[qq * 8 + 2 * e]) * inv,
+                                                               __uint_as_float(o[qq * 8 + 2 * e + 1]) * inv);
+                                w[e] = *reinterpret_cast<uint32_t*>(&hv);
+                            }
+                            reinterpret_cast<uint4*>(dst)[qq] = make_uint4(w[0], w[1], w[2], w[3]);
                         }
-                        reinterpret_cast<uint4*>(dst)[qq] = make_uint4(w[0], w[1], w[2], w[3]);
-                    }
-                } else {
-                    float* dst = static_cast<float*>(a.out) + obase + col;
+                    } else {
+                        float* dst = static_cast<float*>(a.out) + obase + col;
 #pragma unroll
-                    for (int qq = 0; qq < 8; ++qq)
-                        reinterpret_cast<float4*>(dst)[qq] =
-                            make_float4(__uint_as_float(o[4 * qq]) * inv, __uint_as_float(o[4 * qq + 1]) * inv,
-                                        __uint_as_float(o[4 * qq + 2]) * inv, __uint_as_float(o[4 * qq + 3]) * inv);
+                        for (int qq = 0; qq < 8; ++qq)
+                            reinterpret_cast<float4*>(dst)[qq] =
+                                make_float4(__uint_as_float(o[4 * qq]) * inv, __uint_as_float(o[4 * qq + 1]) * inv,
+                                            __uint_as_float(o[4 * qq + 2]) * inv, __uint_as_float(o[4 * qq + 3]) * inv);
+                    }
                 }
             }
+        } else {
+            softmax_rows<INT8, KS>(a, warp, lane, mt, b, h, L, T_pre, T, G, rows_total, tmem, qbars, sp,
+                                   sscale, kv_full, abort_flag);
         }
     } else if (warp >= 12) {
         // ------------------------------------------------------------ converters
@@ -536,14 +791,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         uint8_t* dst = st + kvs * 2 * KV_HALF + hh * KV_HALF;
 #pragma unroll
                         for (int c4 = 0; c4 < 4; ++c4) {
-                            const uint4 raw = src[c4];  // 16 int8 -> two 16-byte f16 chunks
+                            // chunks in a per-row rotation: the 16 rows a warp reads
+                            // (128 B apart) then spread over all banks
+                            const int cc = (c4 + kr) & 3;
+                            const uint4 raw = src[cc];  // 16 int8 -> two 16-byte f16 chunks
                             uint32_t o[8];
                             i8x4_to_f16(raw.x, o[0], o[1]);
                             i8x4_to_f16(raw.y, o[2], o[3]);
                             i8x4_to_f16(raw.z, o[4], o[5]);
                             i8x4_to_f16(raw.w, o[6], o[7]);
-                            *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4)) = make_uint4(o[0], o[1], o[2], o[3]);
-                            *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * c4 + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+                            *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * cc)) = make_uint4(o[0], o[1], o[2], o[3]);
+                            *reinterpret_cast<uint4*>(dst + sw128(kr, 2 * cc + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
                         }
                     }
                     const __half* sc = reinterpret_cast<const __half*>(rs + 2 * RAW_KV);
@@ -560,18 +818,18 @@ done:
     __syncthreads();
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem, 256);
+        tmem_dealloc(tmem, C::kTmemCols);
     }
 }
 
-template <bool INT8>
+template <bool INT8, int QT>
 cudaError_t launch_impl(const TreeAttnArgs& a, cudaStream_t stream) {
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
     std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(tree_attn_kernel<INT8>,
+        attr_err = cudaFuncSetAttribute(tree_attn_kernel<INT8, QT>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)AttnCfg<INT8>::kSmem);
+                                        (int)AttnCfg<INT8, QT>::kSmem);
     });
     if (attr_err != cudaSuccess) return attr_err;
     CUtensorMap tk{}, tv{}, tnk{}, tnv{};
@@ -587,10 +845,27 @@ cudaError_t launch_impl(const TreeAttnArgs& a, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
     }
     const int G = a.Hq / a.Hkv;
-    const int MT = (a.N * G + BMQ - 1) / BMQ;
+    const int MT = (a.N * G + QT * BMQ - 1) / (QT * BMQ);
     const long grid = (long)a.B * a.Hkv * MT;
-    tree_attn_kernel<INT8><<<(unsigned)grid, kThreads, AttnCfg<INT8>::kSmem, stream>>>(tk, tv, tnk, tnv, a);
+    tree_attn_kernel<INT8, QT><<<(unsigned)grid, kThreads, AttnCfg<INT8, QT>::kSmem, stream>>>(tk, tv, tnk,
+                                                                                              tnv, a);
     return cudaGetLastError();
+}
+
+// VELO_ATTN_QUERY_TILES=1 in the environment keeps one query tile per CTA at
+// every size (read at each launch; for comparisons of the two layouts).
+bool force_one_tile() {
+    const char* e = std::getenv("VELO_ATTN_QUERY_TILES");
+    return e != nullptr && e[0] == '1' && e[1] == '\0';
+}
+
+// Query rows per KV head (nodes x group heads) above 128 take two query tiles
+// per CTA, so each K/V tile is fetched (and converted) once for both.
+template <bool INT8>
+cudaError_t launch_rows(const TreeAttnArgs& a, cudaStream_t stream) {
+    const int rows = a.N * (a.Hq / a.Hkv);
+    if (rows > BMQ && !force_one_tile()) return launch_impl<INT8, 2>(a, stream);
+    return launch_impl<INT8, 1>(a, stream);
 }
 
 }  // namespace
@@ -603,7 +878,7 @@ cudaError_t launch_tree_ancestors(const int32_t* parents, int B, int N, uint64_t
 }
 
 cudaError_t launch_tree_attention(const TreeAttnArgs& a, bool kv_int8, cudaStream_t stream) {
-    return kv_int8 ? launch_impl<true>(a, stream) : launch_impl<false>(a, stream);
+    return kv_int8 ? launch_rows<true>(a, stream) : launch_rows<false>(a, stream);
 }
 
 }  // namespace velo
