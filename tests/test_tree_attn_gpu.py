@@ -72,9 +72,10 @@ def test_tree_attention_matches_oracle(ctx, kv_dtype, B, N, Hq, Hkv, ctx_lens):
 
 @pytest.mark.parametrize("kv_dtype", [0, 1])
 def test_one_and_two_query_tiles_agree(ctx, monkeypatch, kv_dtype):
-    # 256 rows per KV head: two query tiles per CTA by default, one per CTA
-    # with VELO_ATTN_QUERY_TILES=1; both layouts meet the oracle
+    # 256 rows per KV head in one CTA of two query tiles or two CTAs of one
+    # (VELO_ATTN_QUERY_TILES forces the layout); both meet the oracle
     d = synthetic.tree_attention_inputs(2, 64, 32, 8, [700, 2100], kv_dtype=kv_dtype, seed=11)
+    monkeypatch.setenv("VELO_ATTN_QUERY_TILES", "2")
     two = _gpu(ctx, d, 8)
     monkeypatch.setenv("VELO_ATTN_QUERY_TILES", "1")
     one = _gpu(ctx, d, 8)
