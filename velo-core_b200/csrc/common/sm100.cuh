@@ -26,6 +26,19 @@ __device__ __forceinline__ uint64_t global_ns() {
 // Wait limit for every barrier in this file (2 s of wall time).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// One lane of the (converged) warp is elected: true there, false elsewhere.
+// Loops that issue tcgen05 work run on the whole warp with warp-uniform state
+// and elect the issuing lane, so their state stays in uniform registers.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

@@ -300,31 +300,37 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = idesc_f16_f32(BM, BN);
-            uint32_t g = 0, it = 0;
-            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-                const int b = it & 1;
-                const uint32_t aph = (it >> 1) & 1;
-                if (!mbar_wait(&aempty[b], aph ^ 1, a.err, kErrWaitAccEmpty, abort_flag)) goto done;
+        // MMA issue: the whole warp runs the loop on warp-uniform state (so it
+        // stays in uniform registers); one elected lane issues the MMAs and
+        // their commits
+        const uint32_t idesc = idesc_f16_f32(BM, BN);
+        uint32_t g = 0, it = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+            const int b = it & 1;
+            const uint32_t aph = (it >> 1) & 1;
+            const bool ok = mbar_wait(&aempty[b], aph ^ 1, a.err, kErrWaitAccEmpty, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) goto done;
+            tc_fence_after();
+            const uint32_t d = tmem + b * BN;
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % XSTAGES, ws = g % WSTAGES;
+                const bool ready = mbar_wait(&xfull[s], (g / XSTAGES) & 1, a.err, kErrWaitFull, abort_flag) &&
+                                   mbar_wait(&wfull[ws], (g / WSTAGES) & 1, a.err, kErrWaitReady, abort_flag);
+                if (!__all_sync(0xffffffffu, ready)) goto done;
                 tc_fence_after();
-                const uint32_t d = tmem + b * BN;
-                for (int kt = 0; kt < KT; ++kt, ++g) {
-                    const int s = g % XSTAGES, ws = g % WSTAGES;
-                    if (!mbar_wait(&xfull[s], (g / XSTAGES) & 1, a.err, kErrWaitFull, abort_flag) ||
-                        !mbar_wait(&wfull[ws], (g / WSTAGES) & 1, a.err, kErrWaitReady, abort_flag))
-                        goto done;
-                    tc_fence_after();
-                    const uint64_t ad = desc_kmajor_sw128(smem_u32(sx + s * X_BYTES));
-                    const uint64_t bd = desc_kmajor_sw128(smem_u32(sw + ws * W_BYTES));
+                const uint64_t ad = desc_kmajor_sw128(smem_u32(sx + s * X_BYTES));
+                const uint64_t bd = desc_kmajor_sw128(smem_u32(sw + ws * W_BYTES));
+                if (elect_one()) {
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
                         mma_f16_ss(d, ad + 2 * k, bd + 2 * k, idesc, (kt | k) != 0);
                     mma_commit(&xempty[s]);
                     mma_commit(&wempty[ws]);
                 }
-                mma_commit(&afull[b]);
+                __syncwarp();
             }
+            if (elect_one()) mma_commit(&afull[b]);
+            __syncwarp();
         }
     } else if (warp >= 4 && warp < C::kEpiWarp0) {
         // dequantisation: thread i owns weight row i of every tile

@@ -542,10 +542,13 @@ __global__ void __launch_bounds__(TmCfg<INT8, QT>::kThreads, 1)
                                     kv_empty, raw_full, raw_empty, abort_flag);
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issue
-        if (lane == 0) {
+        // The whole warp runs the loop on warp-uniform state; one elected lane
+        // issues each group of MMAs and its commits.
+        {
             const uint32_t id_s = idesc_f16_f32(BMQ, TK);
             const uint32_t id_pv = idesc_f16_f32(BMQ, D, /*b_mn_major=*/true);
-            if (!mbar_wait(q_full, 0, a.err, kErrWait, abort_flag)) goto done;
+            const bool qok = mbar_wait(q_full, 0, a.err, kErrWait, abort_flag);
+            if (!__all_sync(0xffffffffu, qok)) goto done;
             tc_fence_after();
             // Per query tile, S_j = Q K_j^T (A: Q in TMEM) and PV_j: O += P_j V_j
             // (A: P_j in TMEM, over S_j's columns), issued in whichever order
@@ -567,37 +570,43 @@ __global__ void __launch_bounds__(TmCfg<INT8, QT>::kThreads, 1)
                     const TileBars tb = tile_bars(qbars, qt);
                     if (ns[qt] < T && npv[qt] >= ns[qt] - (SB - 1)) {
                         const int j = ns[qt], s = j % KS, sb = j % SB;
-                        if (mbar_test_wait(smem_u32(&kv_full[s]), (j / KS) & 1)) {
+                        if (__shfl_sync(0xffffffffu, mbar_test_wait(smem_u32(&kv_full[s]), (j / KS) & 1), 0)) {
                             tc_fence_after();
                             const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
+                            if (elect_one()) {
 #pragma unroll
-                            for (int k = 0; k < D / 16; ++k) {
-                                const uint64_t bd = desc_kmajor_sw128(k_addr + (k >> 2) * KV_HALF) + (k & 3) * 2;
-                                mma_f16_ts(tmem + C::colS(qt, sb), tmem + C::colQ(qt) + k * 8, bd, id_s, k > 0);
+                                for (int k = 0; k < D / 16; ++k) {
+                                    const uint64_t bd = desc_kmajor_sw128(k_addr + (k >> 2) * KV_HALF) + (k & 3) * 2;
+                                    mma_f16_ts(tmem + C::colS(qt, sb), tmem + C::colQ(qt) + k * 8, bd, id_s, k > 0);
+                                }
+                                mma_commit(&tb.s_full[sb]);
                             }
-                            mma_commit(&tb.s_full[sb]);
+                            __syncwarp();
                             ++ns[qt];
                             progressed = true;
                         }
                     }
                     if (npv[qt] < ns[qt]) {
                         const int jj = npv[qt], pb = jj % SB, sv = jj % KS;
-                        if (mbar_test_wait(smem_u32(&tb.p_full[pb]), (jj / SB) & 1)) {
+                        if (__shfl_sync(0xffffffffu, mbar_test_wait(smem_u32(&tb.p_full[pb]), (jj / SB) & 1), 0)) {
                             tc_fence_after();
                             const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
-#pragma unroll
-                            for (int kk = 0; kk < TK / 16; ++kk) {
-                                const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
-                                mma_f16_ts(tmem + C::colO(qt), tmem + C::colS(qt, pb) + kk * 8, bd, id_pv,
-                                           (jj | kk) != 0);
-                            }
                             bool last_of_stage = true;
 #pragma unroll
                             for (int o = 0; o < QT; ++o)
                                 if (o != qt && npv[o] <= jj) last_of_stage = false;
-                            if (last_of_stage) mma_commit(&kv_empty[sv]);
-                            mma_commit(tb.pv_done);
-                            if (jj == T - 1) mma_commit(tb.o_full);
+                            if (elect_one()) {
+#pragma unroll
+                                for (int kk = 0; kk < TK / 16; ++kk) {
+                                    const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
+                                    mma_f16_ts(tmem + C::colO(qt), tmem + C::colS(qt, pb) + kk * 8, bd, id_pv,
+                                               (jj | kk) != 0);
+                                }
+                                if (last_of_stage) mma_commit(&kv_empty[sv]);
+                                mma_commit(tb.pv_done);
+                                if (jj == T - 1) mma_commit(tb.o_full);
+                            }
+                            __syncwarp();
                             ++npv[qt];
                             progressed = true;
                         }
@@ -606,10 +615,12 @@ __global__ void __launch_bounds__(TmCfg<INT8, QT>::kThreads, 1)
                 }
                 if (all_done) break;
                 if (!progressed && (++spins & 255u) == 0) {
-                    if (*abort_flag) goto done;
-                    if (global_ns() - t0 > kWaitLimitNs * 8) {  // a whole item, not one wait
-                        atomicCAS(a.err, 0, kErrWait);
-                        *abort_flag = 1;
+                    const bool stop = *abort_flag != 0 || global_ns() - t0 > kWaitLimitNs * 8;
+                    if (__shfl_sync(0xffffffffu, stop, 0)) {  // a whole item, not one wait
+                        if (lane == 0 && *abort_flag == 0) {
+                            atomicCAS(a.err, 0, kErrWait);
+                            *abort_flag = 1;
+                        }
                         goto done;
                     }
                 }
@@ -667,17 +678,16 @@ cudaError_t launch_impl(const TreeAttnArgs& a, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
-// Int8 pools with more than 128 query rows per KV head (nodes x group heads)
-// take two query tiles per CTA: each K/V tile is then converted once for 256
-// rows (config 4: 1041 us against 1246 with one tile).  f16 pools keep one
-// tile and double-buffered S/P, which measured faster (config-5 layer: 459 us
-// against 479).  VELO_ATTN_QUERY_TILES=1 or 2 in the environment forces one
-// layout (read at each launch; for comparisons).
+// More than 128 query rows per KV head (nodes x group heads) take two query
+// tiles per CTA: each K/V tile is then fetched (and converted) once for 256
+// rows (config 4: 802 us against 1246 with one tile per CTA; config-5 layer:
+// 359 us against 455).  VELO_ATTN_QUERY_TILES=1 or 2 in the environment
+// forces one layout (read at each launch; for comparisons).
 template <bool INT8>
 cudaError_t launch_rows(const TreeAttnArgs& a, cudaStream_t stream) {
     const char* e = std::getenv("VELO_ATTN_QUERY_TILES");
     const bool many_rows = a.N * (a.Hq / a.Hkv) > BMQ;
-    int qt = INT8 && many_rows ? 2 : 1;
+    int qt = many_rows ? 2 : 1;
     if (e != nullptr && std::strcmp(e, "1") == 0) qt = 1;
     if (e != nullptr && std::strcmp(e, "2") == 0 && many_rows) qt = 2;
     return qt == 2 ? launch_impl<INT8, 2>(a, stream) : launch_impl<INT8, 1>(a, stream);
