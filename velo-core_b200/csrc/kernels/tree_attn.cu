@@ -107,88 +107,90 @@ __global__ void tree_ancestors_kernel(const int32_t* __restrict__ parents, int B
     anc[i] = m;
 }
 
-// Producer role (lane 0 of its warp): the K/V tiles of the sequence's pages into the
-// ring -- f16 pools by TMA (128-byte swizzle straight into the operand tiles,
-// the tree tile by a 3-D TMA of the node rows), int8 pools as raw bulk copies
-// of pages and scales for the converters.  Returns early on abort.
+// Producer role (one warp on warp-uniform state; an elected lane issues the
+// copies): the K/V tiles of the sequence's pages into the ring -- f16 pools by
+// TMA (128-byte swizzle straight into the operand tiles, the tree tile by a
+// 3-D TMA of the node rows), int8 pools as raw bulk copies of pages and scales
+// for the converters.  Returns early on abort.
 template <bool INT8, int KS, int RS>
 __device__ __forceinline__ void produce_tiles(const TreeAttnArgs& a, const CUtensorMap* tmk,
                                               const CUtensorMap* tmv, const CUtensorMap* tnk,
-                                              const CUtensorMap* tnv, int lane, int b, int h,
-                                              int T_pre, int T, uint8_t* skv, uint8_t* sraw,
-                                              uint64_t* kv_full, uint64_t* kv_empty, uint64_t* raw_full,
-                                              uint64_t* raw_empty, volatile int* abort_flag) {
-    if (lane == 0) {
-        const uint32_t* pt = a.page_table + (size_t)b * a.max_pages;
-        // page ids of the next tile are read one iteration early, so the
-        // global-memory latency hides behind the wait for a free slot
-        uint32_t pg_next[TK / kKvPage];
-        auto fetch = [&](int j, uint32_t (&dst)[TK / kKvPage]) {
+                                              const CUtensorMap* tnv, int b, int h, int T_pre, int T,
+                                              uint8_t* skv, uint8_t* sraw, uint64_t* kv_full,
+                                              uint64_t* kv_empty, uint64_t* raw_full, uint64_t* raw_empty,
+                                              volatile int* abort_flag) {
+    constexpr int PPT = TK / kKvPage;  // pages per tile
+    const uint32_t* pt = a.page_table + (size_t)b * a.max_pages;
+    // page ids of the next tile are read one iteration early, so the
+    // global-memory latency hides behind the wait for a free slot
+    uint32_t pg_next[PPT];
+    auto fetch = [&](int j, uint32_t (&dst)[PPT]) {
 #pragma unroll
-            for (int i = 0; i < TK / kKvPage; ++i) {
-                const int pi = j * (TK / kKvPage) + i;
-                dst[i] = (j < T_pre && pi < a.max_pages) ? pt[pi] : 0u;
+        for (int i = 0; i < PPT; ++i) {
+            const int pi = j * PPT + i;
+            dst[i] = (j < T_pre && pi < a.max_pages) ? pt[pi] : 0u;
+        }
+    };
+    fetch(0, pg_next);
+    for (int j = 0; j < (INT8 ? T_pre : T); ++j) {
+        uint32_t pg[PPT];
+        bool bad = false;
+#pragma unroll
+        for (int i = 0; i < PPT; ++i) {
+            pg[i] = pg_next[i];
+            if (pg[i] >= (uint32_t)a.pool_pages) {
+                bad = true;
+                pg[i] = 0;
             }
-        };
-        fetch(0, pg_next);
-        for (int j = 0; j < (INT8 ? T_pre : T); ++j) {
-            uint32_t pg_cur[TK / kKvPage];
-#pragma unroll
-            for (int i = 0; i < TK / kKvPage; ++i) pg_cur[i] = pg_next[i];
-            fetch(j + 1, pg_next);
-            if constexpr (!INT8) {
-                const int s = j % KS;
-                if (!mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag, 64))
-                    return;
+        }
+        fetch(j + 1, pg_next);
+        if constexpr (!INT8) {
+            const int s = j % KS;
+            const bool ok = mbar_wait(&kv_empty[s], ((j / KS) & 1) ^ 1, a.err, kErrWait, abort_flag, 64);
+            if (!__all_sync(0xffffffffu, ok)) return;
+            if (elect_one()) {
+                if (bad) atomicCAS(a.err, 0, kErrPage);
+                mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
+                uint8_t* st = skv + s * KV_STAGE;
                 if (j == T_pre) {
                     // tree tile: node K/V rows b*N .. b*N+63 of KV head h (3-D
-                    // maps [B*N][Hkv][128]); rows past this sequence's nodes are
-                    // masked, rows past the tensor read as zero
-                    mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
-                    uint8_t* st = skv + s * KV_STAGE;
+                    // maps [B*N][Hkv][128]); rows past this sequence's nodes
+                    // are masked, rows past the tensor read as zero
                     for (int dh = 0; dh < 2; ++dh) {
                         tma_load_3d(st + dh * KV_HALF, tnk, &kv_full[s], dh * 64, h, b * a.N);
                         tma_load_3d(st + 2 * KV_HALF + dh * KV_HALF, tnv, &kv_full[s], dh * 64, h, b * a.N);
                     }
-                    continue;
-                }
-                mbar_arrive_expect_tx(&kv_full[s], KV_STAGE);
-                uint8_t* st = skv + s * KV_STAGE;
-                for (int i = 0; i < TK / kKvPage; ++i) {
-                    uint32_t pg = pg_cur[i];
-                    if (pg >= (uint32_t)a.pool_pages) {
-                        atomicCAS(a.err, 0, kErrPage);
-                        pg = 0;
+                } else {
+                    for (int i = 0; i < PPT; ++i) {
+                        const int row = (int)((pg[i] * a.Hkv + h) * kKvPage);
+                        for (int dh = 0; dh < 2; ++dh) {
+                            tma_load_2d(st + dh * KV_HALF + i * 2048, tmk, &kv_full[s], dh * 64, row);
+                            tma_load_2d(st + 2 * KV_HALF + dh * KV_HALF + i * 2048, tmv, &kv_full[s], dh * 64,
+                                        row);
+                        }
                     }
-                    const int row = (int)((pg * a.Hkv + h) * kKvPage);
-                    for (int dh = 0; dh < 2; ++dh) {
-                        tma_load_2d(st + dh * KV_HALF + i * 2048, tmk, &kv_full[s], dh * 64, row);
-                        tma_load_2d(st + 2 * KV_HALF + dh * KV_HALF + i * 2048, tmv, &kv_full[s],
-                                    dh * 64, row);
-                    }
-                }
-            } else {
-                const int r = j % RS;
-                if (!mbar_wait(&raw_empty[r], ((j / RS) & 1) ^ 1, a.err, kErrWait, abort_flag, 64))
-                    return;
-                mbar_arrive_expect_tx(&raw_full[r], RAW_STAGE);
-                uint8_t* st = sraw + r * RAW_STAGE;
-                for (int i = 0; i < TK / kKvPage; ++i) {
-                    uint32_t pg = pg_cur[i];
-                    if (pg >= (uint32_t)a.pool_pages) {
-                        atomicCAS(a.err, 0, kErrPage);
-                        pg = 0;
-                    }
-                    const size_t blk = (size_t)pg * a.Hkv + h;  // (page, head) block
-                    bulk_load(st + i * 2048, static_cast<const int8_t*>(a.k_pool) + blk * 2048, 2048,
-                              &raw_full[r]);
-                    bulk_load(st + RAW_KV + i * 2048, static_cast<const int8_t*>(a.v_pool) + blk * 2048,
-                              2048, &raw_full[r]);
-                    bulk_load(st + 2 * RAW_KV + i * 32, a.k_scale + blk * kKvPage, 32, &raw_full[r]);
-                    bulk_load(st + 2 * RAW_KV + TK * 2 + i * 32, a.v_scale + blk * kKvPage, 32,
-                              &raw_full[r]);
                 }
             }
+            __syncwarp();
+        } else {
+            const int r = j % RS;
+            const bool ok = mbar_wait(&raw_empty[r], ((j / RS) & 1) ^ 1, a.err, kErrWait, abort_flag, 64);
+            if (!__all_sync(0xffffffffu, ok)) return;
+            if (elect_one()) {
+                if (bad) atomicCAS(a.err, 0, kErrPage);
+                mbar_arrive_expect_tx(&raw_full[r], RAW_STAGE);
+                uint8_t* st = sraw + r * RAW_STAGE;
+                for (int i = 0; i < PPT; ++i) {
+                    const size_t blk = (size_t)pg[i] * a.Hkv + h;  // (page, head) block
+                    bulk_load(st + i * 2048, static_cast<const int8_t*>(a.k_pool) + blk * 2048, 2048,
+                              &raw_full[r]);
+                    bulk_load(st + RAW_KV + i * 2048, static_cast<const int8_t*>(a.v_pool) + blk * 2048, 2048,
+                              &raw_full[r]);
+                    bulk_load(st + 2 * RAW_KV + i * 32, a.k_scale + blk * kKvPage, 32, &raw_full[r]);
+                    bulk_load(st + 2 * RAW_KV + TK * 2 + i * 32, a.v_scale + blk * kKvPage, 32, &raw_full[r]);
+                }
+            }
+            __syncwarp();
         }
     }
 }
@@ -538,93 +540,72 @@ __global__ void __launch_bounds__(TmCfg<INT8, QT>::kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        produce_tiles<INT8, KS, RS>(a, &tmk, &tmv, &tnk, &tnv, lane, b, h, T_pre, T, skv, sraw, kv_full,
-                                    kv_empty, raw_full, raw_empty, abort_flag);
+        produce_tiles<INT8, KS, RS>(a, &tmk, &tmv, &tnk, &tnv, b, h, T_pre, T, skv, sraw, kv_full, kv_empty,
+                                    raw_full, raw_empty, abort_flag);
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issue
-        // The whole warp runs the loop on warp-uniform state; one elected lane
-        // issues each group of MMAs and its commits.
+        // The whole warp runs on warp-uniform state; an elected lane issues
+        // each group of MMAs and its commits.  Per query tile, S_j = Q K_j^T
+        // (A: Q in TMEM) and PV_j: O += P_j V_j (A: P_j in TMEM, over S_j's
+        // columns).  The tensor pipe runs one CTA's MMAs in issue order, so
+        // S_j may follow PV_{j-SB} (the last reader of its buffer) at once.
+        // Fixed order with blocking waits: after PV_j of a tile comes S_{j+SB}
+        // of that tile, and the query tiles take turns, so one tile's MMAs
+        // run while the other tile's softmax works.  With two buffers, when
+        // S_j completes every PV before j-1 has completed (the softmax waits
+        // for PV_{j-1} by parity).  A K/V stage is released after the last
+        // query tile's PV of it.
         {
             const uint32_t id_s = idesc_f16_f32(BMQ, TK);
             const uint32_t id_pv = idesc_f16_f32(BMQ, D, /*b_mn_major=*/true);
-            const bool qok = mbar_wait(q_full, 0, a.err, kErrWait, abort_flag);
-            if (!__all_sync(0xffffffffu, qok)) goto done;
+            bool ok = mbar_wait(q_full, 0, a.err, kErrWait, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) goto done;
             tc_fence_after();
-            // Per query tile, S_j = Q K_j^T (A: Q in TMEM) and PV_j: O += P_j V_j
-            // (A: P_j in TMEM, over S_j's columns), issued in whichever order
-            // their inputs arrive.  The tensor pipe runs one CTA's MMAs in
-            // issue order, so S_j may be issued once PV_{j-SB} (the last reader
-            // of its buffer) is issued; with two buffers, when S_j completes
-            // every PV before j-1 has completed (the softmax waits for PV_{j-1}
-            // by parity).  A K/V stage is released after the last query tile's
-            // PV of it.
-            int ns[QT], npv[QT];
+            auto issue_s = [&](int qt, int j) -> bool {  // false: gave up
+                const int s = j % KS, sb = j % SB;
+                const bool got = mbar_wait(&kv_full[s], (j / KS) & 1, a.err, kErrWait, abort_flag);
+                if (!__all_sync(0xffffffffu, got)) return false;
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
+                if (elect_one()) {
 #pragma unroll
-            for (int qt = 0; qt < QT; ++qt) ns[qt] = npv[qt] = 0;
-            const uint64_t t0 = global_ns();
-            uint32_t spins = 0;
-            for (;;) {
-                bool progressed = false, all_done = true;
+                    for (int k = 0; k < D / 16; ++k) {
+                        const uint64_t bd = desc_kmajor_sw128(k_addr + (k >> 2) * KV_HALF) + (k & 3) * 2;
+                        mma_f16_ts(tmem + C::colS(qt, sb), tmem + C::colQ(qt) + k * 8, bd, id_s, k > 0);
+                    }
+                    mma_commit(&tile_bars(qbars, qt).s_full[sb]);
+                }
+                __syncwarp();
+                return true;
+            };
+            auto issue_pv = [&](int qt, int j) -> bool {
+                const TileBars tb = tile_bars(qbars, qt);
+                const int pb = j % SB, sv = j % KS;
+                const bool got = mbar_wait(&tb.p_full[pb], (j / SB) & 1, a.err, kErrWait, abort_flag);
+                if (!__all_sync(0xffffffffu, got)) return false;
+                tc_fence_after();
+                const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
+                if (elect_one()) {
 #pragma unroll
+                    for (int kk = 0; kk < TK / 16; ++kk) {
+                        const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
+                        mma_f16_ts(tmem + C::colO(qt), tmem + C::colS(qt, pb) + kk * 8, bd, id_pv, (j | kk) != 0);
+                    }
+                    if (qt == QT - 1) mma_commit(&kv_empty[sv]);  // the stage's last reader
+                    mma_commit(tb.pv_done);
+                    if (j == T - 1) mma_commit(tb.o_full);
+                }
+                __syncwarp();
+                return true;
+            };
+            for (int j = 0; j < SB && j < T; ++j)
+                for (int qt = 0; qt < QT; ++qt)
+                    if (!issue_s(qt, j)) goto done;
+            for (int j = 0; j < T; ++j)
                 for (int qt = 0; qt < QT; ++qt) {
-                    const TileBars tb = tile_bars(qbars, qt);
-                    if (ns[qt] < T && npv[qt] >= ns[qt] - (SB - 1)) {
-                        const int j = ns[qt], s = j % KS, sb = j % SB;
-                        if (__shfl_sync(0xffffffffu, mbar_test_wait(smem_u32(&kv_full[s]), (j / KS) & 1), 0)) {
-                            tc_fence_after();
-                            const uint32_t k_addr = smem_u32(skv + s * KV_STAGE);
-                            if (elect_one()) {
-#pragma unroll
-                                for (int k = 0; k < D / 16; ++k) {
-                                    const uint64_t bd = desc_kmajor_sw128(k_addr + (k >> 2) * KV_HALF) + (k & 3) * 2;
-                                    mma_f16_ts(tmem + C::colS(qt, sb), tmem + C::colQ(qt) + k * 8, bd, id_s, k > 0);
-                                }
-                                mma_commit(&tb.s_full[sb]);
-                            }
-                            __syncwarp();
-                            ++ns[qt];
-                            progressed = true;
-                        }
-                    }
-                    if (npv[qt] < ns[qt]) {
-                        const int jj = npv[qt], pb = jj % SB, sv = jj % KS;
-                        if (__shfl_sync(0xffffffffu, mbar_test_wait(smem_u32(&tb.p_full[pb]), (jj / SB) & 1), 0)) {
-                            tc_fence_after();
-                            const uint32_t v_addr = smem_u32(skv + sv * KV_STAGE + 2 * KV_HALF);
-                            bool last_of_stage = true;
-#pragma unroll
-                            for (int o = 0; o < QT; ++o)
-                                if (o != qt && npv[o] <= jj) last_of_stage = false;
-                            if (elect_one()) {
-#pragma unroll
-                                for (int kk = 0; kk < TK / 16; ++kk) {
-                                    const uint64_t bd = desc_mnmajor_sw128(v_addr + kk * 2048, KV_HALF);
-                                    mma_f16_ts(tmem + C::colO(qt), tmem + C::colS(qt, pb) + kk * 8, bd, id_pv,
-                                               (jj | kk) != 0);
-                                }
-                                if (last_of_stage) mma_commit(&kv_empty[sv]);
-                                mma_commit(tb.pv_done);
-                                if (jj == T - 1) mma_commit(tb.o_full);
-                            }
-                            __syncwarp();
-                            ++npv[qt];
-                            progressed = true;
-                        }
-                    }
-                    if (npv[qt] < T) all_done = false;
+                    if (!issue_pv(qt, j)) goto done;
+                    if (j + SB < T && !issue_s(qt, j + SB)) goto done;
                 }
-                if (all_done) break;
-                if (!progressed && (++spins & 255u) == 0) {
-                    const bool stop = *abort_flag != 0 || global_ns() - t0 > kWaitLimitNs * 8;
-                    if (__shfl_sync(0xffffffffu, stop, 0)) {  // a whole item, not one wait
-                        if (lane == 0 && *abort_flag == 0) {
-                            atomicCAS(a.err, 0, kErrWait);
-                            *abort_flag = 1;
-                        }
-                        goto done;
-                    }
-                }
-            }
         }
     } else if (warp >= 4 && warp < 4 + 4 * QT) {
         softmax_rows<INT8, QT>(a, warp, lane, mt, b, h, L, T_pre, T, G, rows_total, tmem, q_full,
