@@ -264,38 +264,43 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // X producer
-        if (lane == 0) {
-            uint32_t g = 0;
-            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-                const int mt = tile % MT;
-                for (int kt = 0; kt < KT; ++kt, ++g) {
-                    const int s = g % XSTAGES;
-                    if (!mbar_wait(&xempty[s], ((g / XSTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag))
-                        goto done;
-                    const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
+        // X producer (whole warp on warp-uniform state; an elected lane issues)
+        uint32_t g = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            const int mt = tile % MT;
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % XSTAGES;
+                const bool ok = mbar_wait(&xempty[s], ((g / XSTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+                const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
+                if (elect_one()) {
                     mbar_arrive_expect_tx(&xfull[s], X_BYTES);
                     tma_load_2d(sx + s * X_BYTES, &tmx, &xfull[s], kk * BK, mt * BM);
                 }
+                __syncwarp();
             }
         }
     } else if (warp == 3) {
-        // raw q4_0 producer
-        if (lane == 0) {
+        // raw q4_0 producer (whole warp on warp-uniform state; an elected lane issues)
+        {
             uint32_t g = 0;
             for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
                 const int nt = tile / MT;
                 const uint8_t* wt = a.w + (size_t)nt * C::SUB * KT * kQ4TileBytes;
                 for (int kt = 0; kt < KT; ++kt, ++g) {
                     const int s = g % RSTAGES;
-                    if (!mbar_wait(&rempty[s], ((g / RSTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag))
-                        goto done;
+                    const bool ok =
+                        mbar_wait(&rempty[s], ((g / RSTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag);
+                    if (!__all_sync(0xffffffffu, ok)) goto done;
                     const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
-                    mbar_arrive_expect_tx(&rfull[s], RAW_BYTES);
+                    if (elect_one()) {
+                        mbar_arrive_expect_tx(&rfull[s], RAW_BYTES);
 #pragma unroll
-                    for (int sub = 0; sub < C::SUB; ++sub)
-                        bulk_load(sr + s * RAW_BYTES + sub * kQ4TileBytes,
-                                  wt + ((size_t)sub * KT + kk) * kQ4TileBytes, kQ4TileBytes, &rfull[s]);
+                        for (int sub = 0; sub < C::SUB; ++sub)
+                            bulk_load(sr + s * RAW_BYTES + sub * kQ4TileBytes,
+                                      wt + ((size_t)sub * KT + kk) * kQ4TileBytes, kQ4TileBytes, &rfull[s]);
+                    }
+                    __syncwarp();
                 }
             }
         }
