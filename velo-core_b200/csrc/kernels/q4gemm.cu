@@ -45,18 +45,19 @@ constexpr int kEpilogueThreads = 128;     // last four warps, one accumulator la
 template <int BN>
 struct Cfg {
     static constexpr int SUB = BN / kQ4TileN;               // repacked tiles per step
-    static constexpr int XSTAGES = BN == 256 ? 5 : 7;       // activation tile ring (TMA)
-    static constexpr int RSTAGES = BN == 256 ? 4 : 8;       // raw q4_0 ring (bulk copy)
-    static constexpr int WSTAGES = BN == 256 ? 3 : 4;       // dequantised f16 weight ring
     static constexpr int W_BYTES = BN * BK * 2;             // 32 / 16 KiB
     static constexpr int RAW_BYTES = SUB * kQ4TileBytes;    // 9 / 4.5 KiB
+    // input stage: the activation tile and the raw q4_0 tiles of one k step,
+    // one transaction barrier (the copy engine completes about one barrier
+    // stage per ~240 ns per SM, whatever its size, so both share one)
+    static constexpr int IN_BYTES = ((X_BYTES + RAW_BYTES) + 1023) / 1024 * 1024;
+    static constexpr int ISTAGES = BN == 256 ? 6 : 8;       // input ring
+    static constexpr int WSTAGES = BN == 256 ? 2 : 3;       // dequantised f16 weight ring
     static constexpr int kDequantThreads = BN;              // warps 4.. : one weight row each
     static constexpr int kThreads = 128 + BN + kEpilogueThreads;
     static constexpr int kEpiWarp0 = (128 + BN) / 32;
     static constexpr int kTmemCols = 2 * BN;                // double-buffered accumulator
-    static constexpr size_t kSmemBytes = (size_t)XSTAGES * X_BYTES +
-                                         (size_t)RSTAGES * RAW_BYTES +
-                                         (size_t)WSTAGES * W_BYTES + 1024 + 512;
+    static constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + (size_t)WSTAGES * W_BYTES + 1024 + 512;
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -195,11 +196,11 @@ __device__ __forceinline__ void store_row32(const Q4GemmArgs& a, int m, int n, c
 // Persistent: CTA c takes output tiles c, c + grid, ... (activation-row tile
 // fastest, so the CTAs sharing a weight tile run together and read it from
 // HBM once).  The k-step counter g runs on across tiles, so every ring keeps
-// its phase from one tile to the next.  Three rings, each released as early
-// as its consumer allows:
-//   X   (XSTAGES x 16 KiB)  TMA -> MMA; freed by the MMA commit
-//   raw (RSTAGES x 9 KiB)   bulk copy -> dequant; freed once dequantised
-//   W   (WSTAGES x 32 KiB)  dequant -> MMA; freed by the MMA commit
+// its phase from one tile to the next.  Two rings:
+//   in  (ISTAGES x (16 KiB activations + 9 / 4.5 KiB raw q4_0)) TMA + bulk
+//        copies on one barrier -> MMA (activations) and dequant (raw); freed
+//        when the MMA commit and every dequant thread have arrived
+//   W   (WSTAGES x 32 / 16 KiB)  dequant -> MMA; freed by the MMA commit
 // Each CTA walks the k steps of a tile starting at its own offset kt0: all
 // CTAs read the same few activation tiles otherwise, and those L2 lines turn
 // into a hot spot that stretches the TMA latency to ~2 us.
@@ -207,20 +208,17 @@ template <int BN>
 __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     q4_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
     using C = Cfg<BN>;
-    constexpr int XSTAGES = C::XSTAGES, RSTAGES = C::RSTAGES, WSTAGES = C::WSTAGES;
+    constexpr int ISTAGES = C::ISTAGES, WSTAGES = C::WSTAGES, IN_BYTES = C::IN_BYTES;
     constexpr int W_BYTES = C::W_BYTES, RAW_BYTES = C::RAW_BYTES;
     constexpr int kDequantThreads = C::kDequantThreads, kTmemCols = C::kTmemCols;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* sx = base;                              // 1024-aligned tiles
-    uint8_t* sw = sx + XSTAGES * X_BYTES;            // 1024-aligned tiles
-    uint8_t* sr = sw + WSTAGES * W_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sr + RSTAGES * RAW_BYTES);
-    uint64_t* xfull = bars;                          // X tile landed (tx bytes)
-    uint64_t* xempty = xfull + XSTAGES;              // MMAs reading it done
-    uint64_t* rfull = xempty + XSTAGES;              // raw q4_0 tile landed (tx bytes)
-    uint64_t* rempty = rfull + RSTAGES;              // dequant group read it
-    uint64_t* wfull = rempty + RSTAGES;              // f16 weight tile written
+    uint8_t* sin = base;                             // ISTAGES x (X tile | raw tiles), 1024-aligned
+    uint8_t* sw = sin + ISTAGES * IN_BYTES;          // 1024-aligned tiles
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sw + WSTAGES * W_BYTES);
+    uint64_t* ifull = bars;                          // X and raw tiles landed (tx bytes)
+    uint64_t* iempty = ifull + ISTAGES;              // MMAs and dequant done with them
+    uint64_t* wfull = iempty + ISTAGES;              // f16 weight tile written
     uint64_t* wempty = wfull + WSTAGES;              // MMAs reading it done
     uint64_t* afull = wempty + WSTAGES;              // accumulator b complete
     uint64_t* aempty = afull + 2;                    // accumulator b drained
@@ -234,13 +232,9 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     const int kt0 = (int)((blockIdx.x * 5u) % (unsigned)KT);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < XSTAGES; ++s) {
-            mbar_init(&xfull[s], 1);
-            mbar_init(&xempty[s], 1);
-        }
-        for (int s = 0; s < RSTAGES; ++s) {
-            mbar_init(&rfull[s], 1);
-            mbar_init(&rempty[s], kDequantThreads);
+        for (int s = 0; s < ISTAGES; ++s) {
+            mbar_init(&ifull[s], 1);
+            mbar_init(&iempty[s], 1 + kDequantThreads);  // the MMA commit + every dequant thread
         }
         for (int s = 0; s < WSTAGES; ++s) {
             mbar_init(&wfull[s], kDequantThreads);
@@ -264,44 +258,28 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // X producer (whole warp on warp-uniform state; an elected lane issues)
+        // producer (whole warp on warp-uniform state; an elected lane issues):
+        // the activation tile by TMA and the raw q4_0 tiles by bulk copies, one
+        // barrier per stage
         uint32_t g = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-            const int mt = tile % MT;
+            const int mt = tile % MT, nt = tile / MT;
+            const uint8_t* wt = a.w + (size_t)nt * C::SUB * KT * kQ4TileBytes;
             for (int kt = 0; kt < KT; ++kt, ++g) {
-                const int s = g % XSTAGES;
-                const bool ok = mbar_wait(&xempty[s], ((g / XSTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag);
+                const int s = g % ISTAGES;
+                const bool ok = mbar_wait(&iempty[s], ((g / ISTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) goto done;
                 const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
                 if (elect_one()) {
-                    mbar_arrive_expect_tx(&xfull[s], X_BYTES);
-                    tma_load_2d(sx + s * X_BYTES, &tmx, &xfull[s], kk * BK, mt * BM);
+                    uint8_t* st = sin + s * IN_BYTES;
+                    mbar_arrive_expect_tx(&ifull[s], X_BYTES + RAW_BYTES);
+                    tma_load_2d(st, &tmx, &ifull[s], kk * BK, mt * BM);
+#pragma unroll
+                    for (int sub = 0; sub < C::SUB; ++sub)
+                        bulk_load(st + X_BYTES + sub * kQ4TileBytes, wt + ((size_t)sub * KT + kk) * kQ4TileBytes,
+                                  kQ4TileBytes, &ifull[s]);
                 }
                 __syncwarp();
-            }
-        }
-    } else if (warp == 3) {
-        // raw q4_0 producer (whole warp on warp-uniform state; an elected lane issues)
-        {
-            uint32_t g = 0;
-            for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-                const int nt = tile / MT;
-                const uint8_t* wt = a.w + (size_t)nt * C::SUB * KT * kQ4TileBytes;
-                for (int kt = 0; kt < KT; ++kt, ++g) {
-                    const int s = g % RSTAGES;
-                    const bool ok =
-                        mbar_wait(&rempty[s], ((g / RSTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag);
-                    if (!__all_sync(0xffffffffu, ok)) goto done;
-                    const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
-                    if (elect_one()) {
-                        mbar_arrive_expect_tx(&rfull[s], RAW_BYTES);
-#pragma unroll
-                        for (int sub = 0; sub < C::SUB; ++sub)
-                            bulk_load(sr + s * RAW_BYTES + sub * kQ4TileBytes,
-                                      wt + ((size_t)sub * KT + kk) * kQ4TileBytes, kQ4TileBytes, &rfull[s]);
-                    }
-                    __syncwarp();
-                }
             }
         }
     } else if (warp == 1) {
@@ -318,18 +296,18 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
             tc_fence_after();
             const uint32_t d = tmem + b * BN;
             for (int kt = 0; kt < KT; ++kt, ++g) {
-                const int s = g % XSTAGES, ws = g % WSTAGES;
-                const bool ready = mbar_wait(&xfull[s], (g / XSTAGES) & 1, a.err, kErrWaitFull, abort_flag) &&
+                const int s = g % ISTAGES, ws = g % WSTAGES;
+                const bool ready = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag) &&
                                    mbar_wait(&wfull[ws], (g / WSTAGES) & 1, a.err, kErrWaitReady, abort_flag);
                 if (!__all_sync(0xffffffffu, ready)) goto done;
                 tc_fence_after();
-                const uint64_t ad = desc_kmajor_sw128(smem_u32(sx + s * X_BYTES));
+                const uint64_t ad = desc_kmajor_sw128(smem_u32(sin + s * IN_BYTES));
                 const uint64_t bd = desc_kmajor_sw128(smem_u32(sw + ws * W_BYTES));
                 if (elect_one()) {
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
                         mma_f16_ss(d, ad + 2 * k, bd + 2 * k, idesc, (kt | k) != 0);
-                    mma_commit(&xempty[s]);
+                    mma_commit(&iempty[s]);
                     mma_commit(&wempty[ws]);
                 }
                 __syncwarp();
@@ -347,9 +325,9 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
         uint32_t g = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             for (int kt = 0; kt < KT; ++kt, ++g) {
-                const int s = g % RSTAGES, ws = g % WSTAGES;
-                if (!mbar_wait(&rfull[s], (g / RSTAGES) & 1, a.err, kErrWaitFull, abort_flag)) goto done;
-                const uint8_t* raw = sr + s * RAW_BYTES;
+                const int s = g % ISTAGES, ws = g % WSTAGES;
+                if (!mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag)) goto done;
+                const uint8_t* raw = sin + s * IN_BYTES + X_BYTES;
                 const uint4 c0 = *reinterpret_cast<const uint4*>(raw + rsub);
                 const uint4 c1 = *reinterpret_cast<const uint4*>(raw + rsub + kQ4Block1Off);
                 const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + rsc);
@@ -366,10 +344,10 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
                     *reinterpret_cast<uint4*>(wrow + (((4 + q) ^ sx7) << 4)) = dequant8(w1[q], d1);
-                // the raw slot is released only now: the shared loads above have
+                // the input slot is released only now: the shared loads above have
                 // returned (their values were consumed), so the next bulk copy into
                 // it (async proxy) cannot overtake them
-                mbar_arrive(&rempty[s]);
+                mbar_arrive(&iempty[s]);
                 fence_async_smem();
                 mbar_arrive(&wfull[ws]);
             }
