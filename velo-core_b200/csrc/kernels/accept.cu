@@ -180,7 +180,7 @@ __host__ __device__ inline FinishLayout finish_layout(int nrows, int ntiles) {
     L.stage = o;  o += up((nrows * ntiles + 2) * 8);
     L.rowM = o;   o += up(nrows * 4);
     L.rowR = o;   o += up(nrows * 4);
-    L.lane_w = o; o += up(32 * 4);
+    L.lane_w = o; o += up(ntiles * 32 * 4);  // every tile's lane weights (the drawing CTA)
     L.tile_w = o; o += up(ntiles * 4);
     L.elem_w = o; o += up(32 * 4);
     L.misc = o;   o += 64;
@@ -413,7 +413,9 @@ __global__ void __launch_bounds__(kFinThreads) accept_finish_kernel(AcceptParams
     // ---- the CTA with the last ticket draws the token --------------------
     if (tid == 0) p.done[b] = 0u;  // every CTA of b counted: zero for the next launch
     __threadfence();
+    // tile and lane weights of every tile in one round trip to L2
     for (int t = tid; t < p.ntiles; t += kFinThreads) tile_w[t] = __ldcg(g_tile_w + t);
+    for (int e = tid; e < p.ntiles * 32; e += kFinThreads) lane_w[e] = __ldcg(g_lane_w + e);
     __syncthreads();
     if (tid == 0) {
         float total = 0.0f;
@@ -435,6 +437,7 @@ __global__ void __launch_bounds__(kFinThreads) accept_finish_kernel(AcceptParams
         for (int t = warp; t < p.ntiles; t += kFinWarps) weigh_tile(p, trow, drow, d, t, lane, g_lane_w, tile_w);
         __threadfence();
         __syncthreads();
+        for (int e = tid; e < p.ntiles * 32; e += kFinThreads) lane_w[e] = __ldcg(g_lane_w + e);
         if (tid == 0) {
             float total = 0.0f;
             for (int t = 0; t < p.ntiles; ++t) total = __fadd_rn(total, tile_w[t]);
@@ -457,11 +460,9 @@ __global__ void __launch_bounds__(kFinThreads) accept_finish_kernel(AcceptParams
         const int ts = misc[2];
         int token = 0;
         if (ts >= 0) {
-            lane_w[lane] = __ldcg(g_lane_w + ts * 32 + lane);
-            __syncwarp();
             float tau2 = 0.0f;
             int ls = -1;
-            if (lane == 0) ls = select_level(lane_w, 32, miscf[4], &tau2);
+            if (lane == 0) ls = select_level(lane_w + ts * 32, 32, miscf[4], &tau2);
             ls = __shfl_sync(0xffffffffu, ls, 0);
             tau2 = __shfl_sync(0xffffffffu, tau2, 0);
             if (ls >= 0) {
