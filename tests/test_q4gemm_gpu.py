@@ -48,8 +48,8 @@ def _inputs(M, N, K, seed):
     return q4, x16
 
 
-# (640, 7680, 512) and (512, 12288, 1024) have >= 148 tiles of 128 x 256 and take the 256-row
-# path on a 148-SM B200; the others take 128-row tiles.
+# M <= 128 takes the shared-memory-weight kernel (256-row weight tiles when there are >= 148 of
+# them, else 128); M > 128 the kernel with the dequantised weights in tensor memory.
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (5, 300, 96), (128, 512, 256), (200, 1000, 512),
                                    (512, 4096, 4096), (130, 256, 11008), (640, 7680, 512),
                                    (512, 12288, 1024)])
@@ -64,6 +64,25 @@ def test_gemm_f32_matches_oracle(ctx, M, N, K):
     ref16 = x16.astype(np.float64) @ w16.T
     scale = max(1.0, np.abs(ref16).max())
     assert np.abs(y - ref16).max() <= 1e-3 * scale
+
+
+@pytest.mark.parametrize("mode", [0, 2, 3])
+def test_weight_paths_agree(ctx, monkeypatch, mode):
+    # M > 128: weights as the TMEM A operand (VELO_Q4_GEMM=tmem; the default
+    # except for SwiGLU) or as the shared-memory B operand (=smem) agree
+    M, N, K = 384, 1024, 1024
+    q4, x16 = _inputs(M, N, K, seed=31 + mode)
+    q4_b = _inputs(M, N // 2, K, seed=77)[0][: N // 2] if mode == velo_cuda.EPI_SWIGLU else None
+    if mode == velo_cuda.EPI_SWIGLU:
+        q4 = q4[: N // 2]
+    resid = synthetic.rng(4, 4).normal(0, 1, (M, N)).astype(np.float32) if mode == velo_cuda.EPI_ADD_F32 else None
+    monkeypatch.setenv("VELO_Q4_GEMM", "tmem")
+    ta = _run(ctx, q4, N, K, x16, mode, y_init=resid, q4_b=q4_b)
+    monkeypatch.setenv("VELO_Q4_GEMM", "smem")
+    sm = _run(ctx, q4, N, K, x16, mode, y_init=resid, q4_b=q4_b)
+    assert np.isfinite(ta).all() and np.isfinite(sm).all()
+    scale = max(1.0, np.abs(sm).max())
+    assert np.abs(ta - sm).max() <= 1e-3 * scale, np.abs(ta - sm).max()
 
 
 def test_gemm_f16_and_residual_add(ctx):

@@ -5,18 +5,23 @@
 // step, where all drafted tokens of all sequences form the M side of one GEMM:
 //   Y[m][n] = sum_k X[m][k] * W[n][k],   W = q4_0 dequantised (d * (q - 8)).
 //
-// A persistent CTA per SM walks 128 (activation rows) x 256 (weight rows)
-// output tiles with a double-buffered accumulator in tensor memory (all 512
-// columns), so the epilogue of one tile overlaps the main loop of the next.
-// The 256-row weight side halves the activation bytes per MMA compared with
-// 128-row tiles: the main loop is bound by L2 -> SM latency x bytes in flight,
-// not by the tensor pipe, at 128.
-//   warp 0      TMA producer of the X tile (64 k, 128-byte swizzle) per k step
-//   warp 3      bulk-copy producer of the raw q4_0 tile (9216 B) per k step
-//   warp 1      one thread issues tcgen05.mma (M=128, N=256, K=16) x 4 per step
+// Two persistent kernels (one CTA per SM):
+//  * q4_gemm_ta_kernel (M > 128 activation rows, plain and residual-add
+//    stores): the dequantised weights are the A operand straight from tensor
+//    memory (the dequant thread of weight row i writes TMEM lane i), the
+//    activations the B operand from shared memory; 128 weight rows x 256
+//    activation rows per tile.  Per k step the SM's shared memory then carries
+//    the activation tile in (TMA) and out (MMA) and the raw q4_0 tile only.
+//  * q4_gemm_kernel (M <= 128, and SwiGLU): the dequantised weights pass
+//    through shared memory as the B operand; 128 (activation rows) x 256 or
+//    128 (weight rows) tiles with a double-buffered accumulator, so the
+//    epilogue of one tile overlaps the main loop of the next:
+//   warp 0      producer: per k step the activation tile (TMA, 64 k, 128-byte
+//               swizzle) and the raw q4_0 tiles (bulk copies) on one barrier
+//   warp 1      tcgen05.mma (M=128, N=256, K=16) x 4 per step, elected lane
 //   warp 2      allocates / frees 512 TMEM columns
-//   warps 4-11  dequantise their weight row of each k step into a 3-slot ring
-//               of swizzled f16 operand tiles
+//   warps 4-11  dequantise their weight row of each k step into a ring of
+//               swizzled f16 operand tiles
 //   warps 12-15 epilogue out of TMEM (tcgen05.ld), fused store / residual
 //               add / SwiGLU
 // Dequantisation: the nibble order chosen at repack time turns a 32-bit word
@@ -26,6 +31,8 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common/sm100.cuh"
@@ -482,6 +489,269 @@ cudaError_t launch_q4_repack(const uint8_t* src_a, const uint8_t* src_b, bool pa
     return cudaGetLastError();
 }
 
+namespace {
+
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+// ---------------------------------------------------------------- GEMM, weights in TMEM
+// Variant for M > 128: the dequantised weights are the A operand straight
+// from tensor memory.  D[128 weight rows][256 activation rows] += W . X^T per
+// tile, tcgen05.mma (M=128, N=256, K=16) with A = W in TMEM (the dequant
+// thread of weight row i writes its row into TMEM lane i with one 32-column
+// tcgen05.st per k step) and B = X from shared memory.  The f16 weight tile
+// then never passes through shared memory: per k step the SM's shared memory
+// sees 32 KiB of activations in (TMA) and out (MMA) plus the 4.5 KiB raw tile,
+// against 48 KiB of operand reads and 32 KiB of dequantised stores with the
+// weights as the B operand.  The accumulator takes 256 columns, single-
+// buffered; 4 weight slots of 32 columns follow it.
+//   warp 0      producer: per k step one input stage (two 128-row activation
+//               boxes by TMA + the raw q4_0 tile by bulk copy, one barrier)
+//   warp 1      MMA issue (warp-uniform loop, elected lane)
+//   warp 2      TMEM allocation (512 columns)
+//   warps 4-7   dequantisation, thread = weight row of the tile = TMEM lane
+//   warps 8-11  epilogue out of TMEM: thread = weight row, 16 activation rows
+//               per tcgen05.ld; SwiGLU pairs gate rows (lanes 0-63) with up
+//               rows (lanes 64-127) through shared memory
+namespace ta {
+constexpr int BNT = 256;                           // activation rows per tile (MMA N)
+constexpr int X2_BYTES = BNT * BK * 2;             // 32 KiB: two 128-row TMA boxes
+constexpr int IN_BYTES = ((X2_BYTES + kQ4TileBytes) + 1023) / 1024 * 1024;
+constexpr int ISTAGES = 5;
+constexpr int WSLOTS = 4;                          // TMEM weight slots, 32 columns each
+constexpr uint32_t kColW = 256;                    // first weight slot column
+constexpr int kThreads = 384;
+constexpr int kXchgBytes = 64 * 16 * 4;            // SwiGLU up values of one 16-row chunk
+constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + kXchgBytes + 1024 + 512;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+}  // namespace ta
+
+__global__ void __launch_bounds__(ta::kThreads, 1)
+    q4_gemm_ta_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
+    using namespace ta;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sin = base;                                   // ISTAGES x (X 256 rows | raw tile)
+    float* sxchg = reinterpret_cast<float*>(sin + ISTAGES * IN_BYTES);  // [64][16] up values
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sxchg + kXchgBytes / 4);
+    uint64_t* ifull = bars;                                // X and raw landed (tx bytes)
+    uint64_t* iempty = ifull + ISTAGES;                    // MMA commit + 128 dequant threads
+    uint64_t* wfull = iempty + ISTAGES;                    // weight slot written (128 threads)
+    uint64_t* wempty = wfull + WSLOTS;                     // MMAs reading the slot done
+    uint64_t* afull = wempty + WSLOTS;                     // accumulator complete
+    uint64_t* aempty = afull + 1;                          // accumulator drained (128 threads)
+    uint64_t* xfull = aempty + 1;                          // SwiGLU: up values of a chunk written
+    uint64_t* xfree = xfull + 1;                           // SwiGLU: ... and read
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfree + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KT = (a.K + BK - 1) / BK;
+    const int MT = (a.M + BNT - 1) / BNT;
+    const int n_tiles = MT * q4_n_tiles(a.N);
+    const int kt0 = (int)((blockIdx.x * 5u) % (unsigned)KT);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ISTAGES; ++s) {
+            mbar_init(&ifull[s], 1);
+            mbar_init(&iempty[s], 1 + kQ4TileN);
+        }
+        for (int s = 0; s < WSLOTS; ++s) {
+            mbar_init(&wfull[s], kQ4TileN);
+            mbar_init(&wempty[s], 1);
+        }
+        mbar_init(afull, 1);
+        mbar_init(aempty, kEpilogueThreads);
+        mbar_init(xfull, 64);
+        mbar_init(xfree, 64);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) prefetch_tmap(&tmx);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // producer (warp-uniform; an elected lane issues)
+        uint32_t g = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            const int mt = tile % MT, nt = tile / MT;
+            const uint8_t* wt = a.w + (size_t)nt * KT * kQ4TileBytes;
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % ISTAGES;
+                const bool ok = mbar_wait(&iempty[s], ((g / ISTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+                const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
+                if (elect_one()) {
+                    uint8_t* st = sin + s * IN_BYTES;
+                    mbar_arrive_expect_tx(&ifull[s], X2_BYTES + kQ4TileBytes);
+                    tma_load_2d(st, &tmx, &ifull[s], kk * BK, mt * BNT);
+                    tma_load_2d(st + X_BYTES, &tmx, &ifull[s], kk * BK, mt * BNT + BM);
+                    bulk_load(st + X2_BYTES, wt + (size_t)kk * kQ4TileBytes, kQ4TileBytes, &ifull[s]);
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == 1) {
+        // MMA issue (warp-uniform; an elected lane issues the MMAs and commits)
+        const uint32_t idesc = idesc_f16_f32(kQ4TileN, BNT);
+        uint32_t g = 0, it = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+            const bool ok = mbar_wait(aempty, (it & 1) ^ 1, a.err, kErrWaitAccEmpty, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) goto done;
+            tc_fence_after();
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % ISTAGES, ws = g % WSLOTS;
+                const bool ready = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag) &&
+                                   mbar_wait(&wfull[ws], (g / WSLOTS) & 1, a.err, kErrWaitReady, abort_flag);
+                if (!__all_sync(0xffffffffu, ready)) goto done;
+                tc_fence_after();
+                const uint64_t bd = desc_kmajor_sw128(smem_u32(sin + s * IN_BYTES));
+                if (elect_one()) {
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        mma_f16_ts(tmem, tmem + kColW + ws * 32 + k * 8, bd + 2 * k, idesc, (kt | k) != 0);
+                    mma_commit(&iempty[s]);
+                    mma_commit(&wempty[ws]);
+                }
+                __syncwarp();
+            }
+            if (elect_one()) mma_commit(afull);
+            __syncwarp();
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // dequantisation: thread i = weight row i of the tile = TMEM lane i
+        const int i = threadIdx.x - 128;
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        uint32_t g = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % ISTAGES, ws = g % WSLOTS;
+                bool ok = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+                const uint8_t* raw = sin + s * IN_BYTES + X2_BYTES;
+                const uint4 c0 = *reinterpret_cast<const uint4*>(raw + i * 16);
+                const uint4 c1 = *reinterpret_cast<const uint4*>(raw + kQ4Block1Off + i * 16);
+                const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + kQ4ScaleOff + i * 4);
+                ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+                tc_fence_after();
+                const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc & 0xFFFF)));
+                const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc >> 16)));
+                const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
+                const uint32_t w1[4] = {c1.x, c1.y, c1.z, c1.w};
+                uint32_t r[32];  // k 0..63 of row i as 32 f16 pairs (lower k in the low half)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 v = dequant8(w0[q], d0);
+                    r[4 * q] = v.x; r[4 * q + 1] = v.y; r[4 * q + 2] = v.z; r[4 * q + 3] = v.w;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 v = dequant8(w1[q], d1);
+                    r[16 + 4 * q] = v.x; r[16 + 4 * q + 1] = v.y; r[16 + 4 * q + 2] = v.z; r[16 + 4 * q + 3] = v.w;
+                }
+                tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 32, r);
+                // the input slot is released once the raw values were consumed
+                mbar_arrive(&iempty[s]);
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&wfull[ws]);
+            }
+        }
+    } else if (warp >= 8) {
+        // epilogue: thread = weight row (TMEM lane), 32 activation rows per load
+        const int q = warp & 3;
+        const int l = q * 32 + lane;  // weight row within the tile
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        const bool swiglu = a.mode == kEpiSwiGLU;
+        const int F = a.N / 2;
+        uint32_t it = 0, cc = 0;  // tiles, SwiGLU exchange chunks
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+            const int mt = tile % MT, nt = tile / MT;
+            const bool ok = mbar_wait(afull, it & 1, a.err, kErrWaitAccum, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) goto done;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < BNT / 16; ++c) {
+                uint32_t v[16];
+                tmem_ld_32x32b_x16(tmem + lane_base + c * 16, v);
+                tmem_ld_wait();
+                const int m0 = mt * BNT + c * 16;
+                const int mcount = a.M - m0 < 16 ? a.M - m0 : 16;  // rows of this chunk that exist
+                if (!swiglu) {
+                    const int n = nt * kQ4TileN + l;
+                    if (n < a.N && mcount > 0) {
+                        if (a.mode == kEpiStoreF32 || a.mode == kEpiAddF32) {
+                            float* p = static_cast<float*>(a.y) + (size_t)m0 * a.ldy + n;
+                            if (a.mode == kEpiAddF32) {
+                                // one reduction per element (no other adder): the same
+                                // value as a load-add-store, without waiting on the load
+#pragma unroll
+                                for (int j = 0; j < 16; ++j, p += a.ldy)
+                                    if (j < mcount) red_add_f32(p, __uint_as_float(v[j]));
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < 16; ++j, p += a.ldy)
+                                    if (j < mcount) *p = __uint_as_float(v[j]);
+                            }
+                        } else {
+                            __half* p = static_cast<__half*>(a.y) + (size_t)m0 * a.ldy + n;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j, p += a.ldy)
+                                if (j < mcount) *p = __float2half_rn(__uint_as_float(v[j]));
+                        }
+                    }
+                } else {
+                    // rows 0..63 of the tile are gate rows, 64..127 the matching up
+                    // rows: the up warps hand their values over through shared
+                    // memory (xfull / xfree alternate phases chunk by chunk)
+                    if (l >= 64) {
+                        const bool fr = mbar_wait(xfree, (cc & 1) ^ 1, a.err, kErrWaitAccum, abort_flag);
+                        if (!__all_sync(0xffffffffu, fr)) goto done;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) sxchg[(l - 64) * 16 + ((j + l) & 15)] = __uint_as_float(v[j]);
+                        mbar_arrive(xfull);
+                    } else {
+                        const bool fu = mbar_wait(xfull, cc & 1, a.err, kErrWaitAccum, abort_flag);
+                        if (!__all_sync(0xffffffffu, fu)) goto done;
+                        const int n = nt * (kQ4TileN / 2) + l;
+                        float up[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) up[j] = sxchg[l * 16 + ((j + l) & 15)];
+                        mbar_arrive(xfree);
+                        if (n < F && mcount > 0) {
+                            __half* p = static_cast<__half*>(a.y) + (size_t)m0 * a.ldy + n;
+#pragma unroll
+                            for (int j = 0; j < 16; ++j, p += a.ldy)
+                                if (j < mcount) *p = __float2half_rn(silu(__uint_as_float(v[j])) * up[j]);
+                        }
+                    }
+                    ++cc;
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(aempty);
+        }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace
+
 template <int BN>
 cudaError_t launch_width(const Q4GemmArgs& a, const CUtensorMap& map, int tiles, int sm_count,
                          cudaStream_t stream) {
@@ -504,6 +774,27 @@ cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
     CUtensorMap map;
     cudaError_t e = make_tmap_f16_2d(&map, x, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.K * 2, BM);
     if (e != cudaSuccess) return e;
+    // More than 128 activation rows: the kernel with the weights in TMEM
+    // (VELO_Q4_GEMM=smem / tmem in the environment forces one kernel, for
+    // comparisons).
+    // SwiGLU stays on the shared-memory-weight kernel, whose double-buffered
+    // accumulator hides the gate/up pairing behind the next tile.
+    const char* env = std::getenv("VELO_Q4_GEMM");
+    const bool force_smem = env != nullptr && std::strcmp(env, "smem") == 0;
+    const bool force_ta = env != nullptr && std::strcmp(env, "tmem") == 0;
+    if (a.M > BM && !force_smem && (a.mode != kEpiSwiGLU || force_ta)) {
+        static std::once_flag once;
+        static cudaError_t attr_err = cudaSuccess;
+        std::call_once(once, [] {
+            attr_err = cudaFuncSetAttribute(q4_gemm_ta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)ta::kSmemBytes);
+        });
+        if (attr_err != cudaSuccess) return attr_err;
+        const int tiles = ((a.M + ta::BNT - 1) / ta::BNT) * q4_n_tiles(a.N);
+        const int grid = tiles < sm_count ? tiles : sm_count;
+        q4_gemm_ta_kernel<<<grid, ta::kThreads, ta::kSmemBytes, stream>>>(map, a);
+        return cudaGetLastError();
+    }
     // 256-row tiles halve the activation traffic per MMA; 128-row tiles when
     // 256-row ones would leave SMs idle.
     const int mt = (a.M + BM - 1) / BM;
