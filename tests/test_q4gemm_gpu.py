@@ -49,10 +49,11 @@ def _inputs(M, N, K, seed):
 
 
 # M <= 128 takes the shared-memory-weight kernel (256-row weight tiles when there are >= 148 of
-# them, else 128); M > 128 the kernel with the dequantised weights in tensor memory.
+# them, else 128); M > 128 the kernel with the dequantised weights in tensor memory, with
+# 128-row activation tiles except at many waves ((2048, 10240, 256): 256-row tiles).
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (5, 300, 96), (128, 512, 256), (200, 1000, 512),
                                    (512, 4096, 4096), (130, 256, 11008), (640, 7680, 512),
-                                   (512, 12288, 1024)])
+                                   (512, 12288, 1024), (2048, 10240, 256)])
 def test_gemm_f32_matches_oracle(ctx, M, N, K):
     q4, x16 = _inputs(M, N, K, seed=M + N + K)
     y = _run(ctx, q4, N, K, x16, velo_cuda.EPI_STORE_F32)

@@ -514,22 +514,30 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
 //   warps 8-11  epilogue out of TMEM: thread = weight row, 16 activation rows
 //               per tcgen05.ld; SwiGLU pairs gate rows (lanes 0-63) with up
 //               rows (lanes 64-127) through shared memory
-namespace ta {
-constexpr int BNT = 256;                           // activation rows per tile (MMA N)
-constexpr int X2_BYTES = BNT * BK * 2;             // 32 KiB: two 128-row TMA boxes
-constexpr int IN_BYTES = ((X2_BYTES + kQ4TileBytes) + 1023) / 1024 * 1024;
-constexpr int ISTAGES = 5;
-constexpr int WSLOTS = 4;                          // TMEM weight slots, 32 columns each
-constexpr uint32_t kColW = 256;                    // first weight slot column
-constexpr int kThreads = 384;
-constexpr int kXchgBytes = 64 * 16 * 4;            // SwiGLU up values of one 16-row chunk
-constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + kXchgBytes + 1024 + 512;
-static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
-}  // namespace ta
+// BNT activation rows per tile (the MMA N): 256 with one accumulator, or 128
+// with two, so that the epilogue of a tile overlaps the next tile's main loop.
+template <int BNT>
+struct TaCfg {
+    static_assert(BNT == 128 || BNT == 256, "activation tile");
+    static constexpr int ACC = BNT == 128 ? 2 : 1;      // accumulator buffers
+    static constexpr int X2_BYTES = BNT * BK * 2;       // 128-row TMA boxes
+    static constexpr int IN_BYTES = ((X2_BYTES + kQ4TileBytes) + 1023) / 1024 * 1024;
+    static constexpr int ISTAGES = BNT == 128 ? 8 : 5;
+    static constexpr int WSLOTS = 4;                    // TMEM weight slots, 32 columns each
+    static constexpr uint32_t kColW = ACC * BNT;        // first weight slot column (256)
+    static constexpr int kThreads = 384;
+    static constexpr int kXchgBytes = 64 * 16 * 4;      // SwiGLU up values of one 16-row chunk
+    static constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + kXchgBytes + 1024 + 512;
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
 
-__global__ void __launch_bounds__(ta::kThreads, 1)
+template <int BNT>
+__global__ void __launch_bounds__(384, 1)
     q4_gemm_ta_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
-    using namespace ta;
+    using C = TaCfg<BNT>;
+    constexpr int ACC = C::ACC, X2_BYTES = C::X2_BYTES, IN_BYTES = C::IN_BYTES, ISTAGES = C::ISTAGES;
+    constexpr int WSLOTS = C::WSLOTS, kXchgBytes = C::kXchgBytes;
+    constexpr uint32_t kColW = C::kColW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sin = base;                                   // ISTAGES x (X 256 rows | raw tile)
@@ -539,9 +547,9 @@ __global__ void __launch_bounds__(ta::kThreads, 1)
     uint64_t* iempty = ifull + ISTAGES;                    // MMA commit + 128 dequant threads
     uint64_t* wfull = iempty + ISTAGES;                    // weight slot written (128 threads)
     uint64_t* wempty = wfull + WSLOTS;                     // MMAs reading the slot done
-    uint64_t* afull = wempty + WSLOTS;                     // accumulator complete
-    uint64_t* aempty = afull + 1;                          // accumulator drained (128 threads)
-    uint64_t* xfull = aempty + 1;                          // SwiGLU: up values of a chunk written
+    uint64_t* afull = wempty + WSLOTS;                     // ACC: accumulator complete
+    uint64_t* aempty = afull + ACC;                        // ACC: accumulator drained (128 threads)
+    uint64_t* xfull = aempty + ACC;                        // SwiGLU: up values of a chunk written
     uint64_t* xfree = xfull + 1;                           // SwiGLU: ... and read
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfree + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -561,8 +569,10 @@ __global__ void __launch_bounds__(ta::kThreads, 1)
             mbar_init(&wfull[s], kQ4TileN);
             mbar_init(&wempty[s], 1);
         }
-        mbar_init(afull, 1);
-        mbar_init(aempty, kEpilogueThreads);
+        for (int b = 0; b < ACC; ++b) {
+            mbar_init(&afull[b], 1);
+            mbar_init(&aempty[b], kEpilogueThreads);
+        }
         mbar_init(xfull, 64);
         mbar_init(xfree, 64);
         *abort_flag = 0;
@@ -592,8 +602,9 @@ __global__ void __launch_bounds__(ta::kThreads, 1)
                 if (elect_one()) {
                     uint8_t* st = sin + s * IN_BYTES;
                     mbar_arrive_expect_tx(&ifull[s], X2_BYTES + kQ4TileBytes);
-                    tma_load_2d(st, &tmx, &ifull[s], kk * BK, mt * BNT);
-                    tma_load_2d(st + X_BYTES, &tmx, &ifull[s], kk * BK, mt * BNT + BM);
+#pragma unroll
+                    for (int xb = 0; xb < BNT / BM; ++xb)
+                        tma_load_2d(st + xb * X_BYTES, &tmx, &ifull[s], kk * BK, mt * BNT + xb * BM);
                     bulk_load(st + X2_BYTES, wt + (size_t)kk * kQ4TileBytes, kQ4TileBytes, &ifull[s]);
                 }
                 __syncwarp();
@@ -604,9 +615,11 @@ __global__ void __launch_bounds__(ta::kThreads, 1)
         const uint32_t idesc = idesc_f16_f32(kQ4TileN, BNT);
         uint32_t g = 0, it = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
-            const bool ok = mbar_wait(aempty, (it & 1) ^ 1, a.err, kErrWaitAccEmpty, abort_flag);
+            const int b = it % ACC;
+            const bool ok = mbar_wait(&aempty[b], ((it / ACC) & 1) ^ 1, a.err, kErrWaitAccEmpty, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) goto done;
             tc_fence_after();
+            const uint32_t d = tmem + b * BNT;
             for (int kt = 0; kt < KT; ++kt, ++g) {
                 const int s = g % ISTAGES, ws = g % WSLOTS;
                 const bool ready = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag) &&
@@ -617,13 +630,13 @@ __global__ void __launch_bounds__(ta::kThreads, 1)
                 if (elect_one()) {
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
-                        mma_f16_ts(tmem, tmem + kColW + ws * 32 + k * 8, bd + 2 * k, idesc, (kt | k) != 0);
+                        mma_f16_ts(d, tmem + kColW + ws * 32 + k * 8, bd + 2 * k, idesc, (kt | k) != 0);
                     mma_commit(&iempty[s]);
                     mma_commit(&wempty[ws]);
                 }
                 __syncwarp();
             }
-            if (elect_one()) mma_commit(afull);
+            if (elect_one()) mma_commit(&afull[b]);
             __syncwarp();
         }
     } else if (warp >= 4 && warp < 8) {
@@ -676,13 +689,14 @@ __global__ void __launch_bounds__(ta::kThreads, 1)
         uint32_t it = 0, cc = 0;  // tiles, SwiGLU exchange chunks
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
             const int mt = tile % MT, nt = tile / MT;
-            const bool ok = mbar_wait(afull, it & 1, a.err, kErrWaitAccum, abort_flag);
+            const int b = it % ACC;
+            const bool ok = mbar_wait(&afull[b], (it / ACC) & 1, a.err, kErrWaitAccum, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) goto done;
             tc_fence_after();
 #pragma unroll 1
             for (int c = 0; c < BNT / 16; ++c) {
                 uint32_t v[16];
-                tmem_ld_32x32b_x16(tmem + lane_base + c * 16, v);
+                tmem_ld_32x32b_x16(tmem + lane_base + b * BNT + c * 16, v);
                 tmem_ld_wait();
                 const int m0 = mt * BNT + c * 16;
                 const int mcount = a.M - m0 < 16 ? a.M - m0 : 16;  // rows of this chunk that exist
@@ -738,7 +752,7 @@ __global__ void __launch_bounds__(ta::kThreads, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(aempty);
+            mbar_arrive(&aempty[b]);
         }
     }
 done:
@@ -748,6 +762,22 @@ done:
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
+}
+
+template <int BNT>
+cudaError_t launch_ta(const Q4GemmArgs& a, const CUtensorMap& map, int tiles, int sm_count,
+                      cudaStream_t stream) {
+    using C = TaCfg<BNT>;
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(q4_gemm_ta_kernel<BNT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)C::kSmemBytes);
+    });
+    if (attr_err != cudaSuccess) return attr_err;
+    const int grid = tiles < sm_count ? tiles : sm_count;
+    q4_gemm_ta_kernel<BNT><<<grid, C::kThreads, C::kSmemBytes, stream>>>(map, a);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -783,17 +813,15 @@ cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
     const bool force_smem = env != nullptr && std::strcmp(env, "smem") == 0;
     const bool force_ta = env != nullptr && std::strcmp(env, "tmem") == 0;
     if (a.M > BM && !force_smem && (a.mode != kEpiSwiGLU || force_ta)) {
-        static std::once_flag once;
-        static cudaError_t attr_err = cudaSuccess;
-        std::call_once(once, [] {
-            attr_err = cudaFuncSetAttribute(q4_gemm_ta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)ta::kSmemBytes);
-        });
-        if (attr_err != cudaSuccess) return attr_err;
-        const int tiles = ((a.M + ta::BNT - 1) / ta::BNT) * q4_n_tiles(a.N);
-        const int grid = tiles < sm_count ? tiles : sm_count;
-        q4_gemm_ta_kernel<<<grid, ta::kThreads, ta::kSmemBytes, stream>>>(map, a);
-        return cudaGetLastError();
+        // 256 activation rows per tile unless 128-row tiles (two accumulators;
+        // measured at about 0.78 of the time of a 256-row tile on config-3
+        // shapes) finish the waves sooner
+        const int nq = q4_n_tiles(a.N);
+        const int t256 = ((a.M + 255) / 256) * nq, t128 = ((a.M + 127) / 128) * nq;
+        const double c256 = (double)((t256 + sm_count - 1) / sm_count);
+        const double c128 = 0.78 * (double)((t128 + sm_count - 1) / sm_count);
+        return c128 < c256 ? launch_ta<128>(a, map, t128, sm_count, stream)
+                           : launch_ta<256>(a, map, t256, sm_count, stream);
     }
     // 256-row tiles halve the activation traffic per MMA; 128-row tiles when
     // 256-row ones would leave SMs idle.
