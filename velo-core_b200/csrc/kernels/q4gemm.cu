@@ -805,13 +805,13 @@ cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
     cudaError_t e = make_tmap_f16_2d(&map, x, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.K * 2, BM);
     if (e != cudaSuccess) return e;
     // More than 128 activation rows: the kernel with the weights in TMEM
-    // (VELO_Q4_GEMM=smem / tmem in the environment forces one kernel, for
-    // comparisons).
+    // (VELO_Q4_GEMM=smem / tmem / tmem128 / tmem256 in the environment forces
+    // a kernel and tile width, for comparisons).
     // SwiGLU stays on the shared-memory-weight kernel, whose double-buffered
     // accumulator hides the gate/up pairing behind the next tile.
     const char* env = std::getenv("VELO_Q4_GEMM");
     const bool force_smem = env != nullptr && std::strcmp(env, "smem") == 0;
-    const bool force_ta = env != nullptr && std::strcmp(env, "tmem") == 0;
+    const bool force_ta = env != nullptr && std::strncmp(env, "tmem", 4) == 0;
     if (a.M > BM && !force_smem && (a.mode != kEpiSwiGLU || force_ta)) {
         // 256 activation rows per tile unless 128-row tiles (two accumulators;
         // measured at about 0.78 of the time of a 256-row tile on config-3
@@ -820,8 +820,11 @@ cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
         const int t256 = ((a.M + 255) / 256) * nq, t128 = ((a.M + 127) / 128) * nq;
         const double c256 = (double)((t256 + sm_count - 1) / sm_count);
         const double c128 = 0.78 * (double)((t128 + sm_count - 1) / sm_count);
-        return c128 < c256 ? launch_ta<128>(a, map, t128, sm_count, stream)
-                           : launch_ta<256>(a, map, t256, sm_count, stream);
+        bool narrow = c128 < c256;
+        if (env != nullptr && std::strcmp(env, "tmem128") == 0) narrow = true;
+        if (env != nullptr && std::strcmp(env, "tmem256") == 0) narrow = false;
+        return narrow ? launch_ta<128>(a, map, t128, sm_count, stream)
+                      : launch_ta<256>(a, map, t256, sm_count, stream);
     }
     // 256-row tiles halve the activation traffic per MMA; 128-row tiles when
     // 256-row ones would leave SMs idle.
