@@ -12,7 +12,10 @@
 //    activations the B operand from shared memory; 128 weight rows x 256
 //    activation rows per tile.  Per k step the SM's shared memory then carries
 //    the activation tile in (TMA) and out (MMA) and the raw q4_0 tile only.
-//  * q4_gemm_kernel (M <= 128, and SwiGLU): the dequantised weights pass
+//  * q4_gemm_ta_swiglu_kernel (M > 128, SwiGLU at K <= 4096): the same with
+//    the gate and the up row of each output in one TMEM lane (two
+//    accumulators), so silu(gate) * up needs no exchange between warps.
+//  * q4_gemm_kernel (M <= 128, and SwiGLU at larger K): the dequantised weights pass
 //    through shared memory as the B operand; 128 (activation rows) x 256 or
 //    128 (weight rows) tiles with a double-buffered accumulator, so the
 //    epilogue of one tile overlaps the main loop of the next:
@@ -496,24 +499,23 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
 }
 
 // ---------------------------------------------------------------- GEMM, weights in TMEM
-// Variant for M > 128: the dequantised weights are the A operand straight
-// from tensor memory.  D[128 weight rows][256 activation rows] += W . X^T per
-// tile, tcgen05.mma (M=128, N=256, K=16) with A = W in TMEM (the dequant
-// thread of weight row i writes its row into TMEM lane i with one 32-column
-// tcgen05.st per k step) and B = X from shared memory.  The f16 weight tile
-// then never passes through shared memory: per k step the SM's shared memory
-// sees 32 KiB of activations in (TMA) and out (MMA) plus the 4.5 KiB raw tile,
-// against 48 KiB of operand reads and 32 KiB of dequantised stores with the
-// weights as the B operand.  The accumulator takes 256 columns, single-
-// buffered; 4 weight slots of 32 columns follow it.
-//   warp 0      producer: per k step one input stage (two 128-row activation
+// Variant for M > 128, plain and residual-add stores: the dequantised weights
+// are the A operand straight from tensor memory.  D[128 weight rows][BNT
+// activation rows] += W . X^T per tile, tcgen05.mma (M=128, N=BNT, K=16) with
+// A = W in TMEM (the dequant thread of weight row i writes its row into TMEM
+// lane i with one 32-column tcgen05.st per k step) and B = X from shared
+// memory.  The f16 weight tile then never passes through shared memory: per k
+// step the SM's shared memory sees the activation tile in (TMA) and out (MMA)
+// plus the 4.5 KiB raw tile, against 48 KiB of operand reads and 32 KiB of
+// dequantised stores with the weights as the B operand.  4 weight slots of 32
+// columns follow the accumulator(s).
+//   warp 0      producer: per k step one input stage (128-row activation
 //               boxes by TMA + the raw q4_0 tile by bulk copy, one barrier)
 //   warp 1      MMA issue (warp-uniform loop, elected lane)
 //   warp 2      TMEM allocation (512 columns)
 //   warps 4-7   dequantisation, thread = weight row of the tile = TMEM lane
 //   warps 8-11  epilogue out of TMEM: thread = weight row, 16 activation rows
-//               per tcgen05.ld; SwiGLU pairs gate rows (lanes 0-63) with up
-//               rows (lanes 64-127) through shared memory
+//               per tcgen05.ld, coalesced across the warp
 // BNT activation rows per tile (the MMA N): 256 with one accumulator, or 128
 // with two, so that the epilogue of a tile overlaps the next tile's main loop.
 template <int BNT>
@@ -526,8 +528,7 @@ struct TaCfg {
     static constexpr int WSLOTS = 4;                    // TMEM weight slots, 32 columns each
     static constexpr uint32_t kColW = ACC * BNT;        // first weight slot column (256)
     static constexpr int kThreads = 384;
-    static constexpr int kXchgBytes = 64 * 16 * 4;      // SwiGLU up values of one 16-row chunk
-    static constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + kXchgBytes + 1024 + 512;
+    static constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + 1024 + 512;
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -536,22 +537,19 @@ __global__ void __launch_bounds__(384, 1)
     q4_gemm_ta_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
     using C = TaCfg<BNT>;
     constexpr int ACC = C::ACC, X2_BYTES = C::X2_BYTES, IN_BYTES = C::IN_BYTES, ISTAGES = C::ISTAGES;
-    constexpr int WSLOTS = C::WSLOTS, kXchgBytes = C::kXchgBytes;
+    constexpr int WSLOTS = C::WSLOTS;
     constexpr uint32_t kColW = C::kColW;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sin = base;                                   // ISTAGES x (X 256 rows | raw tile)
-    float* sxchg = reinterpret_cast<float*>(sin + ISTAGES * IN_BYTES);  // [64][16] up values
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sxchg + kXchgBytes / 4);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sin + ISTAGES * IN_BYTES);
     uint64_t* ifull = bars;                                // X and raw landed (tx bytes)
     uint64_t* iempty = ifull + ISTAGES;                    // MMA commit + 128 dequant threads
     uint64_t* wfull = iempty + ISTAGES;                    // weight slot written (128 threads)
     uint64_t* wempty = wfull + WSLOTS;                     // MMAs reading the slot done
     uint64_t* afull = wempty + WSLOTS;                     // ACC: accumulator complete
     uint64_t* aempty = afull + ACC;                        // ACC: accumulator drained (128 threads)
-    uint64_t* xfull = aempty + ACC;                        // SwiGLU: up values of a chunk written
-    uint64_t* xfree = xfull + 1;                           // SwiGLU: ... and read
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfree + 1);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + ACC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -573,8 +571,6 @@ __global__ void __launch_bounds__(384, 1)
             mbar_init(&afull[b], 1);
             mbar_init(&aempty[b], kEpilogueThreads);
         }
-        mbar_init(xfull, 64);
-        mbar_init(xfree, 64);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -684,9 +680,7 @@ __global__ void __launch_bounds__(384, 1)
         const int q = warp & 3;
         const int l = q * 32 + lane;  // weight row within the tile
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        const bool swiglu = a.mode == kEpiSwiGLU;
-        const int F = a.N / 2;
-        uint32_t it = 0, cc = 0;  // tiles, SwiGLU exchange chunks
+        uint32_t it = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
             const int mt = tile % MT, nt = tile / MT;
             const int b = it % ACC;
@@ -700,59 +694,248 @@ __global__ void __launch_bounds__(384, 1)
                 tmem_ld_wait();
                 const int m0 = mt * BNT + c * 16;
                 const int mcount = a.M - m0 < 16 ? a.M - m0 : 16;  // rows of this chunk that exist
-                if (!swiglu) {
-                    const int n = nt * kQ4TileN + l;
-                    if (n < a.N && mcount > 0) {
-                        if (a.mode == kEpiStoreF32 || a.mode == kEpiAddF32) {
-                            float* p = static_cast<float*>(a.y) + (size_t)m0 * a.ldy + n;
-                            if (a.mode == kEpiAddF32) {
-                                // one reduction per element (no other adder): the same
-                                // value as a load-add-store, without waiting on the load
+                const int n = nt * kQ4TileN + l;
+                if (n < a.N && mcount > 0) {
+                    if (a.mode == kEpiStoreF32 || a.mode == kEpiAddF32) {
+                        float* p = static_cast<float*>(a.y) + (size_t)m0 * a.ldy + n;
+                        if (a.mode == kEpiAddF32) {
+                            // one reduction per element (no other adder): the same
+                            // value as a load-add-store, without waiting on the load
 #pragma unroll
-                                for (int j = 0; j < 16; ++j, p += a.ldy)
-                                    if (j < mcount) red_add_f32(p, __uint_as_float(v[j]));
-                            } else {
-#pragma unroll
-                                for (int j = 0; j < 16; ++j, p += a.ldy)
-                                    if (j < mcount) *p = __uint_as_float(v[j]);
-                            }
+                            for (int j = 0; j < 16; ++j, p += a.ldy)
+                                if (j < mcount) red_add_f32(p, __uint_as_float(v[j]));
                         } else {
-                            __half* p = static_cast<__half*>(a.y) + (size_t)m0 * a.ldy + n;
 #pragma unroll
                             for (int j = 0; j < 16; ++j, p += a.ldy)
-                                if (j < mcount) *p = __float2half_rn(__uint_as_float(v[j]));
+                                if (j < mcount) *p = __uint_as_float(v[j]);
                         }
-                    }
-                } else {
-                    // rows 0..63 of the tile are gate rows, 64..127 the matching up
-                    // rows: the up warps hand their values over through shared
-                    // memory (xfull / xfree alternate phases chunk by chunk)
-                    if (l >= 64) {
-                        const bool fr = mbar_wait(xfree, (cc & 1) ^ 1, a.err, kErrWaitAccum, abort_flag);
-                        if (!__all_sync(0xffffffffu, fr)) goto done;
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) sxchg[(l - 64) * 16 + ((j + l) & 15)] = __uint_as_float(v[j]);
-                        mbar_arrive(xfull);
                     } else {
-                        const bool fu = mbar_wait(xfull, cc & 1, a.err, kErrWaitAccum, abort_flag);
-                        if (!__all_sync(0xffffffffu, fu)) goto done;
-                        const int n = nt * (kQ4TileN / 2) + l;
-                        float up[16];
+                        __half* p = static_cast<__half*>(a.y) + (size_t)m0 * a.ldy + n;
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) up[j] = sxchg[l * 16 + ((j + l) & 15)];
-                        mbar_arrive(xfree);
-                        if (n < F && mcount > 0) {
-                            __half* p = static_cast<__half*>(a.y) + (size_t)m0 * a.ldy + n;
-#pragma unroll
-                            for (int j = 0; j < 16; ++j, p += a.ldy)
-                                if (j < mcount) *p = __float2half_rn(silu(__uint_as_float(v[j])) * up[j]);
-                        }
+                        for (int j = 0; j < 16; ++j, p += a.ldy)
+                            if (j < mcount) *p = __float2half_rn(__uint_as_float(v[j]));
                     }
-                    ++cc;
                 }
             }
             tc_fence_before();
             mbar_arrive(&aempty[b]);
+        }
+    }
+done:
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---------------------------------------------------------------- SwiGLU GEMM, weights in TMEM
+// y[m][j] = f16(silu(gate_j . x_m) * (up_j . x_m)) with both weight rows of output j as
+// TMEM A operands in the same lane: per tile 128 outputs x 128 activation rows, two
+// accumulators (gate: columns 0..127, up: 128..255) written by two tcgen05.mma
+// (M=128, N=128, K=16) per K16 step that share the activation tile.  The pair-repacked
+// weight holds outputs 64t..64t+63 of tile t as gate rows 0..63 then up rows 64..127,
+// so the dequant thread of lane l reads row (l & 63) and 64 + (l & 63) of tile
+// 2u + (l >> 6) for outputs 128u + l.  With both values in one thread the epilogue
+// needs no exchange between warps.  The accumulator pair is single-buffered (3 weight
+// slots of 2 x 32 columns fill the rest of the 512 columns).
+namespace swi {
+constexpr int BNT = 128;                                // activation rows per tile
+constexpr int RAW2 = 2 * kQ4TileBytes;                  // the two repacked tiles of 128 outputs
+constexpr int IN_BYTES = ((X_BYTES + RAW2) + 1023) / 1024 * 1024;
+constexpr int ISTAGES = 7;
+constexpr int WSLOTS = 3;
+constexpr uint32_t kColUp = 128, kColW = 256;           // up accumulator, first weight slot
+constexpr int kThreads = 384;
+constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + 1024 + 512;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+}  // namespace swi
+
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
+__device__ __forceinline__ void dequant_row64(const uint8_t* tile, int row, uint32_t (&r)[32]) {
+    const uint4 c0 = *reinterpret_cast<const uint4*>(tile + row * 16);
+    const uint4 c1 = *reinterpret_cast<const uint4*>(tile + kQ4Block1Off + row * 16);
+    const uint32_t sc = *reinterpret_cast<const uint32_t*>(tile + kQ4ScaleOff + row * 4);
+    const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc & 0xFFFF)));
+    const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc >> 16)));
+    const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
+    const uint32_t w1[4] = {c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint4 v = dequant8(w0[q], d0);
+        r[4 * q] = v.x; r[4 * q + 1] = v.y; r[4 * q + 2] = v.z; r[4 * q + 3] = v.w;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint4 v = dequant8(w1[q], d1);
+        r[16 + 4 * q] = v.x; r[16 + 4 * q + 1] = v.y; r[16 + 4 * q + 2] = v.z; r[16 + 4 * q + 3] = v.w;
+    }
+}
+
+__global__ void __launch_bounds__(swi::kThreads, 1)
+    q4_gemm_ta_swiglu_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
+    using namespace swi;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sin = base;                                   // ISTAGES x (X 128 rows | 2 raw tiles)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sin + ISTAGES * IN_BYTES);
+    uint64_t* ifull = bars;                                // X and raw landed (tx bytes)
+    uint64_t* iempty = ifull + ISTAGES;                    // MMA commit + 128 dequant threads
+    uint64_t* wfull = iempty + ISTAGES;                    // weight slot pair written (128 threads)
+    uint64_t* wempty = wfull + WSLOTS;                     // MMAs reading the slots done
+    uint64_t* afull = wempty + WSLOTS;                     // accumulators complete
+    uint64_t* aempty = afull + 1;                          // accumulators drained (128 threads)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int KT = (a.K + BK - 1) / BK;
+    const int MT = (a.M + BNT - 1) / BNT;
+    const int n_tiles = MT * (q4_n_tiles(a.N) / 2);       // 128 outputs per tile
+    const int kt0 = (int)((blockIdx.x * 5u) % (unsigned)KT);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ISTAGES; ++s) {
+            mbar_init(&ifull[s], 1);
+            mbar_init(&iempty[s], 1 + kQ4TileN);
+        }
+        for (int s = 0; s < WSLOTS; ++s) {
+            mbar_init(&wfull[s], kQ4TileN);
+            mbar_init(&wempty[s], 1);
+        }
+        mbar_init(afull, 1);
+        mbar_init(aempty, kEpilogueThreads);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) prefetch_tmap(&tmx);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // producer (warp-uniform; an elected lane issues)
+        uint32_t g = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            const int mt = tile % MT, u = tile / MT;
+            const uint8_t* wt = a.w + (size_t)(2 * u) * KT * kQ4TileBytes;
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % ISTAGES;
+                const bool ok = mbar_wait(&iempty[s], ((g / ISTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+                const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
+                if (elect_one()) {
+                    uint8_t* st = sin + s * IN_BYTES;
+                    mbar_arrive_expect_tx(&ifull[s], X_BYTES + RAW2);
+                    tma_load_2d(st, &tmx, &ifull[s], kk * BK, mt * BNT);
+#pragma unroll
+                    for (int sub = 0; sub < 2; ++sub)
+                        bulk_load(st + X_BYTES + sub * kQ4TileBytes, wt + ((size_t)sub * KT + kk) * kQ4TileBytes,
+                                  kQ4TileBytes, &ifull[s]);
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == 1) {
+        // MMA issue (warp-uniform; an elected lane issues the MMAs and commits)
+        const uint32_t idesc = idesc_f16_f32(kQ4TileN, BNT);
+        uint32_t g = 0, it = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+            const bool ok = mbar_wait(aempty, (it & 1) ^ 1, a.err, kErrWaitAccEmpty, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) goto done;
+            tc_fence_after();
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % ISTAGES, ws = g % WSLOTS;
+                const bool ready = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag) &&
+                                   mbar_wait(&wfull[ws], (g / WSLOTS) & 1, a.err, kErrWaitReady, abort_flag);
+                if (!__all_sync(0xffffffffu, ready)) goto done;
+                tc_fence_after();
+                const uint64_t bd = desc_kmajor_sw128(smem_u32(sin + s * IN_BYTES));
+                const uint32_t wg = tmem + kColW + ws * 64;  // gate rows, then up rows at +32
+                if (elect_one()) {
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        mma_f16_ts(tmem, wg + k * 8, bd + 2 * k, idesc, (kt | k) != 0);
+                        mma_f16_ts(tmem + kColUp, wg + 32 + k * 8, bd + 2 * k, idesc, (kt | k) != 0);
+                    }
+                    mma_commit(&iempty[s]);
+                    mma_commit(&wempty[ws]);
+                }
+                __syncwarp();
+            }
+            if (elect_one()) mma_commit(afull);
+            __syncwarp();
+        }
+    } else if (warp >= 4 && warp < 8) {
+        // dequantisation: thread l = output 128u + l = TMEM lane l (gate and up row)
+        const int l = threadIdx.x - 128;
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const int sel = l >> 6, r = l & 63;  // repacked tile 2u + sel, gate row r, up row 64 + r
+        uint32_t g = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+            for (int kt = 0; kt < KT; ++kt, ++g) {
+                const int s = g % ISTAGES, ws = g % WSLOTS;
+                bool ok = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+                const uint8_t* raw = sin + s * IN_BYTES + X_BYTES + sel * kQ4TileBytes;
+                ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+                tc_fence_after();
+                {
+                    uint32_t w[32];
+                    dequant_row64(raw, r, w);
+                    tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 64, w);
+                }
+                {
+                    uint32_t w[32];
+                    dequant_row64(raw, 64 + r, w);
+                    tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 64 + 32, w);
+                }
+                // the input slot is released once the raw values were consumed
+                mbar_arrive(&iempty[s]);
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(&wfull[ws]);
+            }
+        }
+    } else if (warp >= 8) {
+        // epilogue: thread = output column 128u + l, 16 activation rows per load
+        const int q = warp & 3;
+        const int l = q * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        const int F = a.N / 2;
+        uint32_t it = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+            const int mt = tile % MT, u = tile / MT;
+            const bool ok = mbar_wait(afull, it & 1, a.err, kErrWaitAccum, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) goto done;
+            tc_fence_after();
+            const int n = u * 128 + l;
+#pragma unroll 1
+            for (int c = 0; c < BNT / 16; ++c) {
+                uint32_t gv[16], uv[16];
+                tmem_ld_32x32b_x16(tmem + lane_base + c * 16, gv);
+                tmem_ld_32x32b_x16(tmem + lane_base + kColUp + c * 16, uv);
+                tmem_ld_wait();
+                const int m0 = mt * BNT + c * 16;
+                const int mcount = a.M - m0 < 16 ? a.M - m0 : 16;
+                if (n < F && mcount > 0) {
+                    __half* p = static_cast<__half*>(a.y) + (size_t)m0 * a.ldy + n;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j, p += a.ldy)
+                        if (j < mcount)
+                            *p = __float2half_rn(silu_fast(__uint_as_float(gv[j])) * __uint_as_float(uv[j]));
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(aempty);
         }
     }
 done:
@@ -807,12 +990,28 @@ cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
     // More than 128 activation rows: the kernel with the weights in TMEM
     // (VELO_Q4_GEMM=smem / tmem / tmem128 / tmem256 in the environment forces
     // a kernel and tile width, for comparisons).
-    // SwiGLU stays on the shared-memory-weight kernel, whose double-buffered
-    // accumulator hides the gate/up pairing behind the next tile.
+    // Plain and residual-add stores take the TMEM-weight kernel with 128- or
+    // 256-row activation tiles.
     const char* env = std::getenv("VELO_Q4_GEMM");
     const bool force_smem = env != nullptr && std::strcmp(env, "smem") == 0;
-    const bool force_ta = env != nullptr && std::strncmp(env, "tmem", 4) == 0;
-    if (a.M > BM && !force_smem && (a.mode != kEpiSwiGLU || force_ta)) {
+    const bool force_tmem = env != nullptr && std::strncmp(env, "tmem", 4) == 0;
+    // SwiGLU: the paired-accumulator kernel measured faster at K = 4096 (config-3
+    // w1/w3 131 us against 146) and slower at K = 8192 (config 5: 1904 against
+    // 1838), where the shared-memory-weight kernel keeps it
+    if (a.M > BM && !force_smem && a.mode == kEpiSwiGLU && (a.K <= 4096 || force_tmem)) {
+        static std::once_flag once;
+        static cudaError_t attr_err = cudaSuccess;
+        std::call_once(once, [] {
+            attr_err = cudaFuncSetAttribute(q4_gemm_ta_swiglu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            (int)swi::kSmemBytes);
+        });
+        if (attr_err != cudaSuccess) return attr_err;
+        const int tiles = ((a.M + swi::BNT - 1) / swi::BNT) * (q4_n_tiles(a.N) / 2);
+        const int grid = tiles < sm_count ? tiles : sm_count;
+        q4_gemm_ta_swiglu_kernel<<<grid, swi::kThreads, swi::kSmemBytes, stream>>>(map, a);
+        return cudaGetLastError();
+    }
+    if (a.M > BM && !force_smem && a.mode != kEpiSwiGLU) {
         // 256 activation rows per tile unless 128-row tiles (two accumulators;
         // measured at about 0.78 of the time of a 256-row tile on config-3
         // shapes) finish the waves sooner
