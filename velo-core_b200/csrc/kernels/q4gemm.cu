@@ -12,10 +12,10 @@
 //    activations the B operand from shared memory; 128 weight rows x 256
 //    activation rows per tile.  Per k step the SM's shared memory then carries
 //    the activation tile in (TMA) and out (MMA) and the raw q4_0 tile only.
-//  * q4_gemm_ta_swiglu_kernel (M > 128, SwiGLU at K <= 4096): the same with
+//  * q4_gemm_ta_swiglu_kernel (M > 128, SwiGLU): the same with
 //    the gate and the up row of each output in one TMEM lane (two
 //    accumulators), so silu(gate) * up needs no exchange between warps.
-//  * q4_gemm_kernel (M <= 128, and SwiGLU at larger K): the dequantised weights pass
+//  * q4_gemm_kernel (M <= 128): the dequantised weights pass
 //    through shared memory as the B operand; 128 (activation rows) x 256 or
 //    128 (weight rows) tiles with a double-buffered accumulator, so the
 //    epilogue of one tile overlaps the main loop of the next:
@@ -736,8 +736,8 @@ done:
 // accumulators (gate: columns 0..127, up: 128..255) written by two tcgen05.mma
 // (M=128, N=128, K=16) per K16 step that share the activation tile.  The pair-repacked
 // weight holds outputs 64t..64t+63 of tile t as gate rows 0..63 then up rows 64..127,
-// so the dequant thread of lane l reads row (l & 63) and 64 + (l & 63) of tile
-// 2u + (l >> 6) for outputs 128u + l.  With both values in one thread the epilogue
+// so for output 128u + l the dequant threads of lane l (one for the gate row,
+// one for the up row) read row (l & 63), resp. 64 + (l & 63), of tile 2u + (l >> 6).  With both values in one thread the epilogue
 // needs no exchange between warps.  The accumulator pair is single-buffered (3 weight
 // slots of 2 x 32 columns fill the rest of the 512 columns).
 namespace swi {
@@ -747,7 +747,7 @@ constexpr int IN_BYTES = ((X_BYTES + RAW2) + 1023) / 1024 * 1024;
 constexpr int ISTAGES = 7;
 constexpr int WSLOTS = 3;
 constexpr uint32_t kColUp = 128, kColW = 256;           // up accumulator, first weight slot
-constexpr int kThreads = 384;
+constexpr int kThreads = 512;                           // warps 4-7 gate rows, 12-15 up rows
 constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + 1024 + 512;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 }  // namespace swi
@@ -799,10 +799,10 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < ISTAGES; ++s) {
             mbar_init(&ifull[s], 1);
-            mbar_init(&iempty[s], 1 + kQ4TileN);
+            mbar_init(&iempty[s], 1 + 2 * kQ4TileN);
         }
         for (int s = 0; s < WSLOTS; ++s) {
-            mbar_init(&wfull[s], kQ4TileN);
+            mbar_init(&wfull[s], 2 * kQ4TileN);
             mbar_init(&wempty[s], 1);
         }
         mbar_init(afull, 1);
@@ -873,11 +873,13 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
             if (elect_one()) mma_commit(afull);
             __syncwarp();
         }
-    } else if (warp >= 4 && warp < 8) {
-        // dequantisation: thread l = output 128u + l = TMEM lane l (gate and up row)
-        const int l = threadIdx.x - 128;
+    } else if ((warp >= 4 && warp < 8) || warp >= 12) {
+        // dequantisation: warps 4-7 the gate rows, warps 12-15 the up rows; thread
+        // l = output 128u + l = TMEM lane l
+        const int l = (warp & 3) * 32 + lane;
+        const int up = warp >= 12 ? 1 : 0;
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const int sel = l >> 6, r = l & 63;  // repacked tile 2u + sel, gate row r, up row 64 + r
+        const int sel = l >> 6, r = (l & 63) + 64 * up;  // row r of repacked tile 2u + sel
         uint32_t g = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             for (int kt = 0; kt < KT; ++kt, ++g) {
@@ -891,12 +893,7 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
                 {
                     uint32_t w[32];
                     dequant_row64(raw, r, w);
-                    tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 64, w);
-                }
-                {
-                    uint32_t w[32];
-                    dequant_row64(raw, 64 + r, w);
-                    tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 64 + 32, w);
+                    tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 64 + 32 * up, w);
                 }
                 // the input slot is released once the raw values were consumed
                 mbar_arrive(&iempty[s]);
@@ -905,7 +902,7 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
                 mbar_arrive(&wfull[ws]);
             }
         }
-    } else if (warp >= 8) {
+    } else if (warp >= 8 && warp < 12) {
         // epilogue: thread = output column 128u + l, 16 activation rows per load
         const int q = warp & 3;
         const int l = q * 32 + lane;
@@ -994,11 +991,9 @@ cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
     // 256-row activation tiles.
     const char* env = std::getenv("VELO_Q4_GEMM");
     const bool force_smem = env != nullptr && std::strcmp(env, "smem") == 0;
-    const bool force_tmem = env != nullptr && std::strncmp(env, "tmem", 4) == 0;
-    // SwiGLU: the paired-accumulator kernel measured faster at K = 4096 (config-3
-    // w1/w3 131 us against 146) and slower at K = 8192 (config 5: 1904 against
-    // 1838), where the shared-memory-weight kernel keeps it
-    if (a.M > BM && !force_smem && a.mode == kEpiSwiGLU && (a.K <= 4096 || force_tmem)) {
+    // SwiGLU: the paired-accumulator kernel (config-3 w1/w3 130 us against 146
+    // on the shared-memory-weight kernel; config 5 1830 against 1838)
+    if (a.M > BM && !force_smem && a.mode == kEpiSwiGLU) {
         static std::once_flag once;
         static cudaError_t attr_err = cudaSuccess;
         std::call_once(once, [] {
