@@ -53,7 +53,7 @@ def _inputs(M, N, K, seed):
 # 128-row activation tiles except at many waves ((2048, 10240, 256): 256-row tiles).
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (5, 300, 96), (128, 512, 256), (200, 1000, 512),
                                    (512, 4096, 4096), (130, 256, 11008), (640, 7680, 512),
-                                   (512, 12288, 1024), (2048, 10240, 256)])
+                                   (512, 12288, 1024), (2048, 10240, 256), (300, 700, 96)])
 def test_gemm_f32_matches_oracle(ctx, M, N, K):
     q4, x16 = _inputs(M, N, K, seed=M + N + K)
     y = _run(ctx, q4, N, K, x16, velo_cuda.EPI_STORE_F32)
@@ -98,7 +98,7 @@ def test_gemm_f16_and_residual_add(ctx):
     assert np.abs(ya - (resid + ref)).max() <= TOL_ORACLE
 
 
-@pytest.mark.parametrize("M,F,K", [(64, 688, 256), (512, 1408, 1024), (1280, 2048, 256)])
+@pytest.mark.parametrize("M,F,K", [(64, 688, 256), (512, 1408, 1024), (1280, 2048, 256), (200, 688, 96)])
 def test_gemm_swiglu_pair(ctx, M, F, K):
     """w1 (gate) and w3 (up) repacked as a pair: y = silu(x w1^T) * (x w3^T),
     llama_cpu.rs:326-341."""
@@ -118,3 +118,16 @@ def test_gemm_repeated_launches_identical(ctx):
     a = _run(ctx, q4, N, K, x16, velo_cuda.EPI_STORE_F32)
     b = _run(ctx, q4, N, K, x16, velo_cuda.EPI_STORE_F32)
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 700, 96), (2000, 4096, 1024)])
+def test_residual_add_ragged(ctx, M, N, K):
+    # the TMEM-weight kernel adds its tile into the residual with one reduction
+    # per element: ragged rows and columns stay untouched outside [M) x [N)
+    q4, x16 = _inputs(M, N, K, seed=M + 3 * N)
+    resid = synthetic.rng(9, 9).normal(0, 1, (M, N)).astype(np.float32)
+    y = _run(ctx, q4, N, K, x16, velo_cuda.EPI_ADD_F32, y_init=resid)
+    w32 = vo.dequant_matrix(2, q4, N, K).astype(np.float64)
+    ref = resid.astype(np.float64) + x16.astype(np.float64) @ w32.T
+    assert np.abs(y - ref).max() <= TOL_ORACLE
+
