@@ -82,3 +82,78 @@ def test_tp2_verify_matches_oracle():
         assert out[r][2] == len(path) - 1
         assert out[r][3][:len(path)] == path
         assert out[r][4] == bonus
+
+
+def _rank_sampling(rank, tp, nid, meta, tensors, kv, tokens, P, q):
+    try:
+        import velo_cuda
+        ctx = velo_cuda.Context(device=rank, total_pages=32, max_slots=2, max_pages_per_slot=16,
+                                tp_rank=rank, tp_size=tp, nccl_id=nid)
+        ctx.load_model(meta, tensors)
+        ctx.bind_slot(1, np.arange(16) + 7)
+        hk = meta["n_head_kv"] // tp
+        for l, (K, V) in enumerate(kv):
+            for p0 in range(0, P, 64):
+                ctx.write_kv(1, l, p0, K[p0:p0 + 64, rank * hk:(rank + 1) * hk],
+                             V[p0:p0 + 64, rank * hk:(rank + 1) * hk])
+        N = len(tokens)
+        par = np.arange(-1, N - 1, dtype=np.int32)
+        nv = meta["n_vocab"]
+        first = ctx.verify_step([1], [P], tokens[None], par[None], commit=False,
+                                want_logits=True, n_vocab=nv)
+        # the same draft rows and uniforms on every rank (same seed, same logits)
+        g = np.random.default_rng(23)
+        drf = (first["logits"][:, :N - 1] + g.normal(0, 0.5, (1, N - 1, nv))).astype(np.float32)
+        u = g.random((1, N)).astype(np.float32)
+        res = ctx.verify_step([1], [P], tokens[None], par[None], temperature=0.9, draft_logits=drf,
+                              uniforms=u, commit=True, want_logits=True, n_vocab=nv)
+        ctx.close()
+        q.put((rank, res["logits"], drf, u, int(res["accepted_len"][0]), int(res["bonus"][0]), None))
+    except Exception as e:  # report instead of hanging the peer
+        q.put((rank, None, None, None, 0, 0, repr(e)))
+
+
+def test_tp2_sampling_chain_matches_acceptance_spec():
+    """Rejection sampling at T = 0.9 under TP = 2: every rank reassembles the
+    full target rows and draws the same decisions as the acceptance spec on
+    those rows (the oracle's `accept`, the same check as the single-GPU
+    sampling chain test)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    import velo_cuda
+    meta, tensors = synthetic.llama_q4_model(**SHAPE, seed=31)
+    g = synthetic.rng(32, 80)
+    P = 40
+    prompt = g.integers(0, meta["n_vocab"], P).astype(np.uint32)
+    ora = vo.Model(dict(meta, n_ctx=512), synthetic.oracle_tensor_list(meta, tensors))
+    ora.forward_sequence(prompt)
+    Hkv = meta["n_head_kv"]
+    kv = [(ora.read_kv(0, l, P).reshape(P, Hkv, 128).astype(np.float16),
+           ora.read_kv(1, l, P).reshape(P, Hkv, 128).astype(np.float16))
+          for l in range(meta["n_layer"])]
+    tokens = g.integers(0, meta["n_vocab"], 6).astype(np.uint32)
+    ref = ora.verify_tree(tokens, np.arange(-1, 5, dtype=np.int32), P)
+    nid = velo_cuda.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank_sampling, args=(r, 2, nid, meta, tensors, kv, tokens, P, q))
+          for r in range(2)]
+    for p in ps:
+        p.start()
+    out = {}
+    for _ in ps:
+        r = q.get(timeout=300)
+        out[r[0]] = r
+    for p in ps:
+        p.join(timeout=60)
+    for r in range(2):
+        assert out[r][6] is None, out[r][6]
+    lg, drf, u = out[0][1], out[0][2], out[0][3]
+    assert np.array_equal(lg, out[1][1]) and np.array_equal(drf, out[1][2])
+    assert np.abs(lg[0] - ref).max() <= 2e-2
+    ra, rb = vo.accept(lg, drf, tokens[None, 1:], u, 0.9)
+    for r in range(2):
+        assert out[r][4] == int(ra[0])
+        assert out[r][5] == int(rb[0])

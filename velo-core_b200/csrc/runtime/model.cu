@@ -81,8 +81,10 @@ struct Model {
     float* y = nullptr;        // [M][H] partial of a row-split GEMM (tp > 1)
     int2* pairs = nullptr;     // [M] this shard's argmax
     int2* pairs_all = nullptr; // [tp][M]
-    float* logits_all = nullptr;  // [tp][M][V_loc] (logits requested, tp > 1)
+    float* logits_all = nullptr;  // [tp][M][V_loc] gathered shards (tp > 1)
     size_t logits_all_cap = 0;
+    float* logits_full = nullptr;  // [M][V] reassembled rows (tp > 1, sampling)
+    size_t logits_full_cap = 0;
     // per-step inputs, one device block filled by one copy from a pinned
     // host mirror: tokens [M] | parents [M] | ctxlen [B] | slots [B] | pt_batch [B][max_pages]
     uint8_t* din = nullptr;
@@ -133,6 +135,7 @@ void destroy_model(Model* m) {
     for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     if (m->drf) cudaFree(m->drf);
     if (m->logits_all) cudaFree(m->logits_all);
+    if (m->logits_full) cudaFree(m->logits_full);
     delete m;
 }
 
@@ -394,6 +397,44 @@ int32_t allreduce_add(velo_cuda_ctx* c, Model* m, int M) {
                             nc, "ncclAllReduce");
     if (st) return st;
     VELO_CUDA_TRY(launch_add_f32(m->x, m->y, n, c->stream));
+    return VELO_OK;
+}
+
+// Full target rows [M][V] on every rank from the vocabulary shards
+// [M][V_loc]: one all-gather into [tp][M][V_loc], then one strided copy per
+// shard.  Buffers grow on demand (the stream is drained first).
+int32_t gather_full_logits(velo_cuda_ctx* c, Model* m, int M, bool full) {
+    cudaStream_t s = c->stream;
+    const size_t per = (size_t)M * m->V_loc;
+    const size_t all = per * m->tp;
+    if (all > m->logits_all_cap || (full && all > m->logits_full_cap)) {
+        VELO_CUDA_TRY(cudaStreamSynchronize(s));
+        if (all > m->logits_all_cap) {
+            if (m->logits_all) cudaFree(m->logits_all);
+            m->logits_all = nullptr;
+            m->logits_all_cap = 0;
+            VELO_CUDA_TRY(cudaMalloc(&m->logits_all, all * 4));
+            m->logits_all_cap = all;
+        }
+        if (full && all > m->logits_full_cap) {
+            if (m->logits_full) cudaFree(m->logits_full);
+            m->logits_full = nullptr;
+            m->logits_full_cap = 0;
+            VELO_CUDA_TRY(cudaMalloc(&m->logits_full, all * 4));
+            m->logits_full_cap = all;
+        }
+    }
+    const NcclApi* nc = nccl_api();
+    if (!nc) return VELO_ERR_NCCL;
+    int32_t st = nccl_check(nc->AllGather(m->logits, m->logits_all, per, ncclFloat32,
+                                          static_cast<ncclComm_t>(c->nccl_comm), s),
+                            nc, "ncclAllGather");
+    if (st || !full) return st;
+    const size_t row = (size_t)m->V_loc * 4;
+    for (int r = 0; r < m->tp; ++r)
+        VELO_CUDA_TRY(cudaMemcpy2DAsync(m->logits_full + (size_t)r * m->V_loc, row * m->tp,
+                                        m->logits_all + (size_t)r * per, row, row, (size_t)M,
+                                        cudaMemcpyDeviceToDevice, s));
     return VELO_OK;
 }
 
@@ -930,9 +971,17 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     } else if (!sampling || N == 1) {
         VELO_CUDA_TRY(velo::launch_tree_greedy(m->logits, m->tokens, m->parents, B, N, V, m->expected,
                                                m->path, m->path_len, m->bonus, s));
-    } else if (m->tp > 1) {
-        return fail(VELO_ERR_INVALID_ARGUMENT, "sampling acceptance with tp_size > 1 is not supported");
     } else {
+        // Sampling.  With tp > 1 every rank reassembles the full target rows
+        // and runs the same acceptance on the replicated draft logits and
+        // uniforms, so all ranks reach the same decisions as one GPU would
+        // on those rows (the rows are M x V f32, a few MB per step).
+        const float* tgt = m->logits;
+        if (m->tp > 1) {
+            st = velo::gather_full_logits(c, m, M, true);
+            if (st) return st;
+            tgt = m->logits_full;
+        }
         const int k = N - 1;
         const size_t need = (size_t)B * k * V;
         if (need > m->drf_cap) {
@@ -950,7 +999,7 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         VELO_CUDA_TRY(cudaMemcpyAsync(m->uni, in->uniforms, (size_t)B * N * 4, cudaMemcpyHostToDevice, s));
         VELO_CUDA_TRY(cudaMemcpyAsync(m->dtok, dt.data(), dt.size() * 4, cudaMemcpyHostToDevice, s));
         VELO_CUDA_TRY(cudaStreamSynchronize(s));  // dt is host-stack memory
-        st = velo::run_accept(c, m->logits, m->drf, m->dtok, m->uni, B, k, V, in->temperature, m->acc, m->bonus);
+        st = velo::run_accept(c, tgt, m->drf, m->dtok, m->uni, B, k, V, in->temperature, m->acc, m->bonus);
         if (st) return st;
         // chain path: nodes 0..acc
         std::vector<int32_t> acc(B);
@@ -1057,21 +1106,12 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     std::vector<float> gathered;
     if (out->logits && m->tp == 1)
         VELO_CUDA_TRY(cudaMemcpyAsync(out->logits, m->logits, (size_t)M * V * 4, cudaMemcpyDeviceToHost, s));
-    if (out->logits && m->tp > 1) {
+    const bool have_full = m->tp > 1 && sampling && N > 1;  // reassembled by the body
+    if (out->logits && have_full)
+        VELO_CUDA_TRY(cudaMemcpyAsync(out->logits, m->logits_full, (size_t)M * V * 4, cudaMemcpyDeviceToHost, s));
+    if (out->logits && m->tp > 1 && !have_full) {
         const size_t per = (size_t)M * Vl;
-        if (per * m->tp > m->logits_all_cap) {
-            VELO_CUDA_TRY(cudaStreamSynchronize(s));
-            if (m->logits_all) cudaFree(m->logits_all);
-            m->logits_all = nullptr;
-            m->logits_all_cap = 0;
-            VELO_CUDA_TRY(cudaMalloc(&m->logits_all, per * m->tp * 4));
-            m->logits_all_cap = per * m->tp;
-        }
-        const velo::NcclApi* nc = velo::nccl_api();
-        if (!nc) return VELO_ERR_NCCL;
-        st = velo::nccl_check(nc->AllGather(m->logits, m->logits_all, per, ncclFloat32,
-                                            static_cast<ncclComm_t>(c->nccl_comm), s),
-                              nc, "ncclAllGather");
+        st = velo::gather_full_logits(c, m, M, false);
         if (st) return st;
         gathered.resize(per * m->tp);
         VELO_CUDA_TRY(cudaMemcpyAsync(gathered.data(), m->logits_all, per * m->tp * 4, cudaMemcpyDeviceToHost, s));
