@@ -344,7 +344,9 @@ typedef struct velo_verify_result {
  * acceptance (greedy: GreedySampler argmax + find_best_path; sampling: the
  * rejection rule of velo_cuda_accept on chains) and, with commit, the KV of
  * the accepted path written at positions ctx_len.. on the device.  Host
- * buffers; waits for the result.  Replaces TargetModel::verify_tree /
+ * buffers; waits for the result.  With tp_size > 1 every rank makes the same
+ * call with the same batch (draft logits and uniforms included) and gets the
+ * same decisions; logits, when requested, are the full rows.  Replaces TargetModel::verify_tree /
  * verify_batch over CausalLmBackend::verify_logits and the commit of
  * SpeculativeSession (src/speculative.rs:97-129, 217-254, 473-519;
  * src/backend.rs:313-369; src/llama_cpu.rs:401-419). */
