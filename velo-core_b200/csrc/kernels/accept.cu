@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include "common/smem_attr.cuh"
 #include "common/spec_math.cuh"
 #include "kernels/accept.h"
 
@@ -490,13 +491,9 @@ size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
 template <bool kGreedy>
 cudaError_t launch_finish(const AcceptParams& p, cudaStream_t stream) {
     const FinishLayout L = finish_layout(p.nrows, p.ntiles);
-    static int configured = 0;  // bytes the attribute was last raised to
-    if (L.bytes > 48 * 1024 && L.bytes > configured) {
-        cudaError_t e = cudaFuncSetAttribute(accept_finish_kernel<kGreedy>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, L.bytes);
-        if (e != cudaSuccess) return e;
-        configured = L.bytes;
-    }
+    static SmemAttr smem_attr;
+    const cudaError_t ea = ensure_smem(smem_attr, accept_finish_kernel<kGreedy>, L.bytes);
+    if (ea != cudaSuccess) return ea;
     const int ctas_per_seq = kGreedy ? 1 : (p.ntiles + kFinWarps - 1) / kFinWarps;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(p.B * ctas_per_seq));

@@ -3,6 +3,7 @@
 // pages, and the KV commit into f32 pages.
 #include <cmath>
 
+#include "common/smem_attr.cuh"
 #include "kernels/f32_path.h"
 
 namespace velo {
@@ -95,11 +96,9 @@ template <int MT, int MODE>
 cudaError_t gemm_launch(const float* w, const float* x, int M, int N, int K, float* y, int ldy,
                         cudaStream_t s) {
     const size_t smem = (size_t)MT * K * sizeof(float);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_f32_kernel<MT, MODE>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
+    static SmemAttr attr;
+    const cudaError_t ea = ensure_smem(attr, gemm_f32_kernel<MT, MODE>, (int)smem);
+    if (ea != cudaSuccess) return ea;
     int gx = (N + kGemmWarps - 1) / kGemmWarps;
     if (gx > 65535) gx = 65535;
     const dim3 grid(gx, (M + MT - 1) / MT);
@@ -383,13 +382,9 @@ cudaError_t launch_rope_split_f32(const float* qkv, const uint64_t* anc, const i
 template <int DW>
 cudaError_t attn_f32_launch(const TreeAttnF32Args& a, unsigned grid, cudaStream_t s) {
     constexpr int smem = attn_f32_smem(DW * 32);
-    static bool configured = false;
-    if (smem > 48 * 1024 && !configured) {
-        cudaError_t e = cudaFuncSetAttribute(tree_attn_f32_kernel<DW>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    static SmemAttr attr;
+    const cudaError_t ea = ensure_smem(attr, tree_attn_f32_kernel<DW>, smem);
+    if (ea != cudaSuccess) return ea;
     tree_attn_f32_kernel<DW><<<grid, kAttnWarps * 32, smem, s>>>(a);
     return cudaGetLastError();
 }

@@ -39,6 +39,7 @@
 #include <mutex>
 
 #include "common/sm100.cuh"
+#include "common/smem_attr.cuh"
 #include "kernels/q4gemm.h"
 
 namespace velo {
@@ -948,12 +949,8 @@ template <int BNT>
 cudaError_t launch_ta(const Q4GemmArgs& a, const CUtensorMap& map, int tiles, int sm_count,
                       cudaStream_t stream) {
     using C = TaCfg<BNT>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(q4_gemm_ta_kernel<BNT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)C::kSmemBytes);
-    });
+    static SmemAttr attr;
+    const cudaError_t attr_err = ensure_smem(attr, q4_gemm_ta_kernel<BNT>, (int)C::kSmemBytes);
     if (attr_err != cudaSuccess) return attr_err;
     const int grid = tiles < sm_count ? tiles : sm_count;
     q4_gemm_ta_kernel<BNT><<<grid, C::kThreads, C::kSmemBytes, stream>>>(map, a);
@@ -966,13 +963,8 @@ template <int BN>
 cudaError_t launch_width(const Q4GemmArgs& a, const CUtensorMap& map, int tiles, int sm_count,
                          cudaStream_t stream) {
     using C = Cfg<BN>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(q4_gemm_kernel<BN>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)C::kSmemBytes);
-    });
+    static SmemAttr attr;
+    const cudaError_t attr_err = ensure_smem(attr, q4_gemm_kernel<BN>, (int)C::kSmemBytes);
     if (attr_err != cudaSuccess) return attr_err;
     const int grid = tiles < sm_count ? tiles : sm_count;
     q4_gemm_kernel<BN><<<grid, C::kThreads, C::kSmemBytes, stream>>>(map, a);
@@ -994,12 +986,8 @@ cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
     // SwiGLU: the paired-accumulator kernel (config-3 w1/w3 130 us against 146
     // on the shared-memory-weight kernel; config 5 1830 against 1838)
     if (a.M > BM && !force_smem && a.mode == kEpiSwiGLU) {
-        static std::once_flag once;
-        static cudaError_t attr_err = cudaSuccess;
-        std::call_once(once, [] {
-            attr_err = cudaFuncSetAttribute(q4_gemm_ta_swiglu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            (int)swi::kSmemBytes);
-        });
+        static SmemAttr attr;
+        const cudaError_t attr_err = ensure_smem(attr, q4_gemm_ta_swiglu_kernel, (int)swi::kSmemBytes);
         if (attr_err != cudaSuccess) return attr_err;
         const int tiles = ((a.M + swi::BNT - 1) / swi::BNT) * (q4_n_tiles(a.N) / 2);
         const int grid = tiles < sm_count ? tiles : sm_count;

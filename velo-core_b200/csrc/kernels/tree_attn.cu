@@ -29,6 +29,7 @@
 #include <mutex>
 
 #include "common/sm100.cuh"
+#include "common/smem_attr.cuh"
 #include "common/spec_math.cuh"  // max3
 #include "kernels/q4gemm.h"  // make_tmap_f16_2d
 #include "kernels/tree_attn.h"
@@ -642,12 +643,8 @@ cudaError_t make_maps(const TreeAttnArgs& a, CUtensorMap* tk, CUtensorMap* tv, C
 template <bool INT8, int QT>
 cudaError_t launch_impl(const TreeAttnArgs& a, cudaStream_t stream) {
     using C = TmCfg<INT8, QT>;
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(tree_attn_kernel<INT8, QT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)C::kSmem);
-    });
+    static SmemAttr attr;
+    const cudaError_t attr_err = ensure_smem(attr, tree_attn_kernel<INT8, QT>, (int)C::kSmem);
     if (attr_err != cudaSuccess) return attr_err;
     CUtensorMap tk{}, tv{}, tnk{}, tnv{};
     const cudaError_t e = make_maps<INT8>(a, &tk, &tv, &tnk, &tnv);
