@@ -299,6 +299,49 @@ VELO_API int32_t velo_cuda_load_model(velo_cuda_ctx *ctx, const velo_model_desc 
 VELO_API int32_t velo_cuda_bind_slot(velo_cuda_ctx *ctx, uint32_t slot, const uint32_t *pages,
                                      size_t n_pages);
 
+/* The context's own page allocator over its KV pool (block size = the page
+ * size, total_pages of the config), created by velo_cuda_load_model: one call
+ * in place of PagedAttentionBlockManager::allocate + MemoryRuntime::bind_slot
+ * (src/paged_attention.rs:155-186, src/runtime.rs:36).  Takes
+ * ceil(token_len / page_size) pages for handle `slot` and binds the slot's
+ * page-table row to them (the ids are also written to pages_out, or NULL).
+ * VELO_ERR_OUT_OF_PAGES when the pool is short (nothing taken) or the row
+ * is too small.  Allocating a slot that holds pages replaces its mapping
+ * without freeing the old pages, as the reference does.  A context either
+ * allocates every slot here or binds every slot itself (velo_cuda_bind_slot),
+ * not both. */
+VELO_API int32_t velo_cuda_slot_allocate(velo_cuda_ctx *ctx, uint32_t slot, size_t token_len,
+                                         uint32_t *pages_out, size_t pages_cap, size_t *n_pages);
+
+/* Return a slot's pages to the back of the free list
+ * (PagedAttentionBlockManager::release, src/paged_attention.rs:189-198) and
+ * fill its page-table row with an invalid id, so a later step on the slot is
+ * reported (VELO_ERR_DEVICE_FLAG) instead of touching pages it no longer
+ * owns.  VELO_ERR_UNKNOWN_HANDLE for a slot that holds no allocation. */
+VELO_API int32_t velo_cuda_slot_release(velo_cuda_ctx *ctx, uint32_t slot);
+
+/* Free pages left in the context's allocator (free_pages, :201-203). */
+VELO_API int32_t velo_cuda_free_pages(velo_cuda_ctx *ctx, size_t *out);
+
+/* The same allocator without a context or a GPU (host only), for a host that
+ * manages several pools or wants the page ids before it creates a context.
+ * create: VELO_ERR_INVALID_BLOCK_SIZE for block_size 0 (:103-106).
+ * allocate: OutOfPages writes requested / available (either may be NULL);
+ * pages_out (or NULL) must hold the pages needed.  mapped_pages:
+ * VELO_ERR_UNKNOWN_HANDLE when the handle holds nothing. */
+typedef struct velo_page_allocator velo_page_allocator;
+VELO_API int32_t velo_page_allocator_create(size_t block_size, size_t total_pages,
+                                            velo_page_allocator **out);
+VELO_API void velo_page_allocator_destroy(velo_page_allocator *a);
+VELO_API int32_t velo_page_allocator_allocate(velo_page_allocator *a, uint64_t handle, size_t token_len,
+                                              uint32_t *pages_out, size_t pages_cap, size_t *n_pages,
+                                              size_t *requested, size_t *available);
+VELO_API int32_t velo_page_allocator_release(velo_page_allocator *a, uint64_t handle);
+VELO_API int32_t velo_page_allocator_mapped_pages(const velo_page_allocator *a, uint64_t handle,
+                                                  uint32_t *pages_out, size_t pages_cap, size_t *n_pages);
+VELO_API size_t velo_page_allocator_free_pages(const velo_page_allocator *a);
+VELO_API size_t velo_page_allocator_pages_for_tokens(const velo_page_allocator *a, size_t token_len);
+
 /* Write n_tokens K/V rows (host [n_tokens][n_head_kv][head_dim], f16 for f16 /
  * int8 pools, f32 for f32 pools) of one layer at positions pos0.. of `slot`
  * (int8 pools quantise as kv_update_int8, src/kernels.metal:753-802).  The

@@ -245,3 +245,41 @@ def test_device_tensors_load_like_host():
     assert np.array_equal(out[0]["logits"], out[1]["logits"])
     assert np.array_equal(out[0]["accepted_len"], out[1]["accepted_len"])
     assert np.array_equal(out[0]["bonus"], out[1]["bonus"])
+
+
+def test_slot_allocator_binds_pages():
+    """velo_cuda_slot_allocate takes FIFO pages from the context's pool and
+    binds them: two slots filled with the same prompt through allocated pages
+    hold the same cache and predict the same token; release returns the pages
+    (src/paged_attention.rs:155-198)."""
+    shape = dict(n_vocab=512, n_embd=256, n_layer=2, n_head=2, n_head_kv=2, n_ff=512)
+    meta, tensors = synthetic.llama_q4_model(**shape, seed=8)
+    g = synthetic.rng(9, 62)
+    prompt = g.integers(0, meta["n_vocab"], 40).astype(np.uint32)
+    ctx = velo_cuda.Context(device=0, total_pages=8, max_slots=2, max_pages_per_slot=4)
+    try:
+        ctx.load_model(meta, tensors)
+        assert ctx.free_pages() == 8
+        assert list(ctx.slot_allocate(0, 40)) == [0, 1, 2]
+        assert list(ctx.slot_allocate(1, 40)) == [3, 4, 5]
+        assert ctx.free_pages() == 2
+        t0 = velo_cuda.prefill(ctx, 0, prompt, n_vocab=meta["n_vocab"])
+        t1 = velo_cuda.prefill(ctx, 1, prompt, n_vocab=meta["n_vocab"])
+        assert t0 == t1
+        for l in range(meta["n_layer"]):
+            k0, v0 = ctx.read_kv(0, l, 0, 40, 2)
+            k1, v1 = ctx.read_kv(1, l, 0, 40, 2)
+            assert np.array_equal(k0, k1) and np.array_equal(v0, v1)
+        ctx.slot_release(0)
+        assert ctx.free_pages() == 5
+        with pytest.raises(velo_cuda.VeloError) as e:
+            ctx.slot_release(0)
+        assert e.value.status == velo_cuda.ERR_UNKNOWN_HANDLE
+        with pytest.raises(velo_cuda.VeloError) as e:
+            ctx.slot_allocate(0, 4 * 16 + 1)  # five pages: more than a page-table row
+        assert e.value.status == velo_cuda.ERR_OUT_OF_PAGES
+        assert ctx.free_pages() == 5
+        assert list(ctx.slot_allocate(0, 64)) == [6, 7, 0, 1]
+        assert ctx.free_pages() == 1
+    finally:
+        ctx.close()

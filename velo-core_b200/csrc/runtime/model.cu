@@ -21,6 +21,7 @@
 #include "kernels/verify_ops.h"
 #include "runtime/context.h"
 #include "runtime/nccl_dyn.h"
+#include "runtime/page_alloc.h"
 #include "runtime/shard.h"
 
 #include <deque>
@@ -60,6 +61,7 @@ struct Model {
     int pool_pages = 0, kv_int8 = 0, max_slots = 0, max_pages = 0;  // kv_int8: int8 pages
     uint32_t* page_table = nullptr;
     std::vector<uint32_t> page_table_host;
+    velo::PageAllocator* allocator = nullptr;  // velo_cuda_slot_allocate / _release
     // per-step buffers, sized for cap_M rows
     int cap_M = 0, cap_B = 0;
     std::vector<void*> work;
@@ -136,6 +138,7 @@ void destroy_model(Model* m) {
     if (m->drf) cudaFree(m->drf);
     if (m->logits_all) cudaFree(m->logits_all);
     if (m->logits_full) cudaFree(m->logits_full);
+    delete m->allocator;
     delete m;
 }
 
@@ -496,6 +499,19 @@ int32_t forward_f32(velo_cuda_ctx* c, Model* m, int B, int N) {
     return VELO_OK;
 }
 
+// Write page-table row `slot`: ids pages[0..n), then `pad` (0: the rows
+// velo_cuda_bind_slot leaves; an invalid id for a released slot).  Waits for
+// the stream, so no step in flight still reads the old row.
+int32_t write_row(velo_cuda_ctx* c, Model* m, uint32_t slot, const uint32_t* pages, size_t n, uint32_t pad) {
+    uint32_t* row = m->page_table_host.data() + (size_t)slot * m->max_pages;
+    for (int i = 0; i < m->max_pages; ++i) row[i] = (size_t)i < n ? pages[i] : pad;
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    VELO_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    VELO_CUDA_TRY(cudaMemcpy(m->page_table + (size_t)slot * m->max_pages, row, (size_t)m->max_pages * 4,
+                             cudaMemcpyHostToDevice));
+    return VELO_OK;
+}
+
 int32_t check_model(velo_cuda_ctx* c) {
     if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
     if (!c->model) return fail(VELO_ERR_INVALID_ARGUMENT, "no model loaded (velo_cuda_load_model)");
@@ -645,6 +661,7 @@ int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const v
         m->kv_int8 = c->cfg.kv_dtype == VELO_KV_INT8;
         m->max_slots = (int)c->cfg.max_slots;
         m->max_pages = (int)(c->cfg.max_pages_per_slot ? c->cfg.max_pages_per_slot : m->pool_pages);
+        m->allocator = new velo::PageAllocator(16, (size_t)m->pool_pages);
         const size_t pe = (size_t)d->n_layer * m->layer_pool_elems();
         st = velo::dev_alloc(m, reinterpret_cast<uint8_t**>(&m->k_pool), pe * m->kv_elt());
         if (!st) st = velo::dev_alloc(m, reinterpret_cast<uint8_t**>(&m->v_pool), pe * m->kv_elt());
@@ -690,12 +707,55 @@ int32_t velo_cuda_bind_slot(velo_cuda_ctx* c, uint32_t slot, const uint32_t* pag
     for (size_t i = 0; i < n; ++i)
         if (pages[i] >= (uint32_t)m->pool_pages)
             return fail(VELO_ERR_OUT_OF_PAGES, "page id %u >= pool of %d pages", pages[i], m->pool_pages);
-    uint32_t* row = m->page_table_host.data() + (size_t)slot * m->max_pages;
-    for (int i = 0; i < m->max_pages; ++i) row[i] = (size_t)i < n ? pages[i] : 0u;
-    VELO_CUDA_TRY(cudaSetDevice(c->device));
-    VELO_CUDA_TRY(cudaStreamSynchronize(c->stream));
-    VELO_CUDA_TRY(cudaMemcpy(m->page_table + (size_t)slot * m->max_pages, row, (size_t)m->max_pages * 4,
-                             cudaMemcpyHostToDevice));
+    return velo::write_row(c, m, slot, pages, n, 0u);
+}
+
+int32_t velo_cuda_slot_allocate(velo_cuda_ctx* c, uint32_t slot, size_t token_len, uint32_t* pages_out,
+                                size_t pages_cap, size_t* n_pages) {
+    velo::clear_last_error();
+    int32_t st = velo::check_model(c);
+    if (st) return st;
+    Model* m = c->model;
+    if (slot >= (uint32_t)m->max_slots)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "slot %u >= max_slots %d", slot, m->max_slots);
+    const size_t req = m->allocator->pages_for_tokens(token_len);
+    if (req > (size_t)m->max_pages)
+        return fail(VELO_ERR_OUT_OF_PAGES, "OutOfPages { requested: %zu, available: %d } (page-table row)",
+                    req, m->max_pages);
+    if (pages_out && pages_cap < req)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "pages_out holds %zu ids, %zu needed", pages_cap, req);
+    std::vector<uint32_t> got;
+    size_t rq = 0, av = 0;
+    st = m->allocator->allocate(slot, token_len, &got, &rq, &av);
+    if (st) return fail(st, "OutOfPages { requested: %zu, available: %zu }", rq, av);
+    st = velo::write_row(c, m, slot, got.data(), got.size(), 0u);
+    if (st) return st;
+    if (n_pages) *n_pages = got.size();
+    if (pages_out)
+        for (size_t i = 0; i < got.size(); ++i) pages_out[i] = got[i];
+    return VELO_OK;
+}
+
+int32_t velo_cuda_slot_release(velo_cuda_ctx* c, uint32_t slot) {
+    velo::clear_last_error();
+    int32_t st = velo::check_model(c);
+    if (st) return st;
+    Model* m = c->model;
+    if (slot >= (uint32_t)m->max_slots)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "slot %u >= max_slots %d", slot, m->max_slots);
+    if (!m->allocator->mapped(slot)) return fail(VELO_ERR_UNKNOWN_HANDLE, "UnknownHandle(%u)", slot);
+    // unbind first: the pages go back only once no row names them
+    st = velo::write_row(c, m, slot, nullptr, 0, 0xffffffffu);
+    if (st) return st;
+    return m->allocator->release(slot);
+}
+
+int32_t velo_cuda_free_pages(velo_cuda_ctx* c, size_t* out) {
+    velo::clear_last_error();
+    const int32_t st = velo::check_model(c);
+    if (st) return st;
+    if (!out) return fail(VELO_ERR_INVALID_ARGUMENT, "out is NULL");
+    *out = c->model->allocator->free_pages();
     return VELO_OK;
 }
 

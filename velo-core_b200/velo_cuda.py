@@ -37,6 +37,7 @@ KV_F16, KV_INT8, KV_F32 = 0, 1, 2  # KV_F32: the fp32 path of the model
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
+_SZ = ctypes.c_size_t
 _lib = None
 
 
@@ -80,6 +81,17 @@ _SIGS = {
     "velo_cuda_shard_weight": (_I32, [_P, _I32, _I32, _I32, _P, ctypes.c_size_t,
                                       ctypes.POINTER(ctypes.c_uint64),
                                       ctypes.POINTER(ctypes.c_uint64)]),
+    "velo_cuda_slot_allocate": (_I32, [_P, ctypes.c_uint32, _SZ, _P, _SZ, ctypes.POINTER(_SZ)]),
+    "velo_cuda_slot_release": (_I32, [_P, ctypes.c_uint32]),
+    "velo_cuda_free_pages": (_I32, [_P, ctypes.POINTER(_SZ)]),
+    "velo_page_allocator_create": (_I32, [_SZ, _SZ, ctypes.POINTER(_P)]),
+    "velo_page_allocator_destroy": (None, [_P]),
+    "velo_page_allocator_allocate": (_I32, [_P, ctypes.c_uint64, _SZ, _P, _SZ, ctypes.POINTER(_SZ),
+                                            ctypes.POINTER(_SZ), ctypes.POINTER(_SZ)]),
+    "velo_page_allocator_release": (_I32, [_P, ctypes.c_uint64]),
+    "velo_page_allocator_mapped_pages": (_I32, [_P, ctypes.c_uint64, _P, _SZ, ctypes.POINTER(_SZ)]),
+    "velo_page_allocator_free_pages": (_SZ, [_P]),
+    "velo_page_allocator_pages_for_tokens": (_SZ, [_P, _SZ]),
 }
 
 DT_F32, DT_F16, DT_Q4_0 = 0, 1, 2
@@ -132,7 +144,7 @@ def header_functions():
     """Names of the functions include/velo_cuda.h declares."""
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(velo_cuda_\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(velo_(?:cuda|page_allocator)_\w+)\s*\(", src)))
 
 
 def last_error():
@@ -268,6 +280,24 @@ class Context:
         p = np.ascontiguousarray(pages, np.uint32)
         check(lib().velo_cuda_bind_slot(self._h, slot, _ptr(p), p.size))
 
+    def slot_allocate(self, slot, token_len):
+        """Pages for `token_len` tokens from the context's allocator, bound to
+        `slot`; returns their ids."""
+        need = -(-int(token_len) // 16)
+        pages = np.zeros(max(need, 1), np.uint32)
+        n = _SZ()
+        check(lib().velo_cuda_slot_allocate(self._h, slot, token_len, _ptr(pages), pages.size,
+                                            ctypes.byref(n)))
+        return pages[:n.value].copy()
+
+    def slot_release(self, slot):
+        check(lib().velo_cuda_slot_release(self._h, slot))
+
+    def free_pages(self):
+        n = _SZ()
+        check(lib().velo_cuda_free_pages(self._h, ctypes.byref(n)))
+        return n.value
+
     def write_kv(self, slot, layer, pos0, k, v):
         """k, v [n][n_kv][head_dim]: f32 for an f32 pool, else f16."""
         dt = np.float32 if self.kv_dtype == KV_F32 else np.float16
@@ -324,6 +354,65 @@ def prefill(ctx, slot, tokens, pos0=0, chunk=64, n_vocab=None):
                             n_vocab=n_vocab)
         nxt = int(r["bonus"][0])
     return nxt
+
+
+class OutOfPages(VeloError):
+    """PageManagerError::OutOfPages { requested, available }."""
+
+    def __init__(self, requested, available, message):
+        super().__init__(ERR_OUT_OF_PAGES, message)
+        self.requested = requested
+        self.available = available
+
+
+class PageAllocator:
+    """The KV page allocator without a context or GPU
+    (PagedAttentionBlockManager, src/paged_attention.rs:92-211)."""
+
+    def __init__(self, block_size, total_pages):
+        self._h = None
+        h = _P()
+        check(lib().velo_page_allocator_create(block_size, total_pages, ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib().velo_page_allocator_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def pages_for_tokens(self, token_len):
+        return lib().velo_page_allocator_pages_for_tokens(self._h, token_len)
+
+    def allocate(self, handle, token_len):
+        need = self.pages_for_tokens(token_len)
+        pages = np.zeros(max(need, 1), np.uint32)
+        n, rq, av = _SZ(), _SZ(), _SZ()
+        st = lib().velo_page_allocator_allocate(self._h, handle, token_len, _ptr(pages), pages.size,
+                                                ctypes.byref(n), ctypes.byref(rq), ctypes.byref(av))
+        if st == ERR_OUT_OF_PAGES:
+            raise OutOfPages(rq.value, av.value, last_error())
+        check(st)
+        return pages[:n.value].copy()
+
+    def release(self, handle):
+        check(lib().velo_page_allocator_release(self._h, handle))
+
+    def mapped_pages(self, handle):
+        """The handle's pages, or None (mapped_pages returning None)."""
+        n = _SZ()
+        if lib().velo_page_allocator_mapped_pages(self._h, handle, None, 0, ctypes.byref(n)) == \
+                ERR_UNKNOWN_HANDLE:
+            return None
+        pages = np.zeros(max(n.value, 1), np.uint32)
+        check(lib().velo_page_allocator_mapped_pages(self._h, handle, _ptr(pages), pages.size,
+                                                     ctypes.byref(n)))
+        return pages[:n.value].copy()
+
+    def free_pages(self):
+        return lib().velo_page_allocator_free_pages(self._h)
 
 
 def nccl_unique_id():
