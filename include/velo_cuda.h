@@ -48,7 +48,12 @@ typedef enum velo_status {
     VELO_ERR_TIMEOUT = 10,             /* velo_cuda_sync deadline passed */
     VELO_ERR_OUT_OF_MEMORY = 11,
     VELO_ERR_NCCL = 12,
-    VELO_ERR_DEVICE_FLAG = 13          /* a kernel reported a bad input on device */
+    VELO_ERR_DEVICE_FLAG = 13,         /* a kernel reported a bad input on device */
+    VELO_ERR_IO = 14,                  /* LoadError::Io / GgufError::Io (open, short read) */
+    VELO_ERR_GGUF = 15,                /* GgufError::{BadMagic, UnsupportedVersion, UnknownType, Malformed} */
+    VELO_ERR_MISSING_META = 16,        /* LoadError::MissingMeta */
+    VELO_ERR_MISSING_TENSOR = 17,      /* LoadError::MissingTensor */
+    VELO_ERR_INVALID_SHAPE = 18        /* LoadError::InvalidShape */
 } velo_status;
 
 typedef struct velo_cuda_ctx velo_cuda_ctx;
@@ -341,6 +346,77 @@ VELO_API int32_t velo_page_allocator_mapped_pages(const velo_page_allocator *a, 
                                                   uint32_t *pages_out, size_t pages_cap, size_t *n_pages);
 VELO_API size_t velo_page_allocator_free_pages(const velo_page_allocator *a);
 VELO_API size_t velo_page_allocator_pages_for_tokens(const velo_page_allocator *a, size_t token_len);
+
+/* ---- GGUF model files (host only, no GPU) -------------------------------- */
+
+/* A parsed GGUF file whose tensor data stays memory-mapped until
+ * velo_gguf_close.  open = GgufFile::read + read_all_tensors (src/gguf.rs:
+ * 227-320): VELO_ERR_IO (missing file, short data), VELO_ERR_GGUF (bad magic,
+ * version not 1..3, unknown value or ggml type, more than 4 dims, bad UTF-8). */
+typedef struct velo_gguf velo_gguf;
+VELO_API int32_t velo_gguf_open(const char *path, velo_gguf **out);
+VELO_API void velo_gguf_close(velo_gguf *g);
+VELO_API uint32_t velo_gguf_version(const velo_gguf *g);
+VELO_API uint64_t velo_gguf_n_tensors(const velo_gguf *g);
+VELO_API uint64_t velo_gguf_n_metadata(const velo_gguf *g);
+VELO_API uint64_t velo_gguf_data_offset(const velo_gguf *g);
+
+/* One metadata value (GgufValue, gguf.rs:103-118).  type: the GGUF value type
+ * id (0 u8 .. 12 f64); integers in u (unsigned, bool) or i (signed), floats
+ * in f, strings in s / s_len (owned by g, not NUL-safe), arrays give
+ * array_type and array_len (elements via velo_gguf_metadata_elem). */
+typedef struct velo_gguf_value {
+    int32_t type, array_type;
+    uint64_t u;
+    int64_t i;
+    double f;
+    const char *s;
+    uint64_t s_len, array_len;
+} velo_gguf_value;
+/* VELO_ERR_MISSING_META when the key is absent. */
+VELO_API int32_t velo_gguf_metadata(const velo_gguf *g, const char *key, velo_gguf_value *out);
+VELO_API int32_t velo_gguf_metadata_elem(const velo_gguf *g, const char *key, uint64_t index,
+                                         velo_gguf_value *out);
+
+/* TensorInfo (gguf.rs:198-207): shape as stored (innermost first), data
+ * points into the mapping.  VELO_ERR_MISSING_TENSOR when absent. */
+typedef struct velo_gguf_tensor {
+    int32_t ggml_type;
+    uint32_t n_dims;
+    uint64_t shape[4];
+    uint64_t offset, nbytes;
+    const void *data;
+} velo_gguf_tensor;
+VELO_API int32_t velo_gguf_tensor_info(const velo_gguf *g, const char *name, velo_gguf_tensor *out);
+
+/* ModelMeta::from_gguf (src/model_loader.rs:41-127): the velo_model_desc of
+ * the file plus arch, n_ctx and the inferred quantization (0 Q4_0, 1 Q4K;
+ * :143-153).  VELO_ERR_MISSING_META names the absent key. */
+typedef struct velo_gguf_model_meta {
+    uint32_t struct_size;  /* sizeof(velo_gguf_model_meta) */
+    velo_model_desc desc;
+    uint32_t n_ctx;
+    int32_t quantization;
+    char arch[64];
+} velo_gguf_model_meta;
+VELO_API int32_t velo_gguf_read_model_meta(const velo_gguf *g, velo_gguf_model_meta *out);
+
+/* WeightStore::validate (:192-234): every tensor of the Llama layout with the
+ * reference's shapes, in the reference's order (VELO_ERR_MISSING_TENSOR,
+ * VELO_ERR_INVALID_SHAPE). */
+VELO_API int32_t velo_gguf_validate(const velo_gguf *g);
+
+/* The weight descriptors velo_cuda_load_model takes, pointing into the
+ * mapping (valid until velo_gguf_close): the validated tensors, rows = the
+ * second stored dimension (1 for vectors), cols = the first.  F32, F16 and
+ * q4_0 tensors only (VELO_ERR_INVALID_ARGUMENT names another type).  q4_0
+ * bytes are used as stored, with the reference's element order
+ * (src/quant.rs:50-73).  *n gets the count; out may be NULL to ask it. */
+VELO_API int32_t velo_gguf_weights(const velo_gguf *g, velo_weight_desc *out, int32_t cap, int32_t *n);
+
+/* load_gguf (:291-309) then velo_cuda_load_model: parse, model meta,
+ * validate, upload and repack. */
+VELO_API int32_t velo_cuda_load_gguf(velo_cuda_ctx *ctx, const char *path);
 
 /* Write n_tokens K/V rows (host [n_tokens][n_head_kv][head_dim], f16 for f16 /
  * int8 pools, f32 for f32 pools) of one layer at positions pos0.. of `slot`

@@ -283,3 +283,31 @@ def test_slot_allocator_binds_pages():
         assert ctx.free_pages() == 1
     finally:
         ctx.close()
+
+
+def test_load_gguf_matches_load_model(tmp_path):
+    """velo_cuda_load_gguf (load_gguf, src/model_loader.rs:291-309, then the
+    upload) gives the step the same model as velo_cuda_load_model on the same
+    tensors: identical logits."""
+    import gguf_writer
+    shape = dict(n_vocab=512, n_embd=256, n_layer=2, n_head=2, n_head_kv=1, n_ff=512)
+    meta, tensors = synthetic.llama_q4_model(**shape, seed=12)
+    path = tmp_path / "model.gguf"
+    gguf_writer.write_model(path, meta, tensors)
+    g = synthetic.rng(13, 62)
+    tokens = g.integers(0, meta["n_vocab"], (1, 8)).astype(np.uint32)
+    parents = np.arange(-1, 7, dtype=np.int32)[None]
+    out = []
+    for via_file in (False, True):
+        ctx = velo_cuda.Context(device=0, total_pages=4, max_slots=1, max_pages_per_slot=4)
+        try:
+            if via_file:
+                ctx.load_gguf(path)
+            else:
+                ctx.load_model(meta, tensors)
+            ctx.bind_slot(0, [0, 1, 2, 3])
+            out.append(ctx.verify_step([0], [0], tokens, parents, commit=False, want_logits=True,
+                                       n_vocab=meta["n_vocab"])["logits"])
+        finally:
+            ctx.close()
+    assert np.array_equal(out[0], out[1])

@@ -32,6 +32,11 @@ ERR_TIMEOUT = 10
 ERR_OUT_OF_MEMORY = 11
 ERR_NCCL = 12
 ERR_DEVICE_FLAG = 13
+ERR_IO = 14
+ERR_GGUF = 15
+ERR_MISSING_META = 16
+ERR_MISSING_TENSOR = 17
+ERR_INVALID_SHAPE = 18
 
 KV_F16, KV_INT8, KV_F32 = 0, 1, 2  # KV_F32: the fp32 path of the model
 
@@ -92,6 +97,19 @@ _SIGS = {
     "velo_page_allocator_mapped_pages": (_I32, [_P, ctypes.c_uint64, _P, _SZ, ctypes.POINTER(_SZ)]),
     "velo_page_allocator_free_pages": (_SZ, [_P]),
     "velo_page_allocator_pages_for_tokens": (_SZ, [_P, _SZ]),
+    "velo_gguf_open": (_I32, [ctypes.c_char_p, ctypes.POINTER(_P)]),
+    "velo_gguf_close": (None, [_P]),
+    "velo_gguf_version": (ctypes.c_uint32, [_P]),
+    "velo_gguf_n_tensors": (ctypes.c_uint64, [_P]),
+    "velo_gguf_n_metadata": (ctypes.c_uint64, [_P]),
+    "velo_gguf_data_offset": (ctypes.c_uint64, [_P]),
+    "velo_gguf_metadata": (_I32, [_P, ctypes.c_char_p, _P]),
+    "velo_gguf_metadata_elem": (_I32, [_P, ctypes.c_char_p, ctypes.c_uint64, _P]),
+    "velo_gguf_tensor_info": (_I32, [_P, ctypes.c_char_p, _P]),
+    "velo_gguf_read_model_meta": (_I32, [_P, _P]),
+    "velo_gguf_validate": (_I32, [_P]),
+    "velo_gguf_weights": (_I32, [_P, _P, _I32, ctypes.POINTER(_I32)]),
+    "velo_cuda_load_gguf": (_I32, [_P, ctypes.c_char_p]),
 }
 
 DT_F32, DT_F16, DT_Q4_0 = 0, 1, 2
@@ -144,7 +162,7 @@ def header_functions():
     """Names of the functions include/velo_cuda.h declares."""
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(velo_(?:cuda|page_allocator)_\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(velo_(?:cuda|page_allocator|gguf)_\w+)\s*\(", src)))
 
 
 def last_error():
@@ -276,6 +294,10 @@ class Context:
             ws[i] = WeightDesc(nm, dt, flags, ptr, rows, cols)
         check(lib().velo_cuda_load_model(self._h, ctypes.byref(d), ws, len(tensors)))
 
+    def load_gguf(self, path):
+        """load_gguf + upload (velo_cuda_load_gguf)."""
+        check(lib().velo_cuda_load_gguf(self._h, os.fsencode(path)))
+
     def bind_slot(self, slot, pages):
         p = np.ascontiguousarray(pages, np.uint32)
         check(lib().velo_cuda_bind_slot(self._h, slot, _ptr(p), p.size))
@@ -354,6 +376,127 @@ def prefill(ctx, slot, tokens, pos0=0, chunk=64, n_vocab=None):
                             n_vocab=n_vocab)
         nxt = int(r["bonus"][0])
     return nxt
+
+
+class GgufValue(ctypes.Structure):
+    _fields_ = [("type", _I32), ("array_type", _I32), ("u", ctypes.c_uint64), ("i", ctypes.c_int64),
+                ("f", ctypes.c_double), ("s", ctypes.POINTER(ctypes.c_char)), ("s_len", ctypes.c_uint64),
+                ("array_len", ctypes.c_uint64)]
+
+
+class GgufTensor(ctypes.Structure):
+    _fields_ = [("ggml_type", _I32), ("n_dims", ctypes.c_uint32), ("shape", ctypes.c_uint64 * 4),
+                ("offset", ctypes.c_uint64), ("nbytes", ctypes.c_uint64), ("data", _P)]
+
+
+class GgufModelMeta(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("desc", ModelDesc), ("n_ctx", ctypes.c_uint32),
+                ("quantization", _I32), ("arch", ctypes.c_char * 64)]
+
+
+class Gguf:
+    """A GGUF file, parsed on the host with its tensor data mapped
+    (GgufFile + ModelMeta + WeightStore, src/gguf.rs, src/model_loader.rs)."""
+
+    def __init__(self, path):
+        self._h = None
+        h = _P()
+        check(lib().velo_gguf_open(os.fsencode(path), ctypes.byref(h)))
+        self._h = h
+
+    def close(self):
+        if self._h:
+            lib().velo_gguf_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    @property
+    def version(self):
+        return lib().velo_gguf_version(self._h)
+
+    @property
+    def n_tensors(self):
+        return lib().velo_gguf_n_tensors(self._h)
+
+    @property
+    def n_metadata(self):
+        return lib().velo_gguf_n_metadata(self._h)
+
+    @property
+    def data_offset(self):
+        return lib().velo_gguf_data_offset(self._h)
+
+    @staticmethod
+    def _value(v, fetch_elem):
+        t = v.type
+        if t in (0, 2, 4, 10):
+            return ("u", v.u)
+        if t == 7:
+            return ("bool", bool(v.u))
+        if t in (1, 3, 5, 11):
+            return ("i", v.i)
+        if t in (6, 12):
+            return ("f", v.f)
+        if t == 8:
+            return ("str", ctypes.string_at(v.s, v.s_len).decode())
+        return ("array", [fetch_elem(k) for k in range(v.array_len)])
+
+    def metadata(self, key):
+        """(type id, python value); VeloError ERR_MISSING_META when absent."""
+        v = GgufValue()
+        k = key.encode()
+        check(lib().velo_gguf_metadata(self._h, k, ctypes.byref(v)))
+
+        def elem(i):
+            e = GgufValue()
+            check(lib().velo_gguf_metadata_elem(self._h, k, i, ctypes.byref(e)))
+            return self._value(e, None)[1]
+        return v.type, self._value(v, elem)[1]
+
+    def tensor(self, name):
+        """dict(ggml_type, shape, offset, nbytes, data=bytes)."""
+        t = GgufTensor()
+        check(lib().velo_gguf_tensor_info(self._h, name.encode(), ctypes.byref(t)))
+        data = ctypes.string_at(t.data, t.nbytes) if t.data else b""
+        return {"ggml_type": t.ggml_type, "shape": [t.shape[d] for d in range(t.n_dims)],
+                "offset": t.offset, "nbytes": t.nbytes, "data": data}
+
+    def model_meta(self):
+        m = GgufModelMeta()
+        m.struct_size = ctypes.sizeof(GgufModelMeta)
+        check(lib().velo_gguf_read_model_meta(self._h, ctypes.byref(m)))
+        d = m.desc
+        return {"arch": m.arch.decode(), "n_vocab": d.n_vocab, "n_embd": d.n_embd, "n_layer": d.n_layer,
+                "n_head": d.n_head, "n_head_kv": d.n_head_kv, "n_ff": d.n_ff, "head_dim": d.head_dim,
+                "rope_freq_base": d.rope_freq_base, "norm_eps": d.norm_eps, "n_ctx": m.n_ctx,
+                "quantization": m.quantization}
+
+    def validate(self):
+        check(lib().velo_gguf_validate(self._h))
+
+    def weights(self):
+        """[(name, dtype, rows, cols, bytes)] as velo_cuda_load_model takes them."""
+        n = _I32()
+        check(lib().velo_gguf_weights(self._h, None, 0, ctypes.byref(n)))
+        ws = (WeightDesc * n.value)()
+        check(lib().velo_gguf_weights(self._h, ws, n.value, ctypes.byref(n)))
+        out = []
+        for w in ws:
+            nb = q4_0_row_bytes(w.cols) * w.rows if w.dtype == 2 else w.rows * w.cols * (4 if w.dtype == 0 else 2)
+            out.append((w.name.decode(), w.dtype, w.rows, w.cols, ctypes.string_at(w.data, nb)))
+        return out
+
+
+def q4_0_row_bytes(cols):
+    return cols // 32 * 18
 
 
 class OutOfPages(VeloError):
