@@ -9,8 +9,8 @@ import pytest
 import synthetic
 import velo_cuda
 import vo
-from speculative import (CudaDraft, CudaTarget, NextTokenPrediction, SpeculativeDecoder,
-                         VerifyStep)
+from speculative import (CudaBatchDraft, CudaBatchTarget, CudaDraft, CudaTarget, NextTokenPrediction,
+                         SpeculativeDecoder, SpeculativeEngine, VerifyStep)
 
 pytestmark = pytest.mark.gpu
 
@@ -91,3 +91,59 @@ def test_speculative_generate_device_matches_oracle():
     assert out.stats.accepted_tokens > 0 and out.stats.rejected_tokens > 0
     assert out.tokens == ref.tokens
     assert out.stats == ref.stats
+
+
+class PerRequest:
+    """One single-sequence model per request id behind the engine's batch interface."""
+
+    def __init__(self, models):
+        self.models = models
+
+    def draft_batch(self, reqs):
+        return [self.models[rid].draft(c, m) for rid, c, m in reqs]
+
+    def verify_batch(self, reqs):
+        return [self.models[rid].verify(c, d) for rid, c, d in reqs]
+
+
+def test_batched_engine_matches_per_request_device_models():
+    """generate_batch over CudaBatchDraft / CudaBatchTarget (one draft step per
+    position and one verify step per round for all requests) gives every
+    request the tokens and statistics of the same engine over per-request
+    CudaDraft / CudaTarget models (one sequence per call): batching changes
+    no result.  The per-request session path is checked against the oracle in
+    test_speculative_generate_device_matches_oracle."""
+    V = 256
+    meta, target_w = synthetic.llama_q4_model(V, 256, 2, 2, 1, 512, seed=51, sigma=0.05)
+    _, draft_w = synthetic.llama_q4_model(V, 256, 1, 2, 1, 512, seed=51, sigma=0.05)
+    dmeta = dict(meta, n_layer=1)
+    g = synthetic.rng(52, 91)
+    requests = [(list(g.integers(0, V, n)), m) for n, m in ((12, 24), (30, 9), (5, 17))]
+    eng = SpeculativeEngine(3, max_slots=3)
+
+    def run(batched):
+        tctx = velo_cuda.Context(device=0, total_pages=24, max_slots=3, max_pages_per_slot=8)
+        dctx = velo_cuda.Context(device=0, total_pages=24, max_slots=3, max_pages_per_slot=8)
+        try:
+            tctx.load_model(meta, target_w)
+            dctx.load_model(dmeta, draft_w)
+            for s in range(3):
+                tctx.slot_allocate(s, 8 * 16)
+                dctx.slot_allocate(s, 8 * 16)
+            if batched:
+                draft, target = CudaBatchDraft(dctx, [0, 1, 2], V), CudaBatchTarget(tctx, [0, 1, 2], V)
+            else:
+                draft = PerRequest([CudaDraft(dctx, s, V) for s in range(3)])
+                target = PerRequest([CudaTarget(tctx, s, V) for s in range(3)])
+            return eng.generate_batch(draft, target, requests)
+        finally:
+            tctx.close()
+            dctx.close()
+
+    ref, out = run(False), run(True)
+    assert sum(o.stats.rejected_tokens for o in out) > 0
+    assert sum(o.stats.accepted_tokens for o in out) > 0
+    for o, r, (_, m) in zip(out, ref, requests):
+        assert len(o.tokens) == m
+        assert o.tokens == r.tokens
+        assert o.stats == r.stats

@@ -389,3 +389,175 @@ def verify_tree_on_device(ctx, slot, n_vocab, context, tree, commit=True):
     r = ctx.verify_step([slot], [len(context) - 1], nodes[None], parents[None], commit=commit,
                         n_vocab=n_vocab)
     return rt, TreeVerifyResult([int(e) for e in r["expected"][0]]), r
+
+
+# ---------------------------------------------------------------- batched engine
+class SlotsExhausted(SpeculativeError):
+    """SlotPool has no free slot for a request (the engine's acquire failure)."""
+
+    def __init__(self, requested, available):
+        super().__init__(requested, available)
+        self.requested, self.available = requested, available
+
+    def __str__(self):
+        return f"no free slot: {self.requested} requests, {self.available} slots"
+
+
+def _draft_batch(model, reqs):
+    """DraftModel::draft_batch; the trait's default drafts one request at a
+    time (speculative.rs:133-254).  reqs: [(request id, context, max tokens)]."""
+    if hasattr(model, "draft_batch"):
+        return model.draft_batch(reqs)
+    return [model.draft(c, m) for _, c, m in reqs]
+
+
+def _verify_batch(model, reqs):
+    """TargetModel::verify_batch, default one request at a time.
+    reqs: [(request id, context, drafted tokens)]."""
+    if hasattr(model, "verify_batch"):
+        return model.verify_batch(reqs)
+    return [model.verify(c, d) for _, c, d in reqs]
+
+
+class SpeculativeEngine:
+    """VeloEngine::generate_batch (engine.rs:233-420) over the verify step.
+
+    Each round, every request still short of max_new_tokens drafts
+    min(remaining, draft_window) tokens (the decoder's fixed window, as the
+    engine's loop uses it), ONE verify_batch call covers all of them (on the
+    device: one velo_cuda_verify_step for all slots), then each session
+    commits its own result and emits the target's token at a rejection.
+    Requests are numbered 0..n-1 and bound to slots 0..n-1; more requests
+    than `max_slots` is an error, as when the engine's SlotPool runs dry.
+    A round in which no request makes progress (a draft model returning
+    nothing) ends the loop instead of repeating forever."""
+
+    def __init__(self, draft_window, max_window=None, max_slots=None):
+        self.decoder = SpeculativeDecoder(draft_window, max_window)
+        self.max_slots = max_slots
+
+    def generate_batch(self, draft_model, target_model, requests):
+        """requests: [(prompt, max_new_tokens)] -> [SpeculativeOutput]."""
+        if self.max_slots is not None and len(requests) > self.max_slots:
+            raise SlotsExhausted(len(requests), self.max_slots)
+        sessions = [self.decoder.begin(p) for p, _ in requests]
+        limits = [int(m) for _, m in requests]
+        generated = [[] for _ in requests]
+        for model in (draft_model, target_model):
+            if hasattr(model, "bind_slot"):
+                for i in range(len(requests)):
+                    model.bind_slot(i)
+        while True:
+            active = [i for i in range(len(requests)) if len(generated[i]) < limits[i]]
+            if not active:
+                break
+            window = self.decoder.draft_window
+            drafts = _draft_batch(draft_model, [(i, sessions[i].context,
+                                                 min(limits[i] - len(generated[i]), window))
+                                                for i in active])
+            for i in active:
+                sessions[i].record_draft_call()
+            verified = _verify_batch(target_model, [(i, sessions[i].context, [p.token for p in d])
+                                                    for i, d in zip(active, drafts)])
+            for i in active:
+                sessions[i].record_target_call()
+            progressed = False
+            for i, d, v in zip(active, drafts, verified):
+                accepted = sessions[i].commit(d, v)
+                generated[i].extend(accepted)
+                progressed |= bool(accepted)
+                if sessions[i].has_pending_rejection():
+                    token = sessions[i].take_rejected_token()
+                    if token is not None:
+                        generated[i].append(token)
+                        progressed = True
+            if not progressed:
+                break
+        return [SpeculativeOutput(generated[i], sessions[i].stats) for i in range(len(requests))]
+
+
+class CudaBatchTarget:
+    """TargetModel::verify_batch on the device: the chains of all requests
+    with the same draft length run as ONE velo_cuda_verify_step (B requests,
+    N = k + 1 nodes each, every sequence at its own context length), each
+    committing its accepted path into its own slot (`slots[request id]`).
+    Per slot the pages hold the K/V of context[:-1], as for CudaTarget."""
+
+    def __init__(self, ctx, slots, n_vocab):
+        self.ctx, self.slots, self.n_vocab = ctx, list(slots), n_vocab
+        self.cached = {}
+
+    def _prefill(self, rid, context):
+        have, n = self.cached.get(rid, 0), len(context) - 1
+        if n > have:
+            velo_cuda.prefill(self.ctx, self.slots[rid], context[have:n], pos0=have, n_vocab=self.n_vocab)
+            self.cached[rid] = n
+
+    def verify_batch(self, reqs):
+        out = [None] * len(reqs)
+        groups = {}
+        for j, (rid, context, drafted) in enumerate(reqs):
+            self._prefill(rid, context)
+            groups.setdefault(len(drafted), []).append(j)
+        for k, members in groups.items():
+            if k == 0:
+                for j in members:
+                    out[j] = []
+                continue
+            tokens = np.array([[reqs[j][1][-1]] + list(reqs[j][2]) for j in members], np.uint32)
+            parents = np.tile(np.arange(-1, k, dtype=np.int32), (len(members), 1))
+            pos = [len(reqs[j][1]) - 1 for j in members]
+            r = self.ctx.verify_step([self.slots[reqs[j][0]] for j in members], pos, tokens, parents,
+                                     commit=True, n_vocab=self.n_vocab)
+            for b, j in enumerate(members):
+                rid, _, drafted = reqs[j]
+                acc, bonus = int(r["accepted_len"][b]), int(r["bonus"][b])
+                self.cached[rid] = pos[b] + acc + 1
+                out[j] = [VerifyStep(t) for t in drafted[:acc]] + [VerifyStep(bonus)] * (k - acc)
+        return out
+
+
+class CudaBatchDraft:
+    """DraftModel::draft_batch on the device, greedy: each slot's cache is
+    rewound to the prefix it shares with its context (as CudaDraft), then
+    every draft position is ONE velo_cuda_verify_step over all requests that
+    still need a token (B requests, one node each, commit of every node)."""
+
+    def __init__(self, ctx, slots, n_vocab):
+        self.ctx, self.slots, self.n_vocab = ctx, list(slots), n_vocab
+        self.tokens = {}
+
+    def _prefill(self, rid, context):
+        have = self.tokens.get(rid, [])
+        common = 0
+        for a, b in zip(have, context[:-1]):
+            if a != b:
+                break
+            common += 1
+        self.tokens[rid] = list(have[:common])
+        if len(context) - 1 > common:
+            velo_cuda.prefill(self.ctx, self.slots[rid], context[common:-1], pos0=common,
+                              n_vocab=self.n_vocab)
+            self.tokens[rid] = [int(t) for t in context[:-1]]
+
+    def draft_batch(self, reqs):
+        out = [[] for _ in reqs]
+        last = []
+        for rid, context, _ in reqs:
+            self._prefill(rid, context)
+            last.append(int(context[-1]))
+        while True:
+            live = [j for j, (_, _, m) in enumerate(reqs) if len(out[j]) < m]
+            if not live:
+                break
+            rids = [reqs[j][0] for j in live]
+            r = self.ctx.verify_step([self.slots[rid] for rid in rids],
+                                     [len(self.tokens[rid]) for rid in rids],
+                                     np.array([[last[j]] for j in live], np.uint32),
+                                     np.full((len(live), 1), -1, np.int32), commit="all",
+                                     n_vocab=self.n_vocab)
+            for b, j in enumerate(live):
+                self.tokens[rids[b]].append(last[j])
+                last[j] = int(r["bonus"][b])
+                out[j].append(NextTokenPrediction(last[j]))
+        return out
