@@ -541,7 +541,7 @@ int32_t velo_gguf_weights(const velo_gguf* gc, velo_weight_desc* out, int32_t ca
     if (!out) return VELO_OK;
     if (cap < (int32_t)names.size())
         return fail(VELO_ERR_INVALID_ARGUMENT, "out holds %d descriptors, %zu needed", cap, names.size());
-    g->names = std::move(names);
+    if (g->names != names) g->names = std::move(names);  // equal lists keep earlier pointers valid
     for (size_t k = 0; k < g->names.size(); ++k) {
         const velo::GgufTensor& t = g->file.tensors.at(g->names[k]);
         int32_t dt;

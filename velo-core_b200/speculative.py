@@ -500,10 +500,7 @@ class CudaBatchTarget:
             self._prefill(rid, context)
             groups.setdefault(len(drafted), []).append(j)
         for k, members in groups.items():
-            if k == 0:
-                for j in members:
-                    out[j] = []
-                continue
+            # k == 0 still runs: the root's K/V is committed, as CudaTarget does
             tokens = np.array([[reqs[j][1][-1]] + list(reqs[j][2]) for j in members], np.uint32)
             parents = np.tile(np.arange(-1, k, dtype=np.int32), (len(members), 1))
             pos = [len(reqs[j][1]) - 1 for j in members]
