@@ -15,6 +15,7 @@ int32_t velo_cuda_tree_attention(velo_cuda_ctx* c, const void* q, const void* k_
                                  const int32_t* parents, int32_t B, int32_t n_nodes,
                                  int32_t n_head, int32_t n_kv, int32_t head_dim, int32_t kv_dtype,
                                  void* out, int32_t out_dtype) {
+    velo::Range nvtx_range("velo.tree_attention");
     velo::clear_last_error();
     if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
     if (head_dim != velo::kAttnHeadDim)

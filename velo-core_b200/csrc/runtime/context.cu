@@ -278,6 +278,7 @@ static int32_t check_accept_args(int32_t B, int32_t k, int32_t V, float temperat
 int32_t velo_cuda_accept_device(velo_cuda_ctx* c, const float* tgt, const float* drf,
                                 const uint32_t* tok, const float* u, int32_t B, int32_t k,
                                 int32_t V, float temperature, int32_t* acc, uint32_t* bonus) {
+    velo::Range nvtx_range("velo.accept_device");
     velo::clear_last_error();
     if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
     int32_t st = check_accept_args(B, k, V, temperature, tgt, drf, tok, u, acc, bonus);
@@ -289,6 +290,7 @@ int32_t velo_cuda_accept_device(velo_cuda_ctx* c, const float* tgt, const float*
 int32_t velo_cuda_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
                          const uint32_t* tok, const float* u, int32_t B, int32_t k, int32_t V,
                          float temperature, int32_t* acc, uint32_t* bonus) {
+    velo::Range nvtx_range("velo.accept");
     velo::clear_last_error();
     if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
     int32_t st = check_accept_args(B, k, V, temperature, tgt, drf, tok, u, acc, bonus);

@@ -7,9 +7,20 @@
 #include <cstdint>
 #include <string>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "velo_cuda.h"
 
 namespace velo {
+
+// NVTX range over a scope (header-only NVTX v3: a no-op unless a profiler
+// is attached), so a timeline shows each C ABI call and its phases.
+struct Range {
+    explicit Range(const char* name) { nvtxRangePushA(name); }
+    ~Range() { nvtxRangePop(); }
+    Range(const Range&) = delete;
+    Range& operator=(const Range&) = delete;
+};
 
 // Thread-local last-error message (velo_cuda_last_error).
 void set_last_error(const char* fmt, ...);

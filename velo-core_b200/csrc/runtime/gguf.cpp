@@ -426,6 +426,7 @@ void fill_value(const velo::GgufValue& v, velo_gguf_value* out) {
 extern "C" {
 
 int32_t velo_gguf_open(const char* path, velo_gguf** out) {
+    velo::Range nvtx_range("velo.gguf_open");
     velo::clear_last_error();
     if (!out) return fail(VELO_ERR_INVALID_ARGUMENT, "out is NULL");
     *out = nullptr;

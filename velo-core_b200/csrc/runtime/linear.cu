@@ -29,6 +29,7 @@ int32_t velo_cuda_q4_0_repack(velo_cuda_ctx* c, const void* src, const void* src
 
 int32_t velo_cuda_gemm_q4_0(velo_cuda_ctx* c, const void* w, const void* x, int32_t M, int32_t N,
                             int32_t K, void* y, int32_t ldy, int32_t mode) {
+    velo::Range nvtx_range("velo.gemm_q4_0");
     velo::clear_last_error();
     if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
     if (M < 0 || N <= 0 || K <= 0 || K % 32)

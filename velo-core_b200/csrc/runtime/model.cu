@@ -528,6 +528,7 @@ extern "C" {
 
 int32_t velo_cuda_load_model(velo_cuda_ctx* c, const velo_model_desc* d, const velo_weight_desc* w,
                              int32_t n) {
+    velo::Range nvtx_range("velo.load_model");
     velo::clear_last_error();
     if (!c || !d || (n > 0 && !w)) return fail(VELO_ERR_INVALID_ARGUMENT, "NULL argument");
     if (d->struct_size != 0 && d->struct_size != sizeof(velo_model_desc))
@@ -761,6 +762,7 @@ int32_t velo_cuda_free_pages(velo_cuda_ctx* c, size_t* out) {
 
 int32_t velo_cuda_write_kv(velo_cuda_ctx* c, uint32_t slot, int32_t layer, int32_t pos0, int32_t n,
                            const void* k, const void* v) {
+    velo::Range nvtx_range("velo.write_kv");
     velo::clear_last_error();
     int32_t st = velo::check_model(c);
     if (st) return st;
@@ -873,6 +875,7 @@ int32_t velo_cuda_read_kv(velo_cuda_ctx* c, uint32_t slot, int32_t layer, int32_
 }
 
 int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, velo_verify_result* out) {
+    velo::Range nvtx_range("velo.verify_step");
     velo::clear_last_error();
     int32_t st = velo::check_model(c);
     if (st) return st;
@@ -1016,6 +1019,7 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         if (st) return st;
     }
     // acceptance
+    velo::Range accept_range("velo.verify_step.accept_commit");
     if (m->tp > 1 && (!sampling || N == 1)) {
         // vocabulary-sharded greedy: per-shard maxima, gathered, combined
         const velo::NcclApi* nc = velo::nccl_api();
