@@ -10,7 +10,7 @@ import synthetic
 import velo_cuda
 import vo
 from speculative import (CudaBatchDraft, CudaBatchTarget, CudaDraft, CudaTarget, NextTokenPrediction,
-                         SpeculativeDecoder, SpeculativeEngine, VerifyStep)
+                         SpeculativeDecoder, SpeculativeEngine, VerifyStep, native_generate)
 
 pytestmark = pytest.mark.gpu
 
@@ -147,3 +147,34 @@ def test_batched_engine_matches_per_request_device_models():
         assert len(o.tokens) == m
         assert o.tokens == r.tokens
         assert o.stats == r.stats
+
+
+def test_native_session_drives_device_models():
+    """The native session loop (velo_spec_generate) over the device models
+    gives the tokens and statistics of the Python session loop over them."""
+    V = 256
+    meta, target_w = synthetic.llama_q4_model(V, 256, 2, 2, 1, 512, seed=61, sigma=0.05)
+    _, draft_w = synthetic.llama_q4_model(V, 256, 1, 2, 1, 512, seed=61, sigma=0.05)
+    dmeta = dict(meta, n_layer=1)
+    prompt = [int(t) for t in synthetic.rng(62, 91).integers(0, V, 16)]
+
+    def run(native):
+        tctx = velo_cuda.Context(device=0, total_pages=8, max_slots=1, max_pages_per_slot=8)
+        dctx = velo_cuda.Context(device=0, total_pages=8, max_slots=1, max_pages_per_slot=8)
+        try:
+            tctx.load_model(meta, target_w)
+            dctx.load_model(dmeta, draft_w)
+            tctx.slot_allocate(0, 128)
+            dctx.slot_allocate(0, 128)
+            d, t = CudaDraft(dctx, 0, V), CudaTarget(tctx, 0, V)
+            if native:
+                return native_generate(4, d, t, prompt, 30)
+            return SpeculativeDecoder(4).generate(d, t, prompt, 30)
+        finally:
+            tctx.close()
+            dctx.close()
+
+    ref, out = run(False), run(True)
+    assert len(out.tokens) == 30
+    assert out.tokens == ref.tokens
+    assert out.stats == ref.stats

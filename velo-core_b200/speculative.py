@@ -15,6 +15,8 @@ driving device models through the TargetModel / DraftModel shape
 
 The session logic itself is plain Python; every model call is the C ABI.
 """
+import ctypes
+import re
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -558,3 +560,148 @@ class CudaBatchDraft:
                 last[j] = int(r["bonus"][b])
                 out[j].append(NextTokenPrediction(last[j]))
         return out
+
+
+# ---------------------------------------------------------------- native session
+def _native_error(status, errors):
+    """The SpeculativeError (or the model's own exception) for a status of the
+    native session (include/velo_session.h)."""
+    if errors:
+        return errors[0]
+    msg = velo_cuda.last_error()
+    if status == velo_cuda.ERR_EMPTY_DRAFT_WINDOW:
+        return EmptyDraftWindow()
+    if status == velo_cuda.ERR_DRAFT_TOO_MANY:
+        m = re.search(r"returned (\d+) tokens, requested at most (\d+)", msg)
+        return DraftReturnedTooMany(int(m.group(2)), int(m.group(1)))
+    if status == velo_cuda.ERR_TARGET_WRONG_LENGTH:
+        m = re.search(r"returned (\d+) verification steps for (\d+) drafted", msg)
+        return TargetReturnedWrongLength(int(m.group(2)), int(m.group(1)))
+    return velo_cuda.VeloError(status, msg)
+
+
+def _callbacks(draft_model, target_model, errors):
+    """ctypes callbacks over Python DraftModel / TargetModel objects; an
+    exception is kept in `errors` and reported as a model failure."""
+
+    @velo_cuda.DRAFT_FN
+    def draft_fn(_user, ctx, n, max_tokens, out, cap, n_out):
+        try:
+            preds = draft_model.draft([ctx[i] for i in range(n)], max_tokens)
+            for i, p in enumerate(preds[:cap]):
+                out[i] = int(p.token)
+            n_out[0] = len(preds)
+            return 0
+        except Exception as e:  # noqa: BLE001 -- handed back to the caller
+            errors.append(e)
+            return velo_cuda.ERR_INVALID_ARGUMENT
+
+    @velo_cuda.VERIFY_FN
+    def verify_fn(_user, ctx, n, drafted, k, out, cap, n_out):
+        try:
+            steps = target_model.verify([ctx[i] for i in range(n)], [drafted[i] for i in range(k)])
+            for i, st in enumerate(steps[:cap]):
+                out[i] = int(st.expected)
+            n_out[0] = len(steps)
+            return 0
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+            return velo_cuda.ERR_INVALID_ARGUMENT
+
+    return draft_fn, verify_fn
+
+
+def _stats(s):
+    return SpeculativeStats(s.draft_calls, s.target_calls, s.drafted_tokens, s.accepted_tokens,
+                            s.rejected_tokens)
+
+
+def native_generate(draft_window, draft_model, target_model, prompt, max_new_tokens, max_window=None):
+    """SpeculativeDecoder::generate through the native loop (velo_spec_generate)."""
+    errors = []
+    dfn, vfn = _callbacks(draft_model, target_model, errors)
+    p = np.ascontiguousarray(prompt, np.uint32)
+    out = np.zeros(max(int(max_new_tokens), 1), np.uint32)
+    n = ctypes.c_size_t()
+    st = velo_cuda.SpecStats()
+    rc = velo_cuda.lib().velo_spec_generate(draft_window, max_window or 0, dfn, None, vfn, None,
+                                            p.ctypes.data_as(ctypes.c_void_p), p.size, max_new_tokens,
+                                            out.ctypes.data_as(ctypes.c_void_p), out.size, ctypes.byref(n),
+                                            ctypes.byref(st))
+    if rc:
+        raise _native_error(rc, errors)
+    return SpeculativeOutput([int(t) for t in out[:n.value]], _stats(st))
+
+
+class NativeSession:
+    """SpeculativeSession over the native session (velo_spec_session_*)."""
+
+    def __init__(self, draft_window, prompt, max_window=None):
+        self._h = None
+        p = np.ascontiguousarray(prompt, np.uint32)
+        h = ctypes.c_void_p()
+        rc = velo_cuda.lib().velo_spec_session_create(draft_window, max_window or 0,
+                                                      p.ctypes.data_as(ctypes.c_void_p), p.size, ctypes.byref(h))
+        if rc:
+            raise _native_error(rc, [])
+        self._h = h
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            velo_cuda.lib().velo_spec_session_destroy(self._h)
+            self._h = None
+
+    def _accepted(self, call, cap):
+        out = np.zeros(max(cap, 1), np.uint32)
+        n = ctypes.c_size_t()
+        rc = call(out.ctypes.data_as(ctypes.c_void_p), out.size, ctypes.byref(n))
+        return rc, [int(t) for t in out[:n.value]] if not rc else []
+
+    def draft(self, draft_model, target_model, max_new_tokens):
+        errors = []
+        dfn, vfn = _callbacks(draft_model, target_model, errors)
+        rc, acc = self._accepted(lambda o, c, n: velo_cuda.lib().velo_spec_session_draft(
+            self._h, dfn, None, vfn, None, max_new_tokens, o, c, n), max_new_tokens)
+        if rc:
+            raise _native_error(rc, errors)
+        return acc
+
+    def commit(self, drafted, verified):
+        d = np.ascontiguousarray([p.token for p in drafted], np.uint32)
+        v = np.ascontiguousarray([s.expected for s in verified], np.uint32)
+        rc, acc = self._accepted(lambda o, c, n: velo_cuda.lib().velo_spec_session_commit(
+            self._h, d.ctypes.data_as(ctypes.c_void_p), d.size, v.ctypes.data_as(ctypes.c_void_p), v.size,
+            o, c, n), len(drafted))
+        if rc:
+            raise _native_error(rc, [])
+        return acc
+
+    def has_pending_rejection(self):
+        return bool(velo_cuda.lib().velo_spec_session_has_pending_rejection(self._h))
+
+    def take_rejected_token(self):
+        t = ctypes.c_uint32()
+        return int(t.value) if velo_cuda.lib().velo_spec_session_take_rejected(self._h, ctypes.byref(t)) else None
+
+    @property
+    def context(self):
+        n = velo_cuda.lib().velo_spec_session_context(self._h, None, 0)
+        out = np.zeros(max(n, 1), np.uint32)
+        velo_cuda.lib().velo_spec_session_context(self._h, out.ctypes.data_as(ctypes.c_void_p), n)
+        return [int(t) for t in out[:n]]
+
+    @property
+    def draft_window(self):
+        return velo_cuda.lib().velo_spec_session_window(self._h)
+
+    @property
+    def stats(self):
+        s = velo_cuda.SpecStats()
+        velo_cuda.lib().velo_spec_session_stats(self._h, ctypes.byref(s))
+        return _stats(s)
+
+    def record_draft_call(self):
+        velo_cuda.lib().velo_spec_session_record_draft_call(self._h)
+
+    def record_target_call(self):
+        velo_cuda.lib().velo_spec_session_record_target_call(self._h)

@@ -43,6 +43,18 @@ KV_F16, KV_INT8, KV_F32 = 0, 1, 2  # KV_F32: the fp32 path of the model
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
 _SZ = ctypes.c_size_t
+_U32P = ctypes.POINTER(ctypes.c_uint32)
+_SZP = ctypes.POINTER(ctypes.c_size_t)
+# velo_session.h model callbacks
+DRAFT_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, _U32P, ctypes.c_size_t, ctypes.c_size_t, _U32P,
+                            ctypes.c_size_t, _SZP)
+VERIFY_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, _U32P, ctypes.c_size_t, _U32P, ctypes.c_size_t,
+                             _U32P, ctypes.c_size_t, _SZP)
+
+
+class SpecStats(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint64) for n in
+                ("draft_calls", "target_calls", "drafted_tokens", "accepted_tokens", "rejected_tokens")]
 _lib = None
 
 
@@ -110,6 +122,19 @@ _SIGS = {
     "velo_gguf_validate": (_I32, [_P]),
     "velo_gguf_weights": (_I32, [_P, _P, _I32, ctypes.POINTER(_I32)]),
     "velo_cuda_load_gguf": (_I32, [_P, ctypes.c_char_p]),
+    "velo_spec_session_create": (_I32, [ctypes.c_uint32, ctypes.c_uint32, _P, _SZ, ctypes.POINTER(_P)]),
+    "velo_spec_session_destroy": (None, [_P]),
+    "velo_spec_session_draft": (_I32, [_P, DRAFT_FN, _P, VERIFY_FN, _P, _SZ, _P, _SZ, _SZP]),
+    "velo_spec_session_commit": (_I32, [_P, _P, _SZ, _P, _SZ, _P, _SZ, _SZP]),
+    "velo_spec_session_take_rejected": (_I32, [_P, _U32P]),
+    "velo_spec_session_has_pending_rejection": (_I32, [_P]),
+    "velo_spec_session_context": (_SZ, [_P, _P, _SZ]),
+    "velo_spec_session_window": (ctypes.c_uint32, [_P]),
+    "velo_spec_session_stats": (None, [_P, ctypes.POINTER(SpecStats)]),
+    "velo_spec_session_record_draft_call": (None, [_P]),
+    "velo_spec_session_record_target_call": (None, [_P]),
+    "velo_spec_generate": (_I32, [ctypes.c_uint32, ctypes.c_uint32, DRAFT_FN, _P, VERIFY_FN, _P, _P, _SZ, _SZ,
+                                  _P, _SZ, _SZP, ctypes.POINTER(SpecStats)]),
 }
 
 DT_F32, DT_F16, DT_Q4_0 = 0, 1, 2
@@ -159,10 +184,11 @@ def lib():
 
 
 def header_functions():
-    """Names of the functions include/velo_cuda.h declares."""
-    src = open(HEADER).read()
+    """Names of the functions include/*.h declare."""
+    inc = os.path.dirname(HEADER)
+    src = "".join(open(os.path.join(inc, f)).read() for f in sorted(os.listdir(inc)) if f.endswith(".h"))
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(velo_(?:cuda|page_allocator|gguf)_\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(velo_(?:cuda|page_allocator|gguf|spec)_\w+)\s*\(", src)))
 
 
 def last_error():
