@@ -397,7 +397,7 @@ int32_t gguf_validate(const GgufFile& g, const GgufModelMeta& m) {
 
 struct velo_gguf {
     velo::GgufFile file;
-    std::vector<std::string> names;  // storage for velo_gguf_weights' names
+    mutable std::vector<std::string> names;  // storage for velo_gguf_weights' names (a cache)
 };
 
 using velo::fail;
@@ -521,10 +521,9 @@ int32_t velo_gguf_validate(const velo_gguf* g) {
     return st;
 }
 
-int32_t velo_gguf_weights(const velo_gguf* gc, velo_weight_desc* out, int32_t cap, int32_t* n) {
+int32_t velo_gguf_weights(const velo_gguf* g, velo_weight_desc* out, int32_t cap, int32_t* n) {
     velo::clear_last_error();
-    if (!gc || !n) return fail(VELO_ERR_INVALID_ARGUMENT, "NULL argument");
-    velo_gguf* g = const_cast<velo_gguf*>(gc);  // the name storage only
+    if (!g || !n) return fail(VELO_ERR_INVALID_ARGUMENT, "NULL argument");
     velo::GgufModelMeta m;
     int32_t st = velo::gguf_model_meta(g->file, m);
     if (!st) st = velo::gguf_validate(g->file, m);
