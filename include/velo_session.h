@@ -74,6 +74,34 @@ VELO_API int32_t velo_spec_generate(uint32_t draft_window, uint32_t max_window, 
                                     const uint32_t *prompt, size_t n_prompt, size_t max_new_tokens, uint32_t *out,
                                     size_t cap, size_t *n_out, velo_spec_stats *stats);
 
+/* DraftModel::draft_batch for n requests: request i has id ids[i], context
+ * contexts[i] (n_context[i] tokens) and may take up to max_tokens[i] tokens,
+ * written at out + i * out_stride (out_stride >= every max_tokens[i]) with
+ * the count in n_out[i]. */
+typedef int32_t (*velo_draft_batch_fn)(void *user, size_t n, const uint32_t *ids, const uint32_t *const *contexts,
+                                       const size_t *n_context, const size_t *max_tokens, uint32_t *out,
+                                       size_t out_stride, size_t *n_out);
+/* TargetModel::verify_batch for n requests: expected tokens of request i at
+ * out + i * out_stride, count in n_out[i]. */
+typedef int32_t (*velo_verify_batch_fn)(void *user, size_t n, const uint32_t *ids, const uint32_t *const *contexts,
+                                        const size_t *n_context, const uint32_t *const *drafted,
+                                        const size_t *n_drafted, uint32_t *out, size_t out_stride, size_t *n_out);
+
+/* VeloEngine::generate_batch (src/engine.rs:233-420): every round, each
+ * request short of max_new_tokens[i] drafts min(remaining, draft_window)
+ * tokens (the decoder's fixed window), one verify_batch call covers all of
+ * them, each session commits and emits the target's token at a rejection.
+ * Request i has id i (its slot); more than max_slots requests (0: no limit)
+ * is VELO_ERR_INVALID_ARGUMENT, as the engine's SlotPool running dry.  A
+ * round without progress ends the loop.  A draft count above max_tokens[i]
+ * is DraftReturnedTooMany here (the reference engine would verify the
+ * surplus).  out[i] needs room for max_new_tokens[i]; stats (or NULL) is [n]. */
+VELO_API int32_t velo_spec_generate_batch(uint32_t draft_window, uint32_t max_window, size_t max_slots,
+                                          velo_draft_batch_fn draft, void *draft_user, velo_verify_batch_fn verify,
+                                          void *verify_user, size_t n, const uint32_t *const *prompts,
+                                          const size_t *n_prompt, const size_t *max_new_tokens,
+                                          uint32_t *const *out, size_t *n_out, velo_spec_stats *stats);
+
 #ifdef __cplusplus
 }
 #endif

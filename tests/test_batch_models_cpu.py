@@ -95,3 +95,17 @@ def test_native_session_over_device_model_classes():
                     else SpeculativeDecoder(4).generate(d, t, prompt, 20))
     assert len(runs[1].tokens) == 20
     assert runs[1].tokens == runs[0].tokens and runs[1].stats == runs[0].stats
+
+
+def test_native_engine_over_batched_model_classes():
+    from speculative import native_generate_batch
+    meta, target_w, dmeta, draft_w = _models()
+    g = synthetic.rng(53, 91)
+    requests = [(list(g.integers(0, V, n)), m) for n, m in ((9, 10), (20, 7))]
+    ref = SpeculativeEngine(3, max_slots=2).generate_batch(
+        CudaBatchDraft(OracleContext(dmeta, draft_w, 2), [0, 1], V),
+        CudaBatchTarget(OracleContext(meta, target_w, 2), [0, 1], V), requests)
+    out = native_generate_batch(3, CudaBatchDraft(OracleContext(dmeta, draft_w, 2), [0, 1], V),
+                                CudaBatchTarget(OracleContext(meta, target_w, 2), [0, 1], V), requests,
+                                max_slots=2)
+    assert [(o.tokens, o.stats) for o in out] == [(r.tokens, r.stats) for r in ref]

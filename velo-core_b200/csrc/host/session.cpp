@@ -188,4 +188,88 @@ int32_t velo_spec_generate(uint32_t draft_window, uint32_t max_window, velo_draf
     return VELO_OK;
 }
 
+int32_t velo_spec_generate_batch(uint32_t draft_window, uint32_t max_window, size_t max_slots,
+                                 velo_draft_batch_fn draft, void* draft_user, velo_verify_batch_fn verify,
+                                 void* verify_user, size_t n, const uint32_t* const* prompts, const size_t* n_prompt,
+                                 const size_t* max_new_tokens, uint32_t* const* out, size_t* n_out,
+                                 velo_spec_stats* stats) {
+    velo::clear_last_error();
+    if (!draft || !verify || (n && (!prompts || !n_prompt || !max_new_tokens || !out || !n_out)))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (max_slots && n > max_slots)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "no free slot: %zu requests, %zu slots", n, max_slots);
+    std::vector<velo_spec_session*> sess(n, nullptr);
+    auto cleanup = [&](int32_t st) {
+        for (size_t i = 0; i < n; ++i) {
+            if (stats && sess[i]) stats[i] = sess[i]->stats;
+            delete sess[i];
+        }
+        return st;
+    };
+    for (size_t i = 0; i < n; ++i) {
+        const int32_t st = velo_spec_session_create(draft_window, max_window, prompts[i], n_prompt[i], &sess[i]);
+        if (st) return cleanup(st);
+    }
+    std::vector<std::vector<uint32_t>> gen(n);
+    const size_t window = draft_window;  // the engine drafts with the decoder's window
+    for (;;) {
+        std::vector<uint32_t> ids;
+        for (size_t i = 0; i < n; ++i)
+            if (gen[i].size() < max_new_tokens[i]) ids.push_back((uint32_t)i);
+        if (ids.empty()) break;
+        const size_t a = ids.size();
+        std::vector<const uint32_t*> ctx(a);
+        std::vector<size_t> nctx(a), want(a), nd(a, 0);
+        for (size_t j = 0; j < a; ++j) {
+            velo_spec_session* s = sess[ids[j]];
+            ctx[j] = s->context.data();
+            nctx[j] = s->context.size();
+            want[j] = std::min(max_new_tokens[ids[j]] - gen[ids[j]].size(), window);
+        }
+        std::vector<uint32_t> drafted(a * window);
+        int32_t st = draft(draft_user, a, ids.data(), ctx.data(), nctx.data(), want.data(), drafted.data(), window,
+                           nd.data());
+        if (st) return cleanup(fail(st, "draft model failed (status %d)", st));
+        for (size_t j = 0; j < a; ++j) {
+            sess[ids[j]]->stats.draft_calls += 1;
+            if (nd[j] > want[j])
+                return cleanup(fail(VELO_ERR_DRAFT_TOO_MANY, "draft model returned %zu tokens, requested at most %zu",
+                                    nd[j], want[j]));
+        }
+        std::vector<const uint32_t*> dp(a);
+        for (size_t j = 0; j < a; ++j) dp[j] = drafted.data() + j * window;
+        std::vector<uint32_t> expected(a * window);
+        std::vector<size_t> nv(a, 0);
+        st = verify(verify_user, a, ids.data(), ctx.data(), nctx.data(), dp.data(), nd.data(), expected.data(), window,
+                    nv.data());
+        if (st) return cleanup(fail(st, "target model failed (status %d)", st));
+        bool progressed = false;
+        std::vector<uint32_t> acc;
+        for (size_t j = 0; j < a; ++j) {
+            velo_spec_session* s = sess[ids[j]];
+            s->stats.target_calls += 1;
+            if (nv[j] != nd[j])
+                return cleanup(fail(VELO_ERR_TARGET_WRONG_LENGTH,
+                                    "target model returned %zu verification steps for %zu drafted tokens", nv[j],
+                                    nd[j]));
+            s->stats.drafted_tokens += nd[j];
+            accept(s, dp[j], nd[j], expected.data() + j * window, &acc);
+            auto& g = gen[ids[j]];
+            g.insert(g.end(), acc.begin(), acc.end());
+            progressed |= !acc.empty();
+            if (s->pending) {
+                s->pending = false;
+                g.push_back(s->rejected);
+                progressed = true;
+            }
+        }
+        if (!progressed) break;
+    }
+    for (size_t i = 0; i < n; ++i) {
+        n_out[i] = gen[i].size();
+        std::copy(gen[i].begin(), gen[i].end(), out[i]);
+    }
+    return cleanup(VELO_OK);
+}
+
 }  // extern "C"

@@ -705,3 +705,56 @@ class NativeSession:
 
     def record_target_call(self):
         velo_cuda.lib().velo_spec_session_record_target_call(self._h)
+
+
+def native_generate_batch(draft_window, draft_model, target_model, requests, max_window=None, max_slots=None):
+    """SpeculativeEngine.generate_batch through the native engine loop
+    (velo_spec_generate_batch); the models' draft_batch / verify_batch (or
+    their one-request methods) are the callbacks."""
+    errors = []
+
+    @velo_cuda.DRAFT_BATCH_FN
+    def draft_fn(_user, n, ids, ctxs, nctx, want, out, stride, n_out):
+        try:
+            reqs = [(ids[j], [ctxs[j][i] for i in range(nctx[j])], want[j]) for j in range(n)]
+            for j, preds in enumerate(_draft_batch(draft_model, reqs)):
+                for i, p in enumerate(preds[:stride]):
+                    out[j * stride + i] = int(p.token)
+                n_out[j] = len(preds)
+            return 0
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+            return velo_cuda.ERR_INVALID_ARGUMENT
+
+    @velo_cuda.VERIFY_BATCH_FN
+    def verify_fn(_user, n, ids, ctxs, nctx, drafted, nd, out, stride, n_out):
+        try:
+            reqs = [(ids[j], [ctxs[j][i] for i in range(nctx[j])], [drafted[j][i] for i in range(nd[j])])
+                    for j in range(n)]
+            for j, steps in enumerate(_verify_batch(target_model, reqs)):
+                for i, st in enumerate(steps[:stride]):
+                    out[j * stride + i] = int(st.expected)
+                n_out[j] = len(steps)
+            return 0
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+            return velo_cuda.ERR_INVALID_ARGUMENT
+
+    n = len(requests)
+    prompts = [np.ascontiguousarray(p, np.uint32) for p, _ in requests]
+    limits = np.array([int(m) for _, m in requests], np.uintp)
+    outs = [np.zeros(max(int(m), 1), np.uint32) for _, m in requests]
+    pp = (ctypes.c_void_p * max(n, 1))(*[p.ctypes.data for p in prompts])
+    op = (ctypes.c_void_p * max(n, 1))(*[o.ctypes.data for o in outs])
+    npr = np.array([p.size for p in prompts], np.uintp)
+    n_out = np.zeros(max(n, 1), np.uintp)
+    stats = (velo_cuda.SpecStats * max(n, 1))()
+    rc = velo_cuda.lib().velo_spec_generate_batch(
+        draft_window, max_window or 0, max_slots or 0, draft_fn, None, verify_fn, None, n, pp,
+        npr.ctypes.data_as(ctypes.c_void_p), limits.ctypes.data_as(ctypes.c_void_p), op,
+        n_out.ctypes.data_as(ctypes.c_void_p), stats)
+    if rc:
+        if rc == velo_cuda.ERR_INVALID_ARGUMENT and "no free slot" in velo_cuda.last_error() and not errors:
+            raise SlotsExhausted(n, max_slots)
+        raise _native_error(rc, errors)
+    return [SpeculativeOutput([int(t) for t in outs[i][:n_out[i]]], _stats(stats[i])) for i in range(n)]

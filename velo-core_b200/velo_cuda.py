@@ -52,6 +52,13 @@ VERIFY_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, _U32P, ctypes.c_si
                              _U32P, ctypes.c_size_t, _SZP)
 
 
+_U32PP = ctypes.POINTER(_U32P)
+DRAFT_BATCH_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t, _U32P, _U32PP, _SZP, _SZP,
+                                  _U32P, ctypes.c_size_t, _SZP)
+VERIFY_BATCH_FN = ctypes.CFUNCTYPE(ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t, _U32P, _U32PP, _SZP, _U32PP,
+                                   _SZP, _U32P, ctypes.c_size_t, _SZP)
+
+
 class SpecStats(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint64) for n in
                 ("draft_calls", "target_calls", "drafted_tokens", "accepted_tokens", "rejected_tokens")]
@@ -133,6 +140,8 @@ _SIGS = {
     "velo_spec_session_stats": (None, [_P, ctypes.POINTER(SpecStats)]),
     "velo_spec_session_record_draft_call": (None, [_P]),
     "velo_spec_session_record_target_call": (None, [_P]),
+    "velo_spec_generate_batch": (_I32, [ctypes.c_uint32, ctypes.c_uint32, _SZ, DRAFT_BATCH_FN, _P,
+                                        VERIFY_BATCH_FN, _P, _SZ, _P, _P, _P, _P, _P, _P]),
     "velo_spec_generate": (_I32, [ctypes.c_uint32, ctypes.c_uint32, DRAFT_FN, _P, VERIFY_FN, _P, _P, _SZ, _SZ,
                                   _P, _SZ, _SZP, ctypes.POINTER(SpecStats)]),
 }
