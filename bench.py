@@ -1,26 +1,30 @@
 """Verify-step benchmark (driver contract: one JSON line from rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
-                    [--workload accept]
+                    [--workload verify|accept|q4gemm|attn|c1] [--case c5|c3]
 
-Default workload: BASELINE config 2, the acceptance microbench (B=64 sequences,
-k=8 draft tokens, V=32000, fp32 logits, T=0.8, target ~ N(0,2^2), draft =
-target + N(0,0.5^2)).  A step is one fused acceptance launch over one batch:
-vocabulary softmax statistics for the 9 target and 8 draft rows of every
-sequence, accept/reject, and the residual / bonus draw.  Inputs are resident in
-HBM; two input sets (2 x 139 MB > 126 MB L2) alternate so no step reads a
-cache warmed by the previous one.
+Default workload: the north-star path, BASELINE config 5 -- one speculative
+verify step of a Llama-3-70B-shape q4_0 target (80 layers, hidden 8192, GQA
+64/8, FFN 28672, vocab 128256) over B=64 sequences with a 32-node draft tree
+each and 4096 tokens of context in 16-token fp16 KV pages: the target forward
+over all 2048 tree nodes, greedy tree acceptance and the KV commit of the
+accepted paths, through velo_cuda_verify_step.  Under torchrun the N ranks are
+one tensor-parallel group over the same batch ("scaling": "strong").
 
-value  = accepted tokens/s over all ranks = sum_b (accepted_len_b + 1) per
-         step / device time (CUDA events, max over ranks);
-e2e    = the same metric through the host-buffer C ABI call velo_cuda_accept
-         (pinned host inputs copied in, results copied back, every step);
-roofline: algorithmic bytes (every logit read once) / kernel time vs the
-         measured HBM copy bandwidth;
-cpu_baseline: the CPU port of the same step (oracle/) on this host's cores.
+value  = accepted tokens/s = sum_b (accepted_len_b + 1) per step / device time
+         of the step (CUDA events on the context stream, max over ranks);
+e2e    = the same metric through the host-buffer C ABI call (inputs copied
+         from pinned memory, results copied back, every step), wall clock;
+roofline: the dominant kernel (the w1/w3 SwiGLU q4_0 GEMM) -- its algorithmic
+         FLOPs per launch over its measured duration inside the step, against
+         the measured sustained bf16 peak -- plus the whole step against its
+         floor (GEMM FLOPs at peak + KV bytes at HBM bandwidth);
+cpu_baseline: the CPU port of llama_cpu.rs (oracle/) timed on this host at
+         N=1 and extrapolated to the step.
 
-Multi-GPU: one process per GPU (torchrun), each rank runs its own batch (data
-parallel over sequences, no collective on the data path): "scaling": "weak".
+--workload accept is BASELINE config 2 (the acceptance microbench; replicas
+under torchrun, "scaling": "weak"); q4gemm / attn / c1 time single kernels or
+config 1.
 """
 import argparse
 import json
@@ -329,6 +333,119 @@ def run_cuda(args):
     return 0
 
 
+# ---------------------------------------------------------------- tree acceptance
+TREE_C3 = [-1, 0, 0, 0, 0, 1, 1, 2, 2, 3, 3, 4, 4, 5, 5, 6]
+
+
+def tree_walk_rows(par, plen, path):
+    """Vocabulary rows the tree walk reads per sequence (the spec's passes):
+    per visited node its target row, plus its draft row when it has
+    children; two rows per rejected child (the residual pass); one more row
+    pass for the draw when the final distribution is p (leaf, or no
+    rejection)."""
+    rows = 0
+    N = len(par)
+    for i in range(plen):
+        v = path[i]
+        kids = [c for c in range(N) if par[c] == v]
+        rows += 1 + (1 if kids else 0)
+        nxt = path[i + 1] if i + 1 < plen else None
+        rej = sum(1 for c in kids if nxt is None or c < nxt)
+        rows += 2 * rej
+        if nxt is None and rej == 0:
+            rows += 1
+    return rows
+
+
+def run_accept_tree(args):
+    """Rejection sampling over config-3-shaped draft trees (16 nodes,
+    branching 4,2,2 breadth-first), B=64, V=32000, T=0.8, target ~ N(0,2^2),
+    draft = target + N(0,0.5^2), children drawn from their parent's draft
+    distribution: one velo_cuda_accept_tree_device launch per step."""
+    import torch
+    import velo_cuda
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    B, V, T = 64, 32000, 0.8
+    N = len(TREE_C3)
+    par = np.tile(np.array(TREE_C3, np.int32), (B, 1))
+    sets = []
+    for sidx in range(2):  # two input sets of 2 x 64 x 16 x 32000 x 4 B = 262 MB (> L2)
+        g = np.random.Generator(np.random.Philox(key=100 + sidx))
+        tgt = g.normal(0, 2.0, (B, N, V)).astype(np.float32)
+        drf = (tgt[:, :N - 1] + g.normal(0, 0.5, (B, N - 1, V))).astype(np.float32)
+        tok = np.zeros((B, N), np.uint32)
+        import synthetic
+        for b in range(B):
+            c = np.cumsum(synthetic.softmax64(drf[b] / T), axis=-1)
+            for n in range(1, N):
+                tok[b, n] = min(int((c[par[b, n]] < g.random()).sum()), V - 1)
+        u = g.random((B, N)).astype(np.float32)
+        sets.append((tgt, drf, tok, u))
+    ctx = velo_cuda.Context(device=0)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream.cuda_stream)
+    dsets = [tuple(torch.from_numpy(np.ascontiguousarray(a)).to(dev) for a in
+                   (t, d, k.view(np.int32), u)) for t, d, k, u in sets]
+    dpar = torch.from_numpy(par).to(dev)
+    path = torch.empty((B, N), dtype=torch.int32, device=dev)
+    plen = torch.empty(B, dtype=torch.int32, device=dev)
+    bonus = torch.empty(B, dtype=torch.int32, device=dev)
+    torch.cuda.synchronize()
+
+    def step(i):
+        t, d, k, u = dsets[i % 2]
+        ctx.accept_tree_device(t, d, k, dpar, u, T, path, plen, bonus)
+
+    toks, rows = [], []
+    for i in range(2):
+        step(i)
+        torch.cuda.synchronize()
+        pl, pa = plen.cpu().numpy(), path.cpu().numpy()
+        toks.append(int(pl.sum()))  # accepted nodes + bonus = path_len per sequence
+        rows.append(sum(tree_walk_rows(par[b], int(pl[b]), pa[b]) for b in range(B)))
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ctx.sync()
+    ms = e0.elapsed_time(e1) / args.steps
+    tok_step = sum(toks[i % 2] for i in range(args.steps)) / args.steps
+    row_step = sum(rows[i % 2] for i in range(args.steps)) / args.steps
+    alg = row_step * V * 4
+    hbm, peak_kind = load_peaks()
+    ctx.set_stream(None)
+    e2e_steps = max(3, min(args.steps, 50))
+    w0 = time.perf_counter()
+    for i in range(e2e_steps):
+        t, d, k, u = sets[i % 2]
+        ctx.accept_tree(t, d, k, par, u, T)
+    wall = time.perf_counter() - w0
+    line = {"workload": "rejection sampling over draft trees: B=64 config-3 trees (16 nodes, "
+                        "branching 4,2,2), V=32000, T=0.8 (velo_cuda_accept_tree_device)",
+            "metric": BASELINE_METRIC, "value": tok_step / (ms / 1e3), "unit": "accepted tokens/s",
+            "us_per_step": ms * 1e3, "accepted_per_step": tok_step,
+            "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": hbm,
+                         "unit": "GB/s", "frac": alg / (ms * 1e-3) / 1e9 / hbm, "peak_kind": peak_kind,
+                         "algorithmic_bytes": alg,
+                         "note": "bytes of the vocabulary rows the walk must read (stats, residual and "
+                                 "draw passes); the walk is sequential per sequence, one CTA each"},
+            "e2e": {"value": sum(toks[i % 2] for i in range(e2e_steps)) / wall, "unit": "accepted tokens/s",
+                    "h2d_bytes_per_step": sum(a.nbytes for a in sets[0]) + par.nbytes,
+                    "d2h_bytes_per_step": (B * N + 2 * B) * 4},
+            "clocks": clk.summary()}
+    ctx.close()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ---------------------------------------------------------------- q4_0 GEMM workload
 Q4_SHAPES_C3 = [  # (name, N, K, mode) of one Llama-2-7B layer + LM head at M = 32 x 16 nodes
     ("wqkv", 3 * 4096, 4096, 1), ("wo", 4096, 4096, 2), ("w1w3", 2 * 11008, 4096, 3),
@@ -626,25 +743,93 @@ def c3_model_tensors(meta, seed=0):
     return t
 
 
-def verify_cpu_token_seconds(meta, tensors, ctx_len):
-    """Seconds of one forward_one of the CPU port (oracle, one thread) at
-    position ctx_len - 1 of the config-3 model: matvecs of every layer plus
-    attention over ctx_len cached positions (zero K/V: same arithmetic)."""
-    import synthetic
+def host_q4(rows, cols, g, scale=0.0025):
+    """Random q4_0 bytes [rows][cols/32*18] made on the host without the GPU
+    (random nibbles, every block scale `scale`): the CPU port's timing does
+    not depend on the values, and generating 1.5 GB of normals would take
+    longer than timing it."""
+    nb = cols // 32
+    raw = np.frombuffer(g.bytes(rows * nb * 18), np.uint8).reshape(rows, nb, 18).copy()
+    raw[:, :, 0:2] = np.frombuffer(np.float16(scale).tobytes(), np.uint8)
+    return raw.reshape(rows, nb * 18)
+
+
+def cpu_sample_tensors(meta, n_layer, seed=0):
+    """Oracle tensor list of a model with the config's layer shapes but
+    `n_layer` layers (q4_0 matrices and embedding, f32 norms of 1)."""
+    g = np.random.Generator(np.random.Philox(key=seed + 77))
+    H, V, F = meta["n_embd"], meta["n_vocab"], meta["n_ff"]
+    Dq, Dk = meta["n_head"] * 128, meta["n_head_kv"] * 128
+    ones = np.ones(H, np.float32)
+    out = [(2, host_q4(V, H, g)), (0, ones), (2, host_q4(V, H, g))]
+    for _ in range(n_layer):
+        out += [(0, ones), (2, host_q4(Dq, H, g)), (2, host_q4(Dk, H, g)), (2, host_q4(Dk, H, g)),
+                (2, host_q4(H, Dq, g)), (0, ones), (2, host_q4(F, H, g)), (2, host_q4(H, F, g)),
+                (2, host_q4(F, H, g))]
+    return out
+
+
+def cpu_token_model(meta, ctx_len):
+    """forward_one of the CPU port (oracle restatement of llama_cpu.rs, one
+    thread) at position ctx_len - 1 (attention over ctx_len cached positions),
+    timed on 1- and 2-layer models of the config's shapes and extrapolated to
+    all n_layer layers: t = t1 + (n_layer - 1) * (t2 - t1).  Returns
+    (seconds per token over all layers, seconds of the 2-layer sample,
+    the 2-layer tensors)."""
     import vo
-    m = vo.Model(dict(meta, n_ctx=ctx_len), synthetic.oracle_tensor_list(meta, tensors))
-    t0 = time.perf_counter()
-    m.forward_one(1, ctx_len - 1)
-    return time.perf_counter() - t0
+    ts = {}
+    keep = None
+    for nl in (1, 2):
+        tl = cpu_sample_tensors(meta, nl)
+        m = vo.Model(dict(meta, n_layer=nl, n_ctx=ctx_len), tl)
+        m.forward_one(1, ctx_len - 1)  # page the weights in
+        t0 = time.perf_counter()
+        m.forward_one(1, ctx_len - 1)
+        ts[nl] = time.perf_counter() - t0
+        del m
+        if nl == 2:
+            keep = tl
+    per_layer = max(ts[2] - ts[1], 0.0)
+    return ts[1] + (meta["n_layer"] - 1) * per_layer, ts[2], keep
+
+
+def verify_case(case):
+    c5 = case != "c3"
+    meta = dict(C5_META if c5 else C3_META)
+    tree = C5_TREE if c5 else C3_TREE
+    B, ctx_len = (64, 4096) if c5 else (32, 2048)
+    wl = ("BASELINE config 5: Llama-3-70B-shape verify step in q4_0 (80 layers, hidden 8192, "
+          "64/8 heads, FFN 28672, vocab 128256), B=64 sequences, 32-node draft tree each "
+          "(branching 4,2,2,.. breadth-first), context 4096 in 16-token fp16 KV pages" if c5 else
+          "BASELINE config 3: Llama-2-7B-shape verify step in q4_0 (32 layers, hidden 4096, 32 heads, "
+          "FFN 11008, vocab 32000), B=32 sequences, 16-node draft tree each (branching 4,2,2 "
+          "breadth-first), context 2048 in 16-token fp16 KV pages")
+    return c5, meta, tree, B, ctx_len, wl
+
+
+def verify_counts(meta, B, N, ctx_len, tp):
+    """Per-step algorithmic work of the verify step on one rank of `tp`."""
+    H, F, V, L = meta["n_embd"], meta["n_ff"], meta["n_vocab"], meta["n_layer"]
+    Dq, Dk = meta["n_head"] * 128, meta["n_head_kv"] * 128
+    M = B * N
+    params = L * (H * (Dq + 2 * Dk) + Dq * H + 3 * H * F) + V * H
+    return dict(M=M, flops=2.0 * M * params / tp, params=params,
+                ffn_up_flops=2.0 * M * (2 * F // tp) * H,
+                kv_bytes=B * ctx_len * L * Dk * 2 * 2 / tp, w_bytes=params * 18 / 32 / tp)
 
 
 def run_verify(args):
-    """The whole verify step at BASELINE config 3: Llama-2-7B shape in q4_0,
-    B=32 sequences of context 2048 in 16-token fp16 pages, a 16-node draft
-    tree each: target forward over 512 rows, greedy tree acceptance and the KV
-    commit of the accepted paths, through velo_cuda_verify_step.  Under
-    torchrun the ranks form one tensor-parallel group (NCCL all-reduce after
-    o_proj / down_proj, vocabulary-sharded LM head): strong scaling."""
+    """The verify step (the north-star path) through velo_cuda_verify_step:
+    target forward over every draft-tree node of B sequences (q4_0 tcgen05
+    GEMMs, tree-masked paged attention over fp16 pages), greedy tree
+    acceptance (GreedySampler + find_best_path) and the KV commit of the
+    accepted paths.  Default: BASELINE config 5; --case c3 for config 3.
+    Under torchrun the ranks form one tensor-parallel group (column / row
+    split as sharding.rs, bf16 NCCL all-reduce after o_proj and down_proj,
+    vocabulary-sharded LM head): the job is the same batch at every N, so
+    "scaling" is "strong".  Inputs (weights, KV pages) are resident in HBM and
+    each step streams ~40 GB of weights and ~86 GB of KV (config 5), far more
+    than the 126 MB L2."""
     import torch
     import torch.distributed as dist
     import velo_cuda
@@ -657,12 +842,19 @@ def run_verify(args):
         box = [velo_cuda.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
         nid = box[0]
-    c5 = args.case == "c5"
-    meta = dict(C5_META if c5 else C3_META)
-    tree = C5_TREE if c5 else C3_TREE
-    B, ctx_len = (64, 4096) if c5 else (32, 2048)
+
+    def max_over_ranks(vals):
+        if ws == 1:
+            return list(vals)
+        t = torch.tensor(list(vals), dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(x) for x in t]
+
+    c5, meta, tree, B, ctx_len, wl = verify_case(args.case)
     N = len(tree)
     per_seq = (ctx_len + N + 15) // 16
+    cnt = verify_counts(meta, B, N, ctx_len, ws)
+    M = cnt["M"]
     t0 = time.time()
     tensors = c5_shard_tensors(meta, ws, rank) if c5 else c3_model_tensors(meta)
     torch.cuda.synchronize()
@@ -672,9 +864,6 @@ def run_verify(args):
     t0 = time.time()
     ctx.load_model(meta, tensors, shards=c5)
     load_s = time.time() - t0
-    cpu_token_s = None
-    if rank == 0 and not args.no_cpu_baseline and not c5:
-        cpu_token_s = verify_cpu_token_seconds(meta, tensors, ctx_len)
     del tensors
     torch.cuda.empty_cache()
     for b in range(B):
@@ -686,73 +875,185 @@ def run_verify(args):
     ctxl = np.full(B, ctx_len, np.int32)
     stream = torch.cuda.Stream()
     ctx.set_stream(stream.cuda_stream)
-    for _ in range(max(3, args.warmup)):
+
+    def step():
         r = ctx.verify_step(slots, ctxl, tokens, parents, commit=True, n_vocab=meta["n_vocab"])
-    steps = max(3, min(args.steps, 30))
+        return int((r["accepted_len"] + 1).sum())
+
+    for _ in range(args.warmup):
+        step()
+    # ---- device-timed steps (CUDA events on the context stream) ----------
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     acc_tok = 0
     if ws > 1:
         dist.barrier()
+    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        w0 = time.perf_counter()
         e0.record(stream)
-        for _ in range(steps):
-            r = ctx.verify_step(slots, ctxl, tokens, parents, commit=True, n_vocab=meta["n_vocab"])
-            acc_tok += int((r["accepted_len"] + 1).sum())
+        for _ in range(args.steps):
+            acc_tok += step()
         e1.record(stream)
         torch.cuda.synchronize()
-        wall = time.perf_counter() - w0
-    ms = e0.elapsed_time(e1) / steps
     if ws > 1:
-        t = torch.tensor([ms, wall], dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, wall = float(t[0]), float(t[1])
-    H, F, V = meta["n_embd"], meta["n_ff"], meta["n_vocab"]
-    Dq, Dk = meta["n_head"] * 128, meta["n_head_kv"] * 128
-    params = meta["n_layer"] * (H * (Dq + 2 * Dk) + Dq * H + 3 * H * F) + V * H
-    M = B * N
-    flops = 2.0 * M * params
-    kv_bytes = B * ctx_len * meta["n_layer"] * Dk * 2 * 2
-    w_bytes = params * 18 // 32
+        dist.barrier()
+    ms = max_over_ranks([e0.elapsed_time(e1) / args.steps])[0]
+    acc_per_step = acc_tok / args.steps
+    # ---- end to end: the host-buffer C ABI call, wall clock --------------
+    e2e_steps = max(3, min(args.steps, 10))
+    if ws > 1:
+        dist.barrier()
+    w0 = time.perf_counter()
+    e2e_tok = 0
+    for _ in range(e2e_steps):
+        e2e_tok += step()
+    wall = max_over_ranks([time.perf_counter() - w0])[0]
+    # ---- phase profile of two more steps (events between the phases) -----
+    ctx.profile(True)
+    prof_steps = 2
+    for _ in range(prof_steps):
+        step()
+    phases, nsteps = ctx.profile_read()
+    ctx.profile(False)
+    names = list(phases)
+    phase_ms = dict(zip(names, max_over_ranks([phases[n] / max(nsteps, 1) for n in names])))
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peaks = json.load(f)
+        peak_kind = "measured"
     except Exception:
-        pass
-    tfl = float(peaks.get("bf16_tflops_sustained", 1416.2))
+        peak_kind = "fallback"
+    tfl = float(peaks.get("bf16_tflops_sustained", 1400.0))
     hbm = float(peaks.get("hbm_gbs", HBM_FALLBACK_GBS))
-    floor_ms = (flops / (tfl * 1e12) + kv_bytes / (hbm * 1e9)) * 1e3 / ws
-    wl = ("verify step, BASELINE config 5 (Llama-3-70B shape q4_0, B=64, 32-node tree, ctx 4096 "
-          "fp16 pages)" if c5 else
-          "verify step, BASELINE config 3 (Llama-2-7B shape q4_0, B=32, 16-node tree, ctx 2048 fp16 pages)")
-    line = {"workload": wl,
-            "n_gpus": ws, "parallelism": f"tp{ws}" if ws > 1 else "single GPU",
-            "scaling": "strong", "us_per_step": ms * 1e3,
-            "accepted_tokens_per_s": acc_tok / steps / (ms / 1e3),
-            "e2e_ms_per_step": wall / steps * 1e3, "rows": M, "gemm_tflop": flops / 1e12,
-            "kv_gb": kv_bytes / 1e9, "weight_gb": w_bytes / 1e9,
-            "floor_ms_at_measured_peaks": floor_ms, "frac_of_floor": floor_ms / ms,
-            "accepted_per_step": acc_tok / steps, "clocks": clk.summary(),
-            "model_gen_s": gen_s, "load_s": load_s,
-            "data": "random-init N(0,0.02^2) weights quantised to q4_0 on the device"
-                    + ("; each rank generates its own shards, passed as device tensors" if c5 else "")
-                    + "; KV pages zero-filled (timing does not depend on their values)"}
-    if cpu_token_s is not None:
-        cpu_step = cpu_token_s * M  # the reference runs forward_one once per tree node
-        line["cpu_baseline"] = {
-            "value": (acc_tok / steps) / cpu_step, "unit": "accepted tokens/s", "cores": 1,
-            "kind": "port", "us_per_step": cpu_step * 1e6,
-            "sample": f"one forward_one of the CPU port (llama_cpu.rs restatement, single thread) at "
-                      f"position {ctx_len - 1} over all {meta['n_layer']} layers took "
-                      f"{cpu_token_s:.2f} s; a verify step is {M} such calls (B x nodes), "
-                      f"extrapolated linearly"}
+    floor_ms = (cnt["flops"] / (tfl * 1e12) + cnt["kv_bytes"] / (hbm * 1e9)) * 1e3
+    up_ms = phase_ms["gemm_ffn_up"] / meta["n_layer"]  # one launch per layer
+    up_tflops = cnt["ffn_up_flops"] / (up_ms * 1e-3) / 1e12
+    gemm_ms = sum(phase_ms[k] for k in ("gemm_qkv", "gemm_o", "gemm_ffn_up", "gemm_ffn_down",
+                                        "lm_head"))
+    H2D = (2 * M + 2 * B + B * per_seq) * 4  # tokens, parents, ctx_len, slots, page-table rows
+    D2H = (2 * B + 2 * M) * 4                # path lengths, bonus tokens, paths, expected tokens
+    L = meta["n_layer"]
+    launches = 2 + 8 * L + 2 + (2 if ws == 1 else 3) + 1
+    traffic = None
+    if ws == 1:
+        traffic = load_traffic("q4gemm_swiglu_c5" if c5 else "q4gemm_swiglu_c3")
+    line = {
+        "metric": BASELINE_METRIC, "value": acc_per_step / (ms / 1e3),
+        "unit": "accepted tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "us_per_step": ms * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16 operands (q4_0 weights dequantised to f16 in the GEMM), f32 accumulation, f16 KV",
+        "data": "synthetic: random-init N(0,0.02^2) weights quantised to q4_0 on the device"
+                + ("; each rank generates its own shards" if c5 else "")
+                + "; random draft-tree tokens (seeded Philox); KV pages zero-filled (the timing "
+                  "does not depend on their values)",
+        "config": {"workload": wl, "B": B, "nodes": N, "ctx": ctx_len, "rows": M,
+                   "parallelism": f"tp{ws}" if ws > 1 else "tp1 (single GPU)",
+                   "l2": f"inputs > L2: {cnt['w_bytes'] / 1e9:.1f} GB of weights and "
+                         f"{cnt['kv_bytes'] / 1e9:.1f} GB of KV streamed per step and rank"},
+        "accepted_per_step": acc_per_step,
+        "roofline": {"bound": "tensor", "achieved": up_tflops, "peak": tfl, "unit": "TFLOP/s",
+                     "frac": up_tflops / tfl, "traffic": traffic, "peak_kind": peak_kind
+                     + " bf16 sustained (the GEMM runs inside a long step)",
+                     "kernel": "q4_gemm_ta_swiglu_kernel (w1/w3 + SwiGLU, the largest share of the "
+                               "step), one launch per layer",
+                     "algorithmic_flops_per_launch": cnt["ffn_up_flops"],
+                     "us_per_launch": up_ms * 1e3,
+                     "all_gemms_tflops": cnt["flops"] / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None,
+                     "step_floor_ms": floor_ms, "step_frac_of_floor": floor_ms / ms,
+                     "step_floor_note": "GEMM FLOPs at the sustained bf16 peak + KV bytes at the "
+                                        "measured HBM bandwidth, per rank"},
+        "phase_ms_per_step": phase_ms,
+        "clocks": clk.summary(),
+        "e2e": {"value": e2e_tok / e2e_steps / (wall / e2e_steps), "unit": "accepted tokens/s",
+                "h2d_bytes_per_step": H2D, "d2h_bytes_per_step": D2H, "steps": e2e_steps,
+                "ms_per_step": wall / e2e_steps * 1e3,
+                "path": "velo_cuda_verify_step with host buffers (inputs packed into pinned memory "
+                        "and copied in, paths / bonus tokens / expected tokens copied back, every "
+                        "step), wall clock, max over ranks"},
+        "gpu_launches": launches * args.steps,
+        "model_gen_s": gen_s, "load_s": load_s,
+    }
     ctx.close()
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        t_tok, t2, _ = cpu_token_model(meta, ctx_len)
+        cpu_step = t_tok * M  # the reference runs forward_one once per tree node
+        line["cpu_baseline"] = {
+            "value": acc_per_step / cpu_step, "unit": "accepted tokens/s", "cores": 1,
+            "kind": "port", "ms_per_step": cpu_step * 1e3,
+            "sample": f"forward_one of the CPU port (llama_cpu.rs restatement, one thread) at "
+                      f"position {ctx_len - 1} on 1- and 2-layer models of the config's shapes "
+                      f"(2 layers: {t2:.2f} s), extrapolated to {meta['n_layer']} layers "
+                      f"({t_tok:.1f} s per token); a verify step is {M} such calls "
+                      f"(B x nodes), extrapolated linearly"}
     if rank == 0:
         print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_reference_verify(args):
+    """--impl reference for the verify step: the CPU port of the reference's
+    path (oracle restatement of llama_cpu.rs forward_one, the CPU backend the
+    CUDA one replaces) on all host threads, one forward_one per thread (one
+    tree node each) on a 2-layer model of the config's shapes per step;
+    the full step (B x nodes forward_one calls of all layers) is extrapolated
+    from it.  Rank 0 alone runs it."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import threading as th
+    import vo
+    c5, meta, tree, B, ctx_len, wl = verify_case(args.case)
+    N = len(tree)
+    M = B * N
+    threads = max(1, min(os.cpu_count() or 1, M))
+    t_tok, t2, tl = cpu_token_model(meta, ctx_len)
+    scale = t_tok / t2  # all layers over the 2-layer sample, single thread
+    models = [vo.Model(dict(meta, n_layer=2, n_ctx=ctx_len), tl) for _ in range(threads)]
+
+    def one(mm):
+        mm.forward_one(1, ctx_len - 1)
+
+    secs = []
+    for s_ in range(args.warmup + args.steps):
+        ts = [th.Thread(target=one, args=(mm,)) for mm in models]
+        t0 = time.perf_counter()
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        dt = time.perf_counter() - t0
+        if s_ >= args.warmup:
+            secs.append(dt)
+    sample_s = statistics.mean(secs)
+    rounds = -(-M // threads)
+    step_s = sample_s * scale * rounds
+    acc_per_step = float(B)  # random-token drafts are rejected at the root; each sequence emits one
+    value = acc_per_step / step_s
+    line = {
+        "impl": "reference", "metric": BASELINE_METRIC, "value": value,
+        "unit": "accepted tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32 (q4_0 weights dequantised per row)",
+        "data": "synthetic (random q4_0 weights, zero KV of the config's context)",
+        "config": {"workload": wl, "B": B, "nodes": N, "ctx": ctx_len, "rows": M,
+                   "parallelism": f"{threads} host threads, one tree node each"},
+        "cpu_baseline": {"value": value, "unit": "accepted tokens/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"per step {threads} concurrent forward_one calls (one per "
+                                   f"thread) of the CPU port on a 2-layer model of the config's "
+                                   f"shapes at position {ctx_len - 1}, {sample_s:.2f} s; scaled by "
+                                   f"{scale:.1f} to all {meta['n_layer']} layers (single-thread "
+                                   f"1- vs 2-layer timing) and by {rounds} rounds to the step's "
+                                   f"{M} nodes; {acc_per_step:.0f} accepted tokens per step (one "
+                                   f"per sequence, as the CUDA arm measures on random drafts)"},
+        "e2e": {"value": value, "unit": "accepted tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
     return 0
 
 
@@ -1017,17 +1318,27 @@ def cpu_baseline():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
-    ap.add_argument("--workload", default="accept", choices=["accept", "q4gemm", "attn", "verify", "c1"])
+    ap.add_argument("--workload", default="verify", choices=["verify", "accept", "accept_tree", "q4gemm", "attn", "c1"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default="", help="one case of a multi-case workload")
+    ap.add_argument("--case", default="", help="one case of a multi-case workload "
+                                               "(verify: c5 [default] or c3)")
     args = ap.parse_args()
+    quick = args.workload == "verify"  # 0.05-0.4 s per step: a few dozen steps
+    if args.steps is None:
+        args.steps = 20 if quick else 2000
+    if args.warmup is None:
+        args.warmup = 3 if quick else 20
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
+        if args.workload == "verify":
+            return run_reference_verify(args)
         return run_reference(args)
+    if args.workload == "accept_tree":
+        return run_accept_tree(args)
     if args.workload == "q4gemm":
         return run_q4gemm(args)
     if args.workload == "attn":

@@ -168,6 +168,49 @@ VELO_API int32_t velo_cuda_accept_static(const float *target_logits, const float
                                          int32_t *accepted_len, uint32_t *bonus_token,
                                          void *stream);
 
+/* The input check of the last velo_cuda_accept_static call on the current
+ * device: copies its error word (0 = clean; non-zero = a draft token was >= V
+ * and was counted as a rejection, which velo_cuda_accept_device reports as
+ * VELO_ERR_DEVICE_FLAG at velo_cuda_sync) into *flag_out, a device int32, on
+ * `stream`, asynchronously and without allocating.  Issue it on the stream of
+ * the call it checks, before the next velo_cuda_accept_static, which clears
+ * the word.  No counterpart in the reference (velo-core has no device-side
+ * acceptance). */
+VELO_API int32_t velo_cuda_accept_static_error(int32_t *flag_out, void *stream);
+
+/* Rejection sampling over draft trees (temperature > 0).  Multi-candidate
+ * speculative sampling (SpecInfer, Miao et al. 2024): from the root, the
+ * children of the current node are tested in index order, child c with
+ * token x accepted iff u[c-1] * q(x) <= p(x); after each rejected child p is
+ * replaced by norm(max(0, p - q)); the walk moves to the first accepted child;
+ * at a node with no accepted child (or a leaf) the bonus token is drawn from
+ * the current p with u[N-1].  On chains this is velo_cuda_accept's rule, bit
+ * for bit.  Extends the greedy tree walk of SpeculativeTree::find_best_path
+ * (src/speculative.rs:97-129) over trees built by TreeDraftModel::draft_tree
+ * (src/backend.rs:255-294), which the reference only verifies greedily.
+ *   target_logits [B][N][V] f32: row n = the target's logits after node n
+ *   draft_logits  [B][N-1][V] f32: row n = the draft distribution node n's
+ *                 children were drawn from (node N-1 has no children)
+ *   tokens, parents [B][N]: node 0 is the root (-1), parents[n] < n
+ *   uniforms      [B][N] in [0,1)
+ *   path [B][N] out: accepted nodes root first, -1 padded; path_len [B] out
+ *   (root included); bonus [B] out.
+ * Host-buffer form: copies in, runs, copies back and waits. */
+VELO_API int32_t velo_cuda_accept_tree(velo_cuda_ctx *ctx, const float *target_logits,
+                                       const float *draft_logits, const uint32_t *tokens,
+                                       const int32_t *parents, const float *uniforms, int32_t B,
+                                       int32_t N, int32_t V, float temperature, int32_t *path,
+                                       int32_t *path_len, uint32_t *bonus);
+
+/* Device-buffer form of velo_cuda_accept_tree (every pointer device memory),
+ * asynchronous on the context stream; a token >= V is counted as a rejection
+ * and reported by velo_cuda_sync (VELO_ERR_DEVICE_FLAG). */
+VELO_API int32_t velo_cuda_accept_tree_device(velo_cuda_ctx *ctx, const float *target_logits,
+                                              const float *draft_logits, const uint32_t *tokens,
+                                              const int32_t *parents, const float *uniforms,
+                                              int32_t B, int32_t N, int32_t V, float temperature,
+                                              int32_t *path, int32_t *path_len, uint32_t *bonus);
+
 /* ---- q4_0 linear layers ------------------------------------------------- */
 
 /* Epilogues of velo_cuda_gemm_q4_0 (y has row stride ldy elements). */
@@ -175,7 +218,8 @@ typedef enum velo_gemm_epilogue {
     VELO_EPI_STORE_F32 = 0, /* y[m][n] = acc                       f32 */
     VELO_EPI_STORE_F16 = 1, /* y[m][n] = acc                       f16 */
     VELO_EPI_ADD_F32 = 2,   /* y[m][n] += acc (residual stream)    f32 */
-    VELO_EPI_SWIGLU = 3     /* y[m][j] = silu(gate_j) * up_j        f16, j < N/2 */
+    VELO_EPI_SWIGLU = 3,    /* y[m][j] = silu(gate_j) * up_j        f16, j < N/2 */
+    VELO_EPI_STORE_BF16 = 4 /* y[m][n] = acc                       bf16 */
 } velo_gemm_epilogue;
 
 /* Device bytes of a repacked q4_0 weight with N rows of K elements (0 if
@@ -471,6 +515,33 @@ typedef struct velo_verify_result {
  * src/backend.rs:313-369; src/llama_cpu.rs:401-419). */
 VELO_API int32_t velo_cuda_verify_step(velo_cuda_ctx *ctx, const velo_verify_batch *batch,
                                        velo_verify_result *result);
+
+/* ---- step profile ------------------------------------------------------ */
+
+/* Phases of a verify step whose device time velo_cuda_profile accumulates. */
+typedef enum velo_phase {
+    VELO_PHASE_OTHER = 0,          /* ancestor masks, embedding, RMSNorm, RoPE + split */
+    VELO_PHASE_GEMM_QKV = 1,       /* fused q/k/v projection */
+    VELO_PHASE_ATTENTION = 2,      /* tree-masked paged attention */
+    VELO_PHASE_GEMM_O = 3,         /* o_proj */
+    VELO_PHASE_GEMM_FFN_UP = 4,    /* w1/w3 with the SwiGLU epilogue */
+    VELO_PHASE_GEMM_FFN_DOWN = 5,  /* w2 */
+    VELO_PHASE_ALLREDUCE = 6,      /* tensor-parallel sums after o_proj / w2 */
+    VELO_PHASE_LM_HEAD = 7,        /* final RMSNorm excluded: LM head GEMM */
+    VELO_PHASE_ACCEPT_COMMIT = 8,  /* acceptance, logits exchange, KV commit */
+    VELO_PHASE_COUNT = 9
+} velo_phase;
+
+/* enable != 0: the following verify steps run their launches directly (no
+ * CUDA graph) with a CUDA event at the start of every phase, and add each
+ * phase's device time to per-phase totals; enable == 0 stops it.  Either call
+ * clears the totals.  Instrumentation for benchmarks: no counterpart in the
+ * reference.  VELO_ERR_INVALID_ARGUMENT without a model. */
+VELO_API int32_t velo_cuda_profile(velo_cuda_ctx *ctx, int32_t enable);
+
+/* Copy the per-phase totals in milliseconds (ms[i] for velo_phase i, n >=
+ * VELO_PHASE_COUNT) and the number of profiled steps (or NULL). */
+VELO_API int32_t velo_cuda_profile_read(velo_cuda_ctx *ctx, double *ms, int32_t n, int32_t *steps);
 
 #ifdef __cplusplus
 }

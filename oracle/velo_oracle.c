@@ -192,17 +192,61 @@ void vo_softmax(float *x, size_t n) {
 }
 
 /* llama_cpu.rs:75-90: out[r] += dot(dequant(row r), x) */
-void vo_matvec_quant(float *out, const uint8_t *data, int dtype, const float *x,
-                     size_t rows, size_t cols) {
+static void matvec_rows(float *out, const uint8_t *data, int dtype, const float *x,
+                        size_t r0, size_t r1, size_t cols) {
     size_t rb = vo_row_bytes(dtype, cols);
     float *row = (float *)malloc(cols * sizeof(float));
-    for (size_t r = 0; r < rows; ++r) {
+    for (size_t r = r0; r < r1; ++r) {
         vo_dequant_row(dtype, data + r * rb, row, cols);
         float dot = 0.0f;
         for (size_t c = 0; c < cols; ++c) dot += row[c] * x[c];
         out[r] += dot;
     }
     free(row);
+}
+
+/* Rows of a matvec may be split over threads (vo_set_threads, default 1):
+ * each row is still one sequential dot product, so the result is the same
+ * bits as one thread.  Only the tests raise it, to check large shapes. */
+static int g_threads = 1;
+void vo_set_threads(int n) { g_threads = n < 1 ? 1 : n > 256 ? 256 : n; }
+
+typedef struct {
+    float *out;
+    const uint8_t *data;
+    int dtype;
+    const float *x;
+    size_t r0, r1, cols;
+} matvec_job;
+
+static void *matvec_job_run(void *arg) {
+    matvec_job *j = (matvec_job *)arg;
+    matvec_rows(j->out, j->data, j->dtype, j->x, j->r0, j->r1, j->cols);
+    return NULL;
+}
+
+void vo_matvec_quant(float *out, const uint8_t *data, int dtype, const float *x,
+                     size_t rows, size_t cols) {
+    int nt = g_threads;
+    if (nt <= 1 || rows * cols < ((size_t)1 << 20) || rows < (size_t)nt) {
+        matvec_rows(out, data, dtype, x, 0, rows, cols);
+        return;
+    }
+    pthread_t th[256];
+    matvec_job jobs[256];
+    int joined[256];
+    for (int t = 0; t < nt; ++t) {
+        jobs[t] = (matvec_job){out, data, dtype, x, rows * t / nt, rows * (t + 1) / nt, cols};
+        joined[t] = 0;
+        if (t == 0) continue;
+        if (pthread_create(&th[t], NULL, matvec_job_run, &jobs[t]) == 0)
+            joined[t] = 1;
+        else
+            matvec_job_run(&jobs[t]); /* no thread: do its rows here */
+    }
+    matvec_job_run(&jobs[0]);
+    for (int t = 1; t < nt; ++t)
+        if (joined[t]) pthread_join(th[t], NULL);
 }
 
 /* ------------------------------------------------------------------ */
@@ -445,6 +489,17 @@ int vo_commit_path(vo_model *m, const int32_t *path, size_t len, size_t n_cached
                    kv_stride * sizeof(float));
         }
     m->pos = n_cached + len;
+    return 0;
+}
+
+/* Test setup: place n cached rows (positions pos0..) of one layer in the
+ * KvCache, as a prefill would have left them. */
+int vo_write_kv(vo_model *m, int which, size_t layer, size_t pos0, size_t n, const float *src) {
+    const vo_meta *mt = &m->meta;
+    size_t kv_stride = (size_t)mt->n_head_kv * mt->head_dim;
+    if (layer >= mt->n_layer || pos0 + n > mt->n_ctx) return 1;
+    float *dst = (which == 0 ? m->k : m->v) + ((size_t)layer * mt->n_ctx + pos0) * kv_stride;
+    memcpy(dst, src, n * kv_stride * sizeof(float));
     return 0;
 }
 
@@ -783,6 +838,169 @@ int vo_accept(const float *tgt, const float *drf, const uint32_t *tok,
     for (int i = 1; i < n_threads; ++i) pthread_create(&th[i], NULL, accept_worker, &j);
     accept_worker(&j);
     for (int i = 1; i < n_threads; ++i) pthread_join(th[i], NULL);
+    return 0;
+}
+
+/* ------------------------------------------------------------------ */
+/* Rejection sampling over a draft tree.  No reference implementation  */
+/* (velo-core verifies trees greedily, speculative.rs:97-129); the     */
+/* method is multi-candidate speculative sampling (SpecInfer, Miao et  */
+/* al. 2024, Algorithm 2): walk from the root; at node n test its      */
+/* children in index order against the target distribution p_n and    */
+/* the draft distribution q_n the children were drawn from; after each */
+/* rejected child replace p by norm(max(0, p - q)); move to the first  */
+/* accepted child; at a node where no child is accepted (or a leaf)    */
+/* draw the bonus token from the current distribution.  For chains it  */
+/* is the acceptance rule above, bit for bit.                           */
+/* Arithmetic (the spec the CUDA kernel implements):                    */
+/*   P0(x) = E(fma(t_x, 1/T, -Mt)) * Rt, Q(x) = E(fma(d_x, 1/T, -Md)) * Rd */
+/*   W_1 = P0 > Q ? P0 - Q : 0;  W_{j+1} = P_j > Q ? P_j - Q : 0 with    */
+/*   P_j = W_j * R_j, R_j = 1 / total_j, total_j = the spec's ordered sum */
+/*   of W_j over the vocabulary (tiles, lanes, butterfly as above).     */
+/*   Child c (parent n) at level j is accepted iff u[c-1] * Q(x_c) <= P_j */
+/*   (P_0 = P0).  A level whose total is 0 falls back to level 0 (p).   */
+/*   The draw uses u[N-1] and the weights of the final level.           */
+/* ------------------------------------------------------------------ */
+#define TREE_MAX_LEVEL 64
+typedef struct {
+    const float *trow, *drow;
+    float inv_t, Mt, Rt, Md, Rd;
+    int level;
+    float R[TREE_MAX_LEVEL + 1];
+} tree_w;
+
+/* W_level of element e (level 0: P0) */
+static inline float tree_weight(const tree_w *w, int e) {
+    float P = vo_spec_exp(fmaf(w->trow[e], w->inv_t, -w->Mt)) * w->Rt;
+    if (w->level == 0) return P;
+    float Q = vo_spec_exp(fmaf(w->drow[e], w->inv_t, -w->Md)) * w->Rd;
+    float W = 0.0f;
+    for (int j = 1; j <= w->level; ++j) {
+        W = P > Q ? P - Q : 0.0f;
+        if (j < w->level) P = W * w->R[j];
+    }
+    return W;
+}
+
+/* lane / tile weights and their ordered total for the current level */
+static float tree_weigh(const tree_w *w, int V, float *lane_w, float *tile_w) {
+    int nt = (V + SPEC_TILE - 1) / SPEC_TILE;
+    float total = 0.0f;
+    for (int t = 0; t < nt; ++t) {
+        for (int l = 0; l < 32; ++l) {
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int i = 0; i < 8; ++i)
+                for (int c = 0; c < 4; ++c) {
+                    int e = spec_elem(t, l, i, c);
+                    if (e < V) acc[c] = acc[c] + tree_weight(w, e);
+                }
+            lane_w[t * 32 + l] = lane_combine(acc);
+        }
+        tile_w[t] = butterfly32(&lane_w[t * 32]);
+        total = total + tile_w[t];
+    }
+    return total;
+}
+
+static void accept_tree_one(const float *tgt, const float *drf, const uint32_t *tok,
+                            const int32_t *par, const float *u, int N, int V,
+                            float temperature, int32_t *path, int32_t *plen,
+                            uint32_t *bonus) {
+    size_t Vs = (size_t)V;
+    int nt = (V + SPEC_TILE - 1) / SPEC_TILE;
+    float *lane_w = (float *)malloc(sizeof(float) * nt * 32);
+    float *tile_w = (float *)malloc(sizeof(float) * nt);
+    for (int n = 0; n < N; ++n) path[n] = -1;
+    int cur = 0, len = 0;
+    path[len++] = 0;
+    tree_w w;
+    memset(&w, 0, sizeof(w));
+    w.inv_t = 1.0f / temperature;
+    for (;;) {
+        float Z;
+        w.trow = tgt + (size_t)cur * Vs;
+        vo_row_stats(w.trow, V, w.inv_t, &w.Mt, &Z);
+        w.Rt = 1.0f / Z;
+        int has_child = 0;
+        for (int c = cur + 1; c < N; ++c) has_child |= par[c] == cur;
+        w.drow = NULL;
+        if (has_child) {
+            w.drow = drf + (size_t)cur * Vs;
+            vo_row_stats(w.drow, V, w.inv_t, &w.Md, &Z);
+            w.Rd = 1.0f / Z;
+        }
+        w.level = 0;
+        int accepted = -1;
+        for (int c = cur + 1; c < N && accepted < 0; ++c) {
+            if (par[c] != cur) continue;
+            uint32_t x = tok[c];
+            float P;
+            if (w.level == 0) {
+                P = tree_weight(&w, (int)x);
+            } else {
+                P = tree_weight(&w, (int)x) * w.R[w.level];
+            }
+            float Q = vo_spec_exp(fmaf(w.drow[x], w.inv_t, -w.Md)) * w.Rd;
+            if (u[c - 1] * Q <= P) {
+                accepted = c;
+                break;
+            }
+            if (w.level == TREE_MAX_LEVEL) continue; /* cannot happen: <= 63 children */
+            w.level += 1;
+            float total = tree_weigh(&w, V, lane_w, tile_w);
+            if (!(total > 0.0f))
+                w.level = 0; /* residual mass vanished: back to p */
+            else
+                w.R[w.level] = 1.0f / total;
+        }
+        if (accepted >= 0) {
+            path[len++] = accepted;
+            cur = accepted;
+            continue;
+        }
+        /* draw from the final level's weights */
+        float total = tree_weigh(&w, V, lane_w, tile_w);
+        int token = 0;
+        if (total > 0.0f) {
+            float tau = u[N - 1] * total, tau1 = 0.0f, tau2 = 0.0f, tau3 = 0.0f;
+            int ts = select_level(tile_w, nt, tau, &tau1);
+            int ls = select_level(&lane_w[ts * 32], 32, tau1, &tau2);
+            float ew[32];
+            int eidx[32], n = 0;
+            for (int i = 0; i < 8; ++i)
+                for (int c = 0; c < 4; ++c) {
+                    int e = spec_elem(ts, ls, i, c);
+                    ew[n] = e < V ? tree_weight(&w, e) : 0.0f;
+                    eidx[n] = e;
+                    ++n;
+                }
+            int es = select_level(ew, 32, tau2, &tau3);
+            token = eidx[es];
+        }
+        *bonus = (uint32_t)token;
+        break;
+    }
+    *plen = len;
+    free(lane_w);
+    free(tile_w);
+}
+
+int vo_accept_tree(const float *tgt, const float *drf, const uint32_t *tok,
+                   const int32_t *parents, const float *u, int B, int N, int V,
+                   float temperature, int32_t *path, int32_t *path_len, uint32_t *bonus) {
+    if (B < 0 || N < 1 || N > TREE_MAX_LEVEL || V <= 0 || !(temperature > 0.0f)) return 1;
+    for (long b = 0; b < B; ++b) {
+        if (parents[b * N] != -1) return 1;
+        for (int n = 1; n < N; ++n) {
+            int p = parents[b * N + n];
+            if (p < 0 || p >= n || tok[b * N + n] >= (uint32_t)V) return 1;
+        }
+    }
+    size_t Vs = (size_t)V, Ns = (size_t)N;
+    for (long b = 0; b < B; ++b)
+        accept_tree_one(tgt + (size_t)b * Ns * Vs, drf + (size_t)b * (Ns - 1) * Vs,
+                        tok + (size_t)b * Ns, parents + (size_t)b * Ns, u + (size_t)b * Ns, N, V,
+                        temperature, path + (size_t)b * Ns, &path_len[b], &bonus[b]);
     return 0;
 }
 

@@ -57,6 +57,10 @@ float vo_silu(float x);
 void vo_rope(float *q, float *k, size_t pos, size_t n_heads, size_t n_kv_heads,
              size_t head_dim, float freq_base);
 void vo_softmax(float *x, size_t n);
+/* Threads a matvec's rows may be split over (1 = the reference's single
+ * thread; every row stays one sequential dot product, so results do not
+ * change).  Test infrastructure: the timed CPU baseline keeps 1. */
+void vo_set_threads(int n);
 void vo_matvec_quant(float *out, const uint8_t *data, int dtype, const float *x,
                      size_t rows, size_t cols);
 
@@ -91,6 +95,7 @@ int vo_verify_tree(vo_model *m, const uint32_t *tokens, const int32_t *parents,
  * n_cached.. (the commit of an accepted path). */
 int vo_commit_path(vo_model *m, const int32_t *path, size_t len, size_t n_cached);
 /* Read back cached K or V of one layer, positions [0, n): [n][n_kv*hd] */
+int vo_write_kv(vo_model *m, int which, size_t layer, size_t pos0, size_t n, const float *src);
 int vo_read_kv(const vo_model *m, int which, size_t layer, size_t n, float *out);
 
 /* ---- sampling.rs:39-58 ---- */
@@ -112,6 +117,16 @@ int vo_accept(const float *tgt, const float *drf, const uint32_t *tok,
               const float *u, int B, int k, int V, float temperature,
               int32_t *acc_len, uint32_t *bonus, int n_threads);
 /* The spec's exponential (Cody-Waite reduction + degree-6 Taylor). */
+/* Rejection sampling over draft trees (multi-candidate speculative sampling,
+ * SpecInfer): tgt [B][N][V] (row n = target logits after node n), drf
+ * [B][N-1][V] (row n = the draft distribution node n's children were drawn
+ * from), tok / parents [B][N] (node 0 = root, parents[n] < n), u [B][N]
+ * (u[c-1] tests child c, u[N-1] draws the bonus).  Outputs: path [B][N]
+ * (accepted nodes root first, -1 padded), path_len [B], bonus [B].
+ * Chains give vo_accept's decisions.  Returns non-zero on bad input. */
+int vo_accept_tree(const float *tgt, const float *drf, const uint32_t *tok,
+                   const int32_t *parents, const float *u, int B, int N, int V,
+                   float temperature, int32_t *path, int32_t *path_len, uint32_t *bonus);
 float vo_spec_exp(float y);
 /* Row statistics of the spec: M (scaled max) and Z (normaliser). */
 void vo_row_stats(const float *row, int V, float inv_t, float *M, float *Z);

@@ -58,11 +58,15 @@ def lib():
             "vo_verify_tree": (ctypes.c_int, [_P, _P, _P, _SZ, _SZ, _P]),
             "vo_commit_path": (ctypes.c_int, [_P, _P, _SZ, _SZ]),
             "vo_read_kv": (ctypes.c_int, [_P, ctypes.c_int, _SZ, _SZ, _P]),
+            "vo_write_kv": (ctypes.c_int, [_P, ctypes.c_int, _SZ, _SZ, _SZ, _P]),
+            "vo_set_threads": (None, [ctypes.c_int]),
             "vo_greedy": (ctypes.c_uint32, [_P, _SZ, _P, _P]),
             "vo_find_best_path": (_SZ, [_P, _P, _P, _SZ, _P, _P]),
             "vo_accept": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int, ctypes.c_int,
                                          ctypes.c_int, ctypes.c_float, _P, _P, ctypes.c_int]),
             "vo_spec_exp": (ctypes.c_float, [ctypes.c_float]),
+            "vo_accept_tree": (ctypes.c_int, [_P, _P, _P, _P, _P, ctypes.c_int, ctypes.c_int,
+                                              ctypes.c_int, ctypes.c_float, _P, _P, _P]),
             "vo_row_stats": (None, [_P, ctypes.c_int, ctypes.c_float, _P, _P]),
             "vo_pages_for_tokens": (_SZ, [_SZ, _SZ]),
             "vo_allocator_new": (_P, [_SZ, _SZ]),
@@ -93,6 +97,11 @@ def ptr(a):
 
 def c_arr(a, dtype):
     return np.ascontiguousarray(a, dtype=dtype)
+
+
+def set_threads(n):
+    """Split each matvec's rows over n threads (same bits; tests only)."""
+    lib().vo_set_threads(int(n))
 
 
 # ---------------------------------------------------------------- quant.rs
@@ -239,6 +248,16 @@ class Model:
         if rc:
             raise ValueError("commit_path failed")
 
+    def write_kv(self, which, layer, pos0, rows):
+        """Place cached K (which 0) or V (1) rows [n][n_kv * head_dim] of
+        `layer` at positions pos0.. (test setup in place of a prefill)."""
+        r = c_arr(rows, np.float32)
+        kvs = self.meta["n_head_kv"] * self.meta["head_dim"]
+        n = r.size // kvs
+        rc = lib().vo_write_kv(self._h, which, layer, pos0, n, ptr(r))
+        if rc:
+            raise ValueError("write_kv failed")
+
     def read_kv(self, which, layer, n):
         kvs = self.meta["n_head_kv"] * self.meta["head_dim"]
         out = np.zeros((n, kvs), np.float32)
@@ -283,6 +302,26 @@ def accept(tgt, drf, tok, u, temperature, n_threads=0):
     if rc:
         raise ValueError("vo_accept: invalid arguments")
     return acc, bonus
+
+
+def accept_tree(tgt, drf, tok, parents, u, temperature):
+    """Tree rejection sampling spec.  tgt [B][N][V], drf [B][N-1][V],
+    tok / parents [B][N], u [B][N].  Returns (path [B][N] -1 padded,
+    path_len [B], bonus [B])."""
+    tgt = c_arr(tgt, np.float32)
+    B, N, V = tgt.shape
+    drf = c_arr(drf, np.float32).reshape(B, N - 1, V)
+    tok = c_arr(tok, np.uint32).reshape(B, N)
+    par = c_arr(parents, np.int32).reshape(B, N)
+    u = c_arr(u, np.float32).reshape(B, N)
+    path = np.zeros((B, N), np.int32)
+    plen = np.zeros(B, np.int32)
+    bonus = np.zeros(B, np.uint32)
+    rc = lib().vo_accept_tree(ptr(tgt), ptr(drf), ptr(tok), ptr(par), ptr(u), B, N, V,
+                              float(temperature), ptr(path), ptr(plen), ptr(bonus))
+    if rc:
+        raise ValueError("vo_accept_tree: invalid arguments")
+    return path, plen, bonus
 
 
 def spec_exp(y):

@@ -51,3 +51,28 @@ def test_static_rejects_sizes_beyond_its_block(cuda_device):
             0.8, velo_cuda._ptr(t), velo_cuda._ptr(t), None))
     assert e.value.status == velo_cuda.ERR_INVALID_ARGUMENT
     assert "scratch" in e.value.message
+
+
+def test_static_reports_bad_tokens_through_its_error_word(cuda_device):
+    """A draft token >= V is counted as a rejection on the device (the static
+    entry cannot fail the call once it is queued); its error word says so, and
+    the next call clears it."""
+    import torch
+    B, k, V, T = 5, 3, 1000, 0.7
+    tgt, drf, tok, u = synthetic.acceptance_inputs(B, k, V, temperature=T, seed=9)
+    bad = tok.copy()
+    bad[2, 1] = V + 5
+    t_d, d_d, u_d = _device(tgt), _device(drf), _device(u)
+    acc = torch.empty(B, dtype=torch.int32, device="cuda")
+    bon = torch.empty(B, dtype=torch.int32, device="cuda")
+    flag = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    velo_cuda.accept_static(t_d, d_d, _device(bad.view(np.int32)), u_d, T, acc, bon)
+    velo_cuda.accept_static_error(flag)
+    torch.cuda.synchronize()
+    assert int(flag.item()) != 0
+    assert int(acc[2].item()) <= 1  # the bad token ends the accepted prefix
+    velo_cuda.accept_static(t_d, d_d, _device(tok.view(np.int32)), u_d, T, acc, bon)
+    velo_cuda.accept_static_error(flag)
+    torch.cuda.synchronize()
+    assert int(flag.item()) == 0
+

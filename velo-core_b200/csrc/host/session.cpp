@@ -243,11 +243,13 @@ int32_t velo_spec_generate_batch(uint32_t draft_window, uint32_t max_window, siz
         st = verify(verify_user, a, ids.data(), ctx.data(), nctx.data(), dp.data(), nd.data(), expected.data(), window,
                     nv.data());
         if (st) return cleanup(fail(st, "target model failed (status %d)", st));
+        // one target call for every active request, before any per-request
+        // check can end the round (engine.rs records them the same way)
+        for (size_t j = 0; j < a; ++j) sess[ids[j]]->stats.target_calls += 1;
         bool progressed = false;
         std::vector<uint32_t> acc;
         for (size_t j = 0; j < a; ++j) {
             velo_spec_session* s = sess[ids[j]];
-            s->stats.target_calls += 1;
             if (nv[j] != nd[j])
                 return cleanup(fail(VELO_ERR_TARGET_WRONG_LENGTH,
                                     "target model returned %zu verification steps for %zu drafted tokens", nv[j],

@@ -486,6 +486,241 @@ __global__ void __launch_bounds__(kFinThreads) accept_finish_kernel(AcceptParams
     }
 }
 
+// ---------------------------------------------------------------- draft trees
+// Rejection sampling over a draft tree (multi-candidate speculative sampling,
+// SpecInfer: Miao et al. 2024, Algorithm 2), one CTA of 16 warps per
+// sequence.  The walk is sequential by nature (a node's children are tested
+// only after the node was accepted), so the CTA walks it and spreads each
+// vocabulary pass over its warps (warp w takes tiles w, w + 16, ...):
+//   stats pass   target row and draft row of the current node: tile (m, z) as
+//                kernel A, then the row reduction of the finish kernel;
+//   child test   one thread: u * Q(x) <= P_level(x);
+//   residual     after a rejected child, the next level's weights
+//                W_{j+1} = max(0, W_j R_j - Q) (W_1 = max(0, P - Q)) of every
+//                element, their lane / tile sums and the ordered total;
+//   draw         tile -> lane -> element inverse CDF of the final level, as
+//                the finish kernel's draw.
+// Every operation is the spec the CPU oracle restates (vo_accept_tree); on
+// chains it is the chain rule above bit for bit.
+constexpr int kTreeWarps = 16;
+constexpr int kTreeThreads = kTreeWarps * 32;
+constexpr int kTreeMaxLevel = 64;
+
+// W_level of one element (level 0: P)
+__device__ __forceinline__ float tree_weight(float tv, float dv, float inv_t, float Mt, float Rt,
+                                             float Md, float Rd, const float* Rlev, int level) {
+    float P = __fmul_rn(spec_exp(__fmaf_rn(tv, inv_t, -Mt)), Rt);
+    if (level == 0) return P;
+    const float Q = __fmul_rn(spec_exp(__fmaf_rn(dv, inv_t, -Md)), Rd);
+    float W = 0.0f;
+    for (int j = 1; j <= level; ++j) {
+        W = P > Q ? __fadd_rn(P, -Q) : 0.0f;
+        if (j < level) P = __fmul_rn(W, Rlev[j]);
+    }
+    return W;
+}
+
+__global__ void __launch_bounds__(kTreeThreads) accept_tree_kernel(AcceptTreeParams p) {
+    __shared__ float2 st_t[kAcceptMaxTiles], st_d[kAcceptMaxTiles];
+    __shared__ float tile_w[kAcceptMaxTiles];
+    __shared__ float lane_w[kAcceptMaxTiles * 32];
+    __shared__ float Rlev[kTreeMaxLevel + 1];
+    __shared__ float elem_w[32];
+    __shared__ float sf[8];
+    __shared__ int si[4];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int b = blockIdx.x, N = p.N, V = p.V;
+    const int ntiles = (V + kTile - 1) / kTile;
+    const float* tbase = p.tgt + (size_t)b * N * V;
+    const float* dbase = p.drf + (size_t)b * (N - 1) * V;
+    const uint32_t* tok = p.tok + (size_t)b * N;
+    const int32_t* par = p.par + (size_t)b * N;
+    const float* u = p.u + (size_t)b * N;
+    int32_t* path = p.path + (size_t)b * N;
+    for (int n = tid; n < N; n += kTreeThreads) path[n] = n == 0 ? 0 : -1;
+    const float inv_t = p.inv_t;
+    int cur = 0, len = 1;
+    for (;;) {
+        bool has_child = false;
+        for (int c = cur + 1; c < N; ++c) has_child |= __ldg(par + c) == cur;
+        const float* trow = tbase + (size_t)cur * V;
+        const float* drow = has_child ? dbase + (size_t)cur * V : nullptr;
+        // ---- stats pass over the node's target (and draft) row ----------
+        for (int t = warp; t < ntiles; t += kTreeWarps) {
+            const bool full = (t + 1) * kTile <= V;
+            float x[32];
+            load_groups<8>(trow, V, t, lane, 0, p.vec4, x);
+            const float2 a = full ? tile_stats<true>(x, V, t, lane, inv_t) : tile_stats<false>(x, V, t, lane, inv_t);
+            if (lane == 0) st_t[t] = a;
+            if (has_child) {
+                load_groups<8>(drow, V, t, lane, 0, p.vec4, x);
+                const float2 d = full ? tile_stats<true>(x, V, t, lane, inv_t) : tile_stats<false>(x, V, t, lane, inv_t);
+                if (lane == 0) st_d[t] = d;
+            }
+        }
+        __syncthreads();
+        if (warp < 2 && (warp == 0 || has_child)) {
+            const float2* st = warp == 0 ? st_t : st_d;
+            float M = -INFINITY;
+            for (int t = lane; t < ntiles; t += 32) M = fmaxf(M, st[t].x);
+            M = warp_max(M);
+            if (lane == 0) sf[2 * warp] = M;
+        }
+        __syncthreads();
+        for (int e = tid; e < 2 * ntiles; e += kTreeThreads) {
+            const int row = e / ntiles, t = e - row * ntiles;
+            if (row == 1 && !has_child) continue;
+            float2* st = row == 0 ? st_t : st_d;
+            st[t].x = spec_exp(__fadd_rn(st[t].x, -sf[2 * row]));
+        }
+        __syncthreads();
+        if ((tid == 0) || (tid == 32 && has_child)) {
+            const float2* st = tid == 0 ? st_t : st_d;
+            float Z = 0.0f;
+            for (int t = 0; t < ntiles; ++t) Z = __fmaf_rn(st[t].y, st[t].x, Z);
+            sf[tid == 0 ? 1 : 3] = __fdiv_rn(1.0f, Z);
+        }
+        __syncthreads();
+        const float Mt = sf[0], Rt = sf[1], Md = has_child ? sf[2] : 0.0f, Rd = has_child ? sf[3] : 0.0f;
+        // ---- children in index order -------------------------------------
+        int level = 0, weighed = -1, accepted = -1;
+        float total = 0.0f;
+        for (int c = cur + 1; c < N; ++c) {
+            if (__ldg(par + c) != cur) continue;
+            if (tid == 0) {
+                const uint32_t x = __ldg(tok + c);
+                int acc = 0;
+                if (x >= (uint32_t)V) {
+                    atomicOr(p.err_flag, 1);  // bad input: counted as a rejection
+                } else {
+                    const float tv = __ldg(trow + x), dv = __ldg(drow + x);
+                    float P = tree_weight(tv, dv, inv_t, Mt, Rt, Md, Rd, Rlev, level);
+                    if (level > 0) P = __fmul_rn(P, Rlev[level]);
+                    const float Q = __fmul_rn(spec_exp(__fmaf_rn(dv, inv_t, -Md)), Rd);
+                    acc = __fmul_rn(__ldg(u + c - 1), Q) <= P;
+                }
+                si[0] = acc;
+            }
+            __syncthreads();
+            if (si[0]) {
+                accepted = c;
+                break;
+            }
+            ++level;  // the residual of this rejection: weights, sums, total
+            for (int t = warp; t < ntiles; t += kTreeWarps) {
+                float tx[32], dx[32];
+                load_groups<8>(trow, V, t, lane, 0, p.vec4, tx);
+                load_groups<8>(drow, V, t, lane, 0, p.vec4, dx);
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        float w = tree_weight(tx[4 * i + cc], dx[4 * i + cc], inv_t, Mt, Rt, Md, Rd, Rlev, level);
+                        if (!elem_valid(V, t, lane, i, cc)) w = 0.0f;
+                        acc[cc] = __fadd_rn(acc[cc], w);
+                    }
+                const float lw = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+                lane_w[t * 32 + lane] = lw;
+                const float tw = warp_butterfly_sum(lw);
+                if (lane == 0) tile_w[t] = tw;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                float tot = 0.0f;
+                for (int t = 0; t < ntiles; ++t) tot = __fadd_rn(tot, tile_w[t]);
+                sf[4] = tot;
+                if (tot > 0.0f) {
+                    Rlev[level] = __fdiv_rn(1.0f, tot);
+                    si[1] = level;
+                } else {
+                    si[1] = 0;  // residual mass vanished: back to p
+                }
+            }
+            __syncthreads();
+            weighed = level;
+            level = si[1];
+            total = sf[4];
+        }
+        if (accepted >= 0) {
+            if (tid == 0) path[len] = accepted;
+            ++len;
+            cur = accepted;
+            __syncthreads();
+            continue;
+        }
+        // ---- draw from the final level's weights ---------------------------
+        if (weighed != level || level == 0) {
+            for (int t = warp; t < ntiles; t += kTreeWarps) {
+                float tx[32], dx[32];
+                load_groups<8>(trow, V, t, lane, 0, p.vec4, tx);
+                if (level > 0) load_groups<8>(drow, V, t, lane, 0, p.vec4, dx);
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        float w = tree_weight(tx[4 * i + cc], level > 0 ? dx[4 * i + cc] : 0.0f, inv_t, Mt, Rt,
+                                              Md, Rd, Rlev, level);
+                        if (!elem_valid(V, t, lane, i, cc)) w = 0.0f;
+                        acc[cc] = __fadd_rn(acc[cc], w);
+                    }
+                const float lw = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
+                lane_w[t * 32 + lane] = lw;
+                const float tw = warp_butterfly_sum(lw);
+                if (lane == 0) tile_w[t] = tw;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                float tot = 0.0f;
+                for (int t = 0; t < ntiles; ++t) tot = __fadd_rn(tot, tile_w[t]);
+                sf[4] = tot;
+            }
+            __syncthreads();
+            total = sf[4];
+        }
+        if (tid == 0) {
+            float tau1 = 0.0f;
+            const float tau = __fmul_rn(__ldg(u + N - 1), total);
+            int ts = -1;
+            if (total > 0.0f) ts = select_level(tile_w, ntiles, tau, &tau1);
+            si[2] = ts;
+            sf[5] = tau1;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            const int ts = si[2];
+            int token = 0;
+            if (ts >= 0) {
+                float tau2 = 0.0f;
+                int ls = -1;
+                if (lane == 0) ls = select_level(lane_w + ts * 32, 32, sf[5], &tau2);
+                ls = __shfl_sync(0xffffffffu, ls, 0);
+                tau2 = __shfl_sync(0xffffffffu, tau2, 0);
+                if (ls >= 0) {
+                    const int e = ts * kTile + 128 * (lane >> 2) + 4 * ls + (lane & 3);
+                    float ew = 0.0f;
+                    if (e < V)
+                        ew = tree_weight(__ldg(trow + e), level > 0 ? __ldg(drow + e) : 0.0f, inv_t, Mt, Rt, Md,
+                                         Rd, Rlev, level);
+                    elem_w[lane] = ew;
+                    __syncwarp();
+                    if (lane == 0) {
+                        float tau3;
+                        const int es = select_level(elem_w, 32, tau2, &tau3);
+                        token = es >= 0 ? ts * kTile + 128 * (es >> 2) + 4 * ls + (es & 3) : 0;
+                    }
+                }
+            }
+            if (lane == 0) {
+                p.path_len[b] = len;
+                p.bonus[b] = (uint32_t)token;
+            }
+        }
+        break;
+    }
+}
+
 size_t align_up(size_t x) { return (x + 255) & ~(size_t)255; }
 
 template <bool kGreedy>
@@ -509,6 +744,13 @@ cudaError_t launch_finish(const AcceptParams& p, cudaStream_t stream) {
 }
 
 }  // namespace
+
+cudaError_t launch_accept_tree(const AcceptTreeParams& p, cudaStream_t stream) {
+    if (p.B == 0) return cudaSuccess;
+    if (p.N < 1 || p.N > kTreeMaxLevel || p.V < 1 || p.V > kAcceptMaxV) return cudaErrorInvalidValue;
+    accept_tree_kernel<<<p.B, kTreeThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
 
 size_t accept_workspace_bytes(int B, int k, int V, bool greedy) {
     const size_t ntiles = (size_t)(V + kTile - 1) / kTile;

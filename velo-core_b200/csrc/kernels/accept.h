@@ -44,4 +44,21 @@ void accept_bind_buffers(AcceptParams& p, void* ws, void* cnt, bool greedy);
 
 cudaError_t launch_accept(const AcceptParams& p, bool greedy, int sm_count, cudaStream_t stream);
 
+// Rejection sampling over draft trees (sampling only, temperature > 0).
+struct AcceptTreeParams {
+    const float* tgt;       // [B][N][V]: row n = target logits after node n
+    const float* drf;       // [B][N-1][V]: row n = draft distribution of node n's children
+    const uint32_t* tok;    // [B][N], node 0 = the root (its token is not tested)
+    const int32_t* par;     // [B][N], -1 for node 0, parents[n] < n
+    const float* u;         // [B][N]: u[c-1] tests child c, u[N-1] draws the bonus
+    int32_t* path;          // [B][N] out: accepted nodes, root first, -1 padded
+    int32_t* path_len;      // [B] out: nodes on the path (root included)
+    uint32_t* bonus;        // [B] out
+    int* err_flag;          // device flag: a token >= V (counted as a rejection)
+    int B, N, V;
+    float inv_t;
+    bool vec4;              // rows are 16-byte aligned
+};
+cudaError_t launch_accept_tree(const AcceptTreeParams& p, cudaStream_t stream);
+
 }  // namespace velo

@@ -32,6 +32,7 @@
 // (or exact FMA for the high nibbles) gives q - 8, and one HMUL2 by the block
 // scale rounds d * (q - 8) once to f16.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <cstdlib>
@@ -157,6 +158,13 @@ __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
 // ---------------------------------------------------------------- epilogue
 __device__ __forceinline__ void store_row32(const Q4GemmArgs& a, int m, int n, const uint32_t (&r)[32]) {
+    if (a.mode == kEpiStoreBF16) {
+        __nv_bfloat16* y = static_cast<__nv_bfloat16*>(a.y) + (size_t)m * a.ldy + n;
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+            if (n + e < a.N) y[e] = __float2bfloat16_rn(__uint_as_float(r[e]));
+        return;
+    }
     if (a.mode == kEpiStoreF16) {
         __half* y = static_cast<__half*>(a.y) + (size_t)m * a.ldy + n;
         if (n + 32 <= a.N && (a.ldy % 8) == 0 && ((uintptr_t)a.y % 16) == 0) {
@@ -710,6 +718,11 @@ __global__ void __launch_bounds__(384, 1)
                             for (int j = 0; j < 16; ++j, p += a.ldy)
                                 if (j < mcount) *p = __uint_as_float(v[j]);
                         }
+                    } else if (a.mode == kEpiStoreBF16) {
+                        __nv_bfloat16* p = static_cast<__nv_bfloat16*>(a.y) + (size_t)m0 * a.ldy + n;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j, p += a.ldy)
+                            if (j < mcount) *p = __float2bfloat16_rn(__uint_as_float(v[j]));
                     } else {
                         __half* p = static_cast<__half*>(a.y) + (size_t)m0 * a.ldy + n;
 #pragma unroll

@@ -43,6 +43,7 @@ enum Q4Epilogue : int {
     kEpiStoreF16 = 1,  // y[m][n] = f16(acc)                  (f16)
     kEpiAddF32 = 2,    // y[m][n] += acc                      (f32, residual stream)
     kEpiSwiGLU = 3,    // y[m][j] = f16(silu(gate) * up)      (f16, pair-repacked weight)
+    kEpiStoreBF16 = 4, // y[m][n] = bf16(acc)                 (bf16: tensor-parallel partials)
 };
 
 struct Q4GemmArgs {

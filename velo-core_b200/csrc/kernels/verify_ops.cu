@@ -1,5 +1,6 @@
 // verify_ops.cu -- row / elementwise kernels of the verify forward, greedy
 // tree acceptance and the on-device KV commit.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "kernels/verify_ops.h"
@@ -53,6 +54,51 @@ __global__ void rmsnorm_f16_kernel(const float* __restrict__ x, const float* __r
         const float4 v = xr[i], g = wr[i];
         yr[2 * i] = __floats2half2_rn((v.x / rms) * g.x, (v.y / rms) * g.y);
         yr[2 * i + 1] = __floats2half2_rn((v.z / rms) * g.z, (v.w / rms) * g.w);
+    }
+}
+
+// Tensor parallelism: x[m] += sum (the bf16 all-reduced partials of a
+// row-split GEMM), then the RMSNorm of the new x as rmsnorm_f16_kernel.  The
+// block keeps its row in registers between the two passes (H <= 8192: at most
+// 8 float4 per thread of 256).
+__global__ void add_rmsnorm_f16_kernel(float* __restrict__ x, const __nv_bfloat16* __restrict__ sum,
+                                       const float* __restrict__ w, int H, float eps,
+                                       __half* __restrict__ y) {
+    __shared__ float sh[32];
+    constexpr int kMaxPer = 8;
+    const int m = blockIdx.x;
+    float4* xr = reinterpret_cast<float4*>(x + (size_t)m * H);
+    const __nv_bfloat162* sr = reinterpret_cast<const __nv_bfloat162*>(sum + (size_t)m * H);
+    float4 keep[kMaxPer];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < H / 4) {
+            float4 v = xr[i];
+            const float2 a = __bfloat1622float2(sr[2 * i]);
+            const float2 b = __bfloat1622float2(sr[2 * i + 1]);
+            v.x += a.x;
+            v.y += a.y;
+            v.z += b.x;
+            v.w += b.y;
+            xr[i] = v;
+            keep[j] = v;
+            ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    }
+    ss = block_sum(ss, sh);
+    const float rms = sqrtf(ss / (float)H + eps);
+    const float4* wr = reinterpret_cast<const float4*>(w);
+    __half2* yr = reinterpret_cast<__half2*>(y + (size_t)m * H);
+#pragma unroll
+    for (int j = 0; j < kMaxPer; ++j) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < H / 4) {
+            const float4 v = keep[j], g = wr[i];
+            yr[2 * i] = __floats2half2_rn((v.x / rms) * g.x, (v.y / rms) * g.y);
+            yr[2 * i + 1] = __floats2half2_rn((v.z / rms) * g.z, (v.w / rms) * g.w);
+        }
     }
 }
 
@@ -329,6 +375,14 @@ cudaError_t launch_rmsnorm_f16(const float* x, const float* w, int M, int H, flo
                                cudaStream_t s) {
     if (M == 0) return cudaSuccess;
     rmsnorm_f16_kernel<<<M, 256, 0, s>>>(x, w, H, eps, y);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add_rmsnorm_f16(float* x, const __nv_bfloat16* sum, const float* w, int M, int H,
+                                   float eps, __half* y, cudaStream_t s) {
+    if (M == 0) return cudaSuccess;
+    if (H % 4 || H / 4 > 256 * 8) return cudaErrorInvalidValue;
+    add_rmsnorm_f16_kernel<<<M, 256, 0, s>>>(x, sum, w, H, eps, y);
     return cudaGetLastError();
 }
 

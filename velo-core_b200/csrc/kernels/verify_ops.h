@@ -1,6 +1,7 @@
 // verify_ops.h -- the elementwise / row kernels of the verify-step forward and
 // the greedy tree acceptance and KV commit (verify_ops.cu).
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -35,6 +36,11 @@ cudaError_t launch_tree_greedy(const float* logits, const uint32_t* tokens, cons
 
 // Tensor parallelism: x += y (the all-reduced partial of a row-split GEMM).
 cudaError_t launch_add_f32(float* x, const float* y, size_t n, cudaStream_t s);
+
+// x[m] += sum[m] (bf16, the all-reduced partials of a row-split GEMM), then
+// y = f16(x / rms(x) * w) as launch_rmsnorm_f16 (H % 4 == 0, H <= 8192).
+cudaError_t launch_add_rmsnorm_f16(float* x, const __nv_bfloat16* sum, const float* w, int M, int H,
+                                   float eps, __half* y, cudaStream_t s);
 
 // Tensor parallelism, vocabulary-sharded LM head: per row the GreedySampler
 // maximum of this rank's logits [M][v_loc] as (value, global index) pairs

@@ -18,8 +18,15 @@
 // any stream capture.  All calls on a device share the one block, and it keeps
 // the contents of the last call: calls whose work overlaps on the GPU (two
 // streams, or two host threads) race on it and must be serialised by the
-// caller.  The completion tickets that must start at zero are cleared on the
-// caller's stream before each launch.
+// caller.  The completion tickets that must start at zero, and the error word,
+// are cleared on the caller's stream before each launch.
+//
+// The error word sits at a fixed place (the last 256 bytes of the block): a
+// draft token >= V is counted as a rejection and raises it, and
+// velo_cuda_accept_static_error copies it out, so a caller that cannot trust
+// its tokens can check each call without a context.  The block's address is
+// kept for the life of the process: do not use these entry points after a
+// cudaDeviceReset.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -57,6 +64,18 @@ int32_t scratch_address(int device, void** out) {
 
 size_t up256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+constexpr size_t kErrWordOffset = kStaticScratchBytes - 256;  // the error word's place
+
+int32_t current_block(char** base) {
+    int device = 0;
+    VELO_CUDA_TRY(cudaGetDevice(&device));
+    if (device < 0 || device >= kMaxDevices) return fail(VELO_ERR_INVALID_ARGUMENT, "device %d unsupported", device);
+    void* p = nullptr;
+    const int32_t st = scratch_address(device, &p);
+    *base = static_cast<char*>(p);
+    return st;
+}
+
 }  // namespace
 }  // namespace velo
 
@@ -82,7 +101,7 @@ extern "C" int32_t velo_cuda_accept_static(const float* target_logits, const flo
     if (!greedy && ((k > 0 && !draft_logits) || !uniforms))
         return fail(VELO_ERR_INVALID_ARGUMENT, "sampling needs draft_logits and uniforms");
 
-    // scratch layout: [workspace | tickets | device flag]
+    // scratch layout: [workspace | tickets | ... | error word (last 256 bytes)]
     const size_t ws = velo::up256(velo::accept_workspace_bytes(B, k, V, greedy));
     const size_t tk = velo::up256(velo::accept_counter_bytes(B));
     const size_t need = ws + tk + 256;
@@ -104,8 +123,10 @@ extern "C" int32_t velo_cuda_accept_static(const float* target_logits, const flo
 
     cudaStream_t s = (cudaStream_t)stream;
     char* b = (char*)base;
-    // tickets must be zero at launch; clearing them is a memset, not an allocation
-    VELO_CUDA_TRY(cudaMemsetAsync(b + ws, 0, tk + 256, s));
+    // tickets and the error word must be zero at launch; clearing them is a
+    // memset, not an allocation
+    VELO_CUDA_TRY(cudaMemsetAsync(b + ws, 0, tk, s));
+    VELO_CUDA_TRY(cudaMemsetAsync(b + velo::kErrWordOffset, 0, sizeof(int), s));
 
     velo::AcceptParams p{};
     p.tgt = target_logits;
@@ -114,7 +135,7 @@ extern "C" int32_t velo_cuda_accept_static(const float* target_logits, const flo
     p.u = uniforms;
     p.acc_len = accepted_len;
     p.bonus = bonus_token;
-    p.err_flag = (int*)(b + ws + tk);
+    p.err_flag = (int*)(b + velo::kErrWordOffset);
     p.B = B;
     p.k = k;
     p.V = V;
@@ -123,5 +144,16 @@ extern "C" int32_t velo_cuda_accept_static(const float* target_logits, const flo
              (greedy || k == 0 || (uintptr_t)draft_logits % 16 == 0);
     velo::accept_bind_buffers(p, b, b + ws, greedy);
     VELO_CUDA_TRY(velo::launch_accept(p, greedy, sm_count, s));
+    return VELO_OK;
+}
+
+extern "C" int32_t velo_cuda_accept_static_error(int32_t* flag_out, void* stream) {
+    velo::clear_last_error();
+    if (!flag_out) return fail(VELO_ERR_INVALID_ARGUMENT, "flag_out is NULL");
+    char* b = nullptr;
+    const int32_t st = velo::current_block(&b);
+    if (st) return st;
+    VELO_CUDA_TRY(cudaMemcpyAsync(flag_out, b + velo::kErrWordOffset, sizeof(int32_t),
+                                  cudaMemcpyDeviceToDevice, (cudaStream_t)stream));
     return VELO_OK;
 }

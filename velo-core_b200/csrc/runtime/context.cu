@@ -328,4 +328,99 @@ int32_t velo_cuda_accept(velo_cuda_ctx* c, const float* tgt, const float* drf,
     return velo_cuda_sync(c, -1);
 }
 
+// ---------------------------------------------------------------- tree acceptance
+
+static int32_t check_tree_args(int32_t B, int32_t N, int32_t V, float temperature, const void* tgt,
+                               const void* drf, const void* tok, const void* par, const void* u,
+                               const void* path, const void* plen, const void* bonus) {
+    if (B < 0) return fail(VELO_ERR_INVALID_ARGUMENT, "B = %d < 0", B);
+    if (N < 1) return fail(VELO_ERR_EMPTY_DRAFT_WINDOW, "n_nodes = %d: the tree needs its root", N);
+    if (N > velo::kAcceptMaxK) return fail(VELO_ERR_DRAFT_TOO_MANY, "n_nodes = %d > %d", N, velo::kAcceptMaxK);
+    if (V < 1 || V > velo::kAcceptMaxV)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "V = %d outside [1, %d]", V, velo::kAcceptMaxV);
+    if (!(temperature > 0.0f) || std::isinf(temperature))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "tree sampling needs a finite temperature > 0");
+    if (B == 0) return VELO_OK;
+    if (!tgt || !tok || !par || !u || !path || !plen || !bonus || (N > 1 && !drf))
+        return fail(VELO_ERR_INVALID_ARGUMENT, "NULL input / output buffer");
+    return VELO_OK;
+}
+
+static int32_t launch_tree(velo_cuda_ctx* c, const float* tgt, const float* drf, const uint32_t* tok,
+                           const int32_t* par, const float* u, int32_t B, int32_t N, int32_t V, float temperature,
+                           int32_t* path, int32_t* plen, uint32_t* bonus) {
+    velo::AcceptTreeParams p{};
+    p.tgt = tgt;
+    p.drf = drf;
+    p.tok = tok;
+    p.par = par;
+    p.u = u;
+    p.path = path;
+    p.path_len = plen;
+    p.bonus = bonus;
+    p.err_flag = c->err_flag;
+    p.B = B;
+    p.N = N;
+    p.V = V;
+    p.inv_t = 1.0f / temperature;
+    p.vec4 = (V % 4 == 0) && ((uintptr_t)tgt % 16 == 0) && (N == 1 || (uintptr_t)drf % 16 == 0);
+    VELO_CUDA_TRY(velo::launch_accept_tree(p, c->stream));
+    return VELO_OK;
+}
+
+int32_t velo_cuda_accept_tree_device(velo_cuda_ctx* c, const float* tgt, const float* drf,
+                                     const uint32_t* tok, const int32_t* par, const float* u, int32_t B,
+                                     int32_t N, int32_t V, float temperature, int32_t* path,
+                                     int32_t* path_len, uint32_t* bonus) {
+    velo::Range nvtx_range("velo.accept_tree_device");
+    velo::clear_last_error();
+    if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    int32_t st = check_tree_args(B, N, V, temperature, tgt, drf, tok, par, u, path, path_len, bonus);
+    if (st || B == 0) return st;
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    return launch_tree(c, tgt, drf, tok, par, u, B, N, V, temperature, path, path_len, bonus);
+}
+
+int32_t velo_cuda_accept_tree(velo_cuda_ctx* c, const float* tgt, const float* drf, const uint32_t* tok,
+                              const int32_t* par, const float* u, int32_t B, int32_t N, int32_t V,
+                              float temperature, int32_t* path, int32_t* path_len, uint32_t* bonus) {
+    velo::Range nvtx_range("velo.accept_tree");
+    velo::clear_last_error();
+    if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
+    int32_t st = check_tree_args(B, N, V, temperature, tgt, drf, tok, par, u, path, path_len, bonus);
+    if (st || B == 0) return st;
+    for (int32_t b = 0; b < B; ++b) {
+        if (par[(size_t)b * N] != -1)
+            return fail(VELO_ERR_INVALID_ARGUMENT, "node 0 of sequence %d must be the root (parent -1)", b);
+        for (int32_t n = 1; n < N; ++n) {
+            const int32_t q = par[(size_t)b * N + n];
+            if (q < 0 || q >= n) return fail(VELO_ERR_INVALID_ARGUMENT, "parents[%d][%d] = %d", b, n, q);
+            if (tok[(size_t)b * N + n] >= (uint32_t)V)
+                return fail(VELO_ERR_INVALID_ARGUMENT, "token %u >= V = %d", tok[(size_t)b * N + n], V);
+        }
+    }
+    VELO_CUDA_TRY(cudaSetDevice(c->device));
+    const size_t n_t = (size_t)B * N * V * 4, n_d = (size_t)B * (N - 1) * V * 4;
+    const size_t n_i = (size_t)B * N * 4;
+    auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    const size_t o_d = up(n_t), o_tok = o_d + up(n_d), o_par = o_tok + up(n_i), o_u = o_par + up(n_i);
+    const size_t o_path = o_u + up(n_i), o_len = o_path + up(n_i), o_bonus = o_len + up((size_t)B * 4);
+    st = c->io.ensure(o_bonus + up((size_t)B * 4), c->stream);
+    if (st) return st;
+    char* base = (char*)c->io.ptr;
+    VELO_CUDA_TRY(cudaMemcpyAsync(base, tgt, n_t, cudaMemcpyHostToDevice, c->stream));
+    if (n_d) VELO_CUDA_TRY(cudaMemcpyAsync(base + o_d, drf, n_d, cudaMemcpyHostToDevice, c->stream));
+    VELO_CUDA_TRY(cudaMemcpyAsync(base + o_tok, tok, n_i, cudaMemcpyHostToDevice, c->stream));
+    VELO_CUDA_TRY(cudaMemcpyAsync(base + o_par, par, n_i, cudaMemcpyHostToDevice, c->stream));
+    VELO_CUDA_TRY(cudaMemcpyAsync(base + o_u, u, n_i, cudaMemcpyHostToDevice, c->stream));
+    st = launch_tree(c, (const float*)base, (const float*)(base + o_d), (const uint32_t*)(base + o_tok),
+                     (const int32_t*)(base + o_par), (const float*)(base + o_u), B, N, V, temperature,
+                     (int32_t*)(base + o_path), (int32_t*)(base + o_len), (uint32_t*)(base + o_bonus));
+    if (st) return st;
+    VELO_CUDA_TRY(cudaMemcpyAsync(path, base + o_path, n_i, cudaMemcpyDeviceToHost, c->stream));
+    VELO_CUDA_TRY(cudaMemcpyAsync(path_len, base + o_len, (size_t)B * 4, cudaMemcpyDeviceToHost, c->stream));
+    VELO_CUDA_TRY(cudaMemcpyAsync(bonus, base + o_bonus, (size_t)B * 4, cudaMemcpyDeviceToHost, c->stream));
+    return velo_cuda_sync(c, -1);
+}
+
 }  // extern "C"

@@ -273,10 +273,16 @@ int32_t gguf_read_header(const uint8_t* buf, size_t n, GgufFile& g, uint64_t* he
         uint64_t bb, be;
         if (!ggml_block_params(ti.ggml_type, &bb, &be)) return fail(VELO_ERR_GGUF, "unknown ggml type %u", ti.ggml_type);
         if (!r.get(&ti.offset)) return eof();
+        // element count checked before every multiply, so no product can wrap
         unsigned __int128 ne = 1;
-        for (uint64_t d : ti.shape) ne *= d;
-        const unsigned __int128 nb = (ne + be - 1) / be * bb;
-        if (ne >> 64 || nb >> 64)
+        bool too_large = false;
+        for (uint64_t d : ti.shape) {
+            if (d != 0 && ne > (unsigned __int128)UINT64_MAX / d) too_large = true;
+            if (too_large) break;
+            ne *= d;
+        }
+        const unsigned __int128 nb = too_large ? 0 : (ne + be - 1) / be * bb;
+        if (too_large || ne >> 64 || nb >> 64)
             return fail(VELO_ERR_GGUF, "malformed GGUF: tensor %s is too large", ti.name.c_str());
         ti.nbytes = (uint64_t)nb;
         g.tensors[ti.name] = ti;  // a repeated name keeps the last entry
@@ -551,8 +557,18 @@ int32_t velo_gguf_weights(const velo_gguf* g, velo_weight_desc* out, int32_t cap
         else
             return fail(VELO_ERR_INVALID_ARGUMENT, "tensor %s: ggml type %u is not supported (F32, F16, Q4_0)",
                         t.name.c_str(), t.ggml_type);
+        // rows x cols in the tensor's encoding must be exactly its data bytes
+        // (the open-time check bounds every product by 2^64)
         uint64_t rows = 1;
         for (size_t d = 1; d < t.shape.size(); ++d) rows *= t.shape[d];
+        const uint64_t cols = t.shape.empty() ? 0 : t.shape[0];
+        const unsigned __int128 row_bytes = dt == VELO_DT_F32   ? (unsigned __int128)cols * 4
+                                            : dt == VELO_DT_F16 ? (unsigned __int128)cols * 2
+                                                                : (unsigned __int128)(cols / 32) * 18;
+        if ((dt == VELO_DT_Q4_0 && cols % 32) || row_bytes * rows != (unsigned __int128)t.nbytes)
+            return fail(VELO_ERR_INVALID_SHAPE, "tensor %s: %llu x %llu elements do not match its %llu bytes",
+                        t.name.c_str(), (unsigned long long)rows, (unsigned long long)cols,
+                        (unsigned long long)t.nbytes);
         out[k] = velo_weight_desc{g->names[k].c_str(), dt, 0u, g->file.data + t.offset, rows,
                                   t.shape.empty() ? 0 : t.shape[0]};
     }

@@ -34,7 +34,7 @@ int32_t velo_cuda_gemm_q4_0(velo_cuda_ctx* c, const void* w, const void* x, int3
     if (!c) return fail(VELO_ERR_INVALID_ARGUMENT, "ctx is NULL");
     if (M < 0 || N <= 0 || K <= 0 || K % 32)
         return fail(VELO_ERR_INVALID_ARGUMENT, "q4_0 GEMM: M = %d, N = %d, K = %d", M, N, K);
-    if (mode < velo::kEpiStoreF32 || mode > velo::kEpiSwiGLU)
+    if (mode < velo::kEpiStoreF32 || mode > velo::kEpiStoreBF16)
         return fail(VELO_ERR_INVALID_ARGUMENT, "q4_0 GEMM: epilogue mode %d unknown", mode);
     if (mode == velo::kEpiSwiGLU && N % 2)
         return fail(VELO_ERR_INVALID_ARGUMENT, "q4_0 GEMM: SwiGLU needs an even N (gate + up)");

@@ -7,6 +7,7 @@
 // all on the context stream.  The per-token loop of the reference
 // (LlamaCpuModel::forward_one, src/llama_cpu.rs:191-358, called k times by
 // verify_logits :401-419) becomes one pass over all B x N tree nodes.
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include <cmath>
@@ -15,6 +16,7 @@
 #include <string>
 #include <vector>
 
+#include "kernels/accept.h"
 #include "kernels/f32_path.h"
 #include "kernels/q4gemm.h"
 #include "kernels/tree_attn.h"
@@ -80,7 +82,15 @@ struct Model {
     float* attn32 = nullptr;   // [M][Hq D]
     float* h32 = nullptr;      // [M][F]
     float* logits = nullptr;   // [M][V_loc]
-    float* y = nullptr;        // [M][H] partial of a row-split GEMM (tp > 1)
+    float* y = nullptr;        // [M][H] partial of a row-split GEMM (tp > 1, fp32 path)
+    __nv_bfloat16* ybf = nullptr;  // [M][H] bf16 partial of a row-split GEMM (tp > 1)
+    // step profile (velo_cuda_profile): an event at the start of every phase
+    bool profile = false;
+    std::vector<cudaEvent_t> prof_ev;
+    std::vector<int> prof_cls;
+    size_t prof_n = 0;
+    double prof_ms[VELO_PHASE_COUNT] = {};
+    int prof_steps = 0;
     int2* pairs = nullptr;     // [M] this shard's argmax
     int2* pairs_all = nullptr; // [tp][M]
     float* logits_all = nullptr;  // [tp][M][V_loc] gathered shards (tp > 1)
@@ -135,6 +145,7 @@ void destroy_model(Model* m) {
     if (m->hin) cudaFreeHost(m->hin);
     if (m->hout) cudaFreeHost(m->hout);
     for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+    for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
     if (m->drf) cudaFree(m->drf);
     if (m->logits_all) cudaFree(m->logits_all);
     if (m->logits_full) cudaFree(m->logits_full);
@@ -337,7 +348,8 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
         if (!st) st = dev_alloc(m, &m->hbuf, (size_t)cM * F * 2, true);
     }
     if (!st) st = dev_alloc(m, &m->logits, (size_t)cM * m->V_loc * 4, true);
-    if (!st && m->tp > 1) st = dev_alloc(m, &m->y, (size_t)cM * H * 4, true);
+    if (!st && m->tp > 1 && m->f32) st = dev_alloc(m, &m->y, (size_t)cM * H * 4, true);
+    if (!st && m->tp > 1 && !m->f32) st = dev_alloc(m, &m->ybf, (size_t)cM * H * 2, true);
     if (!st) st = dev_alloc(m, &m->pairs, (size_t)cM * 8, true);
     if (!st) st = dev_alloc(m, &m->pairs_all, (size_t)cM * 8 * m->tp, true);
 
@@ -401,6 +413,47 @@ int32_t allreduce_add(velo_cuda_ctx* c, Model* m, int M) {
     if (st) return st;
     VELO_CUDA_TRY(launch_add_f32(m->x, m->y, n, c->stream));
     return VELO_OK;
+}
+
+// ybf (bf16 partials of this rank's row-split GEMM) summed over the group in
+// place; the RMSNorm that follows adds the sum to the residual
+// (launch_add_rmsnorm_f16).  A 16-bit sum moves half the bytes of an f32 one
+// over NVLink (33.5 MB instead of 67 MB per call at M = 2048, H = 8192).
+int32_t allreduce_bf16(velo_cuda_ctx* c, Model* m, int M) {
+    const NcclApi* nc = nccl_api();
+    if (!nc) return VELO_ERR_NCCL;
+    const size_t n = (size_t)M * m->H();
+    return nccl_check(nc->AllReduce(m->ybf, m->ybf, n, ncclBfloat16, ncclSum,
+                                    static_cast<ncclComm_t>(c->nccl_comm), c->stream),
+                      nc, "ncclAllReduce");
+}
+
+// Step profile: an event marks the start of a phase on the context stream.
+cudaError_t prof_mark(velo_cuda_ctx* c, Model* m, int cls) {
+    if (!m->profile) return cudaSuccess;
+    if (m->prof_n == m->prof_ev.size()) {
+        cudaEvent_t e;
+        cudaError_t err = cudaEventCreate(&e);
+        if (err != cudaSuccess) return err;
+        m->prof_ev.push_back(e);
+        m->prof_cls.push_back(0);
+    }
+    m->prof_cls[m->prof_n] = cls;
+    return cudaEventRecord(m->prof_ev[m->prof_n++], c->stream);
+}
+
+// After the step's sync: the time from each mark to the next goes to the
+// phase of the earlier mark.
+void prof_collect(Model* m) {
+    if (!m->profile) return;
+    for (size_t i = 0; i + 1 < m->prof_n; ++i) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, m->prof_ev[i], m->prof_ev[i + 1]) == cudaSuccess &&
+            m->prof_cls[i] >= 0 && m->prof_cls[i] < VELO_PHASE_COUNT)
+            m->prof_ms[m->prof_cls[i]] += ms;
+    }
+    if (m->prof_n) m->prof_steps++;
+    m->prof_n = 0;
 }
 
 // Full target rows [M][V] on every rank from the vocabulary shards
@@ -898,6 +951,7 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     if (in->commit < 0 || in->commit > 2 || (in->commit == 2 && sampling))
         return fail(VELO_ERR_INVALID_ARGUMENT, "commit mode %d (0, 1 or 2; 2 is greedy only)", in->commit);
     const int V = m->V();
+    bool chains = true;  // every sequence a chain: sampling takes the chain kernels
     for (int b = 0; b < B; ++b) {
         if (in->slots[b] >= (uint32_t)m->max_slots)
             return fail(VELO_ERR_INVALID_ARGUMENT, "slot %u >= max_slots", in->slots[b]);
@@ -911,9 +965,9 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         for (int i = 1; i < N; ++i) {
             const int p = in->parents[(size_t)b * N + i];
             if (p < 0 || p >= i) return fail(VELO_ERR_INVALID_ARGUMENT, "parents[%d][%d] = %d", b, i, p);
-            if ((sampling || in->commit == 2) && p != i - 1)
-                return fail(VELO_ERR_INVALID_ARGUMENT,
-                            "sampling and commit of every node take chains only (parents[n] = n-1)");
+            if (in->commit == 2 && p != i - 1)
+                return fail(VELO_ERR_INVALID_ARGUMENT, "commit of every node takes chains only (parents[n] = n-1)");
+            if (p != i - 1) chains = false;
         }
         for (int i = 0; i < N; ++i)
             if (in->tokens[(size_t)b * N + i] >= (uint32_t)V)
@@ -956,6 +1010,7 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     // the launch sequence of the step, from the ancestor masks to the KV commit
     auto body = [&]() -> int32_t {
     int32_t st = VELO_OK;
+    VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_OTHER));
     VELO_CUDA_TRY(velo::launch_tree_ancestors(m->parents, B, N, m->anc, c->err_flag, s));
     VELO_CUDA_TRY(velo::launch_embed(m->emb, m->tokens, M, H, m->V(), m->x, c->err_flag, s));
     const float eps = m->meta.norm_eps;
@@ -963,13 +1018,35 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         st = velo::forward_f32(c, m, B, N);
         if (st) return st;
     }
+    // With tp > 1 a row-split GEMM (o_proj, down_proj) leaves its bf16 partial
+    // in ybf, the group sums it in place, and the RMSNorm that follows adds it
+    // to the residual stream (`pending`).
+    bool pending = false;
+    auto norm = [&](const float* w) -> cudaError_t {
+        cudaError_t e = velo::prof_mark(c, m, VELO_PHASE_OTHER);
+        if (e != cudaSuccess) return e;
+        if (!pending) return velo::launch_rmsnorm_f16(m->x, w, M, H, eps, m->xn, s);
+        pending = false;
+        return velo::launch_add_rmsnorm_f16(m->x, m->ybf, w, M, H, eps, m->xn, s);
+    };
+    auto row_split = [&](const uint8_t* w, const __half* in, int K, int phase) -> int32_t {
+        VELO_CUDA_TRY(velo::prof_mark(c, m, phase));
+        if (m->tp == 1) return velo::gemm(c, w, in, M, H, K, m->x, H, velo::kEpiAddF32);
+        int32_t r = velo::gemm(c, w, in, M, H, K, m->ybf, H, velo::kEpiStoreBF16);
+        if (r) return r;
+        VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_ALLREDUCE));
+        pending = true;
+        return velo::allreduce_bf16(c, m, M);
+    };
     for (int l = 0; !m->f32 && l < L; ++l) {
         const velo::Layer& ly = m->layers[l];
         __half* nk = m->nk + (size_t)l * M * Hkv * 128;
         __half* nv = m->nv + (size_t)l * M * Hkv * 128;
-        VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, ly.attn_norm, M, H, eps, m->xn, s));
+        VELO_CUDA_TRY(norm(ly.attn_norm));
+        VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_GEMM_QKV));
         st = velo::gemm(c, ly.wqkv, m->xn, M, Nqkv, H, m->qkv, Nqkv, velo::kEpiStoreF32);
         if (st) return st;
+        VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_OTHER));
         VELO_CUDA_TRY(velo::launch_rope_split(m->qkv, m->anc, m->ctxlen, B, N, Hq, Hkv, m->meta.rope_freq_base,
                                               m->q, nk, nv, s));
         velo::TreeAttnArgs a{};
@@ -994,30 +1071,23 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         a.pool_pages = m->pool_pages;
         a.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
         a.err = c->err_flag;
+        VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_ATTENTION));
         VELO_CUDA_TRY(velo::launch_tree_attention(a, m->kv_int8 != 0, s));
-        if (m->tp == 1) {
-            st = velo::gemm(c, ly.wo, m->attn, M, H, Hq * 128, m->x, H, velo::kEpiAddF32);
-        } else {  // row-split o_proj: partial, all-reduce, residual add
-            st = velo::gemm(c, ly.wo, m->attn, M, H, Hq * 128, m->y, H, velo::kEpiStoreF32);
-            if (!st) st = velo::allreduce_add(c, m, M);
-        }
-        if (!st) VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, ly.ffn_norm, M, H, eps, m->xn, s));
-        if (!st) st = velo::gemm(c, ly.w13, m->xn, M, 2 * F, H, m->hbuf, F, velo::kEpiSwiGLU);
-        if (!st) {
-            if (m->tp == 1) {
-                st = velo::gemm(c, ly.w2, m->hbuf, M, H, F, m->x, H, velo::kEpiAddF32);
-            } else {  // row-split down_proj
-                st = velo::gemm(c, ly.w2, m->hbuf, M, H, F, m->y, H, velo::kEpiStoreF32);
-                if (!st) st = velo::allreduce_add(c, m, M);
-            }
-        }
+        st = row_split(ly.wo, m->attn, Hq * 128, VELO_PHASE_GEMM_O);
+        if (st) return st;
+        VELO_CUDA_TRY(norm(ly.ffn_norm));
+        VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_GEMM_FFN_UP));
+        st = velo::gemm(c, ly.w13, m->xn, M, 2 * F, H, m->hbuf, F, velo::kEpiSwiGLU);
+        if (!st) st = row_split(ly.w2, m->hbuf, F, VELO_PHASE_GEMM_FFN_DOWN);
         if (st) return st;
     }
     if (!m->f32) {
-        VELO_CUDA_TRY(velo::launch_rmsnorm_f16(m->x, m->out_norm, M, H, eps, m->xn, s));
+        VELO_CUDA_TRY(norm(m->out_norm));
+        VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_LM_HEAD));
         st = velo::gemm(c, m->lm_head, m->xn, M, Vl, H, m->logits, Vl, velo::kEpiStoreF32);
         if (st) return st;
     }
+    VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_ACCEPT_COMMIT));
     // acceptance
     velo::Range accept_range("velo.verify_step.accept_commit");
     if (m->tp > 1 && (!sampling || N == 1)) {
@@ -1056,6 +1126,29 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
             VELO_CUDA_TRY(cudaMalloc(&m->drf, need * 4));
             m->drf_cap = need;
         }
+        if (!chains) {
+            // trees: the walk, residuals and draw on the device, no host round trip
+            VELO_CUDA_TRY(cudaMemcpyAsync(m->drf, in->draft_logits, need * 4, cudaMemcpyHostToDevice, s));
+            VELO_CUDA_TRY(cudaMemcpyAsync(m->uni, in->uniforms, (size_t)B * N * 4, cudaMemcpyHostToDevice, s));
+            velo::AcceptTreeParams tp{};
+            tp.tgt = tgt;
+            tp.drf = m->drf;
+            tp.tok = m->tokens;
+            tp.par = m->parents;
+            tp.u = m->uni;
+            tp.path = m->path;
+            tp.path_len = m->path_len;
+            tp.bonus = m->bonus;
+            tp.err_flag = c->err_flag;
+            tp.B = B;
+            tp.N = N;
+            tp.V = V;
+            tp.inv_t = 1.0f / in->temperature;
+            tp.vec4 = (V % 4) == 0;
+            VELO_CUDA_TRY(velo::launch_accept_tree(tp, s));
+            goto sampled;
+        }
+        {
         std::vector<uint32_t> dt((size_t)B * k);
         for (int b = 0; b < B; ++b)
             for (int i = 0; i < k; ++i) dt[(size_t)b * k + i] = in->tokens[(size_t)b * N + i + 1];
@@ -1077,6 +1170,8 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         VELO_CUDA_TRY(cudaMemcpyAsync(m->path, path.data(), path.size() * 4, cudaMemcpyHostToDevice, s));
         VELO_CUDA_TRY(cudaMemcpyAsync(m->path_len, plen.data(), plen.size() * 4, cudaMemcpyHostToDevice, s));
         VELO_CUDA_TRY(cudaStreamSynchronize(s));
+        }
+    sampled:;
     }
     if (in->commit == 2) {
         // prefill / draft decode: the whole chain is committed and reported as
@@ -1126,13 +1221,14 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         a.err = c->err_flag;
         VELO_CUDA_TRY(velo::launch_kv_commit(a, s));
     }
+    VELO_CUDA_TRY(velo::prof_mark(c, m, -1));  // end of the step
     return st;
     };  // body
 
     // Greedy single-GPU steps replay a captured graph of the body (one
     // launch instead of ~25); sampling (host round trip) and tensor-parallel
     // steps run it directly.
-    const bool graphable = m->tp == 1 && !(sampling && N > 1) && !m->graphs_off;
+    const bool graphable = m->tp == 1 && !(sampling && N > 1) && !m->graphs_off && !m->profile;
     if (graphable) {
         const uint64_t key = ((uint64_t)B << 32) | ((uint64_t)N << 8) | (uint64_t)in->commit;
         auto it = m->graphs.find(key);
@@ -1183,6 +1279,7 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     st = velo_cuda_sync(c, -1);
     if (st) return st;
     m->staging_busy = false;
+    velo::prof_collect(m);
     if (!gathered.empty())  // [tp][M][Vl] -> [M][V]
         for (int r = 0; r < m->tp; ++r)
             for (int i = 0; i < M; ++i)
@@ -1193,6 +1290,29 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     std::memcpy(out->bonus_token, hp + B, (size_t)B * 4);
     if (out->accepted_nodes) std::memcpy(out->accepted_nodes, hp + 2 * B, (size_t)M * 4);
     if (want_expected) std::memcpy(out->expected, hp + 2 * B + M, (size_t)M * 4);
+    return VELO_OK;
+}
+
+int32_t velo_cuda_profile(velo_cuda_ctx* c, int32_t enable) {
+    velo::clear_last_error();
+    int32_t st = velo::check_model(c);
+    if (st) return st;
+    Model* m = c->model;
+    m->profile = enable != 0;
+    m->prof_n = 0;
+    m->prof_steps = 0;
+    for (double& v : m->prof_ms) v = 0.0;
+    return VELO_OK;
+}
+
+int32_t velo_cuda_profile_read(velo_cuda_ctx* c, double* ms, int32_t n, int32_t* steps) {
+    velo::clear_last_error();
+    int32_t st = velo::check_model(c);
+    if (st) return st;
+    if (!ms || n < VELO_PHASE_COUNT)
+        return fail(VELO_ERR_INVALID_ARGUMENT, "profile_read needs %d slots", (int)VELO_PHASE_COUNT);
+    for (int i = 0; i < VELO_PHASE_COUNT; ++i) ms[i] = c->model->prof_ms[i];
+    if (steps) *steps = c->model->prof_steps;
     return VELO_OK;
 }
 

@@ -77,6 +77,68 @@ def dequant_q4_0_f16(data, rows, cols):
     return (d[..., None] * q).astype(np.float16).reshape(rows, cols)
 
 
+def random_q4_0(rows, cols, seed=0, stream=10, sigma=0.02):
+    """q4_0 bytes [rows][cols/32*18] drawn directly in the quantised domain:
+    uniform random nibbles (q - 8 has standard deviation ~4.6) and per-block
+    f16 scales d = sigma / 4.6 * U(0.5, 1.5), so weights have standard
+    deviation ~sigma.  Generating the bytes takes a fraction of the time of
+    drawing and quantising normals at the 70B shapes."""
+    assert cols % 32 == 0
+    g = rng(seed, stream)
+    nb = cols // 32
+    out = np.frombuffer(g.bytes(rows * nb * 18), np.uint8).reshape(rows, nb, 18).copy()
+    d = (sigma / 4.6 * g.uniform(0.5, 1.5, (rows, nb))).astype(np.float16)
+    out[..., 0:2] = d.view(np.uint8).reshape(rows, nb, 2)
+    return out.reshape(rows, nb * 18)
+
+
+def dequant_q4_0_f32(data, rows, cols):
+    """f32 weights of q4_0 bytes as the reference dequantises them
+    (src/quant.rs:50-73: f16 scale widened to f32, times q - 8; the product is
+    exact in f32)."""
+    blk = np.ascontiguousarray(data, np.uint8).reshape(rows, cols // 32, 18)
+    d = blk[..., 0:2].copy().view(np.float16)[..., 0].astype(np.float32)
+    q = np.empty((rows, cols // 32, 32), np.float32)
+    q[..., 0::2] = (blk[..., 2:] & 15).astype(np.float32) - 8
+    q[..., 1::2] = (blk[..., 2:] >> 4).astype(np.float32) - 8
+    return (d[..., None] * q).reshape(rows, cols)
+
+
+def llama_random_q4_model(n_vocab, n_embd, n_layer, n_head, n_head_kv, n_ff, seed=0, sigma=0.02,
+                          norm_sigma=0.1, rope_freq_base=10000.0):
+    """A Llama model of the given shape with q4_0 matrices and embedding from
+    random_q4_0 (fast at the 7B / 70B layer shapes) and f32 norm weights
+    1 + N(0, norm_sigma^2); head_dim 128.  Same return as llama_model."""
+    hd = 128
+    meta = dict(n_vocab=n_vocab, n_embd=n_embd, n_layer=n_layer, n_head=n_head,
+                n_head_kv=n_head_kv, n_ff=n_ff, head_dim=hd, rope_freq_base=rope_freq_base,
+                norm_eps=1e-5)
+    g = rng(seed, 51)
+    st = [100]
+
+    def mat(rows, cols):
+        st[0] += 1
+        return (2, random_q4_0(rows, cols, seed, st[0], sigma), rows, cols)
+
+    def norm():
+        return (0, (1.0 + g.normal(0, norm_sigma, n_embd)).astype(np.float32), 1, n_embd)
+
+    t = {"token_embd.weight": mat(n_vocab, n_embd), "output_norm.weight": norm(),
+         "output.weight": mat(n_vocab, n_embd)}
+    for l in range(n_layer):
+        p = f"layers.{l}."
+        t[p + "attention_norm.weight"] = norm()
+        t[p + "attention.wq.weight"] = mat(n_head * hd, n_embd)
+        t[p + "attention.wk.weight"] = mat(n_head_kv * hd, n_embd)
+        t[p + "attention.wv.weight"] = mat(n_head_kv * hd, n_embd)
+        t[p + "attention.wo.weight"] = mat(n_embd, n_head * hd)
+        t[p + "ffn_norm.weight"] = norm()
+        t[p + "feed_forward.w1.weight"] = mat(n_ff, n_embd)
+        t[p + "feed_forward.w2.weight"] = mat(n_embd, n_ff)
+        t[p + "feed_forward.w3.weight"] = mat(n_ff, n_embd)
+    return meta, t
+
+
 def q4_0_weights(rows, cols, sigma=0.02, seed=0, stream=10):
     """Random-init weight N(0, sigma^2), quantised to q4_0."""
     w = rng(seed, stream).normal(0.0, sigma, (rows, cols)).astype(np.float32)

@@ -90,6 +90,11 @@ _SIGS = {
                                        _P, _P]),
     "velo_cuda_accept_static": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float, _P, _P,
                                        _P]),
+    "velo_cuda_accept_static_error": (_I32, [_P, _P]),
+    "velo_cuda_accept_tree": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float, _P, _P,
+                                     _P]),
+    "velo_cuda_accept_tree_device": (_I32, [_P, _P, _P, _P, _P, _P, _I32, _I32, _I32, ctypes.c_float,
+                                            _P, _P, _P]),
     "velo_cuda_q4_0_repacked_bytes": (ctypes.c_size_t, [_I32, _I32]),
     "velo_cuda_q4_0_repack": (_I32, [_P, _P, _P, _I32, _I32, _P]),
     "velo_cuda_gemm_q4_0": (_I32, [_P, _P, _P, _I32, _I32, _I32, _P, _I32, _I32]),
@@ -101,6 +106,8 @@ _SIGS = {
     "velo_cuda_read_kv": (_I32, [_P, ctypes.c_uint32, _I32, _I32, _I32, _P, _P, _P, _P]),
     "velo_cuda_verify_step": (_I32, [_P, _P, _P]),
     "velo_cuda_nccl_unique_id": (_I32, [_P]),
+    "velo_cuda_profile": (_I32, [_P, _I32]),
+    "velo_cuda_profile_read": (_I32, [_P, ctypes.POINTER(ctypes.c_double), _I32, ctypes.POINTER(_I32)]),
     "velo_cuda_shard_strategy": (_I32, [ctypes.c_char_p]),
     "velo_cuda_shard_weight": (_I32, [_P, _I32, _I32, _I32, _P, ctypes.c_size_t,
                                       ctypes.POINTER(ctypes.c_uint64),
@@ -174,7 +181,11 @@ class VerifyResult(ctypes.Structure):
     _fields_ = [("accepted_len", _P), ("accepted_nodes", _P), ("bonus_token", _P), ("logits", _P),
                 ("expected", _P)]
 
-EPI_STORE_F32, EPI_STORE_F16, EPI_ADD_F32, EPI_SWIGLU = 0, 1, 2, 3
+EPI_STORE_F32, EPI_STORE_F16, EPI_ADD_F32, EPI_SWIGLU, EPI_STORE_BF16 = 0, 1, 2, 3, 4
+
+# velo_phase: the step phases velo_cuda_profile times
+PHASES = ("other", "gemm_qkv", "attention", "gemm_o", "gemm_ffn_up", "gemm_ffn_down", "allreduce",
+          "lm_head", "accept_commit")
 
 
 def lib():
@@ -283,6 +294,31 @@ class Context:
             _ptr(bonus_token)))
 
     # ------------------------------------------------------------ q4_0 GEMM
+    def accept_tree(self, target_logits, draft_logits, tokens, parents, uniforms, temperature):
+        """Tree rejection sampling, host buffers: target [B][N][V], draft
+        [B][N-1][V], tokens / parents / uniforms [B][N].  Returns (path [B][N],
+        path_len [B], bonus [B])."""
+        tgt = np.ascontiguousarray(target_logits, np.float32)
+        B, N, V = tgt.shape
+        drf = np.ascontiguousarray(draft_logits, np.float32)
+        tok = np.ascontiguousarray(tokens, np.uint32).reshape(B, N)
+        par = np.ascontiguousarray(parents, np.int32).reshape(B, N)
+        u = np.ascontiguousarray(uniforms, np.float32).reshape(B, N)
+        path = np.zeros((B, N), np.int32)
+        plen = np.zeros(B, np.int32)
+        bonus = np.zeros(B, np.uint32)
+        check(lib().velo_cuda_accept_tree(self._h, _ptr(tgt), _ptr(drf), _ptr(tok), _ptr(par), _ptr(u), B,
+                                          N, V, float(temperature), _ptr(path), _ptr(plen), _ptr(bonus)))
+        return path, plen, bonus
+
+    def accept_tree_device(self, target_logits, draft_logits, tokens, parents, uniforms, temperature,
+                           path, path_len, bonus):
+        """Device-buffer form (torch CUDA tensors), asynchronous."""
+        B, N, V = target_logits.shape
+        check(lib().velo_cuda_accept_tree_device(
+            self._h, _ptr(target_logits), _ptr(draft_logits), _ptr(tokens), _ptr(parents), _ptr(uniforms),
+            B, N, V, float(temperature), _ptr(path), _ptr(path_len), _ptr(bonus)))
+
     def q4_0_repack(self, src, N, K, out, src_b=None):
         """Repack q4_0 rows (device uint8 [N][K/32*18], or two halves for a
         SwiGLU pair) into `out` (device, q4_0_repacked_bytes(N, K) bytes)."""
@@ -371,6 +407,17 @@ class Context:
         check(lib().velo_cuda_read_kv(self._h, slot, layer, pos0, n, _ptr(k), _ptr(v), _ptr(ks),
                                       _ptr(vs)))
         return (k, v, ks, vs) if int8 else (k, v)
+
+    def profile(self, enable=True):
+        """Start (or stop) timing the phases of the following verify steps."""
+        check(lib().velo_cuda_profile(self._h, 1 if enable else 0))
+
+    def profile_read(self):
+        """({phase name: total device ms}, profiled steps) since profile()."""
+        ms = (ctypes.c_double * len(PHASES))()
+        steps = _I32(0)
+        check(lib().velo_cuda_profile_read(self._h, ms, len(PHASES), ctypes.byref(steps)))
+        return {n: float(ms[i]) for i, n in enumerate(PHASES)}, int(steps.value)
 
     def verify_step(self, slots, ctx_len, tokens, parents, temperature=0.0, draft_logits=None,
                     uniforms=None, commit=True, want_logits=False, n_vocab=None):
@@ -630,3 +677,9 @@ def accept_static(target_logits, draft_logits, draft_tokens, uniforms, temperatu
         _ptr(target_logits), _ptr(draft_logits), _ptr(draft_tokens), _ptr(uniforms), B, k1 - 1,
         V, float(temperature), _ptr(accepted_len), _ptr(bonus_token),
         _P(stream_ptr) if stream_ptr else None))
+
+
+def accept_static_error(flag_out, stream_ptr=None):
+    """velo_cuda_accept_static_error: the last static call's input check into
+    flag_out (a one-element int32 CUDA tensor), asynchronously on stream_ptr."""
+    check(lib().velo_cuda_accept_static_error(_ptr(flag_out), _P(stream_ptr) if stream_ptr else None))
