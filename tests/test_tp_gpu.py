@@ -157,3 +157,63 @@ def test_tp2_sampling_chain_matches_acceptance_spec():
     for r in range(2):
         assert out[r][4] == int(ra[0])
         assert out[r][5] == int(rb[0])
+
+
+def _rank_tree_sampling(rank, tp, nid, meta, tensors, tokens, parents, q):
+    try:
+        import velo_cuda
+        ctx = velo_cuda.Context(device=rank, total_pages=32, max_slots=2, max_pages_per_slot=16,
+                                tp_rank=rank, tp_size=tp, nccl_id=nid)
+        ctx.load_model(meta, tensors)
+        ctx.bind_slot(0, np.arange(16))
+        N = len(tokens)
+        nv = meta["n_vocab"]
+        first = ctx.verify_step([0], [0], tokens[None], parents[None], commit=False,
+                                want_logits=True, n_vocab=nv)
+        g = np.random.default_rng(29)  # the same draft rows and uniforms on every rank
+        drf = (first["logits"][:, :N - 1] + g.normal(0, 0.3, (1, N - 1, nv))).astype(np.float32)
+        u = g.random((1, N)).astype(np.float32)
+        res = ctx.verify_step([0], [0], tokens[None], parents[None], temperature=0.8, draft_logits=drf,
+                              uniforms=u, commit=True, want_logits=True, n_vocab=nv)
+        ctx.close()
+        q.put((rank, res["logits"], drf, u, list(res["accepted_nodes"][0]), int(res["accepted_len"][0]),
+               int(res["bonus"][0]), None))
+    except Exception as e:  # report instead of hanging the peer
+        q.put((rank, None, None, None, [], 0, 0, repr(e)))
+
+
+def test_tp2_sampling_tree_matches_spec():
+    """Tree rejection sampling at T = 0.8 under TP = 2: both ranks take the
+    decisions of the tree spec (oracle vo_accept_tree) on the full rows."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    import velo_cuda
+    meta, tensors = synthetic.llama_q4_model(**SHAPE, seed=33)
+    g = synthetic.rng(34, 80)
+    N = 12
+    parents = synthetic.random_tree(N, 4, g)
+    tokens = g.integers(0, meta["n_vocab"], N).astype(np.uint32)
+    nid = velo_cuda.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank_tree_sampling, args=(r, 2, nid, meta, tensors, tokens, parents, q))
+          for r in range(2)]
+    for p in ps:
+        p.start()
+    out = {}
+    for _ in ps:
+        r = q.get(timeout=300)
+        out[r[0]] = r
+    for p in ps:
+        p.join(timeout=60)
+    for r in range(2):
+        assert out[r][7] is None, out[r][7]
+    lg, drf, u = out[0][1], out[0][2], out[0][3]
+    assert np.array_equal(lg, out[1][1])
+    rp, rl, rb = vo.accept_tree(lg, drf, tokens[None], parents[None], u, 0.8)
+    for r in range(2):
+        assert out[r][4] == list(rp[0])
+        assert out[r][5] == int(rl[0]) - 1
+        assert out[r][6] == int(rb[0])
