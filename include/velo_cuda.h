@@ -1,8 +1,8 @@
 /*
  * velo_cuda.h -- C ABI of the B200 (sm_100a) speculative-decoding verify step.
  *
- * This is the drop-in boundary a velo-core backend binds with `extern "C"`
- * (see INTEGRATION.md for the Rust side).  Plain pointers and sizes only; no
+ * This is the drop-in boundary a velo-core backend binds from Rust with an
+ * `extern "C"` block.  Plain pointers and sizes only; no
  * CUDA or torch types appear in any signature.  Device pointers are passed as
  * `void*` / typed pointers to device memory and are documented as such.
  *

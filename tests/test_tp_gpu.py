@@ -217,3 +217,68 @@ def test_tp2_sampling_tree_matches_spec():
         assert out[r][4] == list(rp[0])
         assert out[r][5] == int(rl[0]) - 1
         assert out[r][6] == int(rb[0])
+
+
+def _rank_halves(rank, tp, nid, meta, tensors, tokens, parents, q):
+    try:
+        import velo_cuda
+        B, N = tokens.shape
+        ctx = velo_cuda.Context(device=rank, total_pages=16 * B, max_slots=B, max_pages_per_slot=16,
+                                tp_rank=rank, tp_size=tp, nccl_id=nid)
+        ctx.load_model(meta, tensors)
+        for b in range(B):
+            ctx.bind_slot(b, np.arange(16 * b, 16 * b + 16))
+        slots = np.arange(B, dtype=np.uint32)
+        cl = np.zeros(B, np.int32)
+        nv = meta["n_vocab"]
+        os.environ.pop("VELO_TP_OVERLAP", None)
+        two = ctx.verify_step(slots, cl, tokens, parents, commit=False, want_logits=True, n_vocab=nv)
+        os.environ["VELO_TP_OVERLAP"] = "0"
+        one = ctx.verify_step(slots, cl, tokens, parents, commit=False, want_logits=True, n_vocab=nv)
+        os.environ.pop("VELO_TP_OVERLAP", None)
+        ctx.close()
+        q.put((rank, two["logits"], one["logits"], two["accepted_len"], two["bonus"], None))
+    except Exception as e:  # report instead of hanging the peer
+        q.put((rank, None, None, None, None, repr(e)))
+
+
+def test_tp2_two_stream_halves_match_one_stream_and_oracle():
+    """B = 3 sequences: the batch is cut into halves of 1 and 2 sequences on
+    two streams with two communicators.  The logits agree with the one-stream
+    loop's up to the order of the GEMMs' f32 k-sums (each persistent CTA
+    starts its k loop at its own offset, and halving M moves tiles between
+    CTAs) and with the unsharded oracle within 2e-2."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    import velo_cuda
+    meta, tensors = synthetic.llama_q4_model(**SHAPE, seed=41)
+    g = synthetic.rng(42, 80)
+    B, N = 3, 8
+    parents = np.stack([synthetic.random_tree(N, 4, g) for _ in range(B)])
+    tokens = g.integers(0, meta["n_vocab"], (B, N)).astype(np.uint32)
+    nid = velo_cuda.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank_halves, args=(r, 2, nid, meta, tensors, tokens, parents, q))
+          for r in range(2)]
+    for p in ps:
+        p.start()
+    out = {}
+    for _ in ps:
+        r = q.get(timeout=300)
+        out[r[0]] = r
+    for p in ps:
+        p.join(timeout=60)
+    for r in range(2):
+        assert out[r][5] is None, out[r][5]
+        assert np.abs(out[r][1] - out[r][2]).max() <= 1e-3
+    assert np.array_equal(out[0][1], out[1][1])
+    for b in range(B):
+        ora = vo.Model(dict(meta, n_ctx=64), synthetic.oracle_tensor_list(meta, tensors))
+        ref = ora.verify_tree(tokens[b], parents[b], 0)
+        assert np.abs(out[0][1][b] - ref).max() <= 2e-2
+        exp = np.array([vo.greedy(out[0][1][b, n])[0] for n in range(N)], np.uint32)
+        path, bonus = vo.find_best_path(parents[b], tokens[b], exp)
+        assert out[0][3][b] == len(path) - 1 and out[0][4][b] == bonus

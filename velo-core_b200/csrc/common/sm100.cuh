@@ -115,6 +115,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     }
 }
 
+// mbar_wait for an issuing warp whose barrier is usually complete already
+// (the MMA warp of a GEMM that its producers keep ahead of): a few
+// non-blocking tests first, which return sooner than a try_wait on a
+// completed phase, then the bounded wait.
+__device__ __forceinline__ bool mbar_wait_hot(uint64_t* bar, uint32_t parity, int* err, int code,
+                                              volatile int* abort) {
+    const uint32_t b = smem_u32(bar);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        if (mbar_test_wait(b, parity)) return true;
+    return mbar_wait(bar, parity, err, code, abort);
+}
+
 // ---------------------------------------------------------------- copies
 // 2-D tiled TMA load of a box at (c0 = inner, c1 = outer) into shared memory.
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, uint64_t* bar, int c0,

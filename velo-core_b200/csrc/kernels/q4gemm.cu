@@ -516,15 +516,17 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
 // memory.  The f16 weight tile then never passes through shared memory: per k
 // step the SM's shared memory sees the activation tile in (TMA) and out (MMA)
 // plus the 4.5 KiB raw tile, against 48 KiB of operand reads and 32 KiB of
-// dequantised stores with the weights as the B operand.  4 weight slots of 32
-// columns follow the accumulator(s).
+// dequantised stores with the weights as the B operand.  8 weight slots of 32
+// columns fill the 256 columns after the accumulator(s).
 //   warp 0      producer: per k step one input stage (128-row activation
 //               boxes by TMA + the raw q4_0 tile by bulk copy, one barrier)
 //   warp 1      MMA issue (warp-uniform loop, elected lane)
 //   warp 2      TMEM allocation (512 columns)
 //   warps 4-7   dequantisation, thread = weight row of the tile = TMEM lane
-//   warps 8-11  epilogue out of TMEM: thread = weight row, 16 activation rows
-//               per tcgen05.ld, coalesced across the warp
+//   warps 8-15  epilogue out of TMEM in two groups (8-11: the first half of
+//               the tile's activation rows, 12-15: the second): thread =
+//               weight row, 16 activation rows per tcgen05.ld, coalesced
+//               across the warp
 // BNT activation rows per tile (the MMA N): 256 with one accumulator, or 128
 // with two, so that the epilogue of a tile overlaps the next tile's main loop.
 template <int BNT>
@@ -534,15 +536,15 @@ struct TaCfg {
     static constexpr int X2_BYTES = BNT * BK * 2;       // 128-row TMA boxes
     static constexpr int IN_BYTES = ((X2_BYTES + kQ4TileBytes) + 1023) / 1024 * 1024;
     static constexpr int ISTAGES = BNT == 128 ? 8 : 5;
-    static constexpr int WSLOTS = 4;                    // TMEM weight slots, 32 columns each
+    static constexpr int WSLOTS = (512 - ACC * BNT) / 32;  // TMEM weight slots, 32 columns each (8)
     static constexpr uint32_t kColW = ACC * BNT;        // first weight slot column (256)
-    static constexpr int kThreads = 384;
+    static constexpr int kThreads = 512;                 // two epilogue groups (warps 8-11, 12-15)
     static constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + 1024 + 512;
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
 template <int BNT>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     q4_gemm_ta_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
     using C = TaCfg<BNT>;
     constexpr int ACC = C::ACC, X2_BYTES = C::X2_BYTES, IN_BYTES = C::IN_BYTES, ISTAGES = C::ISTAGES;
@@ -578,7 +580,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         for (int b = 0; b < ACC; ++b) {
             mbar_init(&afull[b], 1);
-            mbar_init(&aempty[b], kEpilogueThreads);
+            mbar_init(&aempty[b], 2 * kEpilogueThreads);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -627,8 +629,11 @@ __global__ void __launch_bounds__(384, 1)
             const uint32_t d = tmem + b * BNT;
             for (int kt = 0; kt < KT; ++kt, ++g) {
                 const int s = g % ISTAGES, ws = g % WSLOTS;
-                const bool ready = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag) &&
-                                   mbar_wait(&wfull[ws], (g / WSLOTS) & 1, a.err, kErrWaitReady, abort_flag);
+                // wfull implies ifull: the dequantisation threads arrive on
+                // wfull[ws] only after they observed ifull[s] (the stage's
+                // activation boxes and raw tile landed) and consumed it, so the
+                // acquire on wfull orders the activation reads too
+                const bool ready = mbar_wait_hot(&wfull[ws], (g / WSLOTS) & 1, a.err, kErrWaitReady, abort_flag);
                 if (!__all_sync(0xffffffffu, ready)) goto done;
                 tc_fence_after();
                 const uint64_t bd = desc_kmajor_sw128(smem_u32(sin + s * IN_BYTES));
@@ -658,9 +663,7 @@ __global__ void __launch_bounds__(384, 1)
                 const uint4 c0 = *reinterpret_cast<const uint4*>(raw + i * 16);
                 const uint4 c1 = *reinterpret_cast<const uint4*>(raw + kQ4Block1Off + i * 16);
                 const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + kQ4ScaleOff + i * 4);
-                ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
-                if (!__all_sync(0xffffffffu, ok)) goto done;
-                tc_fence_after();
+                // dequantise first: only the TMEM store waits for the slot to be free
                 const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc & 0xFFFF)));
                 const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc >> 16)));
                 const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
@@ -676,6 +679,9 @@ __global__ void __launch_bounds__(384, 1)
                     const uint4 v = dequant8(w1[q], d1);
                     r[16 + 4 * q] = v.x; r[16 + 4 * q + 1] = v.y; r[16 + 4 * q + 2] = v.z; r[16 + 4 * q + 3] = v.w;
                 }
+                ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
+                if (!__all_sync(0xffffffffu, ok)) goto done;
+                tc_fence_after();
                 tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 32, r);
                 // the input slot is released once the raw values were consumed
                 mbar_arrive(&iempty[s]);
@@ -685,8 +691,10 @@ __global__ void __launch_bounds__(384, 1)
             }
         }
     } else if (warp >= 8) {
-        // epilogue: thread = weight row (TMEM lane), 32 activation rows per load
+        // epilogue, two groups (warps 8-11 and 12-15) of one thread per weight
+        // row (TMEM lane), each draining half of the tile's activation rows
         const int q = warp & 3;
+        const int c0 = warp >= 12 ? BNT / 32 : 0;
         const int l = q * 32 + lane;  // weight row within the tile
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         uint32_t it = 0;
@@ -697,7 +705,7 @@ __global__ void __launch_bounds__(384, 1)
             if (!__all_sync(0xffffffffu, ok)) goto done;
             tc_fence_after();
 #pragma unroll 1
-            for (int c = 0; c < BNT / 16; ++c) {
+            for (int c = c0; c < c0 + BNT / 32; ++c) {
                 uint32_t v[16];
                 tmem_ld_32x32b_x16(tmem + lane_base + b * BNT + c * 16, v);
                 tmem_ld_wait();
@@ -752,16 +760,17 @@ done:
 // weight holds outputs 64t..64t+63 of tile t as gate rows 0..63 then up rows 64..127,
 // so for output 128u + l the dequant threads of lane l (one for the gate row,
 // one for the up row) read row (l & 63), resp. 64 + (l & 63), of tile 2u + (l >> 6).  With both values in one thread the epilogue
-// needs no exchange between warps.  The accumulator pair is single-buffered (3 weight
-// slots of 2 x 32 columns fill the rest of the 512 columns).
+// needs no exchange between warps.  The accumulator pair is single-buffered (4 weight
+// slots of 2 x 32 columns fill the other 256 of the 512 columns).
 namespace swi {
 constexpr int BNT = 128;                                // activation rows per tile
 constexpr int RAW2 = 2 * kQ4TileBytes;                  // the two repacked tiles of 128 outputs
 constexpr int IN_BYTES = ((X_BYTES + RAW2) + 1023) / 1024 * 1024;
 constexpr int ISTAGES = 7;
-constexpr int WSLOTS = 3;
+constexpr int WSLOTS = 4;
 constexpr uint32_t kColUp = 128, kColW = 256;           // up accumulator, first weight slot
-constexpr int kThreads = 512;                           // warps 4-7 gate rows, 12-15 up rows
+constexpr int kThreads = 640;                           // warps 4-7 gate rows, 12-15 up rows,
+                                                        // 8-11 and 16-19 the epilogue
 constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + 1024 + 512;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 }  // namespace swi
@@ -820,7 +829,7 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
             mbar_init(&wempty[s], 1);
         }
         mbar_init(afull, 1);
-        mbar_init(aempty, kEpilogueThreads);
+        mbar_init(aempty, 2 * kEpilogueThreads);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -867,8 +876,8 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
             tc_fence_after();
             for (int kt = 0; kt < KT; ++kt, ++g) {
                 const int s = g % ISTAGES, ws = g % WSLOTS;
-                const bool ready = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag) &&
-                                   mbar_wait(&wfull[ws], (g / WSLOTS) & 1, a.err, kErrWaitReady, abort_flag);
+                // wfull implies ifull (see q4_gemm_ta_kernel)
+                const bool ready = mbar_wait_hot(&wfull[ws], (g / WSLOTS) & 1, a.err, kErrWaitReady, abort_flag);
                 if (!__all_sync(0xffffffffu, ready)) goto done;
                 tc_fence_after();
                 const uint64_t bd = desc_kmajor_sw128(smem_u32(sin + s * IN_BYTES));
@@ -887,7 +896,7 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
             if (elect_one()) mma_commit(afull);
             __syncwarp();
         }
-    } else if ((warp >= 4 && warp < 8) || warp >= 12) {
+    } else if ((warp >= 4 && warp < 8) || (warp >= 12 && warp < 16)) {
         // dequantisation: warps 4-7 the gate rows, warps 12-15 the up rows; thread
         // l = output 128u + l = TMEM lane l
         const int l = (warp & 3) * 32 + lane;
@@ -901,12 +910,13 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
                 bool ok = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) goto done;
                 const uint8_t* raw = sin + s * IN_BYTES + X_BYTES + sel * kQ4TileBytes;
-                ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
-                if (!__all_sync(0xffffffffu, ok)) goto done;
-                tc_fence_after();
                 {
+                    // dequantise first: only the TMEM store waits for the slot to be free
                     uint32_t w[32];
                     dequant_row64(raw, r, w);
+                    ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
+                    if (!__all_sync(0xffffffffu, ok)) goto done;
+                    tc_fence_after();
                     tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 64 + 32 * up, w);
                 }
                 // the input slot is released once the raw values were consumed
@@ -916,9 +926,12 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
                 mbar_arrive(&wfull[ws]);
             }
         }
-    } else if (warp >= 8 && warp < 12) {
-        // epilogue: thread = output column 128u + l, 16 activation rows per load
+    } else if ((warp >= 8 && warp < 12) || warp >= 16) {
+        // epilogue, two groups (warps 8-11 and 16-19) of one thread per output
+        // column 128u + l, each draining half of the tile's activation rows,
+        // 16 rows per load
         const int q = warp & 3;
+        const int c0 = warp >= 16 ? BNT / 32 : 0;
         const int l = q * 32 + lane;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         const int F = a.N / 2;
@@ -930,7 +943,7 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
             tc_fence_after();
             const int n = u * 128 + l;
 #pragma unroll 1
-            for (int c = 0; c < BNT / 16; ++c) {
+            for (int c = c0; c < c0 + BNT / 32; ++c) {
                 uint32_t gv[16], uv[16];
                 tmem_ld_32x32b_x16(tmem + lane_base + c * 16, gv);
                 tmem_ld_32x32b_x16(tmem + lane_base + kColUp + c * 16, uv);

@@ -174,6 +174,12 @@ int32_t velo_cuda_create(const velo_cuda_config* cfg, int32_t device, int32_t tp
             return fail(VELO_ERR_NCCL, "ncclCommInitRank(rank %d of %d) failed: %s", tp_rank, tp_size, msg);
         }
         c->nccl_comm = comm;
+        // a second communicator over the same ranks (collective, same order
+        // on every rank); without ncclCommSplit the steps use one stream
+        if (nc->CommSplit) {
+            ncclComm_t comm2 = nullptr;
+            if (nc->CommSplit(comm, 0, tp_rank, &comm2, nullptr) == ncclSuccess) c->nccl_comm2 = comm2;
+        }
     }
     *out = c;
     return VELO_OK;
@@ -202,6 +208,10 @@ void velo_cuda_destroy(velo_cuda_ctx* c) {
     c->attn_ws.release();
     velo::destroy_model(c->model);
     c->model = nullptr;
+    if (c->nccl_comm2) {
+        if (const velo::NcclApi* nc = velo::nccl_api()) nc->CommDestroy(static_cast<ncclComm_t>(c->nccl_comm2));
+        c->nccl_comm2 = nullptr;
+    }
     if (c->nccl_comm) {
         if (const velo::NcclApi* nc = velo::nccl_api()) nc->CommDestroy(static_cast<ncclComm_t>(c->nccl_comm));
         c->nccl_comm = nullptr;

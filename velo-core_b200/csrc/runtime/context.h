@@ -77,4 +77,6 @@ struct velo_cuda_ctx {
     int* err_host = nullptr;       // pinned host copy of err_flag (read at sync)
     velo::Model* model = nullptr;  // weights, KV pool and verify buffers (velo_cuda_load_model)
     void* nccl_comm = nullptr;     // ncclComm_t of the tensor-parallel group (tp_size > 1)
+    void* nccl_comm2 = nullptr;    // a second communicator of the group (ncclCommSplit), so
+                                   // two halves of a batch reduce on two streams at once
 };

@@ -11,6 +11,7 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -84,6 +85,10 @@ struct Model {
     float* logits = nullptr;   // [M][V_loc]
     float* y = nullptr;        // [M][H] partial of a row-split GEMM (tp > 1, fp32 path)
     __nv_bfloat16* ybf = nullptr;  // [M][H] bf16 partial of a row-split GEMM (tp > 1)
+    // tensor parallelism: two halves of the batch on two streams (one NCCL
+    // communicator each) so that one half's all-reduce overlaps the other's GEMMs
+    cudaStream_t half_stream[2] = {nullptr, nullptr};
+    cudaEvent_t half_fork = nullptr, half_join[2] = {nullptr, nullptr};
     // step profile (velo_cuda_profile): an event at the start of every phase
     bool profile = false;
     std::vector<cudaEvent_t> prof_ev;
@@ -146,6 +151,11 @@ void destroy_model(Model* m) {
     if (m->hout) cudaFreeHost(m->hout);
     for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
+    for (int h = 0; h < 2; ++h) {
+        if (m->half_stream[h]) cudaStreamDestroy(m->half_stream[h]);
+        if (m->half_join[h]) cudaEventDestroy(m->half_join[h]);
+    }
+    if (m->half_fork) cudaEventDestroy(m->half_fork);
     if (m->drf) cudaFree(m->drf);
     if (m->logits_all) cudaFree(m->logits_all);
     if (m->logits_full) cudaFree(m->logits_full);
@@ -382,6 +392,21 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
     return VELO_OK;
 }
 
+int32_t gemm_on(velo_cuda_ctx* c, cudaStream_t s, const uint8_t* w, const __half* x, int M, int N, int K,
+                void* y, int ldy, int mode) {
+    Q4GemmArgs a{};
+    a.w = w;
+    a.N = N;
+    a.K = K;
+    a.M = M;
+    a.y = y;
+    a.ldy = ldy;
+    a.mode = mode;
+    a.err = c->err_flag;
+    VELO_CUDA_TRY(launch_q4_gemm(a, x, c->sm_count, s));
+    return VELO_OK;
+}
+
 int32_t gemm(velo_cuda_ctx* c, const uint8_t* w, const __half* x, int M, int N, int K, void* y,
              int ldy, int mode) {
     Q4GemmArgs a{};
@@ -426,6 +451,106 @@ int32_t allreduce_bf16(velo_cuda_ctx* c, Model* m, int M) {
     return nccl_check(nc->AllReduce(m->ybf, m->ybf, n, ncclBfloat16, ncclSum,
                                     static_cast<ncclComm_t>(c->nccl_comm), c->stream),
                       nc, "ncclAllReduce");
+}
+
+// Tensor-parallel layer loop with the batch cut in two halves, sequences
+// [0, B0) and [B0, B), each on its own stream with its own NCCL communicator:
+// the layer's work is issued half by half, so while one half's bf16
+// all-reduce after o_proj or down_proj crosses NVLink the other half's GEMMs
+// and attention keep the SMs busy.  Every row op is row-local (attention
+// reads only its own sequence), so each half runs the same kernels on its
+// row range; the results equal the single-stream loop's up to the order of
+// the GEMMs' f32 k-sums (tiles land on other CTAs, which start their k loops
+// at other offsets).  On return the context stream has joined both halves;
+// x holds the residual rows with the last sums added, xn the final RMSNorm.
+int32_t forward_tp_halves(velo_cuda_ctx* c, Model* m, int B, int N) {
+    const int H = m->H(), Hq = m->Hq(), Hkv = m->Hkv(), F = m->F(), L = m->L();
+    const int M = B * N, Nqkv = (Hq + 2 * Hkv) * 128;
+    const float eps = m->meta.norm_eps;
+    const NcclApi* nc = nccl_api();
+    if (!nc) return VELO_ERR_NCCL;
+    for (int h = 0; h < 2; ++h) {
+        if (!m->half_stream[h]) VELO_CUDA_TRY(cudaStreamCreateWithFlags(&m->half_stream[h], cudaStreamNonBlocking));
+        if (!m->half_join[h]) VELO_CUDA_TRY(cudaEventCreateWithFlags(&m->half_join[h], cudaEventDisableTiming));
+    }
+    if (!m->half_fork) VELO_CUDA_TRY(cudaEventCreateWithFlags(&m->half_fork, cudaEventDisableTiming));
+    const int bh[2] = {B / 2, B - B / 2}, b0[2] = {0, B / 2};
+    void* comm[2] = {c->nccl_comm, c->nccl_comm2};
+    VELO_CUDA_TRY(cudaEventRecord(m->half_fork, c->stream));
+    for (int h = 0; h < 2; ++h) VELO_CUDA_TRY(cudaStreamWaitEvent(m->half_stream[h], m->half_fork, 0));
+    bool pending[2] = {false, false};
+    auto rows = [&](int h) { return bh[h] * N; };
+    auto r0 = [&](int h) { return (size_t)b0[h] * N; };
+    auto norm = [&](int h, const float* w) -> cudaError_t {
+        const size_t o = r0(h) * H;
+        if (!pending[h]) return launch_rmsnorm_f16(m->x + o, w, rows(h), H, eps, m->xn + o, m->half_stream[h]);
+        pending[h] = false;
+        return launch_add_rmsnorm_f16(m->x + o, m->ybf + o, w, rows(h), H, eps, m->xn + o, m->half_stream[h]);
+    };
+    auto reduce = [&](int h) -> int32_t {
+        pending[h] = true;
+        return nccl_check(nc->AllReduce(m->ybf + r0(h) * H, m->ybf + r0(h) * H, (size_t)rows(h) * H, ncclBfloat16,
+                                        ncclSum, static_cast<ncclComm_t>(comm[h]), m->half_stream[h]),
+                          nc, "ncclAllReduce");
+    };
+    int32_t st = VELO_OK;
+    for (int l = 0; l < L; ++l) {
+        const Layer& ly = m->layers[l];
+        for (int h = 0; h < 2 && !st; ++h) {  // attention block
+            if (!bh[h]) continue;
+            cudaStream_t s = m->half_stream[h];
+            const size_t o = r0(h);
+            __half* nk = m->nk + (size_t)l * M * Hkv * 128 + o * Hkv * 128;
+            __half* nv = m->nv + (size_t)l * M * Hkv * 128 + o * Hkv * 128;
+            VELO_CUDA_TRY(norm(h, ly.attn_norm));
+            st = gemm_on(c, s, ly.wqkv, m->xn + o * H, rows(h), Nqkv, H, m->qkv + o * Nqkv, Nqkv, kEpiStoreF32);
+            if (st) return st;
+            VELO_CUDA_TRY(launch_rope_split(m->qkv + o * Nqkv, m->anc + o, m->ctxlen + b0[h], bh[h], N, Hq, Hkv,
+                                            m->meta.rope_freq_base, m->q + o * Hq * 128, nk, nv, s));
+            TreeAttnArgs a{};
+            const size_t lo = (size_t)l * m->layer_pool_elems() * m->kv_elt();
+            a.q = m->q + o * Hq * 128;
+            a.k_pool = static_cast<uint8_t*>(m->k_pool) + lo;
+            a.v_pool = static_cast<uint8_t*>(m->v_pool) + lo;
+            a.k_scale = m->kv_int8 ? m->k_scale + (size_t)l * m->layer_scale_elems() : nullptr;
+            a.v_scale = m->kv_int8 ? m->v_scale + (size_t)l * m->layer_scale_elems() : nullptr;
+            a.page_table = m->pt_batch + (size_t)b0[h] * m->max_pages;
+            a.ctx_len = m->ctxlen + b0[h];
+            a.node_k = nk;
+            a.node_v = nv;
+            a.anc = m->anc + o;
+            a.out = m->attn + o * Hq * 128;
+            a.out_f16 = 1;
+            a.B = bh[h];
+            a.N = N;
+            a.Hq = Hq;
+            a.Hkv = Hkv;
+            a.max_pages = m->max_pages;
+            a.pool_pages = m->pool_pages;
+            a.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
+            a.err = c->err_flag;
+            VELO_CUDA_TRY(launch_tree_attention(a, m->kv_int8 != 0, s));
+            st = gemm_on(c, s, ly.wo, m->attn + o * Hq * 128, rows(h), H, Hq * 128, m->ybf + o * H, H,
+                         kEpiStoreBF16);
+            if (!st) st = reduce(h);
+        }
+        for (int h = 0; h < 2 && !st; ++h) {  // feed-forward block
+            if (!bh[h]) continue;
+            cudaStream_t s = m->half_stream[h];
+            const size_t o = r0(h);
+            VELO_CUDA_TRY(norm(h, ly.ffn_norm));
+            st = gemm_on(c, s, ly.w13, m->xn + o * H, rows(h), 2 * F, H, m->hbuf + o * F, F, kEpiSwiGLU);
+            if (!st) st = gemm_on(c, s, ly.w2, m->hbuf + o * F, rows(h), H, F, m->ybf + o * H, H, kEpiStoreBF16);
+            if (!st) st = reduce(h);
+        }
+        if (st) return st;
+    }
+    for (int h = 0; h < 2; ++h) {
+        if (bh[h]) VELO_CUDA_TRY(norm(h, m->out_norm));
+        VELO_CUDA_TRY(cudaEventRecord(m->half_join[h], m->half_stream[h]));
+        VELO_CUDA_TRY(cudaStreamWaitEvent(c->stream, m->half_join[h], 0));
+    }
+    return VELO_OK;
 }
 
 // Step profile: an event marks the start of a phase on the context stream.
@@ -1038,7 +1163,17 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         pending = true;
         return velo::allreduce_bf16(c, m, M);
     };
-    for (int l = 0; !m->f32 && l < L; ++l) {
+    // tensor parallel with a second communicator: the two-stream loop (which
+    // also leaves the final RMSNorm in xn); profiled steps keep one stream so
+    // each phase can be timed
+    const char* ov = std::getenv("VELO_TP_OVERLAP");
+    const bool halves = m->tp > 1 && !m->f32 && c->nccl_comm2 && B >= 2 && !m->profile &&
+                        !(ov && std::strcmp(ov, "0") == 0);
+    if (halves) {
+        st = velo::forward_tp_halves(c, m, B, N);
+        if (st) return st;
+    }
+    for (int l = 0; !m->f32 && !halves && l < L; ++l) {
         const velo::Layer& ly = m->layers[l];
         __half* nk = m->nk + (size_t)l * M * Hkv * 128;
         __half* nv = m->nv + (size_t)l * M * Hkv * 128;
@@ -1082,7 +1217,7 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         if (st) return st;
     }
     if (!m->f32) {
-        VELO_CUDA_TRY(norm(m->out_norm));
+        if (!halves) VELO_CUDA_TRY(norm(m->out_norm));
         VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_LM_HEAD));
         st = velo::gemm(c, m->lm_head, m->xn, M, Vl, H, m->logits, Vl, velo::kEpiStoreF32);
         if (st) return st;

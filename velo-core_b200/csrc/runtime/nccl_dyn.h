@@ -14,6 +14,7 @@ struct NcclApi {
     decltype(&ncclAllReduce) AllReduce = nullptr;
     decltype(&ncclAllGather) AllGather = nullptr;
     decltype(&ncclGetErrorString) GetErrorString = nullptr;
+    decltype(&ncclCommSplit) CommSplit = nullptr;  // optional (NCCL >= 2.18)
 };
 
 // The resolved API, or nullptr (message via set_last_error) if NCCL cannot be loaded.

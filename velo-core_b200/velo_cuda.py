@@ -1,7 +1,7 @@
 """Python view of the velo_cuda C ABI (include/velo_cuda.h), through ctypes.
 
 This is the host-side harness the tests and bench.py use; it calls the same
-extern "C" entry points a Rust backend binds (see INTEGRATION.md).  There is
+extern "C" entry points a Rust backend binds.  There is
 no fallback: if libvelo_cuda.so is missing, importing fails loudly.
 
 Errors mirror the reference: every non-zero status raises VeloError whose
