@@ -53,7 +53,9 @@ def _inputs(M, N, K, seed):
 # 128-row activation tiles except at many waves ((2048, 10240, 256): 256-row tiles).
 @pytest.mark.parametrize("M,N,K", [(1, 256, 64), (5, 300, 96), (128, 512, 256), (200, 1000, 512),
                                    (512, 4096, 4096), (130, 256, 11008), (640, 7680, 512),
-                                   (512, 12288, 1024), (2048, 10240, 256), (300, 700, 96)])
+                                   (512, 12288, 1024), (2048, 10240, 256), (300, 700, 96),
+                                   # odd k-tile counts (the kernels step over two 64-k tiles)
+                                   (384, 640, 192), (260, 1024, 4160)])
 def test_gemm_f32_matches_oracle(ctx, M, N, K):
     q4, x16 = _inputs(M, N, K, seed=M + N + K)
     y = _run(ctx, q4, N, K, x16, velo_cuda.EPI_STORE_F32)
@@ -98,7 +100,8 @@ def test_gemm_f16_and_residual_add(ctx):
     assert np.abs(ya - (resid + ref)).max() <= TOL_ORACLE
 
 
-@pytest.mark.parametrize("M,F,K", [(64, 688, 256), (512, 1408, 1024), (1280, 2048, 256), (200, 688, 96)])
+@pytest.mark.parametrize("M,F,K", [(64, 688, 256), (512, 1408, 1024), (1280, 2048, 256), (200, 688, 96),
+                                   (300, 640, 192), (256, 512, 4160)])
 def test_gemm_swiglu_pair(ctx, M, F, K):
     """w1 (gate) and w3 (up) repacked as a pair: y = silu(x w1^T) * (x w3^T),
     llama_cpu.rs:326-341."""

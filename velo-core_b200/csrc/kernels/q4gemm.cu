@@ -156,6 +156,27 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, __half2 d2) {
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
+// Row `row` of a repacked q4_0 tile (k 0..63) as 32 f16 pairs, lower k in the low half.
+__device__ __forceinline__ void dequant_row64(const uint8_t* tile, int row, uint32_t (&r)[32]) {
+    const uint4 c0 = *reinterpret_cast<const uint4*>(tile + row * 16);
+    const uint4 c1 = *reinterpret_cast<const uint4*>(tile + kQ4Block1Off + row * 16);
+    const uint32_t sc = *reinterpret_cast<const uint32_t*>(tile + kQ4ScaleOff + row * 4);
+    const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc & 0xFFFF)));
+    const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc >> 16)));
+    const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
+    const uint32_t w1[4] = {c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint4 v = dequant8(w0[q], d0);
+        r[4 * q] = v.x; r[4 * q + 1] = v.y; r[4 * q + 2] = v.z; r[4 * q + 3] = v.w;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint4 v = dequant8(w1[q], d1);
+        r[16 + 4 * q] = v.x; r[16 + 4 * q + 1] = v.y; r[16 + 4 * q + 2] = v.z; r[16 + 4 * q + 3] = v.w;
+    }
+}
+
 // ---------------------------------------------------------------- epilogue
 __device__ __forceinline__ void store_row32(const Q4GemmArgs& a, int m, int n, const uint32_t (&r)[32]) {
     if (a.mode == kEpiStoreBF16) {
@@ -529,14 +550,22 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
 //               across the warp
 // BNT activation rows per tile (the MMA N): 256 with one accumulator, or 128
 // with two, so that the epilogue of a tile overlaps the next tile's main loop.
+// A pipeline step covers KSUB = 2 k tiles of 64 (k 128): one stage holds the
+// activation boxes and the raw q4_0 tiles of both, one weight slot their 64
+// dequantised columns, and the MMA warp waits once and commits twice per 16
+// MMAs instead of per 8, which halves the per-step barrier round trips that
+// leave the tensor pipe idle between steps.  An odd k-tile count ends with a
+// one-tile step.
+constexpr int KSUB = 2;
+
 template <int BNT>
 struct TaCfg {
     static_assert(BNT == 128 || BNT == 256, "activation tile");
     static constexpr int ACC = BNT == 128 ? 2 : 1;      // accumulator buffers
-    static constexpr int X2_BYTES = BNT * BK * 2;       // 128-row TMA boxes
-    static constexpr int IN_BYTES = ((X2_BYTES + kQ4TileBytes) + 1023) / 1024 * 1024;
-    static constexpr int ISTAGES = BNT == 128 ? 8 : 5;
-    static constexpr int WSLOTS = (512 - ACC * BNT) / 32;  // TMEM weight slots, 32 columns each (8)
+    static constexpr int X2_BYTES = BNT * BK * 2;       // one k tile of 128-row TMA boxes
+    static constexpr int IN_BYTES = ((KSUB * (X2_BYTES + kQ4TileBytes)) + 1023) / 1024 * 1024;
+    static constexpr int ISTAGES = BNT == 128 ? 5 : 3;
+    static constexpr int WSLOTS = (512 - ACC * BNT) / (32 * KSUB);  // TMEM weight slots (4)
     static constexpr uint32_t kColW = ACC * BNT;        // first weight slot column (256)
     static constexpr int kThreads = 512;                 // two epilogue groups (warps 8-11, 12-15)
     static constexpr size_t kSmemBytes = (size_t)ISTAGES * IN_BYTES + 1024 + 512;
@@ -564,10 +593,11 @@ __global__ void __launch_bounds__(512, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int KT = (a.K + BK - 1) / BK;
+    const int KT = (a.K + BK - 1) / BK;                 // k tiles of 64
+    const int KS = (KT + KSUB - 1) / KSUB;               // pipeline steps
     const int MT = (a.M + BNT - 1) / BNT;
     const int n_tiles = MT * q4_n_tiles(a.N);
-    const int kt0 = (int)((blockIdx.x * 5u) % (unsigned)KT);
+    const int ks0 = (int)((blockIdx.x * 5u) % (unsigned)KS);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ISTAGES; ++s) {
@@ -601,18 +631,23 @@ __global__ void __launch_bounds__(512, 1)
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             const int mt = tile % MT, nt = tile / MT;
             const uint8_t* wt = a.w + (size_t)nt * KT * kQ4TileBytes;
-            for (int kt = 0; kt < KT; ++kt, ++g) {
+            for (int ks = 0; ks < KS; ++ks, ++g) {
                 const int s = g % ISTAGES;
                 const bool ok = mbar_wait(&iempty[s], ((g / ISTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) goto done;
-                const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
+                const int kj = ks + ks0 < KS ? ks + ks0 : ks + ks0 - KS;
+                const int kk = kj * KSUB, nsub = kk + 1 < KT ? KSUB : 1;
                 if (elect_one()) {
+                    // stage: [k tile kk boxes | k tile kk + 1 boxes | raw tiles kk, kk + 1]
                     uint8_t* st = sin + s * IN_BYTES;
-                    mbar_arrive_expect_tx(&ifull[s], X2_BYTES + kQ4TileBytes);
+                    mbar_arrive_expect_tx(&ifull[s], nsub * (X2_BYTES + kQ4TileBytes));
+                    for (int sub = 0; sub < nsub; ++sub)
 #pragma unroll
-                    for (int xb = 0; xb < BNT / BM; ++xb)
-                        tma_load_2d(st + xb * X_BYTES, &tmx, &ifull[s], kk * BK, mt * BNT + xb * BM);
-                    bulk_load(st + X2_BYTES, wt + (size_t)kk * kQ4TileBytes, kQ4TileBytes, &ifull[s]);
+                        for (int xb = 0; xb < BNT / BM; ++xb)
+                            tma_load_2d(st + sub * X2_BYTES + xb * X_BYTES, &tmx, &ifull[s], (kk + sub) * BK,
+                                        mt * BNT + xb * BM);
+                    bulk_load(st + KSUB * X2_BYTES, wt + (size_t)kk * kQ4TileBytes, nsub * kQ4TileBytes,
+                              &ifull[s]);
                 }
                 __syncwarp();
             }
@@ -627,20 +662,25 @@ __global__ void __launch_bounds__(512, 1)
             if (!__all_sync(0xffffffffu, ok)) goto done;
             tc_fence_after();
             const uint32_t d = tmem + b * BNT;
-            for (int kt = 0; kt < KT; ++kt, ++g) {
+            for (int ks = 0; ks < KS; ++ks, ++g) {
                 const int s = g % ISTAGES, ws = g % WSLOTS;
+                const int kj = ks + ks0 < KS ? ks + ks0 : ks + ks0 - KS;
+                const int nsub = kj * KSUB + 1 < KT ? KSUB : 1;
                 // wfull implies ifull: the dequantisation threads arrive on
                 // wfull[ws] only after they observed ifull[s] (the stage's
-                // activation boxes and raw tile landed) and consumed it, so the
+                // activation boxes and raw tiles landed) and consumed it, so the
                 // acquire on wfull orders the activation reads too
                 const bool ready = mbar_wait_hot(&wfull[ws], (g / WSLOTS) & 1, a.err, kErrWaitReady, abort_flag);
                 if (!__all_sync(0xffffffffu, ready)) goto done;
                 tc_fence_after();
-                const uint64_t bd = desc_kmajor_sw128(smem_u32(sin + s * IN_BYTES));
                 if (elect_one()) {
+                    for (int sub = 0; sub < nsub; ++sub) {
+                        const uint64_t bd = desc_kmajor_sw128(smem_u32(sin + s * IN_BYTES + sub * X2_BYTES));
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k)
-                        mma_f16_ts(d, tmem + kColW + ws * 32 + k * 8, bd + 2 * k, idesc, (kt | k) != 0);
+                        for (int k = 0; k < BK / 16; ++k)
+                            mma_f16_ts(d, tmem + kColW + ws * (32 * KSUB) + sub * 32 + k * 8, bd + 2 * k, idesc,
+                                       (ks | sub | k) != 0);
+                    }
                     mma_commit(&iempty[s]);
                     mma_commit(&wempty[ws]);
                 }
@@ -655,34 +695,22 @@ __global__ void __launch_bounds__(512, 1)
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         uint32_t g = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-            for (int kt = 0; kt < KT; ++kt, ++g) {
+            for (int ks = 0; ks < KS; ++ks, ++g) {
                 const int s = g % ISTAGES, ws = g % WSLOTS;
+                const int kj = ks + ks0 < KS ? ks + ks0 : ks + ks0 - KS;
+                const int nsub = kj * KSUB + 1 < KT ? KSUB : 1;
                 bool ok = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) goto done;
-                const uint8_t* raw = sin + s * IN_BYTES + X2_BYTES;
-                const uint4 c0 = *reinterpret_cast<const uint4*>(raw + i * 16);
-                const uint4 c1 = *reinterpret_cast<const uint4*>(raw + kQ4Block1Off + i * 16);
-                const uint32_t sc = *reinterpret_cast<const uint32_t*>(raw + kQ4ScaleOff + i * 4);
-                // dequantise first: only the TMEM store waits for the slot to be free
-                const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc & 0xFFFF)));
-                const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc >> 16)));
-                const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
-                const uint32_t w1[4] = {c1.x, c1.y, c1.z, c1.w};
-                uint32_t r[32];  // k 0..63 of row i as 32 f16 pairs (lower k in the low half)
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint4 v = dequant8(w0[q], d0);
-                    r[4 * q] = v.x; r[4 * q + 1] = v.y; r[4 * q + 2] = v.z; r[4 * q + 3] = v.w;
+                for (int sub = 0; sub < nsub; ++sub) {
+                    uint32_t r[32];  // k 0..63 of the sub tile as 32 f16 pairs (lower k in the low half)
+                    dequant_row64(sin + s * IN_BYTES + KSUB * X2_BYTES + sub * kQ4TileBytes, i, r);
+                    if (sub == 0) {  // dequantise first: only the TMEM store waits for the slot
+                        ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
+                        if (!__all_sync(0xffffffffu, ok)) goto done;
+                        tc_fence_after();
+                    }
+                    tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * (32 * KSUB) + sub * 32, r);
                 }
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint4 v = dequant8(w1[q], d1);
-                    r[16 + 4 * q] = v.x; r[16 + 4 * q + 1] = v.y; r[16 + 4 * q + 2] = v.z; r[16 + 4 * q + 3] = v.w;
-                }
-                ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
-                if (!__all_sync(0xffffffffu, ok)) goto done;
-                tc_fence_after();
-                tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 32, r);
                 // the input slot is released once the raw values were consumed
                 mbar_arrive(&iempty[s]);
                 tmem_st_wait();
@@ -760,14 +788,15 @@ done:
 // weight holds outputs 64t..64t+63 of tile t as gate rows 0..63 then up rows 64..127,
 // so for output 128u + l the dequant threads of lane l (one for the gate row,
 // one for the up row) read row (l & 63), resp. 64 + (l & 63), of tile 2u + (l >> 6).  With both values in one thread the epilogue
-// needs no exchange between warps.  The accumulator pair is single-buffered (4 weight
-// slots of 2 x 32 columns fill the other 256 of the 512 columns).
+// needs no exchange between warps.  The accumulator pair is single-buffered (2 weight
+// slots of KSUB x 2 x 32 columns fill the other 256 of the 512 columns).
 namespace swi {
 constexpr int BNT = 128;                                // activation rows per tile
 constexpr int RAW2 = 2 * kQ4TileBytes;                  // the two repacked tiles of 128 outputs
-constexpr int IN_BYTES = ((X_BYTES + RAW2) + 1023) / 1024 * 1024;
-constexpr int ISTAGES = 7;
-constexpr int WSLOTS = 4;
+// stage: [k tile kk boxes | k tile kk + 1 boxes | raw tile 2u: kk, kk + 1 | raw tile 2u + 1: kk, kk + 1]
+constexpr int IN_BYTES = ((KSUB * (X_BYTES + RAW2)) + 1023) / 1024 * 1024;
+constexpr int ISTAGES = 4;
+constexpr int WSLOTS = 2;                               // 128 columns each: per k tile gate 32 | up 32
 constexpr uint32_t kColUp = 128, kColW = 256;           // up accumulator, first weight slot
 constexpr int kThreads = 640;                           // warps 4-7 gate rows, 12-15 up rows,
                                                         // 8-11 and 16-19 the epilogue
@@ -777,25 +806,6 @@ static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-__device__ __forceinline__ void dequant_row64(const uint8_t* tile, int row, uint32_t (&r)[32]) {
-    const uint4 c0 = *reinterpret_cast<const uint4*>(tile + row * 16);
-    const uint4 c1 = *reinterpret_cast<const uint4*>(tile + kQ4Block1Off + row * 16);
-    const uint32_t sc = *reinterpret_cast<const uint32_t*>(tile + kQ4ScaleOff + row * 4);
-    const __half2 d0 = __half2half2(__ushort_as_half((uint16_t)(sc & 0xFFFF)));
-    const __half2 d1 = __half2half2(__ushort_as_half((uint16_t)(sc >> 16)));
-    const uint32_t w0[4] = {c0.x, c0.y, c0.z, c0.w};
-    const uint32_t w1[4] = {c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const uint4 v = dequant8(w0[q], d0);
-        r[4 * q] = v.x; r[4 * q + 1] = v.y; r[4 * q + 2] = v.z; r[4 * q + 3] = v.w;
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const uint4 v = dequant8(w1[q], d1);
-        r[16 + 4 * q] = v.x; r[16 + 4 * q + 1] = v.y; r[16 + 4 * q + 2] = v.z; r[16 + 4 * q + 3] = v.w;
-    }
-}
 
 __global__ void __launch_bounds__(swi::kThreads, 1)
     q4_gemm_ta_swiglu_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
@@ -814,10 +824,11 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int KT = (a.K + BK - 1) / BK;
+    const int KT = (a.K + BK - 1) / BK;                 // k tiles of 64
+    const int KS = (KT + KSUB - 1) / KSUB;               // pipeline steps
     const int MT = (a.M + BNT - 1) / BNT;
     const int n_tiles = MT * (q4_n_tiles(a.N) / 2);       // 128 outputs per tile
-    const int kt0 = (int)((blockIdx.x * 5u) % (unsigned)KT);
+    const int ks0 = (int)((blockIdx.x * 5u) % (unsigned)KS);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ISTAGES; ++s) {
@@ -849,19 +860,21 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
             const int mt = tile % MT, u = tile / MT;
             const uint8_t* wt = a.w + (size_t)(2 * u) * KT * kQ4TileBytes;
-            for (int kt = 0; kt < KT; ++kt, ++g) {
+            for (int ks = 0; ks < KS; ++ks, ++g) {
                 const int s = g % ISTAGES;
                 const bool ok = mbar_wait(&iempty[s], ((g / ISTAGES) & 1) ^ 1, a.err, kErrWaitEmpty, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) goto done;
-                const int kk = kt + kt0 < KT ? kt + kt0 : kt + kt0 - KT;
+                const int kj = ks + ks0 < KS ? ks + ks0 : ks + ks0 - KS;
+                const int kk = kj * KSUB, nsub = kk + 1 < KT ? KSUB : 1;
                 if (elect_one()) {
                     uint8_t* st = sin + s * IN_BYTES;
-                    mbar_arrive_expect_tx(&ifull[s], X_BYTES + RAW2);
-                    tma_load_2d(st, &tmx, &ifull[s], kk * BK, mt * BNT);
+                    mbar_arrive_expect_tx(&ifull[s], nsub * (X_BYTES + RAW2));
+                    for (int sub = 0; sub < nsub; ++sub)
+                        tma_load_2d(st + sub * X_BYTES, &tmx, &ifull[s], (kk + sub) * BK, mt * BNT);
 #pragma unroll
-                    for (int sub = 0; sub < 2; ++sub)
-                        bulk_load(st + X_BYTES + sub * kQ4TileBytes, wt + ((size_t)sub * KT + kk) * kQ4TileBytes,
-                                  kQ4TileBytes, &ifull[s]);
+                    for (int sel = 0; sel < 2; ++sel)
+                        bulk_load(st + KSUB * X_BYTES + sel * KSUB * kQ4TileBytes,
+                                  wt + ((size_t)sel * KT + kk) * kQ4TileBytes, nsub * kQ4TileBytes, &ifull[s]);
                 }
                 __syncwarp();
             }
@@ -874,19 +887,24 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
             const bool ok = mbar_wait(aempty, (it & 1) ^ 1, a.err, kErrWaitAccEmpty, abort_flag);
             if (!__all_sync(0xffffffffu, ok)) goto done;
             tc_fence_after();
-            for (int kt = 0; kt < KT; ++kt, ++g) {
+            for (int ks = 0; ks < KS; ++ks, ++g) {
                 const int s = g % ISTAGES, ws = g % WSLOTS;
+                const int kj = ks + ks0 < KS ? ks + ks0 : ks + ks0 - KS;
+                const int nsub = kj * KSUB + 1 < KT ? KSUB : 1;
                 // wfull implies ifull (see q4_gemm_ta_kernel)
                 const bool ready = mbar_wait_hot(&wfull[ws], (g / WSLOTS) & 1, a.err, kErrWaitReady, abort_flag);
                 if (!__all_sync(0xffffffffu, ready)) goto done;
                 tc_fence_after();
-                const uint64_t bd = desc_kmajor_sw128(smem_u32(sin + s * IN_BYTES));
-                const uint32_t wg = tmem + kColW + ws * 64;  // gate rows, then up rows at +32
                 if (elect_one()) {
+                    for (int sub = 0; sub < nsub; ++sub) {
+                        const uint64_t bd = desc_kmajor_sw128(smem_u32(sin + s * IN_BYTES + sub * X_BYTES));
+                        const uint32_t wg = tmem + kColW + ws * 128 + sub * 64;  // gate rows, up rows at +32
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
-                        mma_f16_ts(tmem, wg + k * 8, bd + 2 * k, idesc, (kt | k) != 0);
-                        mma_f16_ts(tmem + kColUp, wg + 32 + k * 8, bd + 2 * k, idesc, (kt | k) != 0);
+                        for (int k = 0; k < BK / 16; ++k) {
+                            const uint32_t acc = (ks | sub | k) != 0;
+                            mma_f16_ts(tmem, wg + k * 8, bd + 2 * k, idesc, acc);
+                            mma_f16_ts(tmem + kColUp, wg + 32 + k * 8, bd + 2 * k, idesc, acc);
+                        }
                     }
                     mma_commit(&iempty[s]);
                     mma_commit(&wempty[ws]);
@@ -905,19 +923,22 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
         const int sel = l >> 6, r = (l & 63) + 64 * up;  // row r of repacked tile 2u + sel
         uint32_t g = 0;
         for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-            for (int kt = 0; kt < KT; ++kt, ++g) {
+            for (int ks = 0; ks < KS; ++ks, ++g) {
                 const int s = g % ISTAGES, ws = g % WSLOTS;
+                const int kj = ks + ks0 < KS ? ks + ks0 : ks + ks0 - KS;
+                const int nsub = kj * KSUB + 1 < KT ? KSUB : 1;
                 bool ok = mbar_wait(&ifull[s], (g / ISTAGES) & 1, a.err, kErrWaitFull, abort_flag);
                 if (!__all_sync(0xffffffffu, ok)) goto done;
-                const uint8_t* raw = sin + s * IN_BYTES + X_BYTES + sel * kQ4TileBytes;
-                {
-                    // dequantise first: only the TMEM store waits for the slot to be free
+                const uint8_t* raw = sin + s * IN_BYTES + KSUB * X_BYTES + sel * KSUB * kQ4TileBytes;
+                for (int sub = 0; sub < nsub; ++sub) {
                     uint32_t w[32];
-                    dequant_row64(raw, r, w);
-                    ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
-                    if (!__all_sync(0xffffffffu, ok)) goto done;
-                    tc_fence_after();
-                    tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 64 + 32 * up, w);
+                    dequant_row64(raw + sub * kQ4TileBytes, r, w);
+                    if (sub == 0) {  // dequantise first: only the TMEM store waits for the slot
+                        ok = mbar_wait(&wempty[ws], ((g / WSLOTS) & 1) ^ 1, a.err, kErrWaitWEmpty, abort_flag);
+                        if (!__all_sync(0xffffffffu, ok)) goto done;
+                        tc_fence_after();
+                    }
+                    tmem_st_32x32b_x32(tmem + lane_base + kColW + ws * 128 + sub * 64 + 32 * up, w);
                 }
                 // the input slot is released once the raw values were consumed
                 mbar_arrive(&iempty[s]);
