@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
     const int KT = (a.K + BK - 1) / BK;
     const int MT = (a.M + BM - 1) / BM;
     const int n_tiles = MT * (q4_n_tiles(a.N) / C::SUB);
-    const int kt0 = (int)((blockIdx.x * 5u) % (unsigned)KT);
+    const int kt0 = a.krot ? (int)((blockIdx.x * 5u) % (unsigned)KT) : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ISTAGES; ++s) {
@@ -597,7 +597,7 @@ __global__ void __launch_bounds__(512, 1)
     const int KS = (KT + KSUB - 1) / KSUB;               // pipeline steps
     const int MT = (a.M + BNT - 1) / BNT;
     const int n_tiles = MT * q4_n_tiles(a.N);
-    const int ks0 = (int)((blockIdx.x * 5u) % (unsigned)KS);
+    const int ks0 = a.krot ? (int)((blockIdx.x * 5u) % (unsigned)KS) : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ISTAGES; ++s) {
@@ -828,7 +828,7 @@ __global__ void __launch_bounds__(swi::kThreads, 1)
     const int KS = (KT + KSUB - 1) / KSUB;               // pipeline steps
     const int MT = (a.M + BNT - 1) / BNT;
     const int n_tiles = MT * (q4_n_tiles(a.N) / 2);       // 128 outputs per tile
-    const int ks0 = (int)((blockIdx.x * 5u) % (unsigned)KS);
+    const int ks0 = a.krot ? (int)((blockIdx.x * 5u) % (unsigned)KS) : 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ISTAGES; ++s) {
@@ -1018,8 +1018,19 @@ cudaError_t launch_width(const Q4GemmArgs& a, const CUtensorMap& map, int tiles,
     return cudaGetLastError();
 }
 
-cudaError_t launch_q4_gemm(const Q4GemmArgs& a, const __half* x, int sm_count,
+cudaError_t launch_q4_gemm(const Q4GemmArgs& args, const __half* x, int sm_count,
                            cudaStream_t stream) {
+    Q4GemmArgs a = args;
+    {
+        // Staggered k starts spread the CTAs sharing a weight tile over its k range, which
+        // helps while the whole activation matrix stays in L2; beyond half the L2 they scatter
+        // the CTAs' live activation windows and L2 misses: the config-5 w2 GEMM (M 2048, K 28672,
+        // 117 MB of activations) read 4.8 GB from DRAM and took 957 us staggered, 798 us aligned
+        // (the K = 8192 GEMMs are ~3 % faster staggered).  VELO_Q4_KROT=0/1 forces either.
+        const char* kr = std::getenv("VELO_Q4_KROT");
+        const size_t act_bytes = (size_t)a.M * a.K * 2;
+        a.krot = kr ? std::atoi(kr) : (act_bytes <= (size_t(64) << 20) ? 1 : 0);
+    }
     CUtensorMap map;
     cudaError_t e = make_tmap_f16_2d(&map, x, (uint64_t)a.M, (uint64_t)a.K, (uint64_t)a.K * 2, BM);
     if (e != cudaSuccess) return e;

@@ -53,6 +53,7 @@ struct Q4GemmArgs {
     int ldy;
     int mode;          // Q4Epilogue
     int* err;          // device error word (a barrier wait gave up)
+    int krot;          // set by launch_q4_gemm: CTAs start their k loops at staggered offsets
 };
 
 // X: f16 [M][K] row-major device buffer (K % 8 == 0, 16-byte aligned base).
