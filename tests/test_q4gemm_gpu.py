@@ -123,7 +123,10 @@ def test_gemm_repeated_launches_identical(ctx):
     assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("M,N,K", [(300, 700, 96), (2000, 4096, 1024)])
+# (512, 4096, 11008) is config 3's down_proj: 64 tiles on 148 SMs, so k is split and the
+# partial sums of each tile meet in the residual; (384, 1536, 4160): an odd step count split
+@pytest.mark.parametrize("M,N,K", [(300, 700, 96), (2000, 4096, 1024), (512, 4096, 11008),
+                                   (384, 1536, 4160)])
 def test_residual_add_ragged(ctx, M, N, K):
     # the TMEM-weight kernel adds its tile into the residual with one reduction
     # per element: ragged rows and columns stay untouched outside [M) x [N)

@@ -304,15 +304,41 @@ __device__ __forceinline__ TileBars tile_bars(uint64_t* qbars, int qt) {
     return TileBars{q, q + 2, q + 4, q + 5};
 }
 
+// 2^y for y <= 0 on the FMA pipe, two lanes at once: y = j + f with j = rn(y)
+// (the 1.5 * 2^23 addition trick), f in [-0.5, 0.5]; 2^f by a cubic fitted for
+// minimax relative error on that interval (coefficients from a reweighted
+// least-squares / Remez iteration: max relative error 7.5e-5, below the 2^-11
+// of the f16 rounding P goes through next); 2^j added to the exponent bits.
+// y is clamped at -126, so masked keys (-inf) give ~1e-38, which is 0 in f16
+// and nothing in an f32 row sum.  The softmax evaluates a quarter of its
+// exponentials this way so that the special-function unit, which takes the
+// rest, stops bounding the softmax (it did: 45 % XU against 45 % tensor pipe).
+__device__ __forceinline__ float2 exp2_fma2(float2 y) {
+    constexpr float kMagic = 12582912.0f;
+    y.x = fmaxf(y.x, -126.0f);
+    y.y = fmaxf(y.y, -126.0f);
+    const float2 t = __fadd2_rn(y, make_float2(kMagic, kMagic));
+    const float2 jf = __fadd2_rn(t, make_float2(-kMagic, -kMagic));
+    const float2 f = __fadd2_rn(y, make_float2(-jf.x, -jf.y));
+    float2 p = __ffma2_rn(make_float2(0.0551705f, 0.0551705f), f, make_float2(0.24260852f, 0.24260852f));
+    p = __ffma2_rn(p, f, make_float2(0.69326094f, 0.69326094f));
+    p = __ffma2_rn(p, f, make_float2(0.99992824f, 0.99992824f));
+    const uint32_t kb = __float_as_uint(kMagic);
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + ((__float_as_uint(t.x) - kb) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + ((__float_as_uint(t.y) - kb) << 23)));
+}
+
 // 2^(x * sl2 - ms) of 16 keys (one packed FMA per pair), packed as 8 f16
-// pairs into pw; returns the pairwise sums.
+// pairs into pw; returns the pairwise sums.  Pairs 1 and 5 take the FMA-pipe
+// exponential, the others the special-function unit.
 __device__ __forceinline__ float2 exp_pack16(const uint32_t* x, float sl2, float ms, uint32_t (&pw)[8]) {
     float2 acc = make_float2(0.0f, 0.0f);
     const float2 s2 = make_float2(sl2, sl2), nm = make_float2(-ms, -ms);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float2 y = __ffma2_rn(make_float2(__uint_as_float(x[2 * i]), __uint_as_float(x[2 * i + 1])), s2, nm);
-        const float2 pp = make_float2(ex2_approx(y.x), ex2_approx(y.y));  // masked (-inf) -> 0
+        const float2 pp = (i & 3) == 1 ? exp2_fma2(y)
+                                       : make_float2(ex2_approx(y.x), ex2_approx(y.y));  // masked (-inf) -> 0
         acc = __fadd2_rn(acc, pp);
         __half2 hp = __floats2half2_rn(pp.x, pp.y);
         pw[i] = *reinterpret_cast<uint32_t*>(&hp);
