@@ -520,6 +520,57 @@ __device__ __forceinline__ float tree_weight(float tv, float dv, float inv_t, fl
     return W;
 }
 
+// tree_weight of two elements at once (two IEEE operations per packed
+// instruction: the same bits as two scalar calls; P - Q as fma(Q, -1, P), one
+// rounding like the subtraction)
+__device__ __forceinline__ float2 tree_weight2(float2 tv, float2 dv, float inv_t, float Mt, float Rt, float Md,
+                                               float Rd, const float* Rlev, int level) {
+    float2 P = __fmul2_rn(spec_exp2(__ffma2_rn(tv, f2(inv_t), f2(-Mt))), f2(Rt));
+    if (level == 0) return P;
+    const float2 Q = __fmul2_rn(spec_exp2(__ffma2_rn(dv, f2(inv_t), f2(-Md))), f2(Rd));
+    float2 W = f2(0.0f);
+    for (int j = 1; j <= level; ++j) {
+        const float2 D = __ffma2_rn(Q, f2(-1.0f), P);
+        W = make_float2(P.x > Q.x ? D.x : 0.0f, P.y > Q.y ? D.y : 0.0f);
+        if (j < level) P = __fmul2_rn(W, f2(Rlev[j]));
+    }
+    return W;
+}
+
+// Weigh tile t at `level`: lane weight -> lane_w[t * 32 + lane], tile weight
+// (warp butterfly) -> tile_w[t]; lane sums (acc0 + acc1) + (acc2 + acc3), acc_c
+// sequential over i, as the chain draw.
+__device__ __forceinline__ void tree_weigh_tile(const float* trow, const float* drow, int V, int t, int lane,
+                                                bool vec4, float inv_t, float Mt, float Rt, float Md, float Rd,
+                                                const float* Rlev, int level, float* lane_w, float* tile_w) {
+    const bool full = (t + 1) * kTile <= V;
+    float tx[32], dx[32];
+    load_groups<8>(trow, V, t, lane, 0, vec4, tx);
+    if (level > 0) load_groups<8>(drow, V, t, lane, 0, vec4, dx);
+    float2 a01 = f2(0.0f), a23 = f2(0.0f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        float2 w01 = tree_weight2(make_float2(tx[4 * i], tx[4 * i + 1]),
+                                  level > 0 ? make_float2(dx[4 * i], dx[4 * i + 1]) : f2(0.0f), inv_t, Mt, Rt,
+                                  Md, Rd, Rlev, level);
+        float2 w23 = tree_weight2(make_float2(tx[4 * i + 2], tx[4 * i + 3]),
+                                  level > 0 ? make_float2(dx[4 * i + 2], dx[4 * i + 3]) : f2(0.0f), inv_t, Mt,
+                                  Rt, Md, Rd, Rlev, level);
+        if (!full) {
+            if (!elem_valid(V, t, lane, i, 0)) w01.x = 0.0f;
+            if (!elem_valid(V, t, lane, i, 1)) w01.y = 0.0f;
+            if (!elem_valid(V, t, lane, i, 2)) w23.x = 0.0f;
+            if (!elem_valid(V, t, lane, i, 3)) w23.y = 0.0f;
+        }
+        a01 = __fadd2_rn(a01, w01);
+        a23 = __fadd2_rn(a23, w23);
+    }
+    const float lw = lane_combine(a01, a23);
+    lane_w[t * 32 + lane] = lw;
+    const float tw = warp_butterfly_sum(lw);
+    if (lane == 0) tile_w[t] = tw;
+}
+
 __global__ void __launch_bounds__(kTreeThreads) accept_tree_kernel(AcceptTreeParams p) {
     __shared__ float2 st_t[kAcceptMaxTiles], st_d[kAcceptMaxTiles];
     __shared__ float tile_w[kAcceptMaxTiles];
@@ -607,24 +658,8 @@ __global__ void __launch_bounds__(kTreeThreads) accept_tree_kernel(AcceptTreePar
                 break;
             }
             ++level;  // the residual of this rejection: weights, sums, total
-            for (int t = warp; t < ntiles; t += kTreeWarps) {
-                float tx[32], dx[32];
-                load_groups<8>(trow, V, t, lane, 0, p.vec4, tx);
-                load_groups<8>(drow, V, t, lane, 0, p.vec4, dx);
-                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {
-                        float w = tree_weight(tx[4 * i + cc], dx[4 * i + cc], inv_t, Mt, Rt, Md, Rd, Rlev, level);
-                        if (!elem_valid(V, t, lane, i, cc)) w = 0.0f;
-                        acc[cc] = __fadd_rn(acc[cc], w);
-                    }
-                const float lw = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
-                lane_w[t * 32 + lane] = lw;
-                const float tw = warp_butterfly_sum(lw);
-                if (lane == 0) tile_w[t] = tw;
-            }
+            for (int t = warp; t < ntiles; t += kTreeWarps)
+                tree_weigh_tile(trow, drow, V, t, lane, p.vec4, inv_t, Mt, Rt, Md, Rd, Rlev, level, lane_w, tile_w);
             __syncthreads();
             if (tid == 0) {
                 float tot = 0.0f;
@@ -651,25 +686,8 @@ __global__ void __launch_bounds__(kTreeThreads) accept_tree_kernel(AcceptTreePar
         }
         // ---- draw from the final level's weights ---------------------------
         if (weighed != level || level == 0) {
-            for (int t = warp; t < ntiles; t += kTreeWarps) {
-                float tx[32], dx[32];
-                load_groups<8>(trow, V, t, lane, 0, p.vec4, tx);
-                if (level > 0) load_groups<8>(drow, V, t, lane, 0, p.vec4, dx);
-                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-#pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {
-                        float w = tree_weight(tx[4 * i + cc], level > 0 ? dx[4 * i + cc] : 0.0f, inv_t, Mt, Rt,
-                                              Md, Rd, Rlev, level);
-                        if (!elem_valid(V, t, lane, i, cc)) w = 0.0f;
-                        acc[cc] = __fadd_rn(acc[cc], w);
-                    }
-                const float lw = __fadd_rn(__fadd_rn(acc[0], acc[1]), __fadd_rn(acc[2], acc[3]));
-                lane_w[t * 32 + lane] = lw;
-                const float tw = warp_butterfly_sum(lw);
-                if (lane == 0) tile_w[t] = tw;
-            }
+            for (int t = warp; t < ntiles; t += kTreeWarps)
+                tree_weigh_tile(trow, drow, V, t, lane, p.vec4, inv_t, Mt, Rt, Md, Rd, Rlev, level, lane_w, tile_w);
             __syncthreads();
             if (tid == 0) {
                 float tot = 0.0f;
