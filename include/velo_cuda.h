@@ -543,6 +543,19 @@ VELO_API int32_t velo_cuda_profile(velo_cuda_ctx *ctx, int32_t enable);
  * VELO_PHASE_COUNT) and the number of profiled steps (or NULL). */
 VELO_API int32_t velo_cuda_profile_read(velo_cuda_ctx *ctx, double *ms, int32_t n, int32_t *steps);
 
+/* How the row-split GEMMs' partials are summed over the tensor-parallel group
+ * (o_proj, down_proj; the reference's all_reduce_sum_and_add,
+ * src/metal/tp_model.rs:199-277).  The peer path is set up by the first verify
+ * step (every rank maps every rank's partial buffer over CUDA IPC) and taken
+ * only when it succeeded on every rank; VELO_TP_AR=nccl in the environment
+ * forces NCCL. */
+typedef enum velo_tp_sum {
+    VELO_TP_SUM_NONE = 0,  /* one GPU, or the f32 path (NCCL f32 all-reduce) */
+    VELO_TP_SUM_NCCL = 1,  /* NCCL bf16 all-reduce */
+    VELO_TP_SUM_PEER = 2   /* one kernel over NVLink peer memory */
+} velo_tp_sum;
+VELO_API int32_t velo_cuda_tp_sum_path(velo_cuda_ctx *ctx, int32_t *path);
+
 #ifdef __cplusplus
 }
 #endif

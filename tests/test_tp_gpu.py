@@ -282,3 +282,87 @@ def test_tp2_two_stream_halves_match_one_stream_and_oracle():
         exp = np.array([vo.greedy(out[0][1][b, n])[0] for n in range(N)], np.uint32)
         path, bonus = vo.find_best_path(parents[b], tokens[b], exp)
         assert out[0][3][b] == len(path) - 1 and out[0][4][b] == bonus
+
+
+def _rank_sum_paths(rank, tp, nid, meta, tensors, tokens, parents, q):
+    try:
+        import velo_cuda
+        B, N = tokens.shape
+        ctx = velo_cuda.Context(device=rank, total_pages=16 * B, max_slots=B, max_pages_per_slot=16,
+                                tp_rank=rank, tp_size=tp, nccl_id=nid)
+        ctx.load_model(meta, tensors)
+        for b in range(B):
+            ctx.bind_slot(b, np.arange(16 * b, 16 * b + 16))
+        slots = np.arange(B, dtype=np.uint32)
+        cl = np.zeros(B, np.int32)
+        nv = meta["n_vocab"]
+
+        def step():
+            return ctx.verify_step(slots, cl, tokens, parents, commit=False, want_logits=True,
+                                   n_vocab=nv)["logits"]
+        runs = {}
+        for mode in ("peer", "nccl"):
+            if mode == "nccl":
+                os.environ["VELO_TP_AR"] = "nccl"
+            for ov in ("1", "0"):
+                os.environ["VELO_TP_OVERLAP"] = ov
+                runs[(mode, ov)] = [step() for _ in range(3)]
+            os.environ.pop("VELO_TP_AR", None)
+        os.environ.pop("VELO_TP_OVERLAP", None)
+        os.environ["VELO_TP_AR"] = "nccl"
+        path_nccl = ctx.tp_sum_path()
+        os.environ.pop("VELO_TP_AR", None)
+        path = ctx.tp_sum_path()
+        ctx.close()
+        q.put((rank, runs, path, path_nccl, None))
+    except Exception as e:  # report instead of hanging the peer
+        q.put((rank, None, None, None, repr(e)))
+
+
+def test_tp2_peer_memory_sum_matches_nccl():
+    """The bf16 partial sums of o_proj and down_proj over NVLink peer memory
+    (one kernel, every rank's partial buffer mapped by CUDA IPC) against NCCL's
+    all-reduce of the same buffers: with two ranks both add the two partials
+    once and round to bf16, so the logits agree to the last f32 ulp of the
+    GEMMs that follow (1e-3 absolute), in the one-stream loop and in the
+    two-stream halves (two slots of call counters).  Three steps in a row per
+    mode give identical logits, so the on-device call counters stay in step,
+    and both ranks hold identical logits."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import multiprocessing as mp
+    import velo_cuda
+    meta, tensors = synthetic.llama_q4_model(**SHAPE, seed=43)
+    g = synthetic.rng(44, 80)
+    B, N = 3, 8
+    parents = np.stack([synthetic.random_tree(N, 4, g) for _ in range(B)])
+    tokens = g.integers(0, meta["n_vocab"], (B, N)).astype(np.uint32)
+    nid = velo_cuda.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank_sum_paths, args=(r, 2, nid, meta, tensors, tokens, parents, q))
+          for r in range(2)]
+    for p in ps:
+        p.start()
+    out = {}
+    for _ in ps:
+        r = q.get(timeout=300)
+        out[r[0]] = r
+    for p in ps:
+        p.join(timeout=60)
+    for r in range(2):
+        assert out[r][4] is None, out[r][4]
+        assert out[r][2] == "peer" and out[r][3] == "nccl"
+        runs = out[r][1]
+        for key, steps in runs.items():
+            for s in steps[1:]:
+                assert np.array_equal(s, steps[0]), key
+        for ov in ("1", "0"):
+            assert np.abs(runs[("peer", ov)][0] - runs[("nccl", ov)][0]).max() <= 1e-3
+    for key in out[0][1]:
+        assert np.array_equal(out[0][1][key][0], out[1][1][key][0]), key
+    ora = vo.Model(dict(meta, n_ctx=64), synthetic.oracle_tensor_list(meta, tensors))
+    for b in range(B):
+        ref = ora.verify_tree(tokens[b], parents[b], 0)
+        assert np.abs(out[0][1][("peer", "1")][0][b] - ref).max() <= 2e-2

@@ -20,6 +20,7 @@
 #include "kernels/accept.h"
 #include "kernels/f32_path.h"
 #include "kernels/q4gemm.h"
+#include "kernels/tp_allreduce.h"
 #include "kernels/tree_attn.h"
 #include "kernels/verify_ops.h"
 #include "runtime/context.h"
@@ -89,6 +90,13 @@ struct Model {
     // communicator each) so that one half's all-reduce overlaps the other's GEMMs
     cudaStream_t half_stream[2] = {nullptr, nullptr};
     cudaEvent_t half_fork = nullptr, half_join[2] = {nullptr, nullptr};
+    // tensor parallelism over NVLink peer memory: this rank's flag block and every
+    // rank's flag block and partial buffer (ybf) mapped by CUDA IPC
+    unsigned long long* ar_flags = nullptr;
+    uint8_t* ipc_stage = nullptr;  // [tp][128] handles and device UUIDs for the all-gather
+    unsigned long long* peer_flags[kPeerMaxRanks] = {};
+    __nv_bfloat16* peer_ybf[kPeerMaxRanks] = {};
+    bool peer_flags_ok = false, peer_ybf_ok = false;
     // step profile (velo_cuda_profile): an event at the start of every phase
     bool profile = false;
     std::vector<cudaEvent_t> prof_ev;
@@ -143,8 +151,17 @@ struct Model {
     size_t layer_scale_elems() const { return (size_t)pool_pages * Hkv() * 16; }
 };
 
+void close_peers(Model* m, void** peers) {
+    for (int p = 0; p < m->tp && p < kPeerMaxRanks; ++p) {
+        if (p != m->rank && peers[p]) cudaIpcCloseMemHandle(peers[p]);
+        peers[p] = nullptr;
+    }
+}
+
 void destroy_model(Model* m) {
     if (!m) return;
+    close_peers(m, reinterpret_cast<void**>(m->peer_ybf));
+    close_peers(m, reinterpret_cast<void**>(m->peer_flags));
     for (void* p : m->allocs) cudaFree(p);
     for (void* p : m->work) cudaFree(p);
     if (m->hin) cudaFreeHost(m->hin);
@@ -328,6 +345,79 @@ int32_t upload_q4(Model* m, const std::vector<const velo_weight_desc*>& parts, s
     return VELO_OK;
 }
 
+int32_t nccl_check(ncclResult_t r, const NcclApi* nc, const char* what);
+
+// Map every rank's `local` allocation (cudaMalloc base) into this process: the
+// CUDA IPC handles are all-gathered over the group's NCCL communicator (every
+// rank calls this at the same point), then opened.  peers[rank] = local.
+// Returns false (and leaves peers null) when IPC is unavailable or two ranks share
+// a GPU (their sum kernels would wait on one another on one device); the callers
+// then keep NCCL for the sums.
+bool ipc_exchange(velo_cuda_ctx* c, Model* m, void* local, void** peers) {
+    constexpr size_t kRec = 128;  // per rank: IPC handle (64 bytes), device UUID (16)
+    close_peers(m, peers);
+    const NcclApi* nc = nccl_api();
+    if (!nc || !m->ipc_stage || m->tp > kPeerMaxRanks) return false;
+    uint8_t rec[kRec] = {};
+    cudaIpcMemHandle_t h;
+    cudaDeviceProp prop;
+    bool ok = cudaIpcGetMemHandle(&h, local) == cudaSuccess && cudaGetDeviceProperties(&prop, c->device) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+    } else {
+        std::memcpy(rec, &h, 64);
+        std::memcpy(rec + 64, &prop.uuid, 16);
+    }
+    std::vector<uint8_t> all(kRec * m->tp);
+    // the all-gather runs on every rank even when this rank's handle failed, so the
+    // collective stays matched; a zero handle then fails the open on the others
+    cudaStream_t s = c->stream;
+    if (cudaMemcpyAsync(m->ipc_stage + kRec * m->rank, rec, kRec, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        nc->AllGather(m->ipc_stage + kRec * m->rank, m->ipc_stage, kRec, ncclUint8,
+                      static_cast<ncclComm_t>(c->nccl_comm), s) != ncclSuccess ||
+        cudaMemcpyAsync(all.data(), m->ipc_stage, all.size(), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    for (int p = 0; p < m->tp && ok; ++p)
+        if (p != m->rank && std::memcmp(all.data() + kRec * p + 64, rec + 64, 16) == 0) ok = false;
+    for (int p = 0; p < m->tp && ok; ++p) {
+        if (p == m->rank) {
+            peers[p] = local;
+            continue;
+        }
+        cudaIpcMemHandle_t hp;
+        std::memcpy(&hp, all.data() + kRec * p, 64);
+        void* ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, hp, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+            continue;
+        }
+        peers[p] = ptr;
+    }
+    if (!ok) close_peers(m, peers);
+    return ok;
+}
+
+// true only if `ok` holds on every rank (a min all-reduce over the group), so that
+// all ranks take the same path for their sums
+bool group_all_ok(velo_cuda_ctx* c, Model* m, bool ok) {
+    const NcclApi* nc = nccl_api();
+    if (!nc || !m->ipc_stage) return false;
+    int v = ok ? 1 : 0;
+    cudaStream_t s = c->stream;
+    int32_t* d = reinterpret_cast<int32_t*>(m->ipc_stage);
+    if (cudaMemcpyAsync(d, &v, 4, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+        nc->AllReduce(d, d, 1, ncclInt32, ncclMin, static_cast<ncclComm_t>(c->nccl_comm), s) != ncclSuccess ||
+        cudaMemcpyAsync(&v, d, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return v == 1;
+}
+
 int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
     const int M = B * N;
     if (M <= m->cap_M && B <= m->cap_B) return VELO_OK;
@@ -359,7 +449,23 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
     }
     if (!st) st = dev_alloc(m, &m->logits, (size_t)cM * m->V_loc * 4, true);
     if (!st && m->tp > 1 && m->f32) st = dev_alloc(m, &m->y, (size_t)cM * H * 4, true);
-    if (!st && m->tp > 1 && !m->f32) st = dev_alloc(m, &m->ybf, (size_t)cM * H * 2, true);
+    if (!st && m->tp > 1 && !m->f32) {
+        st = dev_alloc(m, &m->ybf, (size_t)cM * H * 2, true);
+        // every rank maps every rank's flag block (once) and partial buffer (whenever it
+        // grows); all ranks grow their buffers in the same step, so the exchanges match
+        if (!st && !m->ar_flags) {
+            st = dev_alloc(m, &m->ar_flags, kPeerFlagBytes);
+            if (!st) st = dev_alloc(m, &m->ipc_stage, (size_t)128 * kPeerMaxRanks);
+            if (!st && cudaMemset(m->ar_flags, 0, kPeerFlagBytes) != cudaSuccess)
+                st = fail(VELO_ERR_CUDA, "peer flag block: cudaMemset failed");
+            if (!st) m->peer_flags_ok = ipc_exchange(c, m, m->ar_flags, reinterpret_cast<void**>(m->peer_flags));
+        }
+        if (!st) m->peer_ybf_ok = ipc_exchange(c, m, m->ybf, reinterpret_cast<void**>(m->peer_ybf));
+        if (!st) {
+            const bool all = group_all_ok(c, m, m->peer_flags_ok && m->peer_ybf_ok);
+            m->peer_flags_ok = m->peer_ybf_ok = all;
+        }
+    }
     if (!st) st = dev_alloc(m, &m->pairs, (size_t)cM * 8, true);
     if (!st) st = dev_alloc(m, &m->pairs_all, (size_t)cM * 8 * m->tp, true);
 
@@ -444,10 +550,34 @@ int32_t allreduce_add(velo_cuda_ctx* c, Model* m, int M) {
 // place; the RMSNorm that follows adds the sum to the residual
 // (launch_add_rmsnorm_f16).  A 16-bit sum moves half the bytes of an f32 one
 // over NVLink (33.5 MB instead of 67 MB per call at M = 2048, H = 8192).
+// The sum over NVLink peer memory (launch_peer_allreduce) when every rank's
+// buffers are mapped, else NCCL; VELO_TP_AR=nccl forces NCCL.
+bool use_peer_sum(const Model* m) {
+    const char* e = std::getenv("VELO_TP_AR");
+    return m->peer_flags_ok && m->peer_ybf_ok && !(e && std::strcmp(e, "nccl") == 0);
+}
+
+int32_t peer_sum(velo_cuda_ctx* c, Model* m, size_t offset, size_t n, int slot, cudaStream_t s) {
+    PeerAllReduceArgs a{};
+    for (int p = 0; p < m->tp; ++p) {
+        a.buf[p] = m->peer_ybf[p];
+        a.flags[p] = m->peer_flags[p];
+    }
+    a.offset = offset;
+    a.n = n;
+    a.rank = m->rank;
+    a.tp = m->tp;
+    a.slot = slot;
+    a.err = c->err_flag;
+    VELO_CUDA_TRY(launch_peer_allreduce(a, s));
+    return VELO_OK;
+}
+
 int32_t allreduce_bf16(velo_cuda_ctx* c, Model* m, int M) {
+    const size_t n = (size_t)M * m->H();
+    if (use_peer_sum(m)) return peer_sum(c, m, 0, n, 0, c->stream);
     const NcclApi* nc = nccl_api();
     if (!nc) return VELO_ERR_NCCL;
-    const size_t n = (size_t)M * m->H();
     return nccl_check(nc->AllReduce(m->ybf, m->ybf, n, ncclBfloat16, ncclSum,
                                     static_cast<ncclComm_t>(c->nccl_comm), c->stream),
                       nc, "ncclAllReduce");
@@ -489,6 +619,7 @@ int32_t forward_tp_halves(velo_cuda_ctx* c, Model* m, int B, int N) {
     };
     auto reduce = [&](int h) -> int32_t {
         pending[h] = true;
+        if (use_peer_sum(m)) return peer_sum(c, m, r0(h) * H, (size_t)rows(h) * H, h, m->half_stream[h]);
         return nccl_check(nc->AllReduce(m->ybf + r0(h) * H, m->ybf + r0(h) * H, (size_t)rows(h) * H, ncclBfloat16,
                                         ncclSum, static_cast<ncclComm_t>(comm[h]), m->half_stream[h]),
                           nc, "ncclAllReduce");
@@ -1448,6 +1579,16 @@ int32_t velo_cuda_profile_read(velo_cuda_ctx* c, double* ms, int32_t n, int32_t*
         return fail(VELO_ERR_INVALID_ARGUMENT, "profile_read needs %d slots", (int)VELO_PHASE_COUNT);
     for (int i = 0; i < VELO_PHASE_COUNT; ++i) ms[i] = c->model->prof_ms[i];
     if (steps) *steps = c->model->prof_steps;
+    return VELO_OK;
+}
+
+int32_t velo_cuda_tp_sum_path(velo_cuda_ctx* c, int32_t* path) {
+    velo::clear_last_error();
+    int32_t st = velo::check_model(c);
+    if (st) return st;
+    if (!path) return fail(VELO_ERR_INVALID_ARGUMENT, "tp_sum_path: null output");
+    const Model* m = c->model;
+    *path = m->tp < 2 || m->f32 ? VELO_TP_SUM_NONE : velo::use_peer_sum(m) ? VELO_TP_SUM_PEER : VELO_TP_SUM_NCCL;
     return VELO_OK;
 }
 

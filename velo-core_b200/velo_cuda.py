@@ -108,6 +108,7 @@ _SIGS = {
     "velo_cuda_nccl_unique_id": (_I32, [_P]),
     "velo_cuda_profile": (_I32, [_P, _I32]),
     "velo_cuda_profile_read": (_I32, [_P, ctypes.POINTER(ctypes.c_double), _I32, ctypes.POINTER(_I32)]),
+    "velo_cuda_tp_sum_path": (_I32, [_P, ctypes.POINTER(_I32)]),
     "velo_cuda_shard_strategy": (_I32, [ctypes.c_char_p]),
     "velo_cuda_shard_weight": (_I32, [_P, _I32, _I32, _I32, _P, ctypes.c_size_t,
                                       ctypes.POINTER(ctypes.c_uint64),
@@ -418,6 +419,12 @@ class Context:
         steps = _I32(0)
         check(lib().velo_cuda_profile_read(self._h, ms, len(PHASES), ctypes.byref(steps)))
         return {n: float(ms[i]) for i, n in enumerate(PHASES)}, int(steps.value)
+
+    def tp_sum_path(self):
+        """'none', 'nccl' or 'peer': how the tensor-parallel partial sums run."""
+        v = _I32(0)
+        check(lib().velo_cuda_tp_sum_path(self._h, ctypes.byref(v)))
+        return ("none", "nccl", "peer")[v.value]
 
     def verify_step(self, slots, ctx_len, tokens, parents, temperature=0.0, draft_logits=None,
                     uniforms=None, commit=True, want_logits=False, n_vocab=None):
