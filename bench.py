@@ -935,7 +935,7 @@ def run_verify(args):
     L = meta["n_layer"]
     sum_path = ctx.tp_sum_path()
     # per layer 8 kernels, plus the two partial-sum kernels when they are ours
-    launches = 2 + (8 + (2 if sum_path == "peer" else 0)) * L + 2 + (2 if ws == 1 else 3) + 1
+    launches = 2 + (8 + (2 if sum_path in ("peer", "fused") else 0)) * L + 2 + (2 if ws == 1 else 3) + 1
     traffic = None
     if ws == 1:
         traffic = load_traffic("q4gemm_swiglu_c5" if c5 else "q4gemm_swiglu_c3")
@@ -951,7 +951,9 @@ def run_verify(args):
                   "does not depend on their values)",
         "config": {"workload": wl, "B": B, "nodes": N, "ctx": ctx_len, "rows": M,
                    "parallelism": f"tp{ws}" if ws > 1 else "tp1 (single GPU)",
-                   "tp_sum": {"peer": "one kernel over NVLink peer memory (CUDA IPC)",
+                   "tp_sum": {"fused": "row-split GEMM epilogue pushes each column block to its owner "
+                                       "over NVLink (CUDA IPC); the owner's kernel adds and broadcasts",
+                              "peer": "one kernel over NVLink peer memory (CUDA IPC)",
                               "nccl": "NCCL bf16 all-reduce", "none": None}[sum_path],
                    "l2": f"inputs > L2: {cnt['w_bytes'] / 1e9:.1f} GB of weights and "
                          f"{cnt['kv_bytes'] / 1e9:.1f} GB of KV streamed per step and rank"},

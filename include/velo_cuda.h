@@ -548,11 +548,13 @@ VELO_API int32_t velo_cuda_profile_read(velo_cuda_ctx *ctx, double *ms, int32_t 
  * src/metal/tp_model.rs:199-277).  The peer path is set up by the first verify
  * step (every rank maps every rank's partial buffer over CUDA IPC) and taken
  * only when it succeeded on every rank; VELO_TP_AR=nccl in the environment
- * forces NCCL. */
+ * forces NCCL, VELO_TP_AR=peer the unfused peer kernel. */
 typedef enum velo_tp_sum {
     VELO_TP_SUM_NONE = 0,  /* one GPU, or the f32 path (NCCL f32 all-reduce) */
     VELO_TP_SUM_NCCL = 1,  /* NCCL bf16 all-reduce */
-    VELO_TP_SUM_PEER = 2   /* one kernel over NVLink peer memory */
+    VELO_TP_SUM_PEER = 2,  /* one kernel over NVLink peer memory (VELO_TP_AR=peer) */
+    VELO_TP_SUM_FUSED = 3  /* the GEMM epilogue pushes each column block to its owner
+                              rank, whose gather kernel adds and broadcasts it */
 } velo_tp_sum;
 VELO_API int32_t velo_cuda_tp_sum_path(velo_cuda_ctx *ctx, int32_t *path);
 

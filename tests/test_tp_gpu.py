@@ -300,34 +300,35 @@ def _rank_sum_paths(rank, tp, nid, meta, tensors, tokens, parents, q):
         def step():
             return ctx.verify_step(slots, cl, tokens, parents, commit=False, want_logits=True,
                                    n_vocab=nv)["logits"]
-        runs = {}
-        for mode in ("peer", "nccl"):
-            if mode == "nccl":
-                os.environ["VELO_TP_AR"] = "nccl"
+        runs, paths = {}, {}
+        for mode in ("fused", "peer", "nccl"):
+            if mode != "fused":
+                os.environ["VELO_TP_AR"] = mode
             for ov in ("1", "0"):
                 os.environ["VELO_TP_OVERLAP"] = ov
                 runs[(mode, ov)] = [step() for _ in range(3)]
+            paths[mode] = ctx.tp_sum_path()
             os.environ.pop("VELO_TP_AR", None)
         os.environ.pop("VELO_TP_OVERLAP", None)
-        os.environ["VELO_TP_AR"] = "nccl"
-        path_nccl = ctx.tp_sum_path()
-        os.environ.pop("VELO_TP_AR", None)
-        path = ctx.tp_sum_path()
         ctx.close()
-        q.put((rank, runs, path, path_nccl, None))
+        q.put((rank, runs, paths, None, None))
     except Exception as e:  # report instead of hanging the peer
         q.put((rank, None, None, None, repr(e)))
 
 
 def test_tp2_peer_memory_sum_matches_nccl():
     """The bf16 partial sums of o_proj and down_proj over NVLink peer memory
-    (one kernel, every rank's partial buffer mapped by CUDA IPC) against NCCL's
-    all-reduce of the same buffers: with two ranks both add the two partials
-    once and round to bf16, so the logits agree to the last f32 ulp of the
-    GEMMs that follow (1e-3 absolute), in the one-stream loop and in the
-    two-stream halves (two slots of call counters).  Three steps in a row per
-    mode give identical logits, so the on-device call counters stay in step,
-    and both ranks hold identical logits."""
+    against NCCL's all-reduce of the same partials: fused (the GEMM epilogue
+    pushes each column block to its owner, whose gather kernel adds and
+    broadcasts) and unfused (one sum kernel over every rank's partial buffer,
+    mapped by CUDA IPC).  The two peer paths add the same bf16 partials in the
+    same rank order in f32, so their logits are bit-identical; with two ranks
+    NCCL also adds the two partials once and rounds to bf16, so its logits
+    agree to the last f32 ulp of the GEMMs that follow (1e-3 absolute).  Both
+    in the one-stream loop and in the two-stream halves (two slots of call
+    counters).  Three steps in a row per mode give identical logits, so the
+    on-device call counters stay in step, and both ranks hold identical
+    logits."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -353,16 +354,17 @@ def test_tp2_peer_memory_sum_matches_nccl():
         p.join(timeout=60)
     for r in range(2):
         assert out[r][4] is None, out[r][4]
-        assert out[r][2] == "peer" and out[r][3] == "nccl"
+        assert out[r][2] == {"fused": "fused", "peer": "peer", "nccl": "nccl"}
         runs = out[r][1]
         for key, steps in runs.items():
             for s in steps[1:]:
                 assert np.array_equal(s, steps[0]), key
         for ov in ("1", "0"):
+            assert np.array_equal(runs[("fused", ov)][0], runs[("peer", ov)][0]), ov
             assert np.abs(runs[("peer", ov)][0] - runs[("nccl", ov)][0]).max() <= 1e-3
     for key in out[0][1]:
         assert np.array_equal(out[0][1][key][0], out[1][1][key][0]), key
     ora = vo.Model(dict(meta, n_ctx=64), synthetic.oracle_tensor_list(meta, tensors))
     for b in range(B):
         ref = ora.verify_tree(tokens[b], parents[b], 0)
-        assert np.abs(out[0][1][("peer", "1")][0][b] - ref).max() <= 2e-2
+        assert np.abs(out[0][1][("fused", "1")][0][b] - ref).max() <= 2e-2

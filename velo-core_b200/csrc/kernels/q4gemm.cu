@@ -179,6 +179,24 @@ __device__ __forceinline__ void dequant_row64(const uint8_t* tile, int row, uint
 
 // ---------------------------------------------------------------- epilogue
 __device__ __forceinline__ void store_row32(const Q4GemmArgs& a, int m, int n, const uint32_t (&r)[32]) {
+    if (a.mode == kEpiPeerBF16) {  // 32 columns of one owner (peer_cols % 32 == 0, n % 32 == 0)
+        const int o = n / a.peer_cols;
+        uint4* y = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.peer_y[o]) + (size_t)m * a.peer_cols +
+                                            (n - o * a.peer_cols));
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint4 v;
+            uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const __nv_bfloat162 h =
+                    __floats2bfloat162_rn(__uint_as_float(r[8 * c + 2 * i]), __uint_as_float(r[8 * c + 2 * i + 1]));
+                w[i] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            y[c] = v;
+        }
+        return;
+    }
     if (a.mode == kEpiStoreBF16) {
         __nv_bfloat16* y = static_cast<__nv_bfloat16*>(a.y) + (size_t)m * a.ldy + n;
 #pragma unroll
@@ -246,7 +264,7 @@ __device__ __forceinline__ void store_row32(const Q4GemmArgs& a, int m, int n, c
 // into a hot spot that stretches the TMA latency to ~2 us.
 template <int BN>
 __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
-    q4_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
+    q4_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ Q4GemmArgs a) {
     using C = Cfg<BN>;
     constexpr int ISTAGES = C::ISTAGES, WSTAGES = C::WSTAGES, IN_BYTES = C::IN_BYTES;
     constexpr int W_BYTES = C::W_BYTES, RAW_BYTES = C::RAW_BYTES;
@@ -449,6 +467,9 @@ __global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
         }
     }
 done:
+    // peer stores: performed at system scope before the kernel ends, so that the sum
+    // kernel's cross-rank release that follows on this stream covers them
+    if (a.mode == kEpiPeerBF16) __threadfence_system();
     tc_fence_before();
     __syncthreads();
     if (warp == 2) {
@@ -574,7 +595,7 @@ struct TaCfg {
 
 template <int BNT>
 __global__ void __launch_bounds__(512, 1)
-    q4_gemm_ta_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
+    q4_gemm_ta_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ Q4GemmArgs a) {
     using C = TaCfg<BNT>;
     constexpr int ACC = C::ACC, X2_BYTES = C::X2_BYTES, IN_BYTES = C::IN_BYTES, ISTAGES = C::ISTAGES;
     constexpr int WSLOTS = C::WSLOTS;
@@ -759,6 +780,15 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
                         for (int j = 0; j < 16; ++j, p += a.ldy)
                             if (j < mcount) *p = __float2bfloat16_rn(__uint_as_float(v[j]));
+                    } else if (a.mode == kEpiPeerBF16) {
+                        // the owner's receive area, row stride peer_cols (a warp's 32
+                        // columns belong to one owner: 64 contiguous bytes per row)
+                        const int o = n / a.peer_cols;
+                        __nv_bfloat16* p = static_cast<__nv_bfloat16*>(a.peer_y[o]) + (size_t)m0 * a.peer_cols +
+                                           (n - o * a.peer_cols);
+#pragma unroll
+                        for (int j = 0; j < 16; ++j, p += a.peer_cols)
+                            if (j < mcount) *p = __float2bfloat16_rn(__uint_as_float(v[j]));
                     } else {
                         __half* p = static_cast<__half*>(a.y) + (size_t)m0 * a.ldy + n;
 #pragma unroll
@@ -772,6 +802,9 @@ __global__ void __launch_bounds__(512, 1)
         }
     }
 done:
+    // peer stores: performed at system scope before the kernel ends, so that the sum
+    // kernel's cross-rank release that follows on this stream covers them
+    if (a.mode == kEpiPeerBF16) __threadfence_system();
     tc_fence_before();
     __syncthreads();
     if (warp == 2) {
@@ -808,7 +841,7 @@ __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f 
 
 
 __global__ void __launch_bounds__(swi::kThreads, 1)
-    q4_gemm_ta_swiglu_kernel(const __grid_constant__ CUtensorMap tmx, const Q4GemmArgs a) {
+    q4_gemm_ta_swiglu_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ Q4GemmArgs a) {
     using namespace swi;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);

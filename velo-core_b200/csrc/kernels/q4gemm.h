@@ -44,6 +44,10 @@ enum Q4Epilogue : int {
     kEpiAddF32 = 2,    // y[m][n] += acc                      (f32, residual stream)
     kEpiSwiGLU = 3,    // y[m][j] = f16(silu(gate) * up)      (f16, pair-repacked weight)
     kEpiStoreBF16 = 4, // y[m][n] = bf16(acc)                 (bf16: tensor-parallel partials)
+    // bf16(acc) pushed to the rank that owns output column n: element (m, n) goes to
+    // peer_y[o][m * peer_cols + n - o * peer_cols], o = n / peer_cols (the first half of a
+    // tensor-parallel sum, fused into the row-split GEMM; peer_y are NVLink peer mappings)
+    kEpiPeerBF16 = 5,
 };
 
 struct Q4GemmArgs {
@@ -54,6 +58,8 @@ struct Q4GemmArgs {
     int mode;          // Q4Epilogue
     int* err;          // device error word (a barrier wait gave up)
     int krot;          // set by launch_q4_gemm: CTAs start their k loops at staggered offsets
+    void* peer_y[8];   // kEpiPeerBF16: per owner rank, its receive area for this rank's rows
+    int peer_cols;     // kEpiPeerBF16: output columns per owner (a multiple of 32)
 };
 
 // X: f16 [M][K] row-major device buffer (K % 8 == 0, 16-byte aligned base).

@@ -3,12 +3,16 @@
 //
 // Replaces, for o_proj and down_proj, the reference's CPU all-reduce
 // (LlamaTensorParallelModel::all_reduce_sum_and_add, src/metal/tp_model.rs:199-277)
-// and NCCL's ring in this build.  Every rank's partial buffer is mapped into every
-// other rank's address space (CUDA IPC), so one kernel does the whole sum: rank r
-// owns chunk r of the rows, loads that chunk from all tp buffers (its own from
-// HBM, the others over NVLink), adds them in rank order in f32, and stores the
-// bf16 sum into all tp buffers.  Each byte of partial crosses NVLink once in each
-// direction, in one pass; all ranks end with identical values.
+// and NCCL's ring in this build.  Every rank's buffers are mapped into every other
+// rank's address space (CUDA IPC).  Two forms:
+//   fused (peer_gather_kernel): the row-split GEMM's epilogue already stored column
+//     block r of its partial into rank r's receive area, overlapping the transfer
+//     with the GEMM's tiles; rank r adds its block's tp slabs (local HBM) in rank
+//     order in f32 and stores the bf16 sum into every rank's sum buffer.
+//   unfused (peer_allreduce_kernel): rank r owns chunk r of the rows, loads that
+//     chunk from all tp buffers (its own from HBM, the others over NVLink), adds
+//     them in rank order in f32 and stores the bf16 sum into all tp buffers.
+// Both add the same bf16 partials in the same order: identical results.
 //
 // Ordering: a cross-rank entry barrier (each rank publishes an epoch into every
 // rank's flag block with a system-scope release, after its partial is complete,
@@ -18,10 +22,11 @@
 // every rank after its stores) guarantees every sum has landed before the kernel
 // returns and the next kernel on the stream reads the buffer.  Every wait is
 // bounded by the global timer (2 s): a rank that never arrives makes the others
-// record an error and return instead of spinning forever.  The grid is small
-// (kPeerGrid CTAs of 256 threads, no dynamic shared memory) and fixed; each CTA
-// counts its own calls in its rank's flag block, so the epochs need no host state
-// and every rank's CTAs agree on them.
+// record an error and return instead of spinning forever.  The grid is fixed
+// (kPeerGrid CTAs of 128 threads, under 14 K registers and no dynamic shared
+// memory, so that a CTA fits on an SM beside a GEMM CTA of the other stream);
+// each CTA counts its own calls in its rank's flag block, so the epochs need no
+// host state and every rank's CTAs agree on them.
 #include "kernels/tp_allreduce.h"
 
 #include <cuda_bf16.h>
@@ -29,7 +34,7 @@
 namespace velo {
 namespace {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 128;
 constexpr unsigned long long kWaitNs = 2000000000ull;
 constexpr int kErrPeerEntry = 0x7101, kErrPeerExit = 0x7102;
 
@@ -79,42 +84,14 @@ __device__ __forceinline__ void add8(float (&acc)[8], uint4 v) {
     }
 }
 
-// 8 bf16 of every rank's buffer at element e, summed in rank order (f32), stored
-// as bf16 into every rank's buffer
-__device__ __forceinline__ void sum_vectors(const PeerAllReduceArgs& a, size_t e0, size_t e1, bool two) {
-    uint4 in[2][kPeerMaxRanks];
-#pragma unroll
-    for (int p = 0; p < kPeerMaxRanks; ++p)
-        if (p < a.tp) {
-            in[0][p] = ld_volatile16(a.buf[p] + e0);
-            if (two) in[1][p] = ld_volatile16(a.buf[p] + e1);
-        }
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        if (j == 1 && !two) break;
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int p = 0; p < kPeerMaxRanks; ++p)
-            if (p < a.tp) add8(acc, in[j][p]);
-        uint4 out;
-        uint32_t* o = reinterpret_cast<uint32_t*>(&out);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-            o[i] = *reinterpret_cast<const uint32_t*>(&h);
-        }
-        const size_t e = j ? e1 : e0;
-#pragma unroll
-        for (int p = 0; p < kPeerMaxRanks; ++p)
-            if (p < a.tp) *reinterpret_cast<uint4*>(a.buf[p] + e) = out;
-    }
-}
-
-__global__ void __launch_bounds__(kThreads) peer_allreduce_kernel(PeerAllReduceArgs a) {
+// Entry barrier: this rank's partial is complete (stream order); publish the
+// call's epoch to every rank and wait until every rank's has arrived here.
+// Returns the epoch (0 after a wait ran out; the error word is set then).
+__device__ __forceinline__ unsigned long long peer_entry(const PeerSync& y) {
     __shared__ int ok_sh;
     __shared__ unsigned long long epoch_sh;
     const int tid = threadIdx.x;
-    unsigned long long* my = a.flags[a.rank] + a.slot * kPeerSlotWords;
+    unsigned long long* my = y.flags[y.rank] + y.slot * kPeerSlotWords;
     // this CTA's call number on this slot (only this CTA of this rank touches the word)
     if (tid == 0) {
         epoch_sh = my[16 + blockIdx.x] + 1;
@@ -122,46 +99,152 @@ __global__ void __launch_bounds__(kThreads) peer_allreduce_kernel(PeerAllReduceA
     }
     __syncthreads();
     const unsigned long long epoch = epoch_sh;
-    // ---- entry: this rank's partial is complete (stream order); tell everyone
-    if (blockIdx.x == 0 && tid < a.tp) {
+    if (blockIdx.x == 0 && tid < y.tp) {
         __threadfence_system();
-        st_release_sys(a.flags[tid] + a.slot * kPeerSlotWords + a.rank, epoch);
+        st_release_sys(y.flags[tid] + y.slot * kPeerSlotWords + y.rank, epoch);
     }
-    if (tid < a.tp && !wait_at_least(my + tid, epoch)) {
-        atomicCAS(a.err, 0, kErrPeerEntry);
+    if (tid < y.tp && !wait_at_least(my + tid, epoch)) {
+        atomicCAS(y.err, 0, kErrPeerEntry);
         ok_sh = 0;
     }
     __syncthreads();
-    if (ok_sh) {
-        // ---- chunk `rank` of the vectors (8 bf16 each), two vectors per thread per pass
-        const size_t nvec = a.n / 8;
-        const size_t v0 = nvec * a.rank / a.tp, v1 = nvec * (a.rank + 1) / a.tp;
-        const size_t stride = (size_t)gridDim.x * kThreads;
-        for (size_t v = v0 + (size_t)blockIdx.x * kThreads + tid; v < v1; v += 2 * stride)
-            sum_vectors(a, a.offset + v * 8, a.offset + (v + stride) * 8, v + stride < v1);
-    }
-    // ---- exit: every CTA of every rank counts itself in every rank's block (also
-    // after a failed entry, so that the counts stay in step)
+    return ok_sh ? epoch : 0;
+}
+
+// Exit barrier: every CTA of every rank counts itself in every rank's block
+// after its stores (also after a failed entry, so that the counts stay in step)
+// and waits until all tp x kPeerGrid CTAs of this call have counted in its own.
+__device__ __forceinline__ void peer_exit(const PeerSync& y) {
+    const int tid = threadIdx.x;
+    unsigned long long* my = y.flags[y.rank] + y.slot * kPeerSlotWords;
     __syncthreads();
-    if (tid < a.tp) {
+    const unsigned long long epoch = my[16 + blockIdx.x] + 1;
+    if (tid < y.tp) {
         __threadfence_system();
-        red_release_sys_add(a.flags[tid] + a.slot * kPeerSlotWords + 8, 1ull);
+        red_release_sys_add(y.flags[tid] + y.slot * kPeerSlotWords + 8, 1ull);
     }
     if (tid == 0) {
-        if (!wait_at_least(my + 8, epoch * (unsigned long long)a.tp * kPeerGrid)) atomicCAS(a.err, 0, kErrPeerExit);
+        if (!wait_at_least(my + 8, epoch * (unsigned long long)y.tp * kPeerGrid)) atomicCAS(y.err, 0, kErrPeerExit);
         my[16 + blockIdx.x] = epoch;
     }
     __syncthreads();
 }
 
+__device__ __forceinline__ uint4 round_bf16x8(const float (&acc)[8]) {
+    uint4 out;
+    uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+        o[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    return out;
+}
+
+// vectors (8 bf16) per thread per pass: two while the loads of all ranks fit the
+// register budget
+template <int TP>
+constexpr int kUnroll = TP <= 4 ? 2 : 1;
+
+template <int TP>
+__global__ void __launch_bounds__(kThreads) peer_allreduce_kernel(const __grid_constant__ PeerAllReduceArgs a) {
+    constexpr int U = kUnroll<TP>;
+    if (peer_entry(a.sync)) {
+        // chunk `rank` of the vectors (8 bf16 each)
+        const size_t nvec = a.n / 8;
+        const size_t v0 = nvec * a.sync.rank / TP, v1 = nvec * (a.sync.rank + 1) / TP;
+        const size_t stride = (size_t)gridDim.x * kThreads;
+        for (size_t v = v0 + (size_t)blockIdx.x * kThreads + threadIdx.x; v < v1; v += U * stride) {
+            uint4 in[U][TP];
+#pragma unroll
+            for (int j = 0; j < U; ++j)
+                if (v + j * stride < v1)
+#pragma unroll
+                    for (int p = 0; p < TP; ++p) in[j][p] = ld_volatile16(a.buf[p] + a.offset + (v + j * stride) * 8);
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                if (v + j * stride >= v1) break;
+                float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int p = 0; p < TP; ++p) add8(acc, in[j][p]);
+                const uint4 out = round_bf16x8(acc);
+#pragma unroll
+                for (int p = 0; p < TP; ++p)
+                    *reinterpret_cast<uint4*>(a.buf[p] + a.offset + (v + j * stride) * 8) = out;
+            }
+        }
+    }
+    peer_exit(a.sync);
+}
+
+// rank r's column block: tp slabs read from its own HBM, the sum pushed to all ranks
+template <int TP>
+__global__ void __launch_bounds__(kThreads) peer_gather_kernel(const __grid_constant__ PeerGatherArgs a) {
+    constexpr int U = kUnroll<TP>;
+    if (peer_entry(a.sync)) {
+        const int vpr = a.cols / 8;  // vectors per row
+        const size_t nvec = (size_t)a.rows * vpr;
+        const size_t stride = (size_t)gridDim.x * kThreads;
+        for (size_t v = (size_t)blockIdx.x * kThreads + threadIdx.x; v < nvec; v += U * stride) {
+            size_t src[U], dst[U];
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                const size_t w = v + j * stride;
+                const size_t m = w / vpr, c = (w - m * vpr) * 8;
+                src[j] = m * a.cols + c;
+                dst[j] = m * a.ld + c;
+            }
+            uint4 in[U][TP];
+#pragma unroll
+            for (int j = 0; j < U; ++j)
+                if (v + j * stride < nvec)
+#pragma unroll
+                    for (int p = 0; p < TP; ++p) in[j][p] = ld_volatile16(a.stage + p * a.slab + src[j]);
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                if (v + j * stride >= nvec) break;
+                float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int p = 0; p < TP; ++p) add8(acc, in[j][p]);
+                const uint4 out = round_bf16x8(acc);
+#pragma unroll
+                for (int p = 0; p < TP; ++p) *reinterpret_cast<uint4*>(a.out[p] + dst[j]) = out;
+            }
+        }
+    }
+    peer_exit(a.sync);
+}
+
+bool sync_ok(const PeerSync& y) {
+    return y.tp >= 2 && y.tp <= kPeerMaxRanks && y.rank >= 0 && y.rank < y.tp && y.slot >= 0 && y.slot <= 3 &&
+           y.err != nullptr;
+}
+
 }  // namespace
 
 cudaError_t launch_peer_allreduce(const PeerAllReduceArgs& a, cudaStream_t stream) {
-    if (a.tp < 2 || a.tp > kPeerMaxRanks || a.rank < 0 || a.rank >= a.tp || a.n % 8 || a.offset % 8 ||
-        a.slot < 0 || a.slot > 3)
-        return cudaErrorInvalidValue;
-    peer_allreduce_kernel<<<kPeerGrid, kThreads, 0, stream>>>(a);
+    if (!sync_ok(a.sync) || a.n % 8 || a.offset % 8) return cudaErrorInvalidValue;
+    switch (a.sync.tp) {
+        case 2: peer_allreduce_kernel<2><<<kPeerGrid, kThreads, 0, stream>>>(a); break;
+        case 4: peer_allreduce_kernel<4><<<kPeerGrid, kThreads, 0, stream>>>(a); break;
+        case 8: peer_allreduce_kernel<8><<<kPeerGrid, kThreads, 0, stream>>>(a); break;
+        default: return cudaErrorInvalidValue;
+    }
     return cudaGetLastError();
 }
+
+cudaError_t launch_peer_gather(const PeerGatherArgs& a, cudaStream_t stream) {
+    if (!sync_ok(a.sync) || a.cols <= 0 || a.cols % 8 || a.ld % 8 || a.rows < 0 || a.slab % 8)
+        return cudaErrorInvalidValue;
+    switch (a.sync.tp) {
+        case 2: peer_gather_kernel<2><<<kPeerGrid, kThreads, 0, stream>>>(a); break;
+        case 4: peer_gather_kernel<4><<<kPeerGrid, kThreads, 0, stream>>>(a); break;
+        case 8: peer_gather_kernel<8><<<kPeerGrid, kThreads, 0, stream>>>(a); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+bool peer_tp_supported(int tp) { return tp == 2 || tp == 4 || tp == 8; }
 
 }  // namespace velo

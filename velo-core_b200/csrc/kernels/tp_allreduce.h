@@ -11,28 +11,55 @@ namespace velo {
 constexpr int kPeerMaxRanks = 8;
 // CTAs per launch: fixed, so that the exit count a call waits for (calls x ranks x
 // CTAs) does not depend on the call's size
-constexpr int kPeerGrid = 128;
+constexpr int kPeerGrid = 256;
 // flag block of one rank, per slot (u64 words): [0, 8) the ranks' entry epochs,
 // 8 the exit count, [16, 16 + kPeerGrid) this rank's CTAs' call counters
 constexpr int kPeerSlotWords = 16 + kPeerGrid;
 constexpr size_t kPeerFlagBytes = 4 * kPeerSlotWords * 8;  // 4 slots
 
-struct PeerAllReduceArgs {
-    __nv_bfloat16* buf[kPeerMaxRanks];  // every rank's partial buffer (own one included)
+// The cross-rank barriers of one call.  Every rank makes the same sequence of
+// calls on each slot; the calls are counted on the device, so a captured graph of
+// them stays in step.  All waits are bounded (2 s), after which the kernel
+// records an error in *err and returns.
+struct PeerSync {
     unsigned long long* flags[kPeerMaxRanks];  // every rank's flag block
-    size_t offset;       // elements: where this call's rows start in every buffer
-    size_t n;            // elements to sum (a multiple of 8)
     int rank, tp, slot;  // slot: one of 4 independent call sequences (one per stream)
     int* err;            // device error word (a wait ran out)
+};
+
+struct PeerAllReduceArgs {
+    PeerSync sync;
+    __nv_bfloat16* buf[kPeerMaxRanks];  // every rank's partial buffer (own one included)
+    size_t offset;       // elements: where this call's rows start in every buffer
+    size_t n;            // elements to sum (a multiple of 8)
 };
 
 // Sum n bf16 elements at `offset` over the tp ranks' buffers, in place on every
 // rank: rank r adds chunk r of all buffers in rank order (f32) and writes the
 // bf16 sum back into all of them, between a cross-rank entry barrier (every
-// partial written) and an exit barrier (every sum written).  Every rank makes the
-// same sequence of calls on each slot; the calls are counted on the device, so a
-// captured graph of them stays in step.  All waits are bounded (2 s), after which
-// the kernel records an error and returns.
+// partial written) and an exit barrier (every sum written).
 cudaError_t launch_peer_allreduce(const PeerAllReduceArgs& a, cudaStream_t stream);
+
+struct PeerGatherArgs {
+    PeerSync sync;
+    // this rank's receive area at the call's first row: slab s (at s * slab
+    // elements) holds rank s's partial of this rank's `cols` columns, row stride cols
+    const __nv_bfloat16* stage;
+    size_t slab;
+    // every rank's sum buffer at (the call's first row, this rank's first column),
+    // row stride ld
+    __nv_bfloat16* out[kPeerMaxRanks];
+    int rows, cols, ld;  // cols % 8 == 0
+};
+
+// Second half of the fused sum: the row-split GEMMs pushed their partials of
+// column block r to rank r (kEpiPeerBF16); after the entry barrier rank r adds
+// its tp slabs in rank order (f32), rounds to bf16 and stores the sum into
+// every rank's sum buffer, then waits at the exit barrier.  The values equal
+// launch_peer_allreduce's.
+cudaError_t launch_peer_gather(const PeerGatherArgs& a, cudaStream_t stream);
+
+// Group sizes the kernels are built for (2, 4, 8); others keep NCCL.
+bool peer_tp_supported(int tp);
 
 }  // namespace velo

@@ -96,7 +96,11 @@ struct Model {
     uint8_t* ipc_stage = nullptr;  // [tp][128] handles and device UUIDs for the all-gather
     unsigned long long* peer_flags[kPeerMaxRanks] = {};
     __nv_bfloat16* peer_ybf[kPeerMaxRanks] = {};
-    bool peer_flags_ok = false, peer_ybf_ok = false;
+    // receive area of the fused sum: [tp][cap_M][H / tp], slab s = rank s's partial
+    // of this rank's column block, written by rank s's GEMM epilogue
+    __nv_bfloat16* stage = nullptr;
+    __nv_bfloat16* peer_stage[kPeerMaxRanks] = {};
+    bool peer_flags_ok = false, peer_ybf_ok = false, peer_stage_ok = false;
     // step profile (velo_cuda_profile): an event at the start of every phase
     bool profile = false;
     std::vector<cudaEvent_t> prof_ev;
@@ -161,6 +165,7 @@ void close_peers(Model* m, void** peers) {
 void destroy_model(Model* m) {
     if (!m) return;
     close_peers(m, reinterpret_cast<void**>(m->peer_ybf));
+    close_peers(m, reinterpret_cast<void**>(m->peer_stage));
     close_peers(m, reinterpret_cast<void**>(m->peer_flags));
     for (void* p : m->allocs) cudaFree(p);
     for (void* p : m->work) cudaFree(p);
@@ -461,9 +466,12 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
             if (!st) m->peer_flags_ok = ipc_exchange(c, m, m->ar_flags, reinterpret_cast<void**>(m->peer_flags));
         }
         if (!st) m->peer_ybf_ok = ipc_exchange(c, m, m->ybf, reinterpret_cast<void**>(m->peer_ybf));
+        if (!st) st = dev_alloc(m, &m->stage, (size_t)cM * H * 2, true);
+        if (!st) m->peer_stage_ok = ipc_exchange(c, m, m->stage, reinterpret_cast<void**>(m->peer_stage));
         if (!st) {
             const bool all = group_all_ok(c, m, m->peer_flags_ok && m->peer_ybf_ok);
             m->peer_flags_ok = m->peer_ybf_ok = all;
+            m->peer_stage_ok = group_all_ok(c, m, all && m->peer_stage_ok);
         }
     }
     if (!st) st = dev_alloc(m, &m->pairs, (size_t)cM * 8, true);
@@ -554,23 +562,80 @@ int32_t allreduce_add(velo_cuda_ctx* c, Model* m, int M) {
 // buffers are mapped, else NCCL; VELO_TP_AR=nccl forces NCCL.
 bool use_peer_sum(const Model* m) {
     const char* e = std::getenv("VELO_TP_AR");
-    return m->peer_flags_ok && m->peer_ybf_ok && !(e && std::strcmp(e, "nccl") == 0);
+    return m->peer_flags_ok && m->peer_ybf_ok && peer_tp_supported(m->tp) && !(e && std::strcmp(e, "nccl") == 0);
+}
+
+// The fused sum (the GEMM epilogue pushes each column block to its owner, a
+// gather kernel adds and broadcasts) when the receive areas are mapped and the
+// column blocks are whole 32-column groups; VELO_TP_AR=peer keeps the separate
+// sum kernel.
+bool use_fused_sum(const Model* m) {
+    const char* e = std::getenv("VELO_TP_AR");
+    return use_peer_sum(m) && m->peer_stage_ok && m->H() % (32 * m->tp) == 0 &&
+           !(e && std::strcmp(e, "peer") == 0);
+}
+
+PeerSync peer_sync(velo_cuda_ctx* c, const Model* m, int slot) {
+    PeerSync y{};
+    for (int p = 0; p < m->tp; ++p) y.flags[p] = m->peer_flags[p];
+    y.rank = m->rank;
+    y.tp = m->tp;
+    y.slot = slot;
+    y.err = c->err_flag;
+    return y;
 }
 
 int32_t peer_sum(velo_cuda_ctx* c, Model* m, size_t offset, size_t n, int slot, cudaStream_t s) {
     PeerAllReduceArgs a{};
-    for (int p = 0; p < m->tp; ++p) {
-        a.buf[p] = m->peer_ybf[p];
-        a.flags[p] = m->peer_flags[p];
-    }
+    a.sync = peer_sync(c, m, slot);
+    for (int p = 0; p < m->tp; ++p) a.buf[p] = m->peer_ybf[p];
     a.offset = offset;
     a.n = n;
-    a.rank = m->rank;
-    a.tp = m->tp;
-    a.slot = slot;
-    a.err = c->err_flag;
     VELO_CUDA_TRY(launch_peer_allreduce(a, s));
     return VELO_OK;
+}
+
+// Row-split GEMM (o_proj, down_proj) of `rows` rows from row0 with the
+// tensor-parallel sum fused in: the epilogue stores column block o of the bf16
+// partial into rank o's receive area (slab `rank`; gemm_push), then the gather
+// kernel of this rank adds its block's tp slabs and stores the sum into every
+// rank's ybf (gather_sum).
+int32_t gemm_push(velo_cuda_ctx* c, Model* m, cudaStream_t s, const uint8_t* w, const __half* x, int rows, int K,
+                  size_t row0) {
+    const int H = m->H(), tp = m->tp, Hc = H / tp;
+    Q4GemmArgs a{};
+    a.w = w;
+    a.N = H;
+    a.K = K;
+    a.M = rows;
+    a.y = nullptr;
+    a.ldy = H;
+    a.mode = kEpiPeerBF16;
+    a.err = c->err_flag;
+    a.peer_cols = Hc;
+    for (int o = 0; o < tp; ++o) a.peer_y[o] = m->peer_stage[o] + ((size_t)m->rank * m->cap_M + row0) * Hc;
+    VELO_CUDA_TRY(launch_q4_gemm(a, x, c->sm_count, s));
+    return VELO_OK;
+}
+
+int32_t gather_sum(velo_cuda_ctx* c, Model* m, cudaStream_t s, int rows, size_t row0, int slot) {
+    const int H = m->H(), tp = m->tp, Hc = H / tp;
+    PeerGatherArgs g{};
+    g.sync = peer_sync(c, m, slot);
+    g.stage = m->stage + row0 * Hc;
+    g.slab = (size_t)m->cap_M * Hc;
+    for (int p = 0; p < tp; ++p) g.out[p] = m->peer_ybf[p] + row0 * H + (size_t)m->rank * Hc;
+    g.rows = rows;
+    g.cols = Hc;
+    g.ld = H;
+    VELO_CUDA_TRY(launch_peer_gather(g, s));
+    return VELO_OK;
+}
+
+int32_t gemm_fused_sum(velo_cuda_ctx* c, Model* m, cudaStream_t s, const uint8_t* w, const __half* x, int rows,
+                       int K, size_t row0, int slot) {
+    int32_t st = gemm_push(c, m, s, w, x, rows, K, row0);
+    return st ? st : gather_sum(c, m, s, rows, row0, slot);
 }
 
 int32_t allreduce_bf16(velo_cuda_ctx* c, Model* m, int M) {
@@ -624,6 +689,7 @@ int32_t forward_tp_halves(velo_cuda_ctx* c, Model* m, int B, int N) {
                                         ncclSum, static_cast<ncclComm_t>(comm[h]), m->half_stream[h]),
                           nc, "ncclAllReduce");
     };
+    const bool fused = use_fused_sum(m);
     int32_t st = VELO_OK;
     for (int l = 0; l < L; ++l) {
         const Layer& ly = m->layers[l];
@@ -661,9 +727,14 @@ int32_t forward_tp_halves(velo_cuda_ctx* c, Model* m, int B, int N) {
             a.scale_log2 = (float)(1.4426950408889634 / std::sqrt(128.0));
             a.err = c->err_flag;
             VELO_CUDA_TRY(launch_tree_attention(a, m->kv_int8 != 0, s));
-            st = gemm_on(c, s, ly.wo, m->attn + o * Hq * 128, rows(h), H, Hq * 128, m->ybf + o * H, H,
-                         kEpiStoreBF16);
-            if (!st) st = reduce(h);
+            if (fused) {
+                pending[h] = true;
+                st = gemm_fused_sum(c, m, s, ly.wo, m->attn + o * Hq * 128, rows(h), Hq * 128, o, h);
+            } else {
+                st = gemm_on(c, s, ly.wo, m->attn + o * Hq * 128, rows(h), H, Hq * 128, m->ybf + o * H, H,
+                             kEpiStoreBF16);
+                if (!st) st = reduce(h);
+            }
         }
         for (int h = 0; h < 2 && !st; ++h) {  // feed-forward block
             if (!bh[h]) continue;
@@ -671,8 +742,13 @@ int32_t forward_tp_halves(velo_cuda_ctx* c, Model* m, int B, int N) {
             const size_t o = r0(h);
             VELO_CUDA_TRY(norm(h, ly.ffn_norm));
             st = gemm_on(c, s, ly.w13, m->xn + o * H, rows(h), 2 * F, H, m->hbuf + o * F, F, kEpiSwiGLU);
-            if (!st) st = gemm_on(c, s, ly.w2, m->hbuf + o * F, rows(h), H, F, m->ybf + o * H, H, kEpiStoreBF16);
-            if (!st) st = reduce(h);
+            if (!st && fused) {
+                pending[h] = true;
+                st = gemm_fused_sum(c, m, s, ly.w2, m->hbuf + o * F, rows(h), F, o, h);
+            } else if (!st) {
+                st = gemm_on(c, s, ly.w2, m->hbuf + o * F, rows(h), H, F, m->ybf + o * H, H, kEpiStoreBF16);
+                if (!st) st = reduce(h);
+            }
         }
         if (st) return st;
     }
@@ -1288,6 +1364,15 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
     auto row_split = [&](const uint8_t* w, const __half* in, int K, int phase) -> int32_t {
         VELO_CUDA_TRY(velo::prof_mark(c, m, phase));
         if (m->tp == 1) return velo::gemm(c, w, in, M, H, K, m->x, H, velo::kEpiAddF32);
+        if (velo::use_fused_sum(m)) {
+            // the GEMM pushes the partial to the column blocks' owners; the phase
+            // after it is the gather kernel
+            int32_t r = velo::gemm_push(c, m, s, w, in, M, K, 0);
+            if (r) return r;
+            VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_ALLREDUCE));
+            pending = true;
+            return velo::gather_sum(c, m, s, M, 0, 0);
+        }
         int32_t r = velo::gemm(c, w, in, M, H, K, m->ybf, H, velo::kEpiStoreBF16);
         if (r) return r;
         VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_ALLREDUCE));
@@ -1588,7 +1673,10 @@ int32_t velo_cuda_tp_sum_path(velo_cuda_ctx* c, int32_t* path) {
     if (st) return st;
     if (!path) return fail(VELO_ERR_INVALID_ARGUMENT, "tp_sum_path: null output");
     const Model* m = c->model;
-    *path = m->tp < 2 || m->f32 ? VELO_TP_SUM_NONE : velo::use_peer_sum(m) ? VELO_TP_SUM_PEER : VELO_TP_SUM_NCCL;
+    *path = m->tp < 2 || m->f32         ? VELO_TP_SUM_NONE
+            : velo::use_fused_sum(m) ? VELO_TP_SUM_FUSED
+            : velo::use_peer_sum(m)  ? VELO_TP_SUM_PEER
+                                     : VELO_TP_SUM_NCCL;
     return VELO_OK;
 }
 
