@@ -558,6 +558,14 @@ typedef enum velo_tp_sum {
 } velo_tp_sum;
 VELO_API int32_t velo_cuda_tp_sum_path(velo_cuda_ctx *ctx, int32_t *path);
 
+/* Failure-detection check of the peer sums' cross-rank barriers on one GPU
+ * (no context): launches the gather kernel as rank 0 of a group of 2 whose
+ * rank 1 never arrives; the bounded waits give up (2 s each) and the kernel
+ * returns, leaving the GPU usable.  *code = the error the kernel recorded
+ * (0x7101: the entry barrier ran out).  Instrumentation, no counterpart in the
+ * reference. */
+VELO_API int32_t velo_cuda_tp_wait_selftest(int32_t device, int32_t *code);
+
 #ifdef __cplusplus
 }
 #endif

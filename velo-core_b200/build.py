@@ -82,11 +82,15 @@ def build(force=False, verbose=False):
                     raise RuntimeError(f"nvcc failed on {src}")
     objs = [_obj(s) for s in srcs]
     if todo or not os.path.exists(LIB):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-ldl", "-lpthread"]
+        # linked beside the library and renamed over it, so that a process loading it
+        # meanwhile sees the old or the new file, never a partial one
+        tmp = LIB + ".partial"
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", tmp] + objs + ["-ldl", "-lpthread"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             sys.stderr.write(r.stdout + r.stderr)
             raise RuntimeError("link of libvelo_cuda.so failed")
+        os.replace(tmp, LIB)
     return LIB
 
 

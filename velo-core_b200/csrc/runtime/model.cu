@@ -1680,4 +1680,55 @@ int32_t velo_cuda_tp_sum_path(velo_cuda_ctx* c, int32_t* path) {
     return VELO_OK;
 }
 
+// The peer-sum barriers' time limit, exercised on one GPU: a gather call of rank 0
+// in a group of 2 whose rank 1 never arrives (its flag block is memory nothing
+// writes).  The entry wait and the exit wait each give up after 2 s; *code gets the
+// first error the kernel recorded (0x7101: entry).
+int32_t velo_cuda_tp_wait_selftest(int32_t device, int32_t* code) {
+    velo::clear_last_error();
+    if (!code) return fail(VELO_ERR_INVALID_ARGUMENT, "tp_wait_selftest: null output");
+    VELO_CUDA_TRY(cudaSetDevice(device));
+    unsigned long long* flags = nullptr;
+    int* err = nullptr;
+    __nv_bfloat16* buf = nullptr;
+    cudaStream_t s = nullptr;
+    int32_t st = VELO_OK;
+    auto check = [&](cudaError_t e) {
+        if (e != cudaSuccess && !st) st = fail(VELO_ERR_CUDA, "tp_wait_selftest: %s", cudaGetErrorString(e));
+    };
+    check(cudaMalloc(&flags, 2 * velo::kPeerFlagBytes));
+    if (!st) check(cudaMalloc(&err, sizeof(int)));
+    if (!st) check(cudaMalloc(&buf, 64 * sizeof(__nv_bfloat16)));
+    if (!st) check(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    if (!st) check(cudaMemset(flags, 0, 2 * velo::kPeerFlagBytes));
+    if (!st) check(cudaMemset(err, 0, sizeof(int)));
+    if (!st) check(cudaMemset(buf, 0, 64 * sizeof(__nv_bfloat16)));
+    if (!st) {
+        velo::PeerGatherArgs g{};
+        g.sync.flags[0] = flags;
+        g.sync.flags[1] = flags + velo::kPeerFlagBytes / 8;
+        g.sync.rank = 0;
+        g.sync.tp = 2;
+        g.sync.slot = 0;
+        g.sync.err = err;
+        g.stage = buf;           // slabs 0 and 1: 8 elements each
+        g.slab = 8;
+        g.out[0] = buf + 16;     // both "ranks'" sums land in this process
+        g.out[1] = buf + 32;
+        g.rows = 1;
+        g.cols = 8;
+        g.ld = 8;
+        check(velo::launch_peer_gather(g, s));
+    }
+    if (!st) check(cudaStreamSynchronize(s));
+    int h = 0;
+    if (!st) check(cudaMemcpy(&h, err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (s) cudaStreamDestroy(s);
+    cudaFree(buf);
+    cudaFree(err);
+    cudaFree(flags);
+    if (!st) *code = h;
+    return st;
+}
+
 }  // extern "C"

@@ -109,6 +109,7 @@ _SIGS = {
     "velo_cuda_profile": (_I32, [_P, _I32]),
     "velo_cuda_profile_read": (_I32, [_P, ctypes.POINTER(ctypes.c_double), _I32, ctypes.POINTER(_I32)]),
     "velo_cuda_tp_sum_path": (_I32, [_P, ctypes.POINTER(_I32)]),
+    "velo_cuda_tp_wait_selftest": (_I32, [_I32, ctypes.POINTER(_I32)]),
     "velo_cuda_shard_strategy": (_I32, [ctypes.c_char_p]),
     "velo_cuda_shard_weight": (_I32, [_P, _I32, _I32, _I32, _P, ctypes.c_size_t,
                                       ctypes.POINTER(ctypes.c_uint64),
@@ -653,6 +654,14 @@ def nccl_unique_id():
     buf = (ctypes.c_char * 128)()
     check(lib().velo_cuda_nccl_unique_id(buf))
     return bytes(buf)
+
+
+def tp_wait_selftest(device=0):
+    """velo_cuda_tp_wait_selftest: the error code the peer-sum kernel records
+    when its partner rank never arrives (0x7101), after its bounded waits."""
+    code = _I32(0)
+    check(lib().velo_cuda_tp_wait_selftest(device, ctypes.byref(code)))
+    return int(code.value)
 
 
 def shard_strategy(name):
