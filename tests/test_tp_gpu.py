@@ -368,3 +368,58 @@ def test_tp2_peer_memory_sum_matches_nccl():
     for b in range(B):
         ref = ora.verify_tree(tokens[b], parents[b], 0)
         assert np.abs(out[0][1][("fused", "1")][0][b] - ref).max() <= 2e-2
+
+
+SHAPE_WIDE = dict(n_vocab=1024, n_embd=1024, n_layer=2, n_head=8, n_head_kv=8, n_ff=2048)
+
+
+def test_tp_all_gpus_peer_sums_match_nccl_and_oracle():
+    """The same comparison on every GPU of the box (4 or 8 ranks; skipped with
+    fewer): 8 KV heads so that each rank keeps at least one, hidden 1024 so that
+    every rank owns a whole 32-column block of the fused sum.  Fused and
+    unfused peer sums are bit-identical (same partials, same rank order); NCCL
+    adds in its own order, so all three are held to the unsharded oracle (2e-2)
+    and to each other within 1e-2."""
+    import torch
+    n = torch.cuda.device_count()
+    if n < 4:
+        pytest.skip("needs 4 or more GPUs")
+    tp = 8 if n >= 8 else 4
+    import multiprocessing as mp
+    import velo_cuda
+    meta, tensors = synthetic.llama_q4_model(**SHAPE_WIDE, seed=45)
+    g = synthetic.rng(46, 80)
+    B, N = 3, 8
+    parents = np.stack([synthetic.random_tree(N, 4, g) for _ in range(B)])
+    tokens = g.integers(0, meta["n_vocab"], (B, N)).astype(np.uint32)
+    nid = velo_cuda.nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_rank_sum_paths, args=(r, tp, nid, meta, tensors, tokens, parents, q))
+          for r in range(tp)]
+    for p in ps:
+        p.start()
+    out = {}
+    for _ in ps:
+        r = q.get(timeout=600)
+        out[r[0]] = r
+    for p in ps:
+        p.join(timeout=60)
+    for r in range(tp):
+        assert out[r][4] is None, out[r][4]
+        assert out[r][2] == {"fused": "fused", "peer": "peer", "nccl": "nccl"}
+        runs = out[r][1]
+        for key, steps in runs.items():
+            for s in steps[1:]:
+                assert np.array_equal(s, steps[0]), key
+        for ov in ("1", "0"):
+            assert np.array_equal(runs[("fused", ov)][0], runs[("peer", ov)][0]), ov
+            assert np.abs(runs[("peer", ov)][0] - runs[("nccl", ov)][0]).max() <= 1e-2
+    for key in out[0][1]:
+        for r in range(1, tp):
+            assert np.array_equal(out[0][1][key][0], out[r][1][key][0]), (key, r)
+    ora = vo.Model(dict(meta, n_ctx=64), synthetic.oracle_tensor_list(meta, tensors))
+    for b in range(B):
+        ref = ora.verify_tree(tokens[b], parents[b], 0)
+        for mode in ("fused", "nccl"):
+            assert np.abs(out[0][1][(mode, "1")][0][b] - ref).max() <= 2e-2
