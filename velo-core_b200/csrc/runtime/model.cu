@@ -562,17 +562,21 @@ int32_t allreduce_add(velo_cuda_ctx* c, Model* m, int M) {
 // buffers are mapped, else NCCL; VELO_TP_AR=nccl forces NCCL.
 bool use_peer_sum(const Model* m) {
     const char* e = std::getenv("VELO_TP_AR");
-    return m->peer_flags_ok && m->peer_ybf_ok && peer_tp_supported(m->tp) && !(e && std::strcmp(e, "nccl") == 0);
+    const bool want = e ? std::strcmp(e, "nccl") != 0 : m->tp >= 4;
+    return want && m->peer_flags_ok && m->peer_ybf_ok && peer_tp_supported(m->tp);
 }
 
 // The fused sum (the GEMM epilogue pushes each column block to its owner, a
 // gather kernel adds and broadcasts) when the receive areas are mapped and the
-// column blocks are whole 32-column groups; VELO_TP_AR=peer keeps the separate
-// sum kernel.
+// column blocks are whole 32-column groups, by default from 4 ranks on.  At 2
+// ranks the sums are a small share of the step and two streams already hide
+// NCCL's; the epilogue's NVLink stores then cost the GEMMs more than the gather
+// saves (config 5: 157.6 ms per step with NCCL against 164.2 fused; at 4 ranks
+// 95.5 against 89.2).  VELO_TP_AR=fused / peer / nccl chooses explicitly.
 bool use_fused_sum(const Model* m) {
     const char* e = std::getenv("VELO_TP_AR");
-    return use_peer_sum(m) && m->peer_stage_ok && m->H() % (32 * m->tp) == 0 &&
-           !(e && std::strcmp(e, "peer") == 0);
+    const bool want = e ? std::strcmp(e, "fused") == 0 : m->tp >= 4;
+    return want && use_peer_sum(m) && m->peer_stage_ok && m->H() % (32 * m->tp) == 0;
 }
 
 PeerSync peer_sync(velo_cuda_ctx* c, const Model* m, int slot) {
