@@ -599,7 +599,10 @@ def run_attn(args):
     res = []
     cfgs = [("config4_int8", 128, 64, 32, 8, None, True),
             ("config3_layer_f16", 32, 16, 32, 32, 2048, False),
-            ("config5_layer_f16", 64, 32, 64, 8, 4096, False)]
+            ("config5_layer_f16", 64, 32, 64, 8, 4096, False),
+            # one rank's heads of the config-5 layer under tensor parallelism (4 and 8 GPUs)
+            ("config5_tp4_layer_f16", 64, 32, 16, 2, 4096, False),
+            ("config5_tp8_layer_f16", 64, 32, 8, 1, 4096, False)]
     for name, B, N, Hq, Hkv, fixed_ctx, i8 in cfgs:
         if args.case and args.case != name:
             continue

@@ -685,13 +685,26 @@ cudaError_t launch_impl(const TreeAttnArgs& a, cudaStream_t stream) {
 // More than 128 query rows per KV head (nodes x group heads) take two query
 // tiles per CTA: each K/V tile is then fetched (and converted) once for 256
 // rows (config 4: 802 us against 1246 with one tile per CTA; config-5 layer:
-// 359 us against 455).  VELO_ATTN_QUERY_TILES=1 or 2 in the environment
-// forces one layout (read at each launch; for comparisons).
+// 359 us against 455) -- unless that grid would leave more than half the SMs
+// idle: one rank's heads of the config-5 layer at 8 GPUs (64 sequences x 1 KV
+// head = 64 CTAs of two tiles) took 84.1 us, as 128 CTAs of one tile 53.6 us
+// (at 4 GPUs, 128 CTAs of two tiles 88.3 us against 256 of one 98.7 us).
+// VELO_ATTN_QUERY_TILES=1 or 2 in the environment forces one layout (read at
+// each launch; for comparisons).
 template <bool INT8>
 cudaError_t launch_rows(const TreeAttnArgs& a, cudaStream_t stream) {
     const char* e = std::getenv("VELO_ATTN_QUERY_TILES");
     const bool many_rows = a.N * (a.Hq / a.Hkv) > BMQ;
     int qt = many_rows ? 2 : 1;
+    if (qt == 2) {
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess) {
+            const long rows = (long)a.N * (a.Hq / a.Hkv);
+            const long grid2 = (long)a.B * a.Hkv * ((rows + 2 * BMQ - 1) / (2 * BMQ));
+            if (2 * grid2 <= sms) qt = 1;
+        }
+    }
     if (e != nullptr && std::strcmp(e, "1") == 0) qt = 1;
     if (e != nullptr && std::strcmp(e, "2") == 0 && many_rows) qt = 2;
     return qt == 2 ? launch_impl<INT8, 2>(a, stream) : launch_impl<INT8, 1>(a, stream);

@@ -36,6 +36,12 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
     return t;
 }
 
+// Four floats as four f16 (round to nearest) in one 8-byte word.
+__device__ __forceinline__ uint2 pack_half4(float a, float b, float c, float d) {
+    const __half2 lo = __floats2half2_rn(a, b), hi = __floats2half2_rn(c, d);
+    return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
 __global__ void rmsnorm_f16_kernel(const float* __restrict__ x, const float* __restrict__ w, int H,
                                    float eps, __half* __restrict__ y) {
     __shared__ float sh[32];
@@ -49,11 +55,43 @@ __global__ void rmsnorm_f16_kernel(const float* __restrict__ x, const float* __r
     ss = block_sum(ss, sh);
     const float rms = sqrtf(ss / (float)H + eps);
     const float4* wr = reinterpret_cast<const float4*>(w);
-    __half2* yr = reinterpret_cast<__half2*>(y + (size_t)m * H);
+    uint2* yr = reinterpret_cast<uint2*>(y + (size_t)m * H);
     for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
         const float4 v = xr[i], g = wr[i];
-        yr[2 * i] = __floats2half2_rn((v.x / rms) * g.x, (v.y / rms) * g.y);
-        yr[2 * i + 1] = __floats2half2_rn((v.z / rms) * g.z, (v.w / rms) * g.w);
+        yr[i] = pack_half4((v.x / rms) * g.x, (v.y / rms) * g.y, (v.z / rms) * g.z, (v.w / rms) * g.w);
+    }
+}
+
+// The same for rows of at most kNormMaxPer x 1024 elements: one read of x, the
+// row kept in registers between the sum of squares and the scaling.
+constexpr int kNormMaxPer = 8;
+__global__ void __launch_bounds__(256) rmsnorm_f16_reg_kernel(const float* __restrict__ x,
+                                                              const float* __restrict__ w, int H, float eps,
+                                                              __half* __restrict__ y) {
+    __shared__ float sh[32];
+    const int m = blockIdx.x;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)m * H);
+    float4 keep[kNormMaxPer];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kNormMaxPer; ++j) {
+        const int i = threadIdx.x + j * 256;
+        if (i < H / 4) {
+            keep[j] = xr[i];
+            ss += keep[j].x * keep[j].x + keep[j].y * keep[j].y + keep[j].z * keep[j].z + keep[j].w * keep[j].w;
+        }
+    }
+    ss = block_sum(ss, sh);
+    const float rms = sqrtf(ss / (float)H + eps);
+    const float4* wr = reinterpret_cast<const float4*>(w);
+    uint2* yr = reinterpret_cast<uint2*>(y + (size_t)m * H);
+#pragma unroll
+    for (int j = 0; j < kNormMaxPer; ++j) {
+        const int i = threadIdx.x + j * 256;
+        if (i < H / 4) {
+            const float4 v = keep[j], g = wr[i];
+            yr[i] = pack_half4((v.x / rms) * g.x, (v.y / rms) * g.y, (v.z / rms) * g.z, (v.w / rms) * g.w);
+        }
     }
 }
 
@@ -68,7 +106,7 @@ __global__ void add_rmsnorm_f16_kernel(float* __restrict__ x, const __nv_bfloat1
     constexpr int kMaxPer = 8;
     const int m = blockIdx.x;
     float4* xr = reinterpret_cast<float4*>(x + (size_t)m * H);
-    const __nv_bfloat162* sr = reinterpret_cast<const __nv_bfloat162*>(sum + (size_t)m * H);
+    const uint2* sr = reinterpret_cast<const uint2*>(sum + (size_t)m * H);
     float4 keep[kMaxPer];
     float ss = 0.0f;
 #pragma unroll
@@ -76,8 +114,9 @@ __global__ void add_rmsnorm_f16_kernel(float* __restrict__ x, const __nv_bfloat1
         const int i = threadIdx.x + j * blockDim.x;
         if (i < H / 4) {
             float4 v = xr[i];
-            const float2 a = __bfloat1622float2(sr[2 * i]);
-            const float2 b = __bfloat1622float2(sr[2 * i + 1]);
+            const uint2 sv = sr[i];  // four bf16 of the sum
+            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sv.x));
+            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sv.y));
             v.x += a.x;
             v.y += a.y;
             v.z += b.x;
@@ -90,14 +129,13 @@ __global__ void add_rmsnorm_f16_kernel(float* __restrict__ x, const __nv_bfloat1
     ss = block_sum(ss, sh);
     const float rms = sqrtf(ss / (float)H + eps);
     const float4* wr = reinterpret_cast<const float4*>(w);
-    __half2* yr = reinterpret_cast<__half2*>(y + (size_t)m * H);
+    uint2* yr = reinterpret_cast<uint2*>(y + (size_t)m * H);
 #pragma unroll
     for (int j = 0; j < kMaxPer; ++j) {
         const int i = threadIdx.x + j * blockDim.x;
         if (i < H / 4) {
             const float4 v = keep[j], g = wr[i];
-            yr[2 * i] = __floats2half2_rn((v.x / rms) * g.x, (v.y / rms) * g.y);
-            yr[2 * i + 1] = __floats2half2_rn((v.z / rms) * g.z, (v.w / rms) * g.w);
+            yr[i] = pack_half4((v.x / rms) * g.x, (v.y / rms) * g.y, (v.z / rms) * g.z, (v.w / rms) * g.w);
         }
     }
 }
@@ -374,7 +412,11 @@ cudaError_t launch_embed(const float* emb, const uint32_t* tokens, int M, int H,
 cudaError_t launch_rmsnorm_f16(const float* x, const float* w, int M, int H, float eps, __half* y,
                                cudaStream_t s) {
     if (M == 0) return cudaSuccess;
-    rmsnorm_f16_kernel<<<M, 256, 0, s>>>(x, w, H, eps, y);
+    if (H % 4) return cudaErrorInvalidValue;
+    if (H / 4 <= 256 * kNormMaxPer)
+        rmsnorm_f16_reg_kernel<<<M, 256, 0, s>>>(x, w, H, eps, y);
+    else
+        rmsnorm_f16_kernel<<<M, 256, 0, s>>>(x, w, H, eps, y);
     return cudaGetLastError();
 }
 
