@@ -937,8 +937,9 @@ def run_verify(args):
     D2H = (2 * B + 2 * M) * 4                # path lengths, bonus tokens, paths, expected tokens
     L = meta["n_layer"]
     sum_path = ctx.tp_sum_path()
-    # per layer 8 kernels, plus the two partial-sum kernels when they are ours
-    launches = 2 + (8 + (2 if sum_path in ("peer", "fused") else 0)) * L + 2 + (2 if ws == 1 else 3) + 1
+    # per layer 8 kernels, plus our sum kernels: 2 (peer, fused) or 2 x 5 (ce: signal,
+    # wait, add, signal, wait per sum)
+    launches = 2 + (8 + {"peer": 2, "fused": 2, "ce": 10}.get(sum_path, 0)) * L + 2 + (2 if ws == 1 else 3) + 1
     traffic = None
     if ws == 1:
         traffic = load_traffic("q4gemm_swiglu_c5" if c5 else "q4gemm_swiglu_c3")
@@ -954,7 +955,9 @@ def run_verify(args):
                   "does not depend on their values)",
         "config": {"workload": wl, "B": B, "nodes": N, "ctx": ctx_len, "rows": M,
                    "parallelism": f"tp{ws}" if ws > 1 else "tp1 (single GPU)",
-                   "tp_sum": {"fused": "row-split GEMM epilogue pushes each column block to its owner "
+                   "tp_sum": {"ce": "column blocks cross NVLink as copy-engine copies (CUDA IPC); "
+                                    "the owner's kernel adds, copies back",
+                              "fused": "row-split GEMM epilogue pushes each column block to its owner "
                                        "over NVLink (CUDA IPC); the owner's kernel adds and broadcasts",
                               "peer": "one kernel over NVLink peer memory (CUDA IPC)",
                               "nccl": "NCCL bf16 all-reduce", "none": None}[sum_path],

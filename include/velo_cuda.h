@@ -553,8 +553,10 @@ typedef enum velo_tp_sum {
     VELO_TP_SUM_NONE = 0,  /* one GPU, or the f32 path (NCCL f32 all-reduce) */
     VELO_TP_SUM_NCCL = 1,  /* NCCL bf16 all-reduce */
     VELO_TP_SUM_PEER = 2,  /* one kernel over NVLink peer memory (VELO_TP_AR=peer) */
-    VELO_TP_SUM_FUSED = 3  /* the GEMM epilogue pushes each column block to its owner
+    VELO_TP_SUM_FUSED = 3, /* the GEMM epilogue pushes each column block to its owner
                               rank, whose gather kernel adds and broadcasts it */
+    VELO_TP_SUM_CE = 4     /* VELO_TP_AR=ce: the blocks cross NVLink as copy-engine
+                              copies; kernels only add and order them */
 } velo_tp_sum;
 VELO_API int32_t velo_cuda_tp_sum_path(velo_cuda_ctx *ctx, int32_t *path);
 

@@ -301,7 +301,7 @@ def _rank_sum_paths(rank, tp, nid, meta, tensors, tokens, parents, q):
             return ctx.verify_step(slots, cl, tokens, parents, commit=False, want_logits=True,
                                    n_vocab=nv)["logits"]
         runs, paths = {}, {}
-        for mode in ("fused", "peer", "nccl"):
+        for mode in ("fused", "peer", "ce", "nccl"):
             os.environ["VELO_TP_AR"] = mode
             for ov in ("1", "0"):
                 os.environ["VELO_TP_OVERLAP"] = ov
@@ -353,13 +353,14 @@ def test_tp2_peer_memory_sum_matches_nccl():
         p.join(timeout=60)
     for r in range(2):
         assert out[r][4] is None, out[r][4]
-        assert out[r][2] == {"fused": "fused", "peer": "peer", "nccl": "nccl"}
+        assert out[r][2] == {"fused": "fused", "peer": "peer", "ce": "ce", "nccl": "nccl"}
         runs = out[r][1]
         for key, steps in runs.items():
             for s in steps[1:]:
                 assert np.array_equal(s, steps[0]), key
         for ov in ("1", "0"):
             assert np.array_equal(runs[("fused", ov)][0], runs[("peer", ov)][0]), ov
+            assert np.array_equal(runs[("ce", ov)][0], runs[("peer", ov)][0]), ov
             assert np.abs(runs[("peer", ov)][0] - runs[("nccl", ov)][0]).max() <= 1e-3
     for key in out[0][1]:
         assert np.array_equal(out[0][1][key][0], out[1][1][key][0]), key
@@ -408,13 +409,14 @@ def test_tp_all_gpus_peer_sums_match_nccl_and_oracle():
         p.join(timeout=60)
     for r in range(tp):
         assert out[r][4] is None, out[r][4]
-        assert out[r][2] == {"fused": "fused", "peer": "peer", "nccl": "nccl"}
+        assert out[r][2] == {"fused": "fused", "peer": "peer", "ce": "ce", "nccl": "nccl"}
         runs = out[r][1]
         for key, steps in runs.items():
             for s in steps[1:]:
                 assert np.array_equal(s, steps[0]), key
         for ov in ("1", "0"):
             assert np.array_equal(runs[("fused", ov)][0], runs[("peer", ov)][0]), ov
+            assert np.array_equal(runs[("ce", ov)][0], runs[("peer", ov)][0]), ov
     for key in out[0][1]:
         for r in range(1, tp):
             assert np.array_equal(out[0][1][key][0], out[r][1][key][0]), (key, r)

@@ -36,7 +36,7 @@ namespace {
 
 constexpr int kThreads = 128;
 constexpr unsigned long long kWaitNs = 2000000000ull;
-constexpr int kErrPeerEntry = 0x7101, kErrPeerExit = 0x7102;
+constexpr int kErrPeerEntry = 0x7101, kErrPeerExit = 0x7102, kErrCeWait = 0x7103;
 
 __device__ __forceinline__ unsigned long long now_ns() {
     unsigned long long t;
@@ -215,6 +215,48 @@ __global__ void __launch_bounds__(kThreads) peer_gather_kernel(const __grid_cons
     peer_exit(a.sync);
 }
 
+// ---- copy-engine form
+__device__ __forceinline__ unsigned long long* ce_block(const PeerSync& y, int p) {
+    return y.flags[p] + (kCeSlot0 + y.slot) * kPeerSlotWords;
+}
+
+__global__ void ce_signal_kernel(const __grid_constant__ PeerSync y, int phase) {
+    __shared__ unsigned long long epoch_sh;
+    unsigned long long* ctr = ce_block(y, y.rank) + 16 + phase;
+    if (threadIdx.x == 0) {
+        epoch_sh = *ctr + 1;
+        *ctr = epoch_sh;
+    }
+    __syncthreads();
+    const int p = threadIdx.x;
+    if (p < y.tp) {
+        __threadfence_system();
+        st_release_sys(ce_block(y, p) + 8 * phase + y.rank, epoch_sh);
+    }
+}
+
+__global__ void ce_wait_kernel(const __grid_constant__ PeerSync y, int phase) {
+    const unsigned long long* my = ce_block(y, y.rank);
+    const unsigned long long epoch = my[16 + phase];  // set by this call's signal on this stream
+    const int p = threadIdx.x;
+    if (p < y.tp && !wait_at_least(my + 8 * phase + p, epoch)) atomicCAS(y.err, 0, kErrCeWait);
+}
+
+template <int TP>
+__global__ void __launch_bounds__(256) ce_sum_kernel(const __grid_constant__ CeSumArgs a) {
+    const size_t nvec = a.n / 8;
+    for (size_t v = (size_t)blockIdx.x * 256 + threadIdx.x; v < nvec; v += (size_t)gridDim.x * 256) {
+        uint4 in[TP];
+#pragma unroll
+        for (int p = 0; p < TP; ++p)
+            in[p] = ld_volatile16((p == a.rank ? a.own : a.stage + p * a.slab) + v * 8);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int p = 0; p < TP; ++p) add8(acc, in[p]);
+        *reinterpret_cast<uint4*>(a.out + v * 8) = round_bf16x8(acc);
+    }
+}
+
 bool sync_ok(const PeerSync& y) {
     return y.tp >= 2 && y.tp <= kPeerMaxRanks && y.rank >= 0 && y.rank < y.tp && y.slot >= 0 && y.slot <= 3 &&
            y.err != nullptr;
@@ -246,5 +288,33 @@ cudaError_t launch_peer_gather(const PeerGatherArgs& a, cudaStream_t stream) {
 }
 
 bool peer_tp_supported(int tp) { return tp == 2 || tp == 4 || tp == 8; }
+
+cudaError_t launch_ce_signal(const PeerSync& y, int phase, cudaStream_t stream) {
+    if (!sync_ok(y) || y.slot > 1 || (phase != kCePhaseSlabs && phase != kCePhaseSums)) return cudaErrorInvalidValue;
+    ce_signal_kernel<<<1, 32, 0, stream>>>(y, phase);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ce_wait(const PeerSync& y, int phase, cudaStream_t stream) {
+    if (!sync_ok(y) || y.slot > 1 || (phase != kCePhaseSlabs && phase != kCePhaseSums)) return cudaErrorInvalidValue;
+    ce_wait_kernel<<<1, 32, 0, stream>>>(y, phase);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ce_sum(const CeSumArgs& a, int sm_count, cudaStream_t stream) {
+    if (a.n % 8 || a.slab % 8 || a.rank < 0 || a.rank >= a.tp) return cudaErrorInvalidValue;
+    if (a.n == 0) return cudaSuccess;
+    const size_t nvec = a.n / 8;
+    size_t grid = (nvec + 255) / 256;
+    const size_t cap = (size_t)(sm_count > 0 ? sm_count : 148) * 4;
+    if (grid > cap) grid = cap;
+    switch (a.tp) {
+        case 2: ce_sum_kernel<2><<<(unsigned)grid, 256, 0, stream>>>(a); break;
+        case 4: ce_sum_kernel<4><<<(unsigned)grid, 256, 0, stream>>>(a); break;
+        case 8: ce_sum_kernel<8><<<(unsigned)grid, 256, 0, stream>>>(a); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
 
 }  // namespace velo

@@ -62,4 +62,32 @@ cudaError_t launch_peer_gather(const PeerGatherArgs& a, cudaStream_t stream);
 // Group sizes the kernels are built for (2, 4, 8); others keep NCCL.
 bool peer_tp_supported(int tp);
 
+// ---- copy-engine form: the data crosses NVLink as cudaMemcpyAsync copies
+// (copy engines, no SMs); these kernels only order them and add.
+// Per slot of the flag block (slots 2 and 3; u64 words): [0, 8) the ranks'
+// "slab sent" epochs, [8, 16) the ranks' "sum sent" epochs, 16 / 17 this rank's
+// call counters of the two phases.
+constexpr int kCeSlot0 = 2;
+constexpr int kCePhaseSlabs = 0, kCePhaseSums = 1;
+
+// One warp: count this call on `phase` (a device counter, so graphs stay in
+// step) and publish the count to every rank's entry `rank` of the phase, with a
+// system-scope release.  Issued on the stream after the copies it announces.
+cudaError_t launch_ce_signal(const PeerSync& y, int phase, cudaStream_t stream);
+// One warp: wait (bounded, 2 s; 0x7103 in the error word when it runs out)
+// until every rank has published this call's count of `phase`.
+cudaError_t launch_ce_wait(const PeerSync& y, int phase, cudaStream_t stream);
+
+struct CeSumArgs {
+    const __nv_bfloat16* own;   // this rank's partial of its own column block
+    const __nv_bfloat16* stage; // receive area: slab s at s * slab (s != rank)
+    size_t slab;
+    __nv_bfloat16* out;         // this rank's column block of the sum
+    size_t n;                   // elements per block (rows x cols, a multiple of 8)
+    int rank, tp;
+};
+// out = bf16(sum over s in rank order of the tp partials, in f32): the values of
+// launch_peer_gather / launch_peer_allreduce.
+cudaError_t launch_ce_sum(const CeSumArgs& a, int sm_count, cudaStream_t stream);
+
 }  // namespace velo

@@ -99,14 +99,15 @@ __global__ void __launch_bounds__(256) rmsnorm_f16_reg_kernel(const float* __res
 // row-split GEMM), then the RMSNorm of the new x as rmsnorm_f16_kernel.  The
 // block keeps its row in registers between the two passes (H <= 8192: at most
 // 8 float4 per thread of 256).
+// blk_cols > 0: the sum is stored column-blocked, element (m, n) at
+// sum[(n / blk_cols) * blk_stride + m * blk_cols + n % blk_cols] (blk_cols % 4 == 0).
 __global__ void add_rmsnorm_f16_kernel(float* __restrict__ x, const __nv_bfloat16* __restrict__ sum,
                                        const float* __restrict__ w, int H, float eps,
-                                       __half* __restrict__ y) {
+                                       __half* __restrict__ y, int blk_cols, size_t blk_stride) {
     __shared__ float sh[32];
     constexpr int kMaxPer = 8;
     const int m = blockIdx.x;
     float4* xr = reinterpret_cast<float4*>(x + (size_t)m * H);
-    const uint2* sr = reinterpret_cast<const uint2*>(sum + (size_t)m * H);
     float4 keep[kMaxPer];
     float ss = 0.0f;
 #pragma unroll
@@ -114,7 +115,10 @@ __global__ void add_rmsnorm_f16_kernel(float* __restrict__ x, const __nv_bfloat1
         const int i = threadIdx.x + j * blockDim.x;
         if (i < H / 4) {
             float4 v = xr[i];
-            const uint2 sv = sr[i];  // four bf16 of the sum
+            const int n = 4 * i;
+            const size_t si = blk_cols > 0 ? (size_t)(n / blk_cols) * blk_stride + (size_t)m * blk_cols + n % blk_cols
+                                           : (size_t)m * H + n;
+            const uint2 sv = *reinterpret_cast<const uint2*>(sum + si);  // four bf16 of the sum
             const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sv.x));
             const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sv.y));
             v.x += a.x;
@@ -424,7 +428,15 @@ cudaError_t launch_add_rmsnorm_f16(float* x, const __nv_bfloat16* sum, const flo
                                    float eps, __half* y, cudaStream_t s) {
     if (M == 0) return cudaSuccess;
     if (H % 4 || H / 4 > 256 * 8) return cudaErrorInvalidValue;
-    add_rmsnorm_f16_kernel<<<M, 256, 0, s>>>(x, sum, w, H, eps, y);
+    add_rmsnorm_f16_kernel<<<M, 256, 0, s>>>(x, sum, w, H, eps, y, 0, 0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add_rmsnorm_blocked_f16(float* x, const __nv_bfloat16* sum, int blk_cols, size_t blk_stride,
+                                           const float* w, int M, int H, float eps, __half* y, cudaStream_t s) {
+    if (M == 0) return cudaSuccess;
+    if (H % 4 || H / 4 > 256 * 8 || blk_cols <= 0 || blk_cols % 4 || H % blk_cols) return cudaErrorInvalidValue;
+    add_rmsnorm_f16_kernel<<<M, 256, 0, s>>>(x, sum, w, H, eps, y, blk_cols, blk_stride);
     return cudaGetLastError();
 }
 

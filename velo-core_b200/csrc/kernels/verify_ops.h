@@ -41,6 +41,10 @@ cudaError_t launch_add_f32(float* x, const float* y, size_t n, cudaStream_t s);
 // y = f16(x / rms(x) * w) as launch_rmsnorm_f16 (H % 4 == 0, H <= 8192).
 cudaError_t launch_add_rmsnorm_f16(float* x, const __nv_bfloat16* sum, const float* w, int M, int H,
                                    float eps, __half* y, cudaStream_t s);
+// The same with the sum stored column-blocked (the copy-engine tensor-parallel
+// sum): element (m, n) at sum[(n / blk_cols) * blk_stride + m * blk_cols + n % blk_cols].
+cudaError_t launch_add_rmsnorm_blocked_f16(float* x, const __nv_bfloat16* sum, int blk_cols, size_t blk_stride,
+                                           const float* w, int M, int H, float eps, __half* y, cudaStream_t s);
 
 // Tensor parallelism, vocabulary-sharded LM head: per row the GreedySampler
 // maximum of this rank's logits [M][v_loc] as (value, global index) pairs

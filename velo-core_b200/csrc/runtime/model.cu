@@ -100,6 +100,8 @@ struct Model {
     // of this rank's column block, written by rank s's GEMM epilogue
     __nv_bfloat16* stage = nullptr;
     __nv_bfloat16* peer_stage[kPeerMaxRanks] = {};
+    // copy-engine sum: this rank's partial, column-blocked [tp][cap_M][H / tp] (local)
+    __nv_bfloat16* part = nullptr;
     bool peer_flags_ok = false, peer_ybf_ok = false, peer_stage_ok = false;
     // step profile (velo_cuda_profile): an event at the start of every phase
     bool profile = false;
@@ -467,6 +469,7 @@ int32_t ensure_work(velo_cuda_ctx* c, Model* m, int B, int N) {
         }
         if (!st) m->peer_ybf_ok = ipc_exchange(c, m, m->ybf, reinterpret_cast<void**>(m->peer_ybf));
         if (!st) st = dev_alloc(m, &m->stage, (size_t)cM * H * 2, true);
+        if (!st) st = dev_alloc(m, &m->part, (size_t)cM * H * 2, true);
         if (!st) m->peer_stage_ok = ipc_exchange(c, m, m->stage, reinterpret_cast<void**>(m->peer_stage));
         if (!st) {
             const bool all = group_all_ok(c, m, m->peer_flags_ok && m->peer_ybf_ok);
@@ -579,6 +582,16 @@ bool use_fused_sum(const Model* m) {
     return want && use_peer_sum(m) && m->peer_stage_ok && m->H() % (32 * m->tp) == 0;
 }
 
+// The copy-engine sum (VELO_TP_AR=ce): the GEMM stores its partial locally in
+// column blocks, each block crosses NVLink as one cudaMemcpyAsync to its owner,
+// the owner adds the tp blocks and copies its block of the sum to every rank;
+// one-warp kernels publish and await the copies' completion.
+bool use_ce_sum(const Model* m) {
+    const char* e = std::getenv("VELO_TP_AR");
+    return e && std::strcmp(e, "ce") == 0 && m->peer_flags_ok && m->peer_ybf_ok && m->peer_stage_ok &&
+           peer_tp_supported(m->tp) && m->H() % (32 * m->tp) == 0;
+}
+
 PeerSync peer_sync(velo_cuda_ctx* c, const Model* m, int slot) {
     PeerSync y{};
     for (int p = 0; p < m->tp; ++p) y.flags[p] = m->peer_flags[p];
@@ -636,8 +649,60 @@ int32_t gather_sum(velo_cuda_ctx* c, Model* m, cudaStream_t s, int rows, size_t 
     return VELO_OK;
 }
 
+// Copy-engine form of gemm_fused_sum (use_ce_sum).  Leaves this call's rows of
+// the sum in ybf, column-blocked: block o at ybf + o * cap_M * (H / tp).
+int32_t ce_gemm(velo_cuda_ctx* c, Model* m, cudaStream_t s, const uint8_t* w, const __half* x, int rows, int K,
+                size_t row0) {
+    const int H = m->H(), tp = m->tp, Hc = H / tp;
+    Q4GemmArgs a{};
+    a.w = w;
+    a.N = H;
+    a.K = K;
+    a.M = rows;
+    a.y = nullptr;
+    a.ldy = H;
+    a.mode = kEpiPeerBF16;  // to this rank's own column-blocked buffer: local stores
+    a.err = c->err_flag;
+    a.peer_cols = Hc;
+    for (int o = 0; o < tp; ++o) a.peer_y[o] = m->part + ((size_t)o * m->cap_M + row0) * Hc;
+    VELO_CUDA_TRY(launch_q4_gemm(a, x, c->sm_count, s));
+    return VELO_OK;
+}
+
+int32_t ce_sum(velo_cuda_ctx* c, Model* m, cudaStream_t s, int rows, size_t row0, int slot) {
+    const int tp = m->tp, r = m->rank, Hc = m->H() / tp;
+    const size_t bytes = (size_t)rows * Hc * 2, blk = (size_t)m->cap_M * Hc;
+    const PeerSync y = peer_sync(c, m, slot);
+    for (int o = 0; o < tp; ++o)
+        if (o != r)
+            VELO_CUDA_TRY(cudaMemcpyAsync(m->peer_stage[o] + r * blk + row0 * Hc, m->part + o * blk + row0 * Hc, bytes,
+                                          cudaMemcpyDeviceToDevice, s));
+    VELO_CUDA_TRY(launch_ce_signal(y, kCePhaseSlabs, s));
+    VELO_CUDA_TRY(launch_ce_wait(y, kCePhaseSlabs, s));
+    CeSumArgs g{};
+    g.own = m->part + r * blk + row0 * Hc;
+    g.stage = m->stage + row0 * Hc;
+    g.slab = blk;
+    g.out = m->ybf + r * blk + row0 * Hc;
+    g.n = (size_t)rows * Hc;
+    g.rank = r;
+    g.tp = tp;
+    VELO_CUDA_TRY(launch_ce_sum(g, c->sm_count, s));
+    for (int o = 0; o < tp; ++o)
+        if (o != r)
+            VELO_CUDA_TRY(cudaMemcpyAsync(m->peer_ybf[o] + r * blk + row0 * Hc, m->ybf + r * blk + row0 * Hc, bytes,
+                                          cudaMemcpyDeviceToDevice, s));
+    VELO_CUDA_TRY(launch_ce_signal(y, kCePhaseSums, s));
+    VELO_CUDA_TRY(launch_ce_wait(y, kCePhaseSums, s));
+    return VELO_OK;
+}
+
 int32_t gemm_fused_sum(velo_cuda_ctx* c, Model* m, cudaStream_t s, const uint8_t* w, const __half* x, int rows,
                        int K, size_t row0, int slot) {
+    if (use_ce_sum(m)) {
+        int32_t st = ce_gemm(c, m, s, w, x, rows, K, row0);
+        return st ? st : ce_sum(c, m, s, rows, row0, slot);
+    }
     int32_t st = gemm_push(c, m, s, w, x, rows, K, row0);
     return st ? st : gather_sum(c, m, s, rows, row0, slot);
 }
@@ -678,12 +743,17 @@ int32_t forward_tp_halves(velo_cuda_ctx* c, Model* m, int B, int N) {
     VELO_CUDA_TRY(cudaEventRecord(m->half_fork, c->stream));
     for (int h = 0; h < 2; ++h) VELO_CUDA_TRY(cudaStreamWaitEvent(m->half_stream[h], m->half_fork, 0));
     bool pending[2] = {false, false};
+    const bool ce = use_ce_sum(m);
     auto rows = [&](int h) { return bh[h] * N; };
     auto r0 = [&](int h) { return (size_t)b0[h] * N; };
     auto norm = [&](int h, const float* w) -> cudaError_t {
         const size_t o = r0(h) * H;
         if (!pending[h]) return launch_rmsnorm_f16(m->x + o, w, rows(h), H, eps, m->xn + o, m->half_stream[h]);
         pending[h] = false;
+        if (ce)
+            return launch_add_rmsnorm_blocked_f16(m->x + o, m->ybf + r0(h) * (H / m->tp), H / m->tp,
+                                                  (size_t)m->cap_M * (H / m->tp), w, rows(h), H, eps, m->xn + o,
+                                                  m->half_stream[h]);
         return launch_add_rmsnorm_f16(m->x + o, m->ybf + o, w, rows(h), H, eps, m->xn + o, m->half_stream[h]);
     };
     auto reduce = [&](int h) -> int32_t {
@@ -693,7 +763,7 @@ int32_t forward_tp_halves(velo_cuda_ctx* c, Model* m, int B, int N) {
                                         ncclSum, static_cast<ncclComm_t>(comm[h]), m->half_stream[h]),
                           nc, "ncclAllReduce");
     };
-    const bool fused = use_fused_sum(m);
+    const bool fused = ce || use_fused_sum(m);
     int32_t st = VELO_OK;
     for (int l = 0; l < L; ++l) {
         const Layer& ly = m->layers[l];
@@ -1363,11 +1433,21 @@ int32_t velo_cuda_verify_step(velo_cuda_ctx* c, const velo_verify_batch* in, vel
         if (e != cudaSuccess) return e;
         if (!pending) return velo::launch_rmsnorm_f16(m->x, w, M, H, eps, m->xn, s);
         pending = false;
+        if (velo::use_ce_sum(m))
+            return velo::launch_add_rmsnorm_blocked_f16(m->x, m->ybf, H / m->tp, (size_t)m->cap_M * (H / m->tp), w, M,
+                                                        H, eps, m->xn, s);
         return velo::launch_add_rmsnorm_f16(m->x, m->ybf, w, M, H, eps, m->xn, s);
     };
     auto row_split = [&](const uint8_t* w, const __half* in, int K, int phase) -> int32_t {
         VELO_CUDA_TRY(velo::prof_mark(c, m, phase));
         if (m->tp == 1) return velo::gemm(c, w, in, M, H, K, m->x, H, velo::kEpiAddF32);
+        if (velo::use_ce_sum(m)) {
+            int32_t r = velo::ce_gemm(c, m, s, w, in, M, K, 0);
+            if (r) return r;
+            VELO_CUDA_TRY(velo::prof_mark(c, m, VELO_PHASE_ALLREDUCE));
+            pending = true;
+            return velo::ce_sum(c, m, s, M, 0, 0);
+        }
         if (velo::use_fused_sum(m)) {
             // the GEMM pushes the partial to the column blocks' owners; the phase
             // after it is the gather kernel
@@ -1678,6 +1758,7 @@ int32_t velo_cuda_tp_sum_path(velo_cuda_ctx* c, int32_t* path) {
     if (!path) return fail(VELO_ERR_INVALID_ARGUMENT, "tp_sum_path: null output");
     const Model* m = c->model;
     *path = m->tp < 2 || m->f32         ? VELO_TP_SUM_NONE
+            : velo::use_ce_sum(m)    ? VELO_TP_SUM_CE
             : velo::use_fused_sum(m) ? VELO_TP_SUM_FUSED
             : velo::use_peer_sum(m)  ? VELO_TP_SUM_PEER
                                      : VELO_TP_SUM_NCCL;

@@ -422,11 +422,11 @@ class Context:
         return {n: float(ms[i]) for i, n in enumerate(PHASES)}, int(steps.value)
 
     def tp_sum_path(self):
-        """'none', 'nccl', 'peer' or 'fused': how the tensor-parallel partial
-        sums run."""
+        """'none', 'nccl', 'peer', 'fused' or 'ce': how the tensor-parallel
+        partial sums run."""
         v = _I32(0)
         check(lib().velo_cuda_tp_sum_path(self._h, ctypes.byref(v)))
-        return ("none", "nccl", "peer", "fused")[v.value]
+        return ("none", "nccl", "peer", "fused", "ce")[v.value]
 
     def verify_step(self, slots, ctx_len, tokens, parents, temperature=0.0, draft_logits=None,
                     uniforms=None, commit=True, want_logits=False, n_vocab=None):
