@@ -71,6 +71,8 @@ bool peer_tp_supported(int tp);
 // call counters of the two phases.
 constexpr int kCeSlot0 = 2;
 constexpr int kCePhaseSlabs = 0, kCePhaseSums = 1;
+static_assert(kCeSlot0 + 2 <= 4, "the copy-engine slots lie in the 4-slot flag block");
+static_assert(16 + 2 <= kPeerSlotWords, "a slot holds the copy-engine entries and counters");
 
 // One warp: count this call on `phase` (a device counter, so graphs stay in
 // step) and publish the count to every rank's entry `rank` of the phase, with a
