@@ -4,7 +4,7 @@
 // Replaces, for o_proj and down_proj, the reference's CPU all-reduce
 // (LlamaTensorParallelModel::all_reduce_sum_and_add, src/metal/tp_model.rs:199-277)
 // and NCCL's ring in this build.  Every rank's buffers are mapped into every other
-// rank's address space (CUDA IPC).  Two forms:
+// rank's address space (CUDA IPC).  Three forms:
 //   fused (peer_gather_kernel): the row-split GEMM's epilogue already stored column
 //     block r of its partial into rank r's receive area, overlapping the transfer
 //     with the GEMM's tiles; rank r adds its block's tp slabs (local HBM) in rank
@@ -12,7 +12,11 @@
 //   unfused (peer_allreduce_kernel): rank r owns chunk r of the rows, loads that
 //     chunk from all tp buffers (its own from HBM, the others over NVLink), adds
 //     them in rank order in f32 and stores the bf16 sum into all tp buffers.
-// Both add the same bf16 partials in the same order: identical results.
+//   copy engines (ce_sum_kernel with ce_signal_kernel / ce_wait_kernel): the data
+//     crosses NVLink as cudaMemcpyAsync copies issued by the host; one-warp
+//     kernels publish and await each phase's completion and rank r adds its tp
+//     slabs locally.
+// All add the same bf16 partials in the same order: identical results.
 //
 // Ordering: a cross-rank entry barrier (each rank publishes an epoch into every
 // rank's flag block with a system-scope release, after its partial is complete,
@@ -22,9 +26,10 @@
 // every rank after its stores) guarantees every sum has landed before the kernel
 // returns and the next kernel on the stream reads the buffer.  Every wait is
 // bounded by the global timer (2 s): a rank that never arrives makes the others
-// record an error and return instead of spinning forever.  The grid is fixed
-// (kPeerGrid CTAs of 128 threads, under 14 K registers and no dynamic shared
-// memory, so that a CTA fits on an SM beside a GEMM CTA of the other stream);
+// record an error and return instead of spinning forever.  The grid of the first
+// two forms is fixed (kPeerGrid CTAs of 128 threads, at most 72 registers each and
+// no dynamic shared memory, so that a CTA fits on an SM beside a GEMM or attention
+// CTA of the other stream);
 // each CTA counts its own calls in its rank's flag block, so the epochs need no
 // host state and every rank's CTAs agree on them.
 #include "kernels/tp_allreduce.h"
